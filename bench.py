@@ -1,0 +1,396 @@
+"""Benchmark: packed 2-bit KIVI decode attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload per GPU (config 2): 16 sequences, 28 query / 4 KV heads, head_dim 128,
+8192 KIVI 2-bit (group 32) packed tokens + 128 bf16 residual tokens, K,V ~ N(0,1)
+with 4 key outlier channels x10 (seeded synthetic data).  One step = one decode
+token for every sequence = one launch of the decode kernel.  Inputs (the packed
+caches) are 55 MB per replica, below the 126 MB L2, so steps rotate over 8
+independent cache replicas (438 MB) and no step finds its cache in L2.
+
+Multi-GPU (torchrun): requests are batch-partitioned -- every rank decodes its
+own 16 sequences, no collective in the timed loop (weak scaling); the step time
+is the max over ranks.
+
+Reported: value = decode tokens/s (whole job), e2e = the same through the public
+API with the query copied from pinned host memory and the output read back every
+step, roofline of the decode kernel against the measured HBM copy bandwidth,
+and the CPU baseline (the oracle port of the reference algorithm).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BATCH = 16
+TOKENS = 8192
+RESIDUAL = 128
+Q_HEADS = 28
+KV_HEADS = 4
+HEAD_DIM = 128
+BITS = 2
+GROUP = 32
+REPLICAS = 8
+METRIC = "packed-KV attention HBM GB/s & decode tokens/s/GPU at 1/2/4/8 B200"
+
+
+def algorithmic_bytes_per_pair() -> int:
+    """Bytes one decode step must move per (sequence, KV head)."""
+
+    codes = 2 * TOKENS * HEAD_DIM * BITS // 8
+    key_stats = (TOKENS // GROUP) * HEAD_DIM * 2 * 2
+    value_stats = TOKENS * (HEAD_DIM // GROUP) * 2 * 2
+    residual = RESIDUAL * HEAD_DIM * 2 * 2
+    q_and_o = (Q_HEADS // KV_HEADS) * HEAD_DIM * 2 * 2
+    return codes + key_stats + value_stats + residual + q_and_o
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as handle:
+            return float(json.load(handle)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic() -> float | None:
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+
+    path = os.path.join(ROOT, "profiles", "decode_config2_traffic.json")
+    try:
+        with open(path) as handle:
+            return float(json.load(handle)["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+
+            def loop():
+                while not self._stop.is_set():
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                    mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    for name, bit in self.REASONS.items():
+                        if mask & bit:
+                            self.reasons.add(name)
+                    time.sleep(0.02)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+        except Exception:  # NVML missing: report no clocks rather than fail the run
+            self._thread = None
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def cpu_oracle_sample(seq_seed: int) -> tuple[float, int]:
+    """Decode one sequence of config 2 with the oracle port (dequantize every
+    step, float64 attention): returns (seconds, tokens decoded)."""
+
+    import numpy as np
+    import torch
+
+    from oracle import attention, kivi
+    from unicache_b200.synthetic import make_kv, make_query
+
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    key, value = make_kv(TOKENS + RESIDUAL, KV_HEADS, HEAD_DIM, seed=seq_seed)
+    query = make_query(1, Q_HEADS, HEAD_DIM, seed=seq_seed)
+    k = key.float().numpy()
+    v = value.float().numpy()
+    q = query.float().numpy()
+    cache = kivi.packed_from_dense(k, v, "bfloat16", k_bits=BITS, v_bits=BITS, group_size=GROUP,
+                                   residual_length=RESIDUAL)
+    ctx = threadpool_limits(limits=1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    try:
+        start = time.perf_counter()
+        rk, rv = kivi.packed_dequantize(cache)
+        attention.attention_summary(q, rk, rv)
+        elapsed = time.perf_counter() - start
+    finally:
+        if ctx:
+            ctx.__exit__(None, None, None)
+    _ = np
+    _ = torch
+    return elapsed, 1
+
+
+def run_reference(args) -> None:
+    """The reference algorithm's CPU path (the oracle port) on the host cores."""
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    per_step = max(cores, 4)
+    ctx = mp.get_context("spawn")
+    times = []
+    with ctx.Pool(processes=cores) as pool:
+        for _ in range(args.warmup):
+            pool.map(cpu_oracle_sample, range(per_step))
+        for step in range(args.steps):
+            start = time.perf_counter()
+            pool.map(cpu_oracle_sample, [10_000 + step * per_step + i for i in range(per_step)])
+            times.append(time.perf_counter() - start)
+    total = sum(times)
+    value = per_step * args.steps / total
+    sample = f"{per_step} config-2 sequences per step ({TOKENS}+{RESIDUAL} tokens, 28/4 heads), one decode token each"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config2: packed KIVI 2-bit G32 decode, B=16, T=8192+128, 28/4 heads, D=128",
+                   "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from unicache_b200 import PackedKIVICache, PhysicalDecodeBatch, kernels
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+
+    # ---- build REPLICAS x BATCH packed caches (generated on the GPU, seeded per rank)
+    gen = torch.Generator(device=device).manual_seed(1234 + 7919 * rank)
+    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(device)
+    replicas = []
+    pack_times = []
+    for r in range(REPLICAS):
+        seqs = []
+        dense = []
+        for _ in range(BATCH):
+            k = torch.randn(TOKENS + RESIDUAL, KV_HEADS, HEAD_DIM, generator=gen, device=device)
+            k[:, :, outlier] *= 10.0
+            v = torch.randn(TOKENS + RESIDUAL, KV_HEADS, HEAD_DIM, generator=gen, device=device)
+            dense.append((k.to(torch.bfloat16), v.to(torch.bfloat16)))
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for k, v in dense:
+            seqs.append([PackedKIVICache.from_dense(k, v, logical_token_ids=torch.arange(TOKENS + RESIDUAL, device=device),
+                                                    token_type_id=3, k_bits=BITS, v_bits=BITS, group_size=GROUP,
+                                                    residual_length=RESIDUAL)])
+        stop.record()
+        torch.cuda.synchronize()
+        pack_times.append(start.elapsed_time(stop) / 1000.0)
+        del dense
+        replicas.append(PhysicalDecodeBatch(seqs, num_kv_heads=KV_HEADS, head_dim=HEAD_DIM))
+    torch.cuda.empty_cache()
+    query = (torch.randn(BATCH, Q_HEADS, HEAD_DIM, generator=gen, device=device)).to(torch.bfloat16)
+    out = torch.empty_like(query)
+    lse = torch.empty(BATCH, Q_HEADS, device=device, dtype=torch.float32)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timed loop
+    for i in range(args.warmup):
+        replicas[i % REPLICAS](query, out=out, lse=lse)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        t0.record()
+        for i in range(args.steps):
+            events[i][0].record()
+            replicas[i % REPLICAS](query, out=out, lse=lse)
+            events[i][1].record()
+        t1.record()
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = t0.elapsed_time(t1) / 1000.0
+    kernel_s = [a.elapsed_time(b) / 1000.0 for a, b in events]
+    status = kernels.device_status()
+
+    # ---- end-to-end through the public API with host buffers
+    host_q = torch.empty_like(query, device="cpu").pin_memory()
+    host_q.copy_(query.cpu())
+    host_o = torch.empty_like(out, device="cpu").pin_memory()
+    host_l = torch.empty_like(lse, device="cpu").pin_memory()
+    dev_q = torch.empty_like(query)
+    for i in range(args.warmup):
+        dev_q.copy_(host_q, non_blocking=True)
+        o, l = replicas[i % REPLICAS](dev_q)
+        host_o.copy_(o, non_blocking=True)
+        host_l.copy_(l, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        dev_q.copy_(host_q, non_blocking=True)
+        o, l = replicas[i % REPLICAS](dev_q)
+        host_o.copy_(o, non_blocking=True)
+        host_l.copy_(l, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_elapsed = e0.elapsed_time(e1) / 1000.0
+
+    if world > 1:
+        t = torch.tensor([elapsed, e2e_elapsed, float(status)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, e2e_elapsed, status = float(t[0]), float(t[1]), int(t[2])
+
+    if rank == 0:
+        tokens = BATCH * world * args.steps
+        value = tokens / elapsed
+        step_bytes = algorithmic_bytes_per_pair() * BATCH * KV_HEADS
+        mean_kernel = statistics.mean(kernel_s)
+        achieved = step_bytes / mean_kernel / 1e9
+        peak, peak_kind = measured_peaks()
+        pack_read = BATCH * 2 * (TOKENS + RESIDUAL) * KV_HEADS * HEAD_DIM * 2
+        cpu_s, cpu_tokens = cpu_oracle_sample(4242)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": 1000.0 * elapsed / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "config2: packed KIVI 2-bit G32 decode, 16 seqs/GPU, T=8192+128 bf16 residual, "
+                            "28/4 heads, D=128",
+                "global_batch": BATCH * world,
+                "seq_len": TOKENS + RESIDUAL,
+                "parallelism": f"batch-partitioned x{world}",
+                "l2": f"steps rotate over {REPLICAS} cache replicas ({REPLICAS * step_bytes / 1e6:.0f} MB > 126 MB L2)",
+            },
+            "hbm_gbs": achieved,
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "peak_source": peak_kind,
+                "traffic": ncu_traffic(),
+                "algorithmic_bytes_per_launch": step_bytes,
+                "kernel_ms": 1000.0 * mean_kernel,
+            },
+            "pack": {"seconds_per_16_seqs": statistics.median(pack_times),
+                     "input_gbs": pack_read / statistics.median(pack_times) / 1e9},
+            "e2e": {"value": tokens / e2e_elapsed, "unit": "tokens/s",
+                    "h2d_bytes_per_step": query.numel() * query.element_size(),
+                    "d2h_bytes_per_step": out.numel() * out.element_size() + lse.numel() * lse.element_size()},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "device_status": status,
+            "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+                             "sample": "one config-2 sequence, one decode token (dequantize + float64 attention)"},
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=256)
+    parser.add_argument("--warmup", type=int, default=16)
+    parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    args = parser.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,248 @@
+/*
+ * unicache_b200 -- C ABI of the B200 (sm_100a) physical-engine hot path of
+ * UniCache (Superone77/UniCache): KIVI quantize/pack, dequantize, packed-KV
+ * decode attention, LSE merge, H2O scoring/selection/compaction and dense-cache
+ * compaction.
+ *
+ * Conventions
+ *  - Every pointer argument named *_dev is device memory; sizes and strides are
+ *    in elements unless the name says bytes.  No entry point allocates memory;
+ *    workspaces are passed in.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Return value: UCB_OK (0) or a negative UCB_ERR_* code; ucb_last_error()
+ *    returns the message of the last failure on the calling thread.
+ *  - Layout "b200" of a packed KIVI segment (per layer, per sequence):
+ *        key_code    int32 [H, T/fk, D]   (uint8 [H, T, D] for 8-bit)
+ *        key_scale   stat  [H, T/G, D]    key_minimum same
+ *        value_code  int32 [H, T, D/fv]   (uint8 [H, T, D] for 8-bit)
+ *        value_scale stat  [H, T, D/G]    value_minimum same
+ *    with f = 32/bits codes per word, code i of a word in bits [i*b, i*b+b).
+ *    It is the reference layout of unicache/storage/physical.py:228-332 with its
+ *    first two axes swapped; the int32 words are identical.
+ */
+#ifndef UNICACHE_B200_H
+#define UNICACHE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define UCB_API __attribute__((visibility("default")))
+#else
+#define UCB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UCB_OK 0
+#define UCB_ERR_INVALID (-1)     /* bad argument: shape, size, alignment    */
+#define UCB_ERR_UNSUPPORTED (-2) /* valid request this library does not do  */
+#define UCB_ERR_CUDA (-3)        /* CUDA runtime / launch failure           */
+#define UCB_ERR_DEVICE (-4)      /* a kernel raised its device error flag   */
+
+#define UCB_BF16 0
+#define UCB_F16 1
+#define UCB_F32 2
+
+/* Message of the last failed call on this thread ("" if none). */
+UCB_API const char* ucb_last_error(void);
+
+/* ABI version (major*100 + minor). */
+UCB_API int ucb_version(void);
+
+/* Read and clear the device error word of the current device.  *flags gets the
+ * bits kernels set instead of trapping (1 = a bounded wait timed out,
+ * 2 = an invalid descriptor was met).  Synchronises `stream`. */
+UCB_API int ucb_device_status(unsigned int* flags, void* stream);
+
+/* ------------------------------------------------------------------ KIVI pack
+ * Replaces the quantize-and-pack step of PackedKIVICache.from_dense
+ * (unicache/storage/physical.py:291-304 -> _quantize_grouped :139-175 and
+ * _pack_codes :66-85; on CUDA the KIVI Triton packer, kivi_cuda.py:157-190).
+ * Bit-exact with the reference CPU path: per group mn/mx in fp32,
+ * scale = max((mx-mn)/(2^b-1), FLT_EPSILON), code = clamp(rint((x-mn)/scale)),
+ * scale and minimum stored in the input dtype.
+ *
+ * x_dev: [tokens, heads, head_dim] with strides (stride_token, stride_head, 1).
+ * Key: groups of group_size consecutive tokens per (head, channel);
+ *      tokens % group_size == 0.  Outputs in the b200 layout above.
+ * Value: groups of group_size consecutive channels per (token, head);
+ *      head_dim % group_size == 0.
+ * bits in {2,4,8}; group_size % (32/bits) == 0 for 2/4-bit keys;
+ * head_dim in {64, 128}. */
+UCB_API int ucb_kivi_pack_key(const void* x_dev, int dtype, int64_t tokens, int64_t heads, int64_t head_dim,
+                      int64_t stride_token, int64_t stride_head, int bits, int group_size,
+                      void* codes_dev, void* scale_dev, void* minimum_dev, void* stream);
+UCB_API int ucb_kivi_pack_value(const void* x_dev, int dtype, int64_t tokens, int64_t heads, int64_t head_dim,
+                        int64_t stride_token, int64_t stride_head, int bits, int group_size,
+                        void* codes_dev, void* scale_dev, void* minimum_dev, void* stream);
+
+/* ------------------------------------------------------------------ KIVI dequantize
+ * Replaces PackedKIVICache.dequantize (physical.py:379-423 -> _dequantize_grouped
+ * :178-201) and dequantize_kivi_chunk (unicache/storage/kivi_cuda.py:58-93 ->
+ * kivi_triton.py:690-770).  Bit-exact: out = round_dtype(fp32(code*scale) + minimum).
+ * Dequantizes quantized tokens [token_begin, token_end) of one segment into
+ * out_dev rows [0, token_end-token_begin) with strides (out_stride_token,
+ * out_stride_head, 1); out_dtype may differ from stat_dtype. */
+UCB_API int ucb_kivi_dequant_key(const void* codes_dev, const void* scale_dev, const void* minimum_dev,
+                         int stat_dtype, int64_t quantized_tokens, int64_t heads, int64_t head_dim,
+                         int bits, int group_size, int64_t token_begin, int64_t token_end,
+                         void* out_dev, int out_dtype, int64_t out_stride_token,
+                         int64_t out_stride_head, void* stream);
+UCB_API int ucb_kivi_dequant_value(const void* codes_dev, const void* scale_dev, const void* minimum_dev,
+                           int stat_dtype, int64_t quantized_tokens, int64_t heads, int64_t head_dim,
+                           int bits, int group_size, int64_t token_begin, int64_t token_end,
+                           void* out_dev, int out_dtype, int64_t out_stride_token,
+                           int64_t out_stride_head, void* stream);
+
+/* ------------------------------------------------------------------ fake quantization
+ * Replaces asymmetric_fake_quant / kivi_fake_quant_key / kivi_fake_quant_value
+ * (unicache/operators/builtin.py:31-65).  The tensor is viewed as
+ * [outer, length, inner] (contiguous) and quantized in groups of group_size
+ * along `length` (a partial last group allowed); scale = max(mx-mn, eps)/(2^b-1).
+ * Bit-exact. bits in {2,3,4,8}. out_dev may equal x_dev. */
+UCB_API int ucb_fake_quant(const void* x_dev, void* out_dev, int dtype, int64_t outer, int64_t length,
+                   int64_t inner, int bits, int group_size, void* stream);
+
+/* ------------------------------------------------------------------ decode attention
+ * Replaces single-token attention over a sequence's [dense ‖ physical segments]:
+ * packed_kivi_attention_parts + torch softmax + apply_value (kivi_cuda.py:238-329,
+ * adapters/bagel.py:1201-1297), packed_kivi_quantized_attention_summary
+ * (kivi_cuda.py:96-120) for q_len == 1, and _run_fused_h2o_attention
+ * (bagel.py:1860-1901) without its per-step torch.cat.
+ *
+ * A decode batch is a set of (sequence, kv head) pairs, each owning spans:
+ *  kind 0 (packed KIVI):  key_code..value_minimum point at this head's slice of a
+ *                         b200-layout segment; `tokens` quantized tokens.
+ *  kind 1 (dense):        key/value rows of `tokens` tokens for this head,
+ *                         row i at key + i*key_stride (elements, bf16).
+ * Items split spans into token ranges; one CTA per item.  Every item writes a
+ * partial (max, sum, out) to `partials_dev`; the last item of a pair merges its
+ * pair's partials into out_dev [seq, q_head, :] (bf16) and lse_dev [seq, q_head]
+ * (natural-log LSE, fp32; may be NULL).
+ * Workspaces: partials_dev >= ucb_decode_partial_bytes(head_dim) * num_partials
+ * bytes; counters_dev >= num_pairs int32 zeroed once before first use (the
+ * kernel leaves them zero).  Calls sharing counters must not overlap. */
+typedef struct ucb_span {
+  const void* key_code;      /* packed: int32/uint8 codes; dense: key rows    */
+  const void* key_scale;     /* packed only                                   */
+  const void* key_minimum;   /* packed only                                   */
+  const void* value_code;    /* packed: codes; dense: value rows              */
+  const void* value_scale;   /* packed only                                   */
+  const void* value_minimum; /* packed only                                   */
+  int64_t key_stride;        /* dense only: elements between key rows         */
+  int64_t value_stride;      /* dense only                                    */
+  int32_t kind;              /* 0 packed, 1 dense                             */
+  int32_t tokens;
+} ucb_span;
+
+typedef struct ucb_decode_item {
+  int32_t span;
+  int32_t token_begin;
+  int32_t token_end;
+  int32_t pair;
+  int32_t partial;
+  int32_t reserved[3];
+} ucb_decode_item;
+
+typedef struct ucb_decode_pair {
+  int32_t seq;
+  int32_t kv_head;
+  int32_t partial_begin;
+  int32_t partial_count;
+} ucb_decode_pair;
+
+UCB_API int64_t ucb_decode_partial_bytes(int head_dim);
+
+/* query_dev: bf16 rows [seq, q_head, head_dim], row (seq, h) at
+ * query_dev + seq*query_stride + h*head_dim.  out likewise with out_stride.
+ * All packed spans of one call share (k_bits, v_bits, group_size, stat_dtype).
+ * softmax_scale: multiplier of q.k (1/sqrt(head_dim) in the reference). */
+UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, int num_q_heads, int num_kv_heads,
+                         int head_dim, const ucb_span* spans_dev, const ucb_decode_item* items_dev,
+                         int num_items, const ucb_decode_pair* pairs_dev, int num_pairs, int k_bits,
+                         int v_bits, int group_size, int stat_dtype, float softmax_scale,
+                         void* partials_dev, int* counters_dev, void* out_dev, int64_t out_stride,
+                         float* lse_dev, void* stream);
+
+/* CTAs of ucb_decode_attention that fit on the current device at once. */
+UCB_API int ucb_decode_slots(int k_bits, int v_bits, int group_size, int stat_dtype, int* slots);
+
+/* ------------------------------------------------------------------ LSE merge
+ * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).
+ * n summaries, summary i: out_ptrs[i] -> [rows, heads, head_dim] (dtype),
+ * lse_ptrs[i] -> fp32 [heads, rows].  Pointer arrays are HOST arrays.
+ * Writes out_dev [rows, heads, head_dim] (dtype) and lse_out_dev fp32
+ * [heads, rows]. n <= 64. */
+UCB_API int ucb_lse_merge(int n, const void* const* out_ptrs, const float* const* lse_ptrs, int dtype,
+                  int64_t rows, int64_t heads, int64_t head_dim, void* out_dev, float* lse_out_dev,
+                  void* stream);
+
+/* Merge per-rank decode partials gathered from several GPUs (sequence split):
+ * partials_dev holds n_parts blocks of ucb_decode_partial_bytes(head_dim) bytes per
+ * (pair); layout [part][pair].  Writes out/lse like ucb_decode_attention. */
+UCB_API int ucb_merge_partials(const void* partials_dev, int n_parts, const ucb_decode_pair* pairs_dev,
+                       int num_pairs, int num_q_heads, int num_kv_heads, int head_dim, void* out_dev,
+                       int64_t out_stride, float* lse_dev, void* stream);
+
+/* ------------------------------------------------------------------ H2O
+ * Per-KV-head heavy-hitter selection (GQAH2OCache.from_dense / trim,
+ * unicache/storage/physical.py:508-532 and :624-649): for each of `heads` rows
+ * of scores_dev (fp32, row stride score_stride), keep the heavy_k largest scores
+ * among the first history_end entries (ties: lower index first) in ascending
+ * index order, followed by the recent window [tokens-recent, tokens).
+ * index_out_dev: int64 [heads, heavy_k + recent]. tokens <= 1<<24. */
+UCB_API int ucb_h2o_select(const float* scores_dev, int64_t score_stride, int heads, int64_t tokens,
+                   int64_t history_end, int64_t heavy_k, int64_t recent, int64_t* index_out_dev,
+                   void* stream);
+
+/* Gather rows by per-head indices (physical.py:533-542 and :650-654):
+ * src row (h, i) at src + h*src_stride_head + i*src_stride_token (elements of
+ * elem_bytes each row of row_elems), dst [heads, keep, row_elems] contiguous.
+ * Used for K/V (row_elems = head_dim), logical ids (int64, row_elems = 1) and
+ * scores (fp32, row_elems = 1). */
+UCB_API int ucb_gather_rows(const void* src_dev, int64_t src_stride_head, int64_t src_stride_token,
+                    int64_t row_elems, int elem_bytes, const int64_t* index_dev, int heads,
+                    int64_t keep, void* dst_dev, void* stream);
+
+/* H2O score accumulation from materialised probabilities
+ * (physical.py:598-610, unicache/operators/physical.py:63-65):
+ * probs_dev fp32/bf16 [q_heads, queries, tokens] -> scores_dev[kv, t] (+)=
+ * sum over the kv head's query heads and all queries.  accumulate=0 overwrites. */
+UCB_API int ucb_h2o_accumulate_probs(const void* probs_dev, int dtype, int q_heads, int64_t queries,
+                             int64_t tokens, int kv_heads, float* scores_dev, int accumulate,
+                             void* stream);
+
+/* Fused H2O scoring without materialised probabilities (adapters/bagel.py:1845-1856):
+ * scores[kv, t] (+)= sum_{g, q} exp(scale * q_{kv*G+g, q} . k_t - lse[kv*G+g, q]).
+ * query_dev bf16 [queries, q_heads, head_dim]; key rows bf16, row (t, kv) at
+ * key_dev + t*key_stride_token + kv*key_stride_head; lse_dev fp32 [q_heads, queries]
+ * (natural log). */
+UCB_API int ucb_h2o_scores_from_lse(const void* query_dev, int64_t queries, int q_heads, const void* key_dev,
+                            int64_t key_stride_token, int64_t key_stride_head, int64_t tokens,
+                            int kv_heads, int head_dim, const float* lse_dev, float softmax_scale,
+                            float* scores_dev, int accumulate, void* stream);
+
+/* ------------------------------------------------------------------ dense compaction
+ * Replaces TensorCacheStorageBackend.compact's per-sample boolean gather
+ * (unicache/storage/tensor_backend.py:54-100).  mask_dev uint8 [rows];
+ * rows with mask != 0 are copied in order to dst (row_bytes each, 16-byte
+ * aligned rows), and to types_out (int64) when types_dev is not NULL.
+ * prefix_dev: int64 workspace of rows+1 entries; *kept_host receives the
+ * number of kept rows (synchronises `stream`). */
+UCB_API int ucb_compact_rows(const void* src_dev, int64_t row_bytes, const uint8_t* mask_dev, int64_t rows,
+                     const int64_t* types_dev, void* dst_dev, int64_t* types_out_dev,
+                     int64_t* prefix_dev, int64_t* kept_host, void* stream);
+
+/* ------------------------------------------------------------------ self test
+ * Checks on the current device that mma.sync f16 consumes fp16 subnormal
+ * operands exactly (the decode kernel feeds small integer codes as subnormals).
+ * *max_abs_err receives the largest deviation from an fp32 reference. */
+UCB_API int ucb_selftest_mma_subnormal(float* max_abs_err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNICACHE_B200_H */

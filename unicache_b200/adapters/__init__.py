@@ -1,0 +1,17 @@
+"""Attention fast paths over physical segments (counterpart of unicache/adapters)."""
+
+from .attention import (
+    PhysicalDecodeBatch,
+    fused_h2o_decode,
+    fused_mixed_decode,
+    long_query_attention_summary,
+    merge_attention_summaries,
+)
+
+__all__ = [
+    "PhysicalDecodeBatch",
+    "fused_h2o_decode",
+    "fused_mixed_decode",
+    "long_query_attention_summary",
+    "merge_attention_summaries",
+]

@@ -1,0 +1,505 @@
+"""Tensor-level wrappers over the C ABI (include/unicache_b200.h).
+
+PyTorch only supplies device memory and the current CUDA stream; every
+computation runs in ``libunicache_b200.so``.  All inputs must be CUDA tensors:
+there is no CPU path, and a CPU tensor raises ``RuntimeError`` exactly like the
+reference's fail-closed CUDA backend (unicache/storage/kivi_cuda.py:174-175,
+242-243).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _capi
+from ._capi import UcbDecodeItem, UcbDecodePair, UcbSpan, call
+
+_DTYPE_CODES = {torch.bfloat16: _capi.UCB_BF16, torch.float16: _capi.UCB_F16, torch.float32: _capi.UCB_F32}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}; expected bfloat16, float16 or float32") from None
+
+
+def require_cuda(tensor: torch.Tensor, name: str) -> None:
+    if not isinstance(tensor, torch.Tensor) or tensor.device.type != "cuda":
+        raise RuntimeError(f"{name} must be a CUDA tensor: the b200 backend has no CPU path")
+
+
+def stream_of(tensor: torch.Tensor) -> int:
+    return torch.cuda.current_stream(tensor.device).cuda_stream
+
+
+def ptr(tensor: torch.Tensor | None) -> int | None:
+    return None if tensor is None else tensor.data_ptr()
+
+
+def codes_per_word(bits: int) -> int:
+    return 32 // bits
+
+
+# ---------------------------------------------------------------- KIVI pack / dequant
+def kivi_pack_key(key: torch.Tensor, *, bits: int, group_size: int):
+    """Quantize and pack keys [T, H, D] along tokens -> b200 layout
+    (codes [H, T/f, D] int32 or [H, T, D] uint8; scale/min [H, T/G, D])."""
+
+    require_cuda(key, "key")
+    if key.dim() != 3 or key.stride(2) != 1:
+        raise ValueError("key must be [tokens, heads, head_dim] with unit channel stride")
+    tokens, heads, head_dim = map(int, key.shape)
+    if tokens % group_size:
+        raise ValueError("key tokens must be a multiple of group_size")
+    if bits == 8:
+        codes = torch.empty((heads, tokens, head_dim), device=key.device, dtype=torch.uint8)
+    else:
+        codes = torch.empty((heads, tokens // codes_per_word(bits), head_dim), device=key.device, dtype=torch.int32)
+    scale = torch.empty((heads, tokens // group_size, head_dim), device=key.device, dtype=key.dtype)
+    minimum = torch.empty_like(scale)
+    call("ucb_kivi_pack_key", key.data_ptr(), dtype_code(key.dtype), tokens, heads, head_dim,
+         key.stride(0), key.stride(1), bits, group_size, codes.data_ptr(), scale.data_ptr(),
+         minimum.data_ptr(), stream_of(key))
+    return codes, scale, minimum
+
+
+def kivi_pack_value(value: torch.Tensor, *, bits: int, group_size: int):
+    """Quantize and pack values [T, H, D] along channels -> b200 layout
+    (codes [H, T, D/f] int32 or [H, T, D] uint8; scale/min [H, T, D/G])."""
+
+    require_cuda(value, "value")
+    if value.dim() != 3 or value.stride(2) != 1:
+        raise ValueError("value must be [tokens, heads, head_dim] with unit channel stride")
+    tokens, heads, head_dim = map(int, value.shape)
+    if head_dim % group_size:
+        raise ValueError("value head_dim must be a multiple of group_size")
+    if bits == 8:
+        codes = torch.empty((heads, tokens, head_dim), device=value.device, dtype=torch.uint8)
+    else:
+        codes = torch.empty((heads, tokens, head_dim // codes_per_word(bits)), device=value.device, dtype=torch.int32)
+    scale = torch.empty((heads, tokens, head_dim // group_size), device=value.device, dtype=value.dtype)
+    minimum = torch.empty_like(scale)
+    call("ucb_kivi_pack_value", value.data_ptr(), dtype_code(value.dtype), tokens, heads, head_dim,
+         value.stride(0), value.stride(1), bits, group_size, codes.data_ptr(), scale.data_ptr(),
+         minimum.data_ptr(), stream_of(value))
+    return codes, scale, minimum
+
+
+def kivi_dequant(which: str, codes, scale, minimum, *, bits: int, group_size: int, quantized_tokens: int,
+                 heads: int, head_dim: int, start: int, stop: int, out: torch.Tensor) -> torch.Tensor:
+    """Dequantize tokens [start, stop) into ``out`` rows [0, stop-start) ([N, H, D] view)."""
+
+    require_cuda(codes, "codes")
+    require_cuda(out, "out")
+    if out.dim() != 3 or out.stride(2) != 1 or tuple(out.shape[1:]) != (heads, head_dim):
+        raise ValueError("dequantization output must be [tokens, heads, head_dim] with unit channel stride")
+    if int(out.shape[0]) < stop - start:
+        raise ValueError("dequantization output has too few rows")
+    name = "ucb_kivi_dequant_key" if which == "key" else "ucb_kivi_dequant_value"
+    call(name, codes.data_ptr(), scale.data_ptr(), minimum.data_ptr(), dtype_code(scale.dtype), quantized_tokens,
+         heads, head_dim, bits, group_size, start, stop, out.data_ptr(), dtype_code(out.dtype), out.stride(0),
+         out.stride(1), stream_of(out))
+    return out
+
+
+def fake_quant(data: torch.Tensor, *, bits: int, dim: int, group_size: int) -> torch.Tensor:
+    """asymmetric_fake_quant (unicache/operators/builtin.py:31-53) on the GPU."""
+
+    require_cuda(data, "data")
+    if data.numel() == 0 or bits >= 16:
+        return data
+    if bits not in (2, 3, 4, 8):
+        raise ValueError(f"Unsupported fake quant bits: {bits}")
+    x = data.contiguous()
+    dim = dim if dim >= 0 else x.dim() + dim
+    outer = math.prod(x.shape[:dim])
+    length = int(x.shape[dim])
+    inner = math.prod(x.shape[dim + 1:])
+    out = torch.empty_like(x)
+    call("ucb_fake_quant", x.data_ptr(), out.data_ptr(), dtype_code(x.dtype), outer, length, inner, bits,
+         int(group_size), stream_of(x))
+    return out
+
+
+# ---------------------------------------------------------------- LSE merge
+def lse_merge(summaries: list[tuple[torch.Tensor, torch.Tensor]]):
+    """merge_attention_summaries (unicache/adapters/bagel.py:57-72): summaries of
+    (out [rows, heads, D], lse [heads, rows] fp32) -> merged (out, lse)."""
+
+    if not summaries:
+        raise ValueError("At least one attention summary is required")
+    o0, _ = summaries[0]
+    require_cuda(o0, "summary output")
+    rows, heads, head_dim = map(int, o0.shape)
+    outs, lses = [], []
+    for o, lse in summaries:
+        if tuple(o.shape) != (rows, heads, head_dim) or tuple(lse.shape) != (heads, rows):
+            raise ValueError("attention summaries must share [rows, heads, head_dim] / [heads, rows] shapes")
+        outs.append(o.to(o0.dtype).contiguous())
+        lses.append(lse.float().contiguous())
+    merged = torch.empty_like(outs[0])
+    total = torch.empty((heads, rows), device=o0.device, dtype=torch.float32)
+    n = len(outs)
+    optrs = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    lptrs = (ctypes.c_void_p * n)(*[l.data_ptr() for l in lses])
+    call("ucb_lse_merge", n, optrs, lptrs, dtype_code(o0.dtype), rows, heads, head_dim, merged.data_ptr(),
+         total.data_ptr(), stream_of(o0))
+    return merged, total
+
+
+# ---------------------------------------------------------------- H2O
+def h2o_select(scores: torch.Tensor, *, history_end: int, heavy_k: int, recent: int) -> torch.Tensor:
+    """Per-row heavy top-k (ascending indices) followed by the recent window
+    (unicache/storage/physical.py:508-532).  scores: fp32 [H, T]."""
+
+    require_cuda(scores, "scores")
+    if scores.dim() != 2 or scores.dtype != torch.float32 or scores.stride(1) != 1:
+        raise ValueError("scores must be float32 [heads, tokens] with unit token stride")
+    heads, tokens = map(int, scores.shape)
+    index = torch.empty((heads, heavy_k + recent), device=scores.device, dtype=torch.int64)
+    call("ucb_h2o_select", scores.data_ptr(), scores.stride(0), heads, tokens, history_end, heavy_k, recent,
+         index.data_ptr(), stream_of(scores))
+    return index
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor, *, head_stride: int, token_stride: int,
+                row_elems: int, out: torch.Tensor) -> torch.Tensor:
+    """out[h, j, :] = src[h*head_stride + index[h, j]*token_stride : ... + row_elems]."""
+
+    require_cuda(src, "src")
+    heads, keep = map(int, index.shape)
+    call("ucb_gather_rows", src.data_ptr(), head_stride, token_stride, row_elems, src.element_size(),
+         index.data_ptr(), heads, keep, out.data_ptr(), stream_of(src))
+    return out
+
+
+def accumulate_probs(probs: torch.Tensor, kv_heads: int, scores: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-KV-head received attention (unicache/operators/physical.py:63-65):
+    probs [Hq, Lq, N] -> [Hkv, N]; added into ``scores`` when given."""
+
+    require_cuda(probs, "probabilities")
+    if probs.dim() != 3:
+        raise ValueError("H2O probabilities must be [query_heads, queries, tokens]")
+    q_heads, queries, tokens = map(int, probs.shape)
+    if q_heads % kv_heads:
+        raise ValueError("Query heads must be divisible by KV heads for GQA H2O")
+    probs = probs.contiguous()
+    accumulate = scores is not None
+    if scores is None:
+        scores = torch.empty((kv_heads, tokens), device=probs.device, dtype=torch.float32)
+    call("ucb_h2o_accumulate_probs", probs.data_ptr(), dtype_code(probs.dtype), q_heads, queries, tokens,
+         kv_heads, scores.data_ptr(), int(accumulate), stream_of(probs))
+    return scores
+
+
+def scores_from_lse(query: torch.Tensor, key: torch.Tensor, lse: torch.Tensor, *, kv_heads: int,
+                    softmax_scale: float, scores: torch.Tensor | None = None) -> torch.Tensor:
+    """H2O scores without materialised probabilities: query [Lq, Hq, D] bf16,
+    key [N, Hkv, D] (any token/head strides), lse fp32 [Hq, Lq]."""
+
+    require_cuda(query, "query")
+    q = query.contiguous()
+    queries, q_heads, head_dim = map(int, q.shape)
+    tokens = int(key.shape[0])
+    accumulate = scores is not None
+    if scores is None:
+        scores = torch.empty((kv_heads, tokens), device=q.device, dtype=torch.float32)
+    call("ucb_h2o_scores_from_lse", q.data_ptr(), queries, q_heads, key.data_ptr(), key.stride(0), key.stride(1),
+         tokens, kv_heads, head_dim, lse.contiguous().data_ptr(), float(softmax_scale), scores.data_ptr(),
+         int(accumulate), stream_of(q))
+    return scores
+
+
+# ---------------------------------------------------------------- dense compaction
+def compact_rows(src: torch.Tensor, mask: torch.Tensor, types: torch.Tensor | None = None):
+    """Keep rows of ``src`` (first axis) where ``mask`` is true, in order."""
+
+    require_cuda(src, "src")
+    rows = int(src.shape[0])
+    src = src.contiguous()
+    m = mask.to(device=src.device, dtype=torch.uint8).contiguous()
+    prefix = torch.empty(rows + 1, device=src.device, dtype=torch.int64)
+    dst = torch.empty_like(src)
+    types_out = None
+    if types is not None:
+        types = types.to(device=src.device, dtype=torch.int64).contiguous()
+        types_out = torch.empty_like(types)
+    kept = ctypes.c_int64(0)
+    row_bytes = src[0].numel() * src.element_size() if rows else 1
+    call("ucb_compact_rows", src.data_ptr(), row_bytes, m.data_ptr(), rows, ptr(types), dst.data_ptr(),
+         ptr(types_out), prefix.data_ptr(), ctypes.byref(kept), stream_of(src))
+    n = int(kept.value)
+    return dst[:n], (types_out[:n] if types_out is not None else None)
+
+
+# ---------------------------------------------------------------- decode attention
+PACKED_STAGE = 64
+DENSE_STAGE = 16
+
+
+@dataclass
+class DenseRows:
+    """A dense bf16 K/V span for one KV head: row i at base + i*stride."""
+
+    key: torch.Tensor
+    value: torch.Tensor
+    key_offset: int
+    value_offset: int
+    key_stride: int
+    value_stride: int
+    tokens: int
+
+
+@dataclass
+class DecodePlan:
+    """Device tables of a decode batch over immutable (frozen) physical caches.
+
+    Built once per cache layout and reused for every decode step: pairs are
+    (sequence, KV head), spans are a pair's packed or dense token ranges and
+    items are the CTA work units (see include/unicache_b200.h).
+    """
+
+    device: torch.device
+    num_seqs: int
+    num_kv_heads: int
+    head_dim: int
+    k_bits: int
+    v_bits: int
+    group_size: int
+    spans: torch.Tensor
+    items: torch.Tensor
+    pairs: torch.Tensor
+    num_items: int
+    num_pairs: int
+    partials: torch.Tensor
+    counters: torch.Tensor
+    keepalive: list = field(default_factory=list)
+    bytes_per_step: int = 0
+
+    def run(self, query: torch.Tensor, *, softmax_scale: float | None = None, out: torch.Tensor | None = None,
+            lse: torch.Tensor | None = None):
+        """query [B, Hq, D] bf16 -> (out [B, Hq, D] bf16, lse [B, Hq] fp32)."""
+
+        require_cuda(query, "query")
+        if query.dtype != torch.bfloat16:
+            raise ValueError("decode attention expects a bfloat16 query")
+        if query.dim() != 3 or int(query.shape[0]) != self.num_seqs or int(query.shape[2]) != self.head_dim:
+            raise ValueError("query must be [num_seqs, q_heads, head_dim]")
+        if query.stride(2) != 1 or query.stride(1) != self.head_dim:
+            query = query.contiguous()
+        q_heads = int(query.shape[1])
+        if q_heads % self.num_kv_heads:
+            raise ValueError("Query heads must be divisible by KV heads")
+        scale = (1.0 / math.sqrt(self.head_dim)) if softmax_scale is None else float(softmax_scale)
+        if out is None:
+            out = torch.empty_like(query)
+        if lse is None:
+            lse = torch.empty((self.num_seqs, q_heads), device=query.device, dtype=torch.float32)
+        call("ucb_decode_attention", query.data_ptr(), query.stride(0), q_heads, self.num_kv_heads,
+             self.head_dim, self.spans.data_ptr(), self.items.data_ptr(), self.num_items, self.pairs.data_ptr(),
+             self.num_pairs, self.k_bits, self.v_bits, self.group_size, _capi.UCB_BF16, scale,
+             self.partials.data_ptr(), self.counters.data_ptr(), out.data_ptr(), out.stride(0),
+             lse.data_ptr(), stream_of(query))
+        return out, lse
+
+
+def decode_slots(k_bits: int, v_bits: int, group_size: int) -> int:
+    slots = ctypes.c_int(0)
+    call("ucb_decode_slots", k_bits, v_bits, group_size, _capi.UCB_BF16, ctypes.byref(slots))
+    return int(slots.value)
+
+
+def _packed_span(cache, head: int) -> UcbSpan:
+    sp = UcbSpan()
+    sp.key_code = cache.key_code[head].data_ptr()
+    sp.key_scale = cache.key_scale[head].data_ptr()
+    sp.key_minimum = cache.key_minimum[head].data_ptr()
+    sp.value_code = cache.value_code[head].data_ptr()
+    sp.value_scale = cache.value_scale[head].data_ptr()
+    sp.value_minimum = cache.value_minimum[head].data_ptr()
+    sp.kind = 0
+    sp.tokens = int(cache.quantized_tokens)
+    return sp
+
+
+def _dense_span(rows: DenseRows) -> UcbSpan:
+    sp = UcbSpan()
+    es = rows.key.element_size()
+    sp.key_code = rows.key.data_ptr() + rows.key_offset * es
+    sp.value_code = rows.value.data_ptr() + rows.value_offset * es
+    sp.key_stride = rows.key_stride
+    sp.value_stride = rows.value_stride
+    sp.kind = 1
+    sp.tokens = rows.tokens
+    for name, base, off, stride in (("key", rows.key, rows.key_offset, rows.key_stride),
+                                    ("value", rows.value, rows.value_offset, rows.value_stride)):
+        if base.dtype != torch.bfloat16:
+            raise ValueError(f"dense {name} rows must be bfloat16")
+        if (base.data_ptr() + off * es) % 16 or (stride * es) % 16:
+            raise ValueError(f"dense {name} rows must start on 16-byte boundaries")
+    return sp
+
+
+def dense_rows_token_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
+    """[N, H, D] tensors (dense cache, KIVI residual)."""
+
+    return DenseRows(key, value, head * key.stride(1), head * value.stride(1),
+                     key.stride(0), value.stride(0), int(key.shape[0]))
+
+
+def dense_rows_head_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
+    """[H, N, D] tensors (compacted H2O segment)."""
+
+    return DenseRows(key, value, head * key.stride(0), head * value.stride(0), key.stride(1), value.stride(1),
+                     int(key.shape[1]))
+
+
+def packed_bytes_per_token(k_bits: int, v_bits: int, group_size: int, head_dim: int, stat_bytes: int = 2) -> float:
+    return head_dim * (k_bits + v_bits) / 8 + 2 * stat_bytes * head_dim / group_size * 2
+
+
+def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int = 128,
+                      target_items: int | None = None, min_packed_stages: int = 4) -> DecodePlan:
+    """Build device tables for decode over ``sequences``: one list of segments
+    per sequence, each segment a b200 ``PackedKIVICache`` (its residual rides
+    along as a dense span), a ``GQAH2OCache`` or a ``(key, value)`` pair of dense
+    [N, H, D] bf16 tensors."""
+
+    from .storage.physical import GQAH2OCache, PackedKIVICache
+
+    spans: list[UcbSpan] = []
+    span_pair: list[int] = []
+    span_bytes: list[float] = []
+    keepalive: list = []
+    pairs_info: list[tuple[int, int]] = []
+    cfg = None
+    device = None
+    for b, segments in enumerate(sequences):
+        for h in range(num_kv_heads):
+            pair = len(pairs_info)
+            pairs_info.append((b, h))
+            for seg in segments:
+                if isinstance(seg, PackedKIVICache):
+                    if seg.backend != "b200":
+                        raise ValueError("decode plans need b200-layout packed segments")
+                    if seg.quantized_tokens:
+                        key = (seg.k_bits, seg.v_bits, seg.group_size, seg.key_scale.dtype)
+                        if cfg is None:
+                            cfg = key
+                        elif cfg != key:
+                            raise ValueError("all packed segments of a decode plan must share bits, group and dtype")
+                        if seg.k_bits == 8 or seg.v_bits == 8:
+                            raise ValueError("8-bit packed segments are not supported by the decode kernel")
+                        if seg.head_dim != head_dim:
+                            raise ValueError("packed segment head_dim mismatch")
+                        spans.append(_packed_span(seg, h))
+                        span_pair.append(pair)
+                        span_bytes.append(seg.quantized_tokens * packed_bytes_per_token(
+                            seg.k_bits, seg.v_bits, seg.group_size, head_dim))
+                        keepalive.append(seg)
+                        device = seg.key_code.device
+                    if int(seg.residual_key.shape[0]):
+                        rows = dense_rows_token_major(seg.residual_key, seg.residual_value, h)
+                        spans.append(_dense_span(rows))
+                        span_pair.append(pair)
+                        span_bytes.append(rows.tokens * head_dim * 4)
+                        keepalive.append(seg)
+                        device = seg.residual_key.device
+                elif isinstance(seg, GQAH2OCache):
+                    rows = dense_rows_head_major(seg.key, seg.value, h)
+                    spans.append(_dense_span(rows))
+                    span_pair.append(pair)
+                    span_bytes.append(rows.tokens * head_dim * 4)
+                    keepalive.append(seg)
+                    device = seg.key.device
+                else:
+                    key, value = seg
+                    if int(key.shape[0]) == 0:
+                        continue
+                    rows = dense_rows_token_major(key, value, h)
+                    spans.append(_dense_span(rows))
+                    span_pair.append(pair)
+                    span_bytes.append(rows.tokens * head_dim * 4)
+                    keepalive.append((key, value))
+                    device = key.device
+    if device is None:
+        raise ValueError("decode plan has no tokens")
+    k_bits, v_bits, group, stat_dtype = cfg if cfg is not None else (2, 2, 64, torch.bfloat16)
+    if stat_dtype != torch.bfloat16:
+        raise ValueError("the decode kernel reads bfloat16 packed statistics")
+    if target_items is None:
+        with torch.cuda.device(device):
+            target_items = decode_slots(k_bits, v_bits, group)
+    # Split spans into items of about equal bytes (one wave of CTAs).
+    total = sum(span_bytes)
+    budget = max(total / max(1, target_items), 1.0)
+    items_by_pair: dict[int, list[tuple[int, int, int]]] = {p: [] for p in range(len(pairs_info))}
+    for s, sp in enumerate(spans):
+        align = PACKED_STAGE if sp.kind == 0 else DENSE_STAGE
+        units = max(1, math.ceil(sp.tokens / align))
+        want = max(1, round(span_bytes[s] / budget))
+        if sp.kind == 0:
+            want = min(want, max(1, units // min_packed_stages))
+        want = min(want, units)
+        for k in range(want):
+            u0 = k * units // want
+            u1 = (k + 1) * units // want
+            t0, t1 = u0 * align, min(sp.tokens, u1 * align)
+            if t1 > t0:
+                items_by_pair[span_pair[s]].append((s, t0, t1))
+    items: list[UcbDecodeItem] = []
+    pairs: list[UcbDecodePair] = []
+    for p, (b, h) in enumerate(pairs_info):
+        entries = items_by_pair[p]
+        if not entries:
+            raise ValueError(f"sequence {b} has no tokens for KV head {h}")
+        pr = UcbDecodePair()
+        pr.seq, pr.kv_head, pr.partial_begin, pr.partial_count = b, h, len(items), len(entries)
+        pairs.append(pr)
+        for s, t0, t1 in entries:
+            it = UcbDecodeItem()
+            it.span, it.token_begin, it.token_end, it.pair, it.partial = s, t0, t1, p, len(items)
+            items.append(it)
+
+    def upload(structs) -> torch.Tensor:
+        raw = _capi.struct_array_bytes(structs)
+        host = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
+        return host.to(device)
+
+    partial_bytes = int(_capi.load().ucb_decode_partial_bytes(head_dim))
+    return DecodePlan(
+        device=device,
+        num_seqs=len(sequences),
+        num_kv_heads=num_kv_heads,
+        head_dim=head_dim,
+        k_bits=k_bits,
+        v_bits=v_bits,
+        group_size=group,
+        spans=upload(spans),
+        items=upload(items),
+        pairs=upload(pairs),
+        num_items=len(items),
+        num_pairs=len(pairs),
+        partials=torch.empty(len(items) * partial_bytes, device=device, dtype=torch.uint8),
+        counters=torch.zeros(len(pairs), device=device, dtype=torch.int32),
+        keepalive=keepalive,
+        bytes_per_step=int(total),
+    )
+
+
+def device_status(device: torch.device | None = None) -> int:
+    flags = ctypes.c_uint(0)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    call("ucb_device_status", ctypes.byref(flags), stream)
+    return int(flags.value)
+
+
+def selftest_mma_subnormal() -> float:
+    err = ctypes.c_float(-1.0)
+    call("ucb_selftest_mma_subnormal", ctypes.byref(err), torch.cuda.current_stream().cuda_stream)
+    return float(err.value)
