@@ -112,18 +112,24 @@ UCB_API int ucb_fake_quant(const void* x_dev, void* out_dev, int dtype, int64_t 
  * (kivi_cuda.py:96-120) for q_len == 1, and _run_fused_h2o_attention
  * (bagel.py:1860-1901) without its per-step torch.cat.
  *
- * A decode batch is a set of (sequence, kv head) pairs, each owning spans:
+ * A decode batch is a set of (sequence, kv head) pairs; each pair owns spans:
  *  kind 0 (packed KIVI):  key_code..value_minimum point at this head's slice of a
  *                         b200-layout segment; `tokens` quantized tokens.
  *  kind 1 (dense):        key/value rows of `tokens` tokens for this head,
  *                         row i at key + i*key_stride (elements, bf16).
- * Items split spans into token ranges; one CTA per item.  Every item writes a
- * partial (max, sum, out) to `partials_dev`; the last item of a pair merges its
- * pair's partials into out_dev [seq, q_head, :] (bf16) and lse_dev [seq, q_head]
- * (natural-log LSE, fp32; may be NULL).
- * Workspaces: partials_dev >= ucb_decode_partial_bytes(head_dim) * num_partials
- * bytes; counters_dev >= num_pairs int32 zeroed once before first use (the
- * kernel leaves them zero).  Calls sharing counters must not overlap. */
+ * Spans are cut into units (64 packed or 8 dense tokens) numbered in span order
+ * (spans sorted by pair; span.unit_begin = its first unit).  CTA i processes
+ * units [ctas[i].unit_begin, ctas[i].unit_end), which touch pairs
+ * [pair_begin, pair_begin + num_pairs) (at most 4); its warp w processes units
+ * [warp_bounds[i*(W+1) + w], warp_bounds[i*(W+1) + w + 1]) where W comes from
+ * ucb_decode_config, and each warp range may cross at most one segment
+ * boundary (a change of pair or of span kind).  CTA i writes one partial per
+ * touched pair at partials[pair.partial_begin + i - pair.cta_first].  The last
+ * CTA of a pair merges its partials into out_dev [seq, q_head, :] (bf16) and
+ * lse_dev [seq, q_head] (natural-log LSE, fp32; may be NULL).
+ * Workspaces: partials_dev >= ucb_decode_partial_bytes(head_dim) * sum of
+ * partial_count bytes; counters_dev >= num_pairs int32 zeroed once before first
+ * use (the kernel leaves them zero).  Calls sharing counters must not overlap. */
 typedef struct ucb_span {
   const void* key_code;      /* packed: int32/uint8 codes; dense: key rows    */
   const void* key_scale;     /* packed only                                   */
@@ -135,22 +141,26 @@ typedef struct ucb_span {
   int64_t value_stride;      /* dense only                                    */
   int32_t kind;              /* 0 packed, 1 dense                             */
   int32_t tokens;
+  int32_t pair;              /* owning (sequence, kv head) pair               */
+  int32_t unit_begin;        /* first unit of this span                       */
 } ucb_span;
 
-typedef struct ucb_decode_item {
-  int32_t span;
-  int32_t token_begin;
-  int32_t token_end;
-  int32_t pair;
-  int32_t partial;
+typedef struct ucb_decode_cta {
+  int32_t unit_begin;
+  int32_t unit_end;
+  int32_t span_begin;        /* span containing unit_begin                    */
+  int32_t pair_begin;
+  int32_t num_pairs;         /* 1..4                                          */
   int32_t reserved[3];
-} ucb_decode_item;
+} ucb_decode_cta;
 
 typedef struct ucb_decode_pair {
   int32_t seq;
   int32_t kv_head;
   int32_t partial_begin;
-  int32_t partial_count;
+  int32_t partial_count;     /* CTAs touching this pair                       */
+  int32_t cta_first;         /* first CTA touching this pair                  */
+  int32_t reserved[3];
 } ucb_decode_pair;
 
 UCB_API int64_t ucb_decode_partial_bytes(int head_dim);
@@ -160,14 +170,22 @@ UCB_API int64_t ucb_decode_partial_bytes(int head_dim);
  * All packed spans of one call share (k_bits, v_bits, group_size, stat_dtype).
  * softmax_scale: multiplier of q.k (1/sqrt(head_dim) in the reference). */
 UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, int num_q_heads, int num_kv_heads,
-                         int head_dim, const ucb_span* spans_dev, const ucb_decode_item* items_dev,
-                         int num_items, const ucb_decode_pair* pairs_dev, int num_pairs, int k_bits,
+                         int head_dim, const ucb_span* spans_dev, int num_spans, const ucb_decode_cta* ctas_dev,
+                         int num_ctas, const int32_t* warp_bounds_dev, const ucb_decode_pair* pairs_dev,
+                         int num_pairs, int k_bits,
                          int v_bits, int group_size, int stat_dtype, float softmax_scale,
                          void* partials_dev, int* counters_dev, void* out_dev, int64_t out_stride,
                          float* lse_dev, void* stream);
 
-/* CTAs of ucb_decode_attention that fit on the current device at once. */
-UCB_API int ucb_decode_slots(int k_bits, int v_bits, int group_size, int stat_dtype, int* slots);
+/* Diagnostics: when trace_dev (device memory, 4 uint64 per CTA) is not NULL,
+ * later ucb_decode_attention calls record per CTA {start ns, end ns, SM id,
+ * pairs it merged}.  NULL switches it off. */
+UCB_API int ucb_decode_set_trace(void* trace_dev);
+
+/* Launch shape of ucb_decode_attention on the current device: CTAs that run at
+ * once (one per SM) and warps per CTA for the given packed configuration. */
+UCB_API int ucb_decode_config(int k_bits, int v_bits, int group_size, int stat_dtype, int* ctas,
+                              int* warps_per_cta);
 
 /* ------------------------------------------------------------------ LSE merge
  * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).

@@ -60,16 +60,16 @@ def test_pack_rejects_unsupported_configurations(bits, group, head_dim, expected
 def test_decode_rejects_bad_shapes_without_a_gpu():
     lib = _capi.load()
     fake = ctypes.c_void_p(256)
-    rc = lib.ucb_decode_attention(fake, 28 * 128, 28, 4, 64, fake, fake, 1, fake, 1, 2, 2, 32, 0, 0.1,
+    rc = lib.ucb_decode_attention(fake, 28 * 128, 28, 4, 64, fake, 1, fake, 1, fake, fake, 1, 2, 2, 32, 0, 0.1,
                                   fake, fake, fake, 28 * 128, None, None)
     assert rc == _capi.UCB_ERR_UNSUPPORTED and "head_dim" in lib.ucb_last_error().decode()
-    rc = lib.ucb_decode_attention(fake, 28 * 128, 28, 5, 128, fake, fake, 1, fake, 1, 2, 2, 32, 0, 0.1,
+    rc = lib.ucb_decode_attention(fake, 28 * 128, 28, 5, 128, fake, 1, fake, 1, fake, fake, 1, 2, 2, 32, 0, 0.1,
                                   fake, fake, fake, 28 * 128, None, None)
     assert rc == _capi.UCB_ERR_UNSUPPORTED
 
 
 def test_struct_layouts_match_the_header():
-    assert ctypes.sizeof(_capi.UcbSpan) == 72
-    assert ctypes.sizeof(_capi.UcbDecodeItem) == 32
-    assert ctypes.sizeof(_capi.UcbDecodePair) == 16
+    assert ctypes.sizeof(_capi.UcbSpan) == 80
+    assert ctypes.sizeof(_capi.UcbDecodeCta) == 32
+    assert ctypes.sizeof(_capi.UcbDecodePair) == 32
     assert _capi.load().ucb_decode_partial_bytes(128) == (16 + 8 * 128) * 4

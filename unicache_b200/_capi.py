@@ -47,16 +47,18 @@ class UcbSpan(ctypes.Structure):
         ("value_stride", c_int64),
         ("kind", ctypes.c_int32),
         ("tokens", ctypes.c_int32),
+        ("pair", ctypes.c_int32),
+        ("unit_begin", ctypes.c_int32),
     ]
 
 
-class UcbDecodeItem(ctypes.Structure):
+class UcbDecodeCta(ctypes.Structure):
     _fields_ = [
-        ("span", ctypes.c_int32),
-        ("token_begin", ctypes.c_int32),
-        ("token_end", ctypes.c_int32),
-        ("pair", ctypes.c_int32),
-        ("partial", ctypes.c_int32),
+        ("unit_begin", ctypes.c_int32),
+        ("unit_end", ctypes.c_int32),
+        ("span_begin", ctypes.c_int32),
+        ("pair_begin", ctypes.c_int32),
+        ("num_pairs", ctypes.c_int32),
         ("reserved", ctypes.c_int32 * 3),
     ]
 
@@ -67,6 +69,8 @@ class UcbDecodePair(ctypes.Structure):
         ("kv_head", ctypes.c_int32),
         ("partial_begin", ctypes.c_int32),
         ("partial_count", ctypes.c_int32),
+        ("cta_first", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
     ]
 
 
@@ -85,10 +89,11 @@ SIGNATURES = {
                                        c_int, c_int64, c_int64, c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "ucb_fake_quant": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_void_p]),
     "ucb_decode_partial_bytes": (c_int64, [c_int]),
-    "ucb_decode_attention": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
-                                     c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p,
-                                     c_int64, c_void_p, c_void_p]),
-    "ucb_decode_slots": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
+    "ucb_decode_attention": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int,
+                                     c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
+                                     c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "ucb_decode_config": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "ucb_decode_set_trace": (c_int, [c_void_p]),
     "ucb_lse_merge": (c_int, [c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int, c_int64, c_int64,
                               c_int64, c_void_p, c_void_p, c_void_p]),
     "ucb_merge_partials": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,

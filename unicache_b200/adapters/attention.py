@@ -47,9 +47,9 @@ class PhysicalDecodeBatch:
     kernel per decode step."""
 
     def __init__(self, sequences: list[list], *, num_kv_heads: int, head_dim: int = 128,
-                 target_items: int | None = None):
+                 target_ctas: int | None = None):
         self.plan = kernels.build_decode_plan(sequences, num_kv_heads=num_kv_heads, head_dim=head_dim,
-                                              target_items=target_items)
+                                              target_ctas=target_ctas)
 
     @property
     def bytes_per_step(self) -> int:

@@ -58,14 +58,28 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// try_wait with a suspend-time hint (ns): a waiting warp sleeps instead of
+// spinning, leaving issue slots to the warps that have data.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t s;
+  asm volatile("mov.u32 %0, %smid;" : "=r"(s));
+  return s;
 }
 
 // Bounded wait: gives up after `limit` polls (each poll may itself suspend for a
@@ -140,6 +154,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// (x - 128) * s + m on bf16 pairs, where x holds 128 + code in each half (exact):
+// the subtraction is exact and the fused multiply-add rounds once to bf16.
+__device__ __forceinline__ uint32_t bf16x2_dequant(uint32_t x, uint32_t s, uint32_t m) {
+  uint32_t c, d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(c) : "r"(x), "r"(0x3F803F80u), "r"(0xC300C300u));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(c), "r"(s), "r"(m));
   return d;
 }
 

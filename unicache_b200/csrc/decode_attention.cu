@@ -5,23 +5,29 @@
 // (kivi_cuda.py:96-120) and the frozen-H2O concat path
 // (unicache/adapters/bagel.py:1860-1901).
 //
-// Design (B200, HBM-bound):
-//  * One CTA = one work item = a token range of one span of one (sequence,
-//    KV head) pair; 4 warps split the range into contiguous runs of stages.
-//  * Each warp streams its stages with the TMA bulk-copy engine
-//    (cp.async.bulk, no tensor map, no multicast) into a private two-slot
-//    shared-memory ring guarded by mbarriers; every wait is bounded.
-//  * The 7 query heads of a GQA group are the N=8 columns of mma.sync
-//    m16n8k16; 16 tokens (QK) or 16 channels (AV) are the M rows.  Packed
-//    codes never become bf16 values: a PRMT + AND puts each 2/4-bit code into
-//    an fp16 *subnormal* (code * 2^(p-24)) that the tensor core multiplies
-//    exactly, and the group scales are folded into the other operand:
-//       q.k_t  = sum_d (q_d s_gd) c_td + sum_d q_d m_gd          (keys, per channel)
-//       sum_t p_t v_td = sum_t (p_t s_tg) c_td + sum_t p_t m_tg  (values, per token)
-//    The per-row power of two (p) is undone on the fp32 accumulator.
-//  * Online softmax in the log2 domain per warp; warps merge in shared
-//    memory; CTAs write (max, sum, out) partials and the last CTA of a pair
-//    (atomic ticket, no waiting) merges them into the output and the LSE.
+// Design (B200, HBM-bound, one persistent CTA per SM):
+//  * The batch is a set of (sequence, KV head) pairs; each pair owns spans
+//    (packed KIVI segments or dense bf16 rows).  Spans are cut into stages
+//    (64 packed tokens or 8 dense tokens) and all stages of all pairs form
+//    one flattened sequence of units.  The host gives every CTA a contiguous
+//    range of units of equal bytes and every warp a contiguous sub-range that
+//    crosses at most one segment boundary (segment = a pair's packed or dense
+//    units), so the result does not depend on scheduling.
+//  * Each warp streams its units with the TMA bulk-copy engine (cp.async.bulk,
+//    no tensor map, no multicast) into a private two-slot ring guarded by
+//    mbarriers; every wait is bounded.
+//  * The query heads of a GQA group are the N=8 columns of mma.sync m16n8k16.
+//    Keys: each code is dequantized to bf16 in registers exactly as the
+//    reference restores its cache (one rounding of code*scale + minimum),
+//    then QK runs on the tensor cores.  Values: the code is placed in an fp16
+//    *subnormal* (code * 2^(p-24), multiplied exactly by the tensor core) and
+//    the per-token group scale is folded into the probabilities:
+//       sum_t p_t v_td = sum_t (p_t s_tg) c_td + sum_t p_t m_tg.
+//  * Online softmax in the log2 domain per warp.  A warp that crosses a
+//    segment boundary parks its first state in a private shared-memory block;
+//    at the end the CTA merges the warp states of each pair it touched into
+//    one (max, sum, out) partial, and the last CTA of a pair (atomic ticket,
+//    no waiting) merges the partials into out and LSE.
 #include <cfloat>
 
 #include "common.cuh"
@@ -31,12 +37,12 @@ namespace decode {
 
 constexpr int D = 128;
 constexpr int KCH = D / 16;       // k-chunks of 16 channels
-constexpr int WARPS = 4;
 constexpr int NT = 64;            // tokens per packed stage
-constexpr int DT = 16;            // tokens per dense stage
-constexpr int DROW = 272;         // dense shared-memory row stride (bytes)
+constexpr int DT = 8;             // tokens per dense stage
+constexpr int DROW = 272;         // dense shared-memory row stride (bytes), conflict-free ldmatrix
 constexpr int DENSE_STAGE = 2 * DT * DROW;
-constexpr uint32_t WAIT_LIMIT = 1u << 24;
+constexpr int MAXC = 4;           // pairs one CTA may touch
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr int PARTIAL_FLOATS = 16 + 8 * D;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -45,7 +51,9 @@ __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / 
 
 template <int KB, int VB, int G, typename ST>
 struct Cfg {
-  static constexpr int NG = D / G;                   // value groups per token
+  static constexpr int WARPS = (KB == 2 && VB == 2) ? 12 : 8;
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int NG = D / G;                    // value groups per token
   static constexpr int GPS = (G >= NT) ? 1 : NT / G;  // key groups per stage
   static constexpr int KC = NT * D * KB / 8;
   static constexpr int VC = NT * D * VB / 8;
@@ -59,9 +67,14 @@ struct Cfg {
   static constexpr int OFF_VM = OFF_VS + VS;
   static constexpr int PACKED_STAGE = OFF_VM + VS;
   static constexpr int SLOT = round_up(PACKED_STAGE > DENSE_STAGE ? PACKED_STAGE : DENSE_STAGE, 128);
-  static constexpr int WARP_SMEM = 2 * SLOT;
-  static constexpr int SMEM = WARPS * WARP_SMEM + 128;  // + mbarriers and flags
-  static_assert(WARP_SMEM >= PARTIAL_FLOATS * 4, "warp ring must hold a warp state");
+  static constexpr int OFF_STASH = WARPS * 2 * SLOT;                // WARPS first-segment states
+  static constexpr int OFF_Q = OFF_STASH + WARPS * PARTIAL_FLOATS * 4; // MAXC x 8 query rows (bf16)
+  static constexpr int OFF_ZERO = OFF_Q + MAXC * 8 * D * 2;           // one zero row
+  static constexpr int OFF_BAR = OFF_ZERO + D * 2;                    // WARPS x 2 mbarriers
+  static constexpr int OFF_TAG = OFF_BAR + WARPS * 2 * 8;             // WARPS x 2 state tags
+  static constexpr int OFF_MISC = OFF_TAG + WARPS * 2 * 4;            // last-CTA flags
+  static constexpr int SMEM = OFF_MISC + 64;
+  static_assert(SLOT >= PARTIAL_FLOATS * 4, "a ring slot must hold a warp state");
 };
 
 // Token <-> MMA-row map inside a 16-token tile.  Row r and row r+8 of lane
@@ -92,10 +105,10 @@ __device__ __forceinline__ float warp_sum_r(float v) {
   return v;
 }
 
-// Online-softmax update for `NTILE` C fragments; returns the rescale factors.
+// Online-softmax update for NTILE C fragments (logits in, probabilities out).
+// Returns whether any lane's running max moved (then accumulators need alpha).
 template <int NTILE>
-__device__ __forceinline__ void softmax_update(float (&lg)[NTILE][4], WarpState& st, float& alpha0,
-                                               float& alpha1) {
+__device__ __forceinline__ bool softmax_update(float (&lg)[NTILE][4], WarpState& st, float& alpha0, float& alpha1) {
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int j = 0; j < NTILE; ++j) {
@@ -105,6 +118,7 @@ __device__ __forceinline__ void softmax_update(float (&lg)[NTILE][4], WarpState&
   mx0 = warp_max_r(mx0);
   mx1 = warp_max_r(mx1);
   const float n0 = fmaxf(st.mrun[0], mx0), n1 = fmaxf(st.mrun[1], mx1);
+  const bool moved = __any_sync(0xffffffffu, n0 != st.mrun[0] || n1 != st.mrun[1]);
   alpha0 = fast_exp2(st.mrun[0] - n0);
   alpha1 = fast_exp2(st.mrun[1] - n1);
   float s0 = 0.f, s1 = 0.f;
@@ -121,6 +135,7 @@ __device__ __forceinline__ void softmax_update(float (&lg)[NTILE][4], WarpState&
   st.lrun[1] = st.lrun[1] * alpha1 + s1;
   st.mrun[0] = n0;
   st.mrun[1] = n1;
+  return moved;
 }
 
 __device__ __forceinline__ uint2 lds64(const unsigned char* p) { return *reinterpret_cast<const uint2*>(p); }
@@ -132,7 +147,9 @@ struct Params {
   int grp;  // query heads per KV head
   int hq;   // query heads per sequence (row length of lse)
   const ucb_span* spans;
-  const ucb_decode_item* items;
+  int num_spans;
+  const ucb_decode_cta* ctas;
+  const int32_t* warp_bounds;  // per CTA: WARPS+1 unit boundaries
   const ucb_decode_pair* pairs;
   float scale_log2;  // softmax_scale * log2(e)
   float* partials;
@@ -141,6 +158,7 @@ struct Params {
   int64_t out_stride;
   float* lse;
   unsigned int* err;
+  uint64_t* trace;  // optional: per CTA {start ns, end ns, sm id, pairs merged}
 };
 
 template <int KB, int VB, int G, typename ST>
@@ -181,9 +199,9 @@ struct Kernel {
       mbar_arrive_expect_tx(bar, 2u * n * D * 2u);
     }
     __syncwarp();
-    const int row = lane & 15;
-    if (row < n) {
-      const bool is_v = lane >= 16;
+    const int row = lane & 7;
+    if (lane < 16 && row < n) {
+      const bool is_v = lane >= 8;
       const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(is_v ? sp.value_code : sp.key_code);
       const int64_t stride = is_v ? sp.value_stride : sp.key_stride;
       bulk_g2s(slot + (is_v ? DT * DROW : 0) + row * DROW, base + (t0 + row) * stride, D * 2, bar);
@@ -191,120 +209,101 @@ struct Kernel {
   }
 
   // -------------------------------------------------------------- packed stage
-  __device__ static void packed_stage(const unsigned char* slot, int n_valid, int lane, const float (&qf)[KCH][4],
-                                      const uint32_t (&qbp)[KCH][2], float scale_log2, WarpState& st,
-                                      float (&o)[8][4], float (&accm)[C::NG][2]) {
+  template <bool FULL>
+  __device__ static void packed_stage(const unsigned char* slot, int n_valid, int lane, const uint32_t (&qbp)[KCH][2],
+                                      float scale_log2, WarpState& st, float (&o)[8][4], float (&accm)[C::NG][2]) {
     const int r = lane >> 2, c = lane & 3;
     const int pr = tile_pos(r), pr2 = (pr + 1) & 3;
     const int tok_lo = 4 * (r & 3) + pr, tok_hi = 4 * (r & 3) + pr2;
 
-    // Per-group key bias  sum_d q_d m_gd  for the groups of this stage (rows = groups).
-    const int gps_valid = (G >= NT) ? 1 : (n_valid + G - 1) / G;
-    float cb[4] = {0.f, 0.f, 0.f, 0.f};
+    // Keys: every code is dequantized to bf16 exactly as the reference stores
+    // its restored cache (physical.py:178-201: one rounding of code*scale+min),
+    // then QK runs on the tensor cores against the raw bf16 query.  The four
+    // 16-token tiles are interleaved so four MMA chains are in flight.
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    uint32_t sel_lo, sel_hi, msk, sh_lo, sh_hi;
+    if constexpr (KB == 2) {
+      sel_lo = sel_hi = (r & 3) | ((4 + (r & 3)) << 8);
+      sh_lo = 2 * pr;
+      sh_hi = 2 * pr2;
+      msk = 0x00030003u;
+    } else {
+      const int blo = (r & 1) * 2 + (pr >> 1), bhi = (r & 1) * 2 + (pr2 >> 1);
+      sel_lo = blo | ((4 + blo) << 8);
+      sel_hi = bhi | ((4 + bhi) << 8);
+      sh_lo = 4 * (pr & 1);
+      sh_hi = 4 * (pr2 & 1);
+      msk = 0x000F000Fu;
+    }
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) {
-      uint32_t a[4] = {0u, 0u, 0u, 0u};
-      if (r < gps_valid) {
-        const uint2 m = lds64(slot + C::OFF_KM + (r * D + 16 * kk + 4 * c) * (int)sizeof(ST));
-        a[0] = m.x;
-        a[2] = m.y;
+      uint2 ks[C::GPS], km[C::GPS];
+#pragma unroll
+      for (int gi = 0; gi < C::GPS; ++gi) {
+        ks[gi] = lds64(slot + C::OFF_KS + (gi * D + 16 * kk + 4 * c) * (int)sizeof(ST));
+        km[gi] = lds64(slot + C::OFF_KM + (gi * D + 16 * kk + 4 * c) * (int)sizeof(ST));
       }
-      mma_bf16(cb, a, qbp[kk][0], qbp[kk][1]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int gi = (G >= NT) ? 0 : (16 * j) / G;
+        const int wr = (KB == 2) ? j : 2 * j + ((r & 3) >> 1);
+        const uint4 w = lds128(slot + C::OFF_KC + (wr * D + 16 * kk + 4 * c) * 4);
+        const uint32_t y0l = prmt(w.x, w.y, sel_lo), y1l = prmt(w.z, w.w, sel_lo);
+        const uint32_t y0h = (KB == 2) ? y0l : prmt(w.x, w.y, sel_hi);
+        const uint32_t y1h = (KB == 2) ? y1l : prmt(w.z, w.w, sel_hi);
+        uint32_t a[4];
+        a[0] = bf16x2_dequant(((y0l >> sh_lo) & msk) | 0x43004300u, ks[gi].x, km[gi].x);
+        a[1] = bf16x2_dequant(((y0h >> sh_hi) & msk) | 0x43004300u, ks[gi].x, km[gi].x);
+        a[2] = bf16x2_dequant(((y1l >> sh_lo) & msk) | 0x43004300u, ks[gi].y, km[gi].y);
+        a[3] = bf16x2_dequant(((y1h >> sh_hi) & msk) | 0x43004300u, ks[gi].y, km[gi].y);
+        mma_bf16(acc[j], a, qbp[kk][0], qbp[kk][1]);
+      }
     }
-
     float lg[4][4];
 #pragma unroll
-    for (int gi = 0; gi < C::GPS; ++gi) {
-      // q~ = q * key scale of this group, fp16, B-fragment order.
-      uint32_t bq[KCH][2];
-#pragma unroll
-      for (int kk = 0; kk < KCH; ++kk) {
-        const uint2 s = lds64(slot + C::OFF_KS + (gi * D + 16 * kk + 4 * c) * (int)sizeof(ST));
-        bq[kk][0] = pack_f16x2(qf[kk][0] * bf16lo(s.x), qf[kk][1] * bf16hi(s.x));
-        bq[kk][1] = pack_f16x2(qf[kk][2] * bf16lo(s.y), qf[kk][3] * bf16hi(s.y));
-      }
-      const float b0 = __shfl_sync(0xffffffffu, cb[0], gi * 4 + c) * scale_log2;
-      const float b1 = __shfl_sync(0xffffffffu, cb[1], gi * 4 + c) * scale_log2;
-      constexpr int TPG = 4 / C::GPS;  // 16-token tiles per group in this stage
-#pragma unroll
-      for (int jj = 0; jj < TPG; ++jj) {
-        const int j = gi * TPG + jj;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float fac_lo, fac_hi;
-        if constexpr (KB == 2) {
-          const unsigned char* kc = slot + C::OFF_KC + j * D * 4;
-          const uint32_t sel = (r & 3) | ((4 + (r & 3)) << 8);
-          const uint32_t mlo = 0x00030003u << (2 * pr), mhi = 0x00030003u << (2 * pr2);
-#pragma unroll
-          for (int kk = 0; kk < KCH; ++kk) {
-            const uint4 w = lds128(kc + (16 * kk + 4 * c) * 4);
-            const uint32_t y01 = prmt(w.x, w.y, sel), y23 = prmt(w.z, w.w, sel);
-            const uint32_t a[4] = {y01 & mlo, y01 & mhi, y23 & mlo, y23 & mhi};
-            mma_f16(acc, a, bq[kk][0], bq[kk][1]);
-          }
-          fac_lo = __int_as_float((127 + 24 - 2 * pr) << 23);
-          fac_hi = __int_as_float((127 + 24 - 2 * pr2) << 23);
-        } else {
-          const int wr = 2 * j + ((r & 3) >> 1);
-          const int blo = (r & 1) * 2 + (pr >> 1), bhi = (r & 1) * 2 + (pr2 >> 1);
-          const int plo = 4 * (pr & 1), phi = 4 * (pr2 & 1);
-          const uint32_t slo = blo | ((4 + blo) << 8), shi = bhi | ((4 + bhi) << 8);
-          const uint32_t mlo = 0x000F000Fu << plo, mhi = 0x000F000Fu << phi;
-          const unsigned char* kc = slot + C::OFF_KC + wr * D * 4;
-#pragma unroll
-          for (int kk = 0; kk < KCH; ++kk) {
-            const uint4 w = lds128(kc + (16 * kk + 4 * c) * 4);
-            const uint32_t a[4] = {prmt(w.x, w.y, slo) & mlo, prmt(w.x, w.y, shi) & mhi,
-                                   prmt(w.z, w.w, slo) & mlo, prmt(w.z, w.w, shi) & mhi};
-            mma_f16(acc, a, bq[kk][0], bq[kk][1]);
-          }
-          fac_lo = __int_as_float((127 + 24 - plo) << 23);
-          fac_hi = __int_as_float((127 + 24 - phi) << 23);
-        }
-        const bool vlo = 16 * j + tok_lo < n_valid, vhi = 16 * j + tok_hi < n_valid;
-        lg[j][0] = vlo ? fmaf(acc[0], fac_lo, b0) : -INFINITY;
-        lg[j][1] = vlo ? fmaf(acc[1], fac_lo, b1) : -INFINITY;
-        lg[j][2] = vhi ? fmaf(acc[2], fac_hi, b0) : -INFINITY;
-        lg[j][3] = vhi ? fmaf(acc[3], fac_hi, b1) : -INFINITY;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const bool vlo = FULL || 16 * j + tok_lo < n_valid, vhi = FULL || 16 * j + tok_hi < n_valid;
+      lg[j][0] = vlo ? acc[j][0] * scale_log2 : -INFINITY;
+      lg[j][1] = vlo ? acc[j][1] * scale_log2 : -INFINITY;
+      lg[j][2] = vhi ? acc[j][2] * scale_log2 : -INFINITY;
+      lg[j][3] = vhi ? acc[j][3] * scale_log2 : -INFINITY;
     }
 
     float alpha0, alpha1;
-    softmax_update<4>(lg, st, alpha0, alpha1);
+    if (softmax_update<4>(lg, st, alpha0, alpha1)) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= alpha0;
-      o[i][1] *= alpha1;
-      o[i][2] *= alpha0;
-      o[i][3] *= alpha1;
-    }
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] *= alpha0;
+        o[i][1] *= alpha1;
+        o[i][2] *= alpha0;
+        o[i][3] *= alpha1;
+      }
 #pragma unroll
-    for (int g = 0; g < C::NG; ++g) {
-      accm[g][0] *= alpha0;
-      accm[g][1] *= alpha1;
+      for (int g = 0; g < C::NG; ++g) {
+        accm[g][0] *= alpha0;
+        accm[g][1] *= alpha1;
+      }
     }
 
-    // AV: one 16-token k-chunk per tile.
+    // Values: one 16-token k-chunk per tile.
     const int u0 = tile_tok(2 * c), u1 = tile_tok(2 * c + 1), u2 = tile_tok(2 * c + 8), u3 = tile_tok(2 * c + 9);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const bool vlo = 16 * j + tok_lo < n_valid, vhi = 16 * j + tok_hi < n_valid;
+      const bool vlo = FULL || 16 * j + tok_lo < n_valid, vhi = FULL || 16 * j + tok_hi < n_valid;
       const unsigned char* vs_lo = slot + C::OFF_VS + (16 * j + tok_lo) * C::NG * (int)sizeof(ST);
       const unsigned char* vs_hi = slot + C::OFF_VS + (16 * j + tok_hi) * C::NG * (int)sizeof(ST);
       const int moff = C::OFF_VM - C::OFF_VS;
       float slo[C::NG], shi[C::NG], mlo[C::NG], mhi[C::NG];
+      if constexpr (C::NG == 1) {
+        slo[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_lo));
+        shi[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_hi));
+        mlo[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_lo + moff));
+        mhi[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_hi + moff));
+      } else {
 #pragma unroll
-      for (int g = 0; g < C::NG; g += 2) {
-        if constexpr (C::NG == 1) {
-          const uint32_t s_l = *reinterpret_cast<const uint16_t*>(vs_lo);
-          const uint32_t s_h = *reinterpret_cast<const uint16_t*>(vs_hi);
-          const uint32_t m_l = *reinterpret_cast<const uint16_t*>(vs_lo + moff);
-          const uint32_t m_h = *reinterpret_cast<const uint16_t*>(vs_hi + moff);
-          slo[0] = bf16lo(s_l);
-          shi[0] = bf16lo(s_h);
-          mlo[0] = bf16lo(m_l);
-          mhi[0] = bf16lo(m_h);
-        } else {
+        for (int g = 0; g < C::NG; g += 2) {
           const uint32_t s_l = *reinterpret_cast<const uint32_t*>(vs_lo + 2 * g);
           const uint32_t s_h = *reinterpret_cast<const uint32_t*>(vs_hi + 2 * g);
           const uint32_t m_l = *reinterpret_cast<const uint32_t*>(vs_lo + moff + 2 * g);
@@ -322,6 +321,7 @@ struct Kernel {
       uint32_t bp[C::NG][2];
 #pragma unroll
       for (int g = 0; g < C::NG; ++g) {
+        // Past the end the shared memory holds stale bytes: select, never multiply by 0.
         const float sl = vlo ? slo[g] : 0.f, sh = vhi ? shi[g] : 0.f;
         const float ml = vlo ? mlo[g] : 0.f, mh = vhi ? mhi[g] : 0.f;
         bp[g][0] = movmatrix_trans(pack_f16x2(lg[j][0] * sl, lg[j][1] * sl));
@@ -381,29 +381,26 @@ struct Kernel {
   }
 
   // -------------------------------------------------------------- dense stage
-  __device__ static void dense_stage(const unsigned char* slot, int n_valid, int lane, const uint32_t (&qb)[KCH][2],
-                                     float scale_log2, WarpState& st, float (&o)[8][4]) {
+  // 8 tokens of bf16 rows; MMA rows beyond them read a shared zero row.
+  __device__ static void dense_stage(const unsigned char* slot, int n_valid, int lane, const unsigned char* qrow_smem,
+                                     uint32_t zero_row, float scale_log2, WarpState& st, float (&o)[8][4]) {
     const int r = lane >> 2, c = lane & 3;
     const int pr = tile_pos(r), pr2 = (pr + 1) & 3;
     const int tok_lo = 4 * (r & 3) + pr, tok_hi = 4 * (r & 3) + pr2;
-    // Zero value rows past the end so that 0 * stale never poisons the MMA.
-    if (n_valid < DT) {
-      unsigned char* vbase = const_cast<unsigned char*>(slot) + DT * DROW;
-      for (int idx = lane; idx < (DT - n_valid) * (D * 2 / 16); idx += 32) {
-        const int row = n_valid + idx / (D * 2 / 16), chunk = idx % (D * 2 / 16);
-        *reinterpret_cast<uint4*>(vbase + row * DROW + chunk * 16) = make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
-    }
     const uint32_t kbase = smem_u32(slot), vbase = smem_u32(slot + DT * DROW);
     const int q = lane >> 3, krow = lane & 7;
+    const int tk = tile_tok((q & 1) * 8 + krow), tv = tile_tok((q >> 1) * 8 + krow);
+    const uint32_t kaddr = (tk < n_valid ? kbase + tk * DROW : zero_row) + (q >> 1) * 16;
+    const uint32_t vaddr = (tv < n_valid ? vbase + tv * DROW : zero_row) + (q & 1) * 16;
+    const unsigned char* qh = qrow_smem + r * D * 2;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t kaddr = kbase + tile_tok((q & 1) * 8 + krow) * DROW + (q >> 1) * 16;
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) {
       uint32_t a[4];
       ldmatrix_x4(a, kaddr + kk * 32);
-      mma_bf16(acc, a, qb[kk][0], qb[kk][1]);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(qh + (16 * kk + 2 * c) * 2);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(qh + (16 * kk + 2 * c + 8) * 2);
+      mma_bf16(acc, a, b0, b1);
     }
     float lg[1][4];
     lg[0][0] = tok_lo < n_valid ? acc[0] * scale_log2 : -INFINITY;
@@ -411,148 +408,51 @@ struct Kernel {
     lg[0][2] = tok_hi < n_valid ? acc[2] * scale_log2 : -INFINITY;
     lg[0][3] = tok_hi < n_valid ? acc[3] * scale_log2 : -INFINITY;
     float alpha0, alpha1;
-    softmax_update<1>(lg, st, alpha0, alpha1);
+    if (softmax_update<1>(lg, st, alpha0, alpha1)) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] *= alpha0;
+        o[i][1] *= alpha1;
+        o[i][2] *= alpha0;
+        o[i][3] *= alpha1;
+      }
+    }
     const uint32_t b0 = movmatrix_trans(pack_bf16x2(lg[0][0], lg[0][1]));
     const uint32_t b1 = movmatrix_trans(pack_bf16x2(lg[0][2], lg[0][3]));
-    const uint32_t vaddr = vbase + tile_tok((q >> 1) * 8 + krow) * DROW + (q & 1) * 16;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      o[i][0] *= alpha0;
-      o[i][1] *= alpha1;
-      o[i][2] *= alpha0;
-      o[i][3] *= alpha1;
       uint32_t a[4];
       ldmatrix_x4_trans(a, vaddr + i * 32);
       mma_bf16(o[i], a, b0, b1);
     }
   }
 
-  // -------------------------------------------------------------- kernel body
-  __device__ static void run(const Params& P, unsigned char* smem) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // -------------------------------------------------------------- write a warp state
+  // Stores (max, sum, out) of the warp's current segment, in natural channel
+  // order, into a private shared-memory block [m 8][l 8][O 8 x D].
+  __device__ static void store_state(float* dst, bool packed, const WarpState& st, float (&o)[8][4],
+                                     float (&accm)[C::NG][2], int lane) {
     const int r = lane >> 2, c = lane & 3;
-    const ucb_decode_item item = P.items[blockIdx.x];
-    const ucb_span sp = P.spans[item.span];
-    const ucb_decode_pair pair = P.pairs[item.pair];
-    const bool packed = sp.kind == 0;
-    const int stage_tokens = packed ? NT : DT;
-
-    unsigned char* ring = smem + warp * C::WARP_SMEM;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + WARPS * C::WARP_SMEM) + warp * 2;
-    int* shared_flag = reinterpret_cast<int*>(smem + WARPS * C::WARP_SMEM + 64);
-    if (lane == 0) {
-      mbar_init(&bars[0], 1);
-      mbar_init(&bars[1], 1);
-      fence_mbarrier_init();
-    }
-    __syncwarp();
-
-    const int total_stages = (item.token_end - item.token_begin + stage_tokens - 1) / stage_tokens;
-    const int s_begin = warp * total_stages / WARPS, s_end = (warp + 1) * total_stages / WARPS;
-    const int n_stages = s_end - s_begin;
-    auto stage_range = [&](int s, int& t0, int& t1) {
-      t0 = item.token_begin + (s_begin + s) * stage_tokens;
-      t1 = min(item.token_end, t0 + stage_tokens);
-    };
-    auto issue = [&](int s) {
-      int t0, t1;
-      stage_range(s, t0, t1);
-      unsigned char* slot = ring + (s & 1) * C::SLOT;
-      if (packed)
-        issue_packed(sp, t0, t1, slot, &bars[s & 1], lane);
-      else
-        issue_dense(sp, t0, t1, slot, &bars[s & 1], lane);
-    };
-    if (n_stages > 0) issue(0);
-    if (n_stages > 1) issue(1);
-
-    // Query fragments for this KV head's query heads (row r of B = head r).
-    const int head = pair.kv_head * P.grp + r;
-    const bool head_ok = r < P.grp;
-    const __nv_bfloat16* qrow = P.query + pair.seq * P.query_stride + (int64_t)head * D;
-
-    WarpState st;
-    st.mrun[0] = st.mrun[1] = -INFINITY;
-    st.lrun[0] = st.lrun[1] = 0.f;
-    float o[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float accm[C::NG][2];
-#pragma unroll
-    for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
-
-    int failed_at = -1;
-    if (packed) {
-      float qf[KCH][4];
-      uint32_t qbp[KCH][2];
-#pragma unroll
-      for (int kk = 0; kk < KCH; ++kk) {
-        uint2 u = make_uint2(0u, 0u);
-        if (head_ok) u = *reinterpret_cast<const uint2*>(qrow + 16 * kk + 4 * c);
-        qbp[kk][0] = u.x;
-        qbp[kk][1] = u.y;
-        qf[kk][0] = bf16lo(u.x) * P.scale_log2;
-        qf[kk][1] = bf16hi(u.x) * P.scale_log2;
-        qf[kk][2] = bf16lo(u.y) * P.scale_log2;
-        qf[kk][3] = bf16hi(u.y) * P.scale_log2;
-      }
-      for (int s = 0; s < n_stages; ++s) {
-        if (!mbar_wait_bounded(&bars[s & 1], (s >> 1) & 1, WAIT_LIMIT)) {
-          failed_at = s;
-          break;
-        }
-        int t0, t1;
-        stage_range(s, t0, t1);
-        packed_stage(ring + (s & 1) * C::SLOT, t1 - t0, lane, qf, qbp, P.scale_log2, st, o, accm);
-        __syncwarp();
-        if (s + 2 < n_stages) issue(s + 2);
-      }
-    } else {
-      uint32_t qb[KCH][2];
-#pragma unroll
-      for (int kk = 0; kk < KCH; ++kk) {
-        qb[kk][0] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * c) : 0u;
-        qb[kk][1] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * c + 8) : 0u;
-      }
-      for (int s = 0; s < n_stages; ++s) {
-        if (!mbar_wait_bounded(&bars[s & 1], (s >> 1) & 1, WAIT_LIMIT)) {
-          failed_at = s;
-          break;
-        }
-        int t0, t1;
-        stage_range(s, t0, t1);
-        dense_stage(ring + (s & 1) * C::SLOT, t1 - t0, lane, qb, P.scale_log2, st, o);
-        __syncwarp();
-        if (s + 2 < n_stages) issue(s + 2);
-      }
-    }
-    if (failed_at >= 0) {
-      // Let copies still in flight land before this CTA's shared memory is released.
-      for (int s = failed_at; s < failed_at + 2 && s < n_stages; ++s)
-        mbar_wait_bounded(&bars[s & 1], (s >> 1) & 1, WAIT_LIMIT);
-      if (lane == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
-      st.mrun[0] = st.mrun[1] = -INFINITY;
-    }
-
-    // ---------------------------------------------------------- warp epilogue
-    float l0 = warp_sum_r(st.lrun[0]), l1 = warp_sum_r(st.lrun[1]);
-    float* ws = reinterpret_cast<float*>(ring);  // [m2 8][l 8][O 8 x D]
-    if (r == 0) {
-      ws[2 * c] = st.mrun[0];
-      ws[2 * c + 1] = st.mrun[1];
-      ws[8 + 2 * c] = l0;
-      ws[8 + 2 * c + 1] = l1;
-    }
-    float* wo = ws + 16;
+    const float l0 = warp_sum_r(st.lrun[0]), l1 = warp_sum_r(st.lrun[1]);
     if (packed) {
 #pragma unroll
       for (int g = 0; g < C::NG; ++g) {
         accm[g][0] = warp_sum_r(accm[g][0]);
         accm[g][1] = warp_sum_r(accm[g][1]);
       }
+    }
+    if (r == 0) {
+      dst[2 * c] = st.mrun[0];
+      dst[2 * c + 1] = st.mrun[1];
+      dst[8 + 2 * c] = l0;
+      dst[8 + 2 * c + 1] = l1;
+    }
+    float* ao = dst + 16;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        int d_lo, d_hi;
+    for (int i = 0; i < 8; ++i) {
+      int d_lo, d_hi;
+      float v[4];
+      if (packed) {
         float f_lo, f_hi;
         if constexpr (VB == 2) {
           d_lo = 16 * i + 2 * r;
@@ -565,121 +465,289 @@ struct Kernel {
           f_lo = f_hi = __int_as_float((127 + 24 - 4 * (r & 1)) << 23);
         }
         const int g = (16 * i) / G;
-        wo[(2 * c) * D + d_lo] = fmaf(o[i][0], f_lo, accm[g][0]);
-        wo[(2 * c + 1) * D + d_lo] = fmaf(o[i][1], f_lo, accm[g][1]);
-        wo[(2 * c) * D + d_hi] = fmaf(o[i][2], f_hi, accm[g][0]);
-        wo[(2 * c + 1) * D + d_hi] = fmaf(o[i][3], f_hi, accm[g][1]);
+        v[0] = fmaf(o[i][0], f_lo, accm[g][0]);
+        v[1] = fmaf(o[i][1], f_lo, accm[g][1]);
+        v[2] = fmaf(o[i][2], f_hi, accm[g][0]);
+        v[3] = fmaf(o[i][3], f_hi, accm[g][1]);
+      } else {
+        d_lo = 16 * i + r;
+        d_hi = d_lo + 8;
+        v[0] = o[i][0];
+        v[1] = o[i][1];
+        v[2] = o[i][2];
+        v[3] = o[i][3];
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int d_lo = 16 * i + r, d_hi = d_lo + 8;
-        wo[(2 * c) * D + d_lo] = o[i][0];
-        wo[(2 * c + 1) * D + d_lo] = o[i][1];
-        wo[(2 * c) * D + d_hi] = o[i][2];
-        wo[(2 * c + 1) * D + d_hi] = o[i][3];
+      ao[(2 * c) * D + d_lo] = v[0];
+      ao[(2 * c + 1) * D + d_lo] = v[1];
+      ao[(2 * c) * D + d_hi] = v[2];
+      ao[(2 * c + 1) * D + d_hi] = v[3];
+    }
+  }
+
+  // -------------------------------------------------------------- kernel body
+  __device__ static void run(const Params& P, unsigned char* smem) {
+    const uint64_t t_start = P.trace ? global_timer_ns() : 0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const ucb_decode_cta cta = P.ctas[blockIdx.x];
+    const int32_t* bounds = P.warp_bounds + (int64_t)blockIdx.x * (C::WARPS + 1);
+    const int u_begin = bounds[warp], u_end = bounds[warp + 1];
+
+    float* stash = reinterpret_cast<float*>(smem + C::OFF_STASH) + warp * PARTIAL_FLOATS;
+    unsigned char* qs = smem + C::OFF_Q;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR) + warp * 2;
+    int* tags = reinterpret_cast<int*>(smem + C::OFF_TAG);      // [warp][2]: pair_local or -1
+    int* last_flags = reinterpret_cast<int*>(smem + C::OFF_MISC);
+    const uint32_t zero_row = smem_u32(smem + C::OFF_ZERO);
+    unsigned char* ring = smem + warp * 2 * C::SLOT;
+
+    // ---- CTA set-up: query rows of its pairs, zero row, barriers.
+    for (int i = tid; i < MAXC * 8 * D / 8; i += C::THREADS) {  // 16-byte chunks
+      const int pl = i / (8 * D / 8), rem = i % (8 * D / 8);
+      const int h = rem / (D / 8), chunk = rem % (D / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (pl < cta.num_pairs && h < P.grp) {
+        const ucb_decode_pair pr = P.pairs[cta.pair_begin + pl];
+        const __nv_bfloat16* src = P.query + pr.seq * P.query_stride + (int64_t)(pr.kv_head * P.grp + h) * D;
+        v = reinterpret_cast<const uint4*>(src)[chunk];
       }
+      reinterpret_cast<uint4*>(qs)[i] = v;
+    }
+    for (int i = tid; i < D * 2 / 16; i += C::THREADS)
+      reinterpret_cast<uint4*>(smem + C::OFF_ZERO)[i] = make_uint4(0, 0, 0, 0);
+    if (lane == 0) {
+      tags[2 * warp] = tags[2 * warp + 1] = -1;
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
+      fence_mbarrier_init();
     }
     __syncthreads();
 
-    // ---------------------------------------------------------- CTA merge -> partial
-    const int tid = threadIdx.x;  // one thread per channel (D == 128 == blockDim)
-    float* part = P.partials + (int64_t)item.partial * PARTIAL_FLOATS;
-    for (int h = 0; h < P.grp; ++h) {
-      float M = -INFINITY;
+    // ---- the warp's units, in order; an issue cursor runs two units ahead.
+    int issue_u = u_begin, issue_span = cta.span_begin;
+    auto issue_next = [&](int slot_idx) {
+      while (issue_span + 1 < P.num_spans && P.spans[issue_span + 1].unit_begin <= issue_u) ++issue_span;
+      const ucb_span& sp = P.spans[issue_span];
+      const int stage = sp.kind == 0 ? NT : DT;
+      const int t0 = (issue_u - sp.unit_begin) * stage;
+      const int t1 = min(sp.tokens, t0 + stage);
+      unsigned char* slot = ring + slot_idx * C::SLOT;
+      if (sp.kind == 0)
+        issue_packed(sp, t0, t1, slot, &bars[slot_idx], lane);
+      else
+        issue_dense(sp, t0, t1, slot, &bars[slot_idx], lane);
+      ++issue_u;
+    };
+    if (issue_u < u_end) issue_next(0);
+    if (issue_u < u_end) issue_next(1);
+
+    WarpState st;
+    st.mrun[0] = st.mrun[1] = -INFINITY;
+    st.lrun[0] = st.lrun[1] = 0.f;
+    float o[8][4];
+    float accm[C::NG][2];
+    uint32_t qbp[KCH][2];
 #pragma unroll
-      for (int w = 0; w < WARPS; ++w) M = fmaxf(M, reinterpret_cast<float*>(smem + w * C::WARP_SMEM)[h]);
-      float acc = 0.f, lsum = 0.f;
-      if (M != -INFINITY) {
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 #pragma unroll
-        for (int w = 0; w < WARPS; ++w) {
-          const float* wsw = reinterpret_cast<float*>(smem + w * C::WARP_SMEM);
-          const float f = fast_exp2(wsw[h] - M);
-          acc = fmaf(f, wsw[16 + h * D + tid], acc);
-          lsum = fmaf(f, wsw[8 + h], lsum);
+    for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KCH; ++kk) qbp[kk][0] = qbp[kk][1] = 0u;
+    int cur_pl = -1, cur_kind = -1, span = cta.span_begin;
+    bool ok = true, stashed = false;
+    int s = 0;
+    for (int u = u_begin; u < u_end; ++u, ++s) {
+      const int slot_idx = s & 1;
+      if (!mbar_wait_bounded(&bars[slot_idx], (s >> 1) & 1, WAIT_LIMIT)) {
+        ok = false;
+        break;
+      }
+      while (span + 1 < P.num_spans && P.spans[span + 1].unit_begin <= u) ++span;
+      const ucb_span& sp = P.spans[span];
+      const int pl = sp.pair - cta.pair_begin;
+      const int kind = sp.kind;
+      if (pl != cur_pl || kind != cur_kind) {
+        if (cur_pl >= 0) {
+          // At most one segment boundary per warp (the planner guarantees it).
+          if (stashed) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+          store_state(stash, cur_kind == 0, st, o, accm, lane);
+          if (lane == 0) tags[2 * warp] = cur_pl;
+          stashed = true;
+        }
+        st.mrun[0] = st.mrun[1] = -INFINITY;
+        st.lrun[0] = st.lrun[1] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+        for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
+        if (kind == 0) {
+#pragma unroll
+          for (int kk = 0; kk < KCH; ++kk) {
+            const uint2 q2 = lds64(qs + ((pl * 8 + r) * D + 16 * kk + 4 * c) * 2);
+            qbp[kk][0] = q2.x;
+            qbp[kk][1] = q2.y;
+          }
+        }
+        cur_pl = pl;
+        cur_kind = kind;
+      }
+      unsigned char* slot = ring + slot_idx * C::SLOT;
+      const int stage = kind == 0 ? NT : DT;
+      const int t0 = (u - sp.unit_begin) * stage;
+      const int n = min(sp.tokens, t0 + stage) - t0;
+      if (kind == 0) {
+        if (n == NT)
+          packed_stage<true>(slot, n, lane, qbp, P.scale_log2, st, o, accm);
+        else
+          packed_stage<false>(slot, n, lane, qbp, P.scale_log2, st, o, accm);
+      } else {
+        dense_stage(slot, n, lane, qs + pl * 8 * D * 2, zero_row, P.scale_log2, st, o);
+      }
+      __syncwarp();
+      if (issue_u < u_end) issue_next(slot_idx);
+    }
+    if (!ok) {
+      // Let copies still in flight land before the shared memory is reused.
+      for (int k = s; k < s + 2; ++k) {
+        if (u_begin + k < u_end) mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1, WAIT_LIMIT);
+      }
+      if (lane == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
+    } else if (cur_pl >= 0) {
+      store_state(reinterpret_cast<float*>(ring), cur_kind == 0, st, o, accm, lane);
+      if (lane == 0) tags[2 * warp + 1] = cur_pl;
+    }
+    __syncthreads();
+
+    // ---- merge the warp states of each pair into one partial
+    for (int pl = 0; pl < cta.num_pairs; ++pl) {
+      const ucb_decode_pair pr = P.pairs[cta.pair_begin + pl];
+      float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
+      for (int hd = tid; hd < 8 * D + 8; hd += C::THREADS) {
+        const bool is_l = hd >= 8 * D;
+        const int h = is_l ? hd - 8 * D : hd / D, d = hd % D;
+        float M = -INFINITY;
+        for (int w = 0; w < C::WARPS; ++w) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            if (tags[2 * w + k] != pl) continue;
+            const float* src = k ? reinterpret_cast<const float*>(smem + w * 2 * C::SLOT)
+                                 : reinterpret_cast<const float*>(smem + C::OFF_STASH) + w * PARTIAL_FLOATS;
+            M = fmaxf(M, src[h]);
+          }
+        }
+        float acc = 0.f;
+        for (int w = 0; w < C::WARPS; ++w) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            if (tags[2 * w + k] != pl) continue;
+            const float* src = k ? reinterpret_cast<const float*>(smem + w * 2 * C::SLOT)
+                                 : reinterpret_cast<const float*>(smem + C::OFF_STASH) + w * PARTIAL_FLOATS;
+            if (src[h] == -INFINITY) continue;
+            acc = fmaf(fast_exp2(src[h] - M), is_l ? src[8 + h] : src[16 + h * D + d], acc);
+          }
+        }
+        if (is_l) {
+          part[h] = M;
+          part[8 + h] = acc;
+        } else {
+          part[16 + h * D + d] = acc;
         }
       }
-      part[16 + h * D + tid] = acc;
-      if (tid == 0) {
-        part[h] = M;
-        part[8 + h] = lsum;
-      }
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) {
-      const int prev = atomicAdd(&P.counters[item.pair], 1);
-      *shared_flag = (prev == pair.partial_count - 1) ? 1 : 0;
+    if (tid < cta.num_pairs) {
+      const ucb_decode_pair pr = P.pairs[cta.pair_begin + tid];
+      const int prev = atomicAdd(&P.counters[cta.pair_begin + tid], 1);
+      last_flags[tid] = (prev == pr.partial_count - 1) ? 1 : 0;
     }
     __syncthreads();
-    if (*shared_flag == 0) return;
-    __threadfence();
-
-    // ---------------------------------------------------------- last CTA: pair merge
-    const float* base = P.partials + (int64_t)pair.partial_begin * PARTIAL_FLOATS;
-    for (int h = 0; h < P.grp; ++h) {
-      float M = -INFINITY;
-      for (int p = 0; p < pair.partial_count; ++p) M = fmaxf(M, __ldcg(base + (int64_t)p * PARTIAL_FLOATS + h));
-      float acc = 0.f, lsum = 0.f;
-      for (int p = 0; p < pair.partial_count; ++p) {
-        const float* pp = base + (int64_t)p * PARTIAL_FLOATS;
-        const float mp = __ldcg(pp + h);
-        if (mp == -INFINITY) continue;
-        const float f = fast_exp2(mp - M);
-        acc = fmaf(f, __ldcg(pp + 16 + h * D + tid), acc);
-        lsum = fmaf(f, __ldcg(pp + 8 + h), lsum);
+    int merged = 0;
+    for (int pl = 0; pl < cta.num_pairs; ++pl) {
+      if (!last_flags[pl]) continue;
+      ++merged;
+      __threadfence();
+      const int pidx = cta.pair_begin + pl;
+      const ucb_decode_pair pr = P.pairs[pidx];
+      const float* base = P.partials + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
+      for (int hd = tid; hd < P.grp * D; hd += C::THREADS) {
+        const int h = hd / D, d = hd % D;
+        float M = -INFINITY;
+        for (int p = 0; p < pr.partial_count; ++p) M = fmaxf(M, __ldcg(base + (int64_t)p * PARTIAL_FLOATS + h));
+        float sum = 0.f, lsum = 0.f;
+        for (int p = 0; p < pr.partial_count; ++p) {
+          const float* pp = base + (int64_t)p * PARTIAL_FLOATS;
+          const float mp = __ldcg(pp + h);
+          if (mp == -INFINITY) continue;
+          const float f = fast_exp2(mp - M);
+          sum = fmaf(f, __ldcg(pp + 16 + h * D + d), sum);
+          lsum = fmaf(f, __ldcg(pp + 8 + h), lsum);
+        }
+        const float val = sum / lsum;
+        const int qh = pr.kv_head * P.grp + h;
+        P.out[pr.seq * P.out_stride + (int64_t)qh * D + d] = __float2bfloat16_rn(val);
+        if (!isfinite(val)) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+        if (d == 0 && P.lse != nullptr) P.lse[(int64_t)pr.seq * P.hq + qh] = (M + __log2f(lsum)) * LN2;
       }
-      const float val = acc / lsum;
-      const int qh = pair.kv_head * P.grp + h;
-      P.out[pair.seq * P.out_stride + (int64_t)qh * D + tid] = __float2bfloat16_rn(val);
-      if (!isfinite(val)) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-      if (tid == 0 && P.lse != nullptr) P.lse[(int64_t)pair.seq * P.hq + qh] = (M + __log2f(lsum)) * LN2;
+      if (tid == 0) P.counters[pidx] = 0;
     }
-    if (tid == 0) P.counters[item.pair] = 0;
+    if (P.trace && tid == 0) {
+      P.trace[4 * blockIdx.x + 0] = t_start;
+      P.trace[4 * blockIdx.x + 1] = global_timer_ns();
+      P.trace[4 * blockIdx.x + 2] = sm_id();
+      P.trace[4 * blockIdx.x + 3] = merged;
+    }
   }
 };
 
 template <int KB, int VB, int G, typename ST>
-__global__ void __launch_bounds__(WARPS * 32) decode_kernel(Params P) {
+__global__ void __launch_bounds__(Cfg<KB, VB, G, ST>::THREADS, 1) decode_kernel(Params P) {
   extern __shared__ __align__(128) unsigned char smem[];
   Kernel<KB, VB, G, ST>::run(P, smem);
 }
 
 template <int KB, int VB, int G, typename ST>
-int launch(const Params& P, int num_items, cudaStream_t s) {
+int configure() {
   using C = Cfg<KB, VB, G, ST>;
-  auto fn = decode_kernel<KB, VB, G, ST>;
-  static bool configured[64] = {false};
+  static bool done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-      return ucb_host::set_error(UCB_ERR_CUDA, "decode kernel: cannot reserve %d bytes of shared memory", C::SMEM);
-    configured[dev] = true;
-  }
-  fn<<<num_items, WARPS * 32, C::SMEM, s>>>(P);
+  if (dev >= 0 && dev < 64 && done[dev]) return UCB_OK;
+  if (cudaFuncSetAttribute(decode_kernel<KB, VB, G, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+      cudaSuccess)
+    return ucb_host::set_error(UCB_ERR_CUDA, "decode kernel: cannot reserve %d bytes of shared memory", C::SMEM);
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return UCB_OK;
+}
+
+template <int KB, int VB, int G, typename ST>
+int launch(const Params& P, int num_ctas, cudaStream_t s) {
+  using C = Cfg<KB, VB, G, ST>;
+  int rc = configure<KB, VB, G, ST>();
+  if (rc) return rc;
+  decode_kernel<KB, VB, G, ST><<<num_ctas, C::THREADS, C::SMEM, s>>>(P);
   return ucb_host::check_launch("decode_kernel");
 }
 
 template <int KB, int VB, int G, typename ST>
-int slots(int* out) {
+int slots(int* out, int* warps) {
   using C = Cfg<KB, VB, G, ST>;
-  auto fn = decode_kernel<KB, VB, G, ST>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-    return ucb_host::set_error(UCB_ERR_CUDA, "decode kernel: shared memory attribute failed");
+  int rc = configure<KB, VB, G, ST>();
+  if (rc) return rc;
+  *warps = C::WARPS;
   int per_sm = 0, dev = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, WARPS * 32, C::SMEM) != cudaSuccess ||
-      cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<KB, VB, G, ST>, C::THREADS, C::SMEM) !=
+          cudaSuccess ||
+      cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return ucb_host::set_error(UCB_ERR_CUDA, "decode kernel: occupancy query failed");
+  if (per_sm < 1) return ucb_host::set_error(UCB_ERR_CUDA, "decode kernel does not fit on an SM");
   *out = per_sm * sms;
   return UCB_OK;
 }
 
-// Dispatch over the packed configuration.
 template <template <int, int, int, typename> class Fn, typename... Args>
 int dispatch(int kb, int vb, int g, Args... args) {
-#define UCB_CASE(KB_, VB_, G_)                                                             \
+#define UCB_CASE(KB_, VB_, G_) \
   if (kb == KB_ && vb == VB_ && g == G_) return Fn<KB_, VB_, G_, __nv_bfloat16>::call(args...);
   UCB_CASE(2, 2, 32) UCB_CASE(2, 2, 64) UCB_CASE(2, 2, 128)
   UCB_CASE(4, 4, 32) UCB_CASE(4, 4, 64) UCB_CASE(4, 4, 128)
@@ -695,10 +763,10 @@ struct LaunchFn {
 };
 template <int KB, int VB, int G, typename ST>
 struct SlotsFn {
-  static int call(int* out) { return slots<KB, VB, G, ST>(out); }
+  static int call(int* out, int* warps) { return slots<KB, VB, G, ST>(out, warps); }
 };
 
-// ---------------------------------------------------------------- partial merge
+// ---------------------------------------------------------------- partial merge (cross-GPU)
 // Merge n_parts partial blocks per pair (layout [part][pair]) into the output.
 __global__ void merge_partials_kernel(const float* __restrict__ parts, int n_parts, const ucb_decode_pair* pairs,
                                       int num_pairs, int grp, int num_kv_heads, __nv_bfloat16* out,
@@ -707,8 +775,7 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int n_par
   const ucb_decode_pair pair = pairs[pidx];
   for (int h = 0; h < grp; ++h) {
     float M = -INFINITY;
-    for (int p = 0; p < n_parts; ++p)
-      M = fmaxf(M, parts[((int64_t)p * num_pairs + pidx) * PARTIAL_FLOATS + h]);
+    for (int p = 0; p < n_parts; ++p) M = fmaxf(M, parts[((int64_t)p * num_pairs + pidx) * PARTIAL_FLOATS + h]);
     float acc = 0.f, lsum = 0.f;
     for (int p = 0; p < n_parts; ++p) {
       const float* pp = parts + ((int64_t)p * num_pairs + pidx) * PARTIAL_FLOATS;
@@ -728,30 +795,39 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int n_par
 
 using ucb_host::set_error;
 
-extern "C" int64_t ucb_decode_partial_bytes(int head_dim) {
-  return (int64_t)(16 + 8 * head_dim) * 4;
+namespace {
+uint64_t* g_decode_trace = nullptr;  // diagnostics only; see ucb_decode_set_trace
 }
 
-extern "C" int ucb_decode_slots(int k_bits, int v_bits, int group_size, int stat_dtype, int* slots) {
-  if (!slots) return set_error(UCB_ERR_INVALID, "ucb_decode_slots: null output");
-  if (stat_dtype != UCB_BF16) return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_slots: bf16 statistics only");
-  return ucb::decode::dispatch<ucb::decode::SlotsFn>(k_bits, v_bits, group_size, slots);
+extern "C" int ucb_decode_set_trace(void* trace_dev) {
+  g_decode_trace = static_cast<uint64_t*>(trace_dev);
+  return UCB_OK;
+}
+
+extern "C" int64_t ucb_decode_partial_bytes(int head_dim) { return (int64_t)(16 + 8 * head_dim) * 4; }
+
+extern "C" int ucb_decode_config(int k_bits, int v_bits, int group_size, int stat_dtype, int* ctas,
+                                 int* warps_per_cta) {
+  if (!ctas || !warps_per_cta) return set_error(UCB_ERR_INVALID, "ucb_decode_config: null output");
+  if (stat_dtype != UCB_BF16) return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_config: bf16 statistics only");
+  return ucb::decode::dispatch<ucb::decode::SlotsFn>(k_bits, v_bits, group_size, ctas, warps_per_cta);
 }
 
 extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int num_q_heads, int num_kv_heads,
-                                    int head_dim, const ucb_span* spans, const ucb_decode_item* items,
-                                    int num_items, const ucb_decode_pair* pairs, int num_pairs, int k_bits,
-                                    int v_bits, int group_size, int stat_dtype, float softmax_scale,
-                                    void* partials, int* counters, void* out, int64_t out_stride, float* lse,
-                                    void* stream) {
-  if (!query || !spans || !items || !pairs || !partials || !counters || !out)
+                                    int head_dim, const ucb_span* spans, int num_spans, const ucb_decode_cta* ctas,
+                                    int num_ctas, const int32_t* warp_bounds, const ucb_decode_pair* pairs,
+                                    int num_pairs, int k_bits, int v_bits,
+                                    int group_size, int stat_dtype, float softmax_scale, void* partials,
+                                    int* counters, void* out, int64_t out_stride, float* lse, void* stream) {
+  if (!query || !spans || !ctas || !warp_bounds || !pairs || !partials || !counters || !out)
     return set_error(UCB_ERR_INVALID, "ucb_decode_attention: null pointer");
   if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention: head_dim must be 128");
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > 8)
     return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention: need q_heads/kv_heads in [1, 8]");
   if (stat_dtype != UCB_BF16)
     return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention: packed statistics must be bf16");
-  if (num_items <= 0 || num_pairs <= 0) return set_error(UCB_ERR_INVALID, "ucb_decode_attention: empty batch");
+  if (num_ctas <= 0 || num_pairs <= 0 || num_spans <= 0)
+    return set_error(UCB_ERR_INVALID, "ucb_decode_attention: empty batch");
   if (query_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(query) & 15))
     return set_error(UCB_ERR_INVALID, "ucb_decode_attention: query/out rows must be 16-byte aligned");
   unsigned int* err = ucb_host::device_error_word();
@@ -762,7 +838,9 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.grp = num_q_heads / num_kv_heads;
   P.hq = num_q_heads;
   P.spans = spans;
-  P.items = items;
+  P.num_spans = num_spans;
+  P.ctas = ctas;
+  P.warp_bounds = warp_bounds;
   P.pairs = pairs;
   P.scale_log2 = softmax_scale * ucb::decode::LOG2E;
   P.partials = static_cast<float*>(partials);
@@ -771,7 +849,8 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.out_stride = out_stride;
   P.lse = lse;
   P.err = err;
-  return ucb::decode::dispatch<ucb::decode::LaunchFn>(k_bits, v_bits, group_size, P, num_items,
+  P.trace = g_decode_trace;
+  return ucb::decode::dispatch<ucb::decode::LaunchFn>(k_bits, v_bits, group_size, P, num_ctas,
                                                       static_cast<cudaStream_t>(stream));
 }
 

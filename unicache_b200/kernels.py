@@ -16,7 +16,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _capi
-from ._capi import UcbDecodeItem, UcbDecodePair, UcbSpan, call
+from ._capi import UcbDecodeCta, UcbDecodePair, UcbSpan, call
 
 _DTYPE_CODES = {torch.bfloat16: _capi.UCB_BF16, torch.float16: _capi.UCB_F16, torch.float32: _capi.UCB_F32}
 
@@ -238,8 +238,9 @@ def compact_rows(src: torch.Tensor, mask: torch.Tensor, types: torch.Tensor | No
 
 
 # ---------------------------------------------------------------- decode attention
-PACKED_STAGE = 64
-DENSE_STAGE = 16
+PACKED_STAGE = 64   # tokens per packed unit (decode kernel stage)
+DENSE_STAGE = 8     # tokens per dense unit
+MAX_PAIRS_PER_CTA = 4
 
 
 @dataclass
@@ -260,8 +261,9 @@ class DecodePlan:
     """Device tables of a decode batch over immutable (frozen) physical caches.
 
     Built once per cache layout and reused for every decode step: pairs are
-    (sequence, KV head), spans are a pair's packed or dense token ranges and
-    items are the CTA work units (see include/unicache_b200.h).
+    (sequence, KV head), spans are a pair's packed or dense token ranges, and
+    CTA records give every persistent CTA an equal-bytes range of stage units
+    (see include/unicache_b200.h).
     """
 
     device: torch.device
@@ -272,9 +274,11 @@ class DecodePlan:
     v_bits: int
     group_size: int
     spans: torch.Tensor
-    items: torch.Tensor
+    ctas: torch.Tensor
+    warp_bounds: torch.Tensor
     pairs: torch.Tensor
-    num_items: int
+    num_spans: int
+    num_ctas: int
     num_pairs: int
     partials: torch.Tensor
     counters: torch.Tensor
@@ -301,17 +305,21 @@ class DecodePlan:
         if lse is None:
             lse = torch.empty((self.num_seqs, q_heads), device=query.device, dtype=torch.float32)
         call("ucb_decode_attention", query.data_ptr(), query.stride(0), q_heads, self.num_kv_heads,
-             self.head_dim, self.spans.data_ptr(), self.items.data_ptr(), self.num_items, self.pairs.data_ptr(),
-             self.num_pairs, self.k_bits, self.v_bits, self.group_size, _capi.UCB_BF16, scale,
-             self.partials.data_ptr(), self.counters.data_ptr(), out.data_ptr(), out.stride(0),
+             self.head_dim, self.spans.data_ptr(), self.num_spans, self.ctas.data_ptr(), self.num_ctas,
+             self.warp_bounds.data_ptr(), self.pairs.data_ptr(), self.num_pairs, self.k_bits, self.v_bits,
+             self.group_size, _capi.UCB_BF16,
+             scale, self.partials.data_ptr(), self.counters.data_ptr(), out.data_ptr(), out.stride(0),
              lse.data_ptr(), stream_of(query))
         return out, lse
 
 
-def decode_slots(k_bits: int, v_bits: int, group_size: int) -> int:
-    slots = ctypes.c_int(0)
-    call("ucb_decode_slots", k_bits, v_bits, group_size, _capi.UCB_BF16, ctypes.byref(slots))
-    return int(slots.value)
+def decode_config(k_bits: int, v_bits: int, group_size: int) -> tuple[int, int]:
+    """(CTAs that run at once, warps per CTA) of the decode kernel on this device."""
+
+    ctas = ctypes.c_int(0)
+    warps = ctypes.c_int(0)
+    call("ucb_decode_config", k_bits, v_bits, group_size, _capi.UCB_BF16, ctypes.byref(ctas), ctypes.byref(warps))
+    return int(ctas.value), int(warps.value)
 
 
 def _packed_span(cache, head: int) -> UcbSpan:
@@ -340,6 +348,8 @@ def _dense_span(rows: DenseRows) -> UcbSpan:
                                     ("value", rows.value, rows.value_offset, rows.value_stride)):
         if base.dtype != torch.bfloat16:
             raise ValueError(f"dense {name} rows must be bfloat16")
+        if base.stride(-1) != 1:
+            raise ValueError(f"dense {name} rows must have a unit channel stride")
         if (base.data_ptr() + off * es) % 16 or (stride * es) % 16:
             raise ValueError(f"dense {name} rows must start on 16-byte boundaries")
     return sp
@@ -348,8 +358,8 @@ def _dense_span(rows: DenseRows) -> UcbSpan:
 def dense_rows_token_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
     """[N, H, D] tensors (dense cache, KIVI residual)."""
 
-    return DenseRows(key, value, head * key.stride(1), head * value.stride(1),
-                     key.stride(0), value.stride(0), int(key.shape[0]))
+    return DenseRows(key, value, head * key.stride(1), head * value.stride(1), key.stride(0), value.stride(0),
+                     int(key.shape[0]))
 
 
 def dense_rows_head_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
@@ -363,8 +373,78 @@ def packed_bytes_per_token(k_bits: int, v_bits: int, group_size: int, head_dim: 
     return head_dim * (k_bits + v_bits) / 8 + 2 * stat_bytes * head_dim / group_size * 2
 
 
+def _split_warps(weights: list[float], segs: list[int], u0: int, u1: int, warps: int) -> list[int] | None:
+    """Cut [u0, u1) into ``warps`` contiguous ranges of about equal weight, each
+    crossing at most one segment boundary; None if that is impossible."""
+
+    total = sum(weights[u0:u1])
+    bounds = [u0]
+    u, acc = u0, 0.0
+    for w in range(warps - 1):
+        target = total * (w + 1) / warps
+        start, crossed = u, 0
+        while u < u1 and acc + weights[u] / 2 <= target:
+            if u > start and segs[u] != segs[u - 1]:
+                if crossed:
+                    break
+                crossed = 1
+            acc += weights[u]
+            u += 1
+        bounds.append(u)
+    bounds.append(u1)
+    last = bounds[-2]
+    if sum(1 for k in range(last + 1, u1) if segs[k] != segs[k - 1]) > 1:
+        return None
+    return bounds
+
+
+def _assign_ctas(unit_weights: list[float], unit_pair: list[int], unit_seg: list[int], num_ctas: int,
+                 warps: int) -> list[list[int]]:
+    """Cut the unit sequence into about ``num_ctas`` contiguous ranges of equal
+    weight, each touching at most MAX_PAIRS_PER_CTA pairs, and split every range
+    into per-warp bounds.  Returns one bounds list (warps + 1 entries) per CTA."""
+
+    total = sum(unit_weights)
+    n = len(unit_weights)
+    ranges = []
+    u, acc = 0, 0.0
+    for c in range(num_ctas):
+        if u >= n:
+            break
+        target = total * (c + 1) / num_ctas
+        begin = u
+        pairs = {unit_pair[u]}
+        acc += unit_weights[u]
+        u += 1
+        while u < n and acc + unit_weights[u] / 2 <= target:
+            if unit_pair[u] not in pairs and len(pairs) == MAX_PAIRS_PER_CTA:
+                break
+            pairs.add(unit_pair[u])
+            acc += unit_weights[u]
+            u += 1
+        ranges.append((begin, u))
+    while u < n:  # leftovers, only when the pair cap cut ranges short
+        begin, pairs = u, set()
+        while u < n and (unit_pair[u] in pairs or len(pairs) < MAX_PAIRS_PER_CTA):
+            pairs.add(unit_pair[u])
+            u += 1
+        ranges.append((begin, u))
+    out = []
+    stack = list(reversed(ranges))
+    while stack:
+        u0, u1 = stack.pop()
+        bounds = _split_warps(unit_weights, unit_seg, u0, u1, warps)
+        if bounds is None:
+            mid = (u0 + u1) // 2
+            stack.append((mid, u1))
+            stack.append((u0, mid))
+            continue
+        out.append(bounds)
+    return out
+
+
 def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int = 128,
-                      target_items: int | None = None, min_packed_stages: int = 4) -> DecodePlan:
+                      target_ctas: int | None = None) -> DecodePlan:
     """Build device tables for decode over ``sequences``: one list of segments
     per sequence, each segment a b200 ``PackedKIVICache`` (its residual rides
     along as a dense span), a ``GQAH2OCache`` or a ``(key, value)`` pair of dense
@@ -373,12 +453,17 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
     from .storage.physical import GQAH2OCache, PackedKIVICache
 
     spans: list[UcbSpan] = []
-    span_pair: list[int] = []
     span_bytes: list[float] = []
     keepalive: list = []
     pairs_info: list[tuple[int, int]] = []
     cfg = None
     device = None
+
+    def add(sp: UcbSpan, pair: int, nbytes: float):
+        sp.pair = pair
+        spans.append(sp)
+        span_bytes.append(nbytes)
+
     for b, segments in enumerate(sequences):
         for h in range(num_kv_heads):
             pair = len(pairs_info)
@@ -397,24 +482,18 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
                             raise ValueError("8-bit packed segments are not supported by the decode kernel")
                         if seg.head_dim != head_dim:
                             raise ValueError("packed segment head_dim mismatch")
-                        spans.append(_packed_span(seg, h))
-                        span_pair.append(pair)
-                        span_bytes.append(seg.quantized_tokens * packed_bytes_per_token(
+                        add(_packed_span(seg, h), pair, seg.quantized_tokens * packed_bytes_per_token(
                             seg.k_bits, seg.v_bits, seg.group_size, head_dim))
                         keepalive.append(seg)
                         device = seg.key_code.device
                     if int(seg.residual_key.shape[0]):
                         rows = dense_rows_token_major(seg.residual_key, seg.residual_value, h)
-                        spans.append(_dense_span(rows))
-                        span_pair.append(pair)
-                        span_bytes.append(rows.tokens * head_dim * 4)
+                        add(_dense_span(rows), pair, rows.tokens * head_dim * 4)
                         keepalive.append(seg)
                         device = seg.residual_key.device
                 elif isinstance(seg, GQAH2OCache):
                     rows = dense_rows_head_major(seg.key, seg.value, h)
-                    spans.append(_dense_span(rows))
-                    span_pair.append(pair)
-                    span_bytes.append(rows.tokens * head_dim * 4)
+                    add(_dense_span(rows), pair, rows.tokens * head_dim * 4)
                     keepalive.append(seg)
                     device = seg.key.device
                 else:
@@ -422,9 +501,7 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
                     if int(key.shape[0]) == 0:
                         continue
                     rows = dense_rows_token_major(key, value, h)
-                    spans.append(_dense_span(rows))
-                    span_pair.append(pair)
-                    span_bytes.append(rows.tokens * head_dim * 4)
+                    add(_dense_span(rows), pair, rows.tokens * head_dim * 4)
                     keepalive.append((key, value))
                     device = key.device
     if device is None:
@@ -432,39 +509,64 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
     k_bits, v_bits, group, stat_dtype = cfg if cfg is not None else (2, 2, 64, torch.bfloat16)
     if stat_dtype != torch.bfloat16:
         raise ValueError("the decode kernel reads bfloat16 packed statistics")
-    if target_items is None:
-        with torch.cuda.device(device):
-            target_items = decode_slots(k_bits, v_bits, group)
-    # Split spans into items of about equal bytes (one wave of CTAs).
-    total = sum(span_bytes)
-    budget = max(total / max(1, target_items), 1.0)
-    items_by_pair: dict[int, list[tuple[int, int, int]]] = {p: [] for p in range(len(pairs_info))}
-    for s, sp in enumerate(spans):
-        align = PACKED_STAGE if sp.kind == 0 else DENSE_STAGE
-        units = max(1, math.ceil(sp.tokens / align))
-        want = max(1, round(span_bytes[s] / budget))
-        if sp.kind == 0:
-            want = min(want, max(1, units // min_packed_stages))
-        want = min(want, units)
-        for k in range(want):
-            u0 = k * units // want
-            u1 = (k + 1) * units // want
-            t0, t1 = u0 * align, min(sp.tokens, u1 * align)
-            if t1 > t0:
-                items_by_pair[span_pair[s]].append((s, t0, t1))
-    items: list[UcbDecodeItem] = []
-    pairs: list[UcbDecodePair] = []
+    covered = {sp.pair for sp in spans}
     for p, (b, h) in enumerate(pairs_info):
-        entries = items_by_pair[p]
-        if not entries:
+        if p not in covered:
             raise ValueError(f"sequence {b} has no tokens for KV head {h}")
+
+    # Units: 64-token packed stages and 8-token dense stages, in span order; a
+    # segment is a run of units with the same (pair, kind).
+    unit_weights: list[float] = []
+    unit_pair: list[int] = []
+    unit_seg: list[int] = []
+    seg_id, last_key = -1, None
+    for s, sp in enumerate(spans):
+        stage = PACKED_STAGE if sp.kind == 0 else DENSE_STAGE
+        units = math.ceil(sp.tokens / stage)
+        sp.unit_begin = len(unit_weights)
+        if (sp.pair, sp.kind) != last_key:
+            seg_id += 1
+            last_key = (sp.pair, sp.kind)
+        per_token = span_bytes[s] / sp.tokens
+        for k in range(units):
+            n = min(stage, sp.tokens - k * stage)
+            unit_weights.append(per_token * n)
+            unit_pair.append(sp.pair)
+            unit_seg.append(seg_id)
+    with torch.cuda.device(device):
+        slots, warps = decode_config(k_bits, v_bits, group)
+    if target_ctas is None:
+        target_ctas = slots
+    cta_bounds = _assign_ctas(unit_weights, unit_pair, unit_seg, target_ctas, warps)
+
+    span_starts = [sp.unit_begin for sp in spans]
+    ctas: list[UcbDecodeCta] = []
+    touched: dict[int, list[int]] = {}
+    flat_bounds: list[int] = []
+    for c, bounds in enumerate(cta_bounds):
+        u0, u1 = bounds[0], bounds[-1]
+        flat_bounds.extend(bounds)
+        rec = UcbDecodeCta()
+        rec.unit_begin, rec.unit_end = u0, u1
+        rec.span_begin = max(i for i, st in enumerate(span_starts) if st <= u0)
+        p0, p1 = unit_pair[u0], unit_pair[u1 - 1]
+        rec.pair_begin, rec.num_pairs = p0, p1 - p0 + 1
+        if rec.num_pairs > MAX_PAIRS_PER_CTA:
+            raise AssertionError("decode planner produced a CTA range over too many pairs")
+        ctas.append(rec)
+        for p in range(p0, p1 + 1):
+            touched.setdefault(p, []).append(c)
+    pairs: list[UcbDecodePair] = []
+    partial_total = 0
+    for p, (b, h) in enumerate(pairs_info):
+        cs = touched[p]
+        if cs != list(range(cs[0], cs[0] + len(cs))):
+            raise AssertionError("CTAs of a pair must be consecutive")
         pr = UcbDecodePair()
-        pr.seq, pr.kv_head, pr.partial_begin, pr.partial_count = b, h, len(items), len(entries)
+        pr.seq, pr.kv_head = b, h
+        pr.partial_begin, pr.partial_count, pr.cta_first = partial_total, len(cs), cs[0]
+        partial_total += len(cs)
         pairs.append(pr)
-        for s, t0, t1 in entries:
-            it = UcbDecodeItem()
-            it.span, it.token_begin, it.token_end, it.pair, it.partial = s, t0, t1, p, len(items)
-            items.append(it)
 
     def upload(structs) -> torch.Tensor:
         raw = _capi.struct_array_bytes(structs)
@@ -481,14 +583,16 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         v_bits=v_bits,
         group_size=group,
         spans=upload(spans),
-        items=upload(items),
+        ctas=upload(ctas),
+        warp_bounds=torch.tensor(flat_bounds, dtype=torch.int32).to(device),
         pairs=upload(pairs),
-        num_items=len(items),
+        num_spans=len(spans),
+        num_ctas=len(ctas),
         num_pairs=len(pairs),
-        partials=torch.empty(len(items) * partial_bytes, device=device, dtype=torch.uint8),
+        partials=torch.empty(partial_total * partial_bytes, device=device, dtype=torch.uint8),
         counters=torch.zeros(len(pairs), device=device, dtype=torch.int32),
         keepalive=keepalive,
-        bytes_per_step=int(total),
+        bytes_per_step=int(sum(span_bytes)),
     )
 
 
