@@ -151,14 +151,14 @@ typedef struct ucb_decode_cta {
   int32_t span_begin;        /* span containing unit_begin                    */
   int32_t pair_begin;
   int32_t num_pairs;         /* 1..4                                          */
-  int32_t reserved[3];
+  int32_t reserved[3];       /* [0]: span_end, one past the last span (<= span_begin + 16) */
 } ucb_decode_cta;
 
 typedef struct ucb_decode_pair {
   int32_t seq;
   int32_t kv_head;
   int32_t partial_begin;
-  int32_t partial_count;     /* CTAs touching this pair                       */
+  int32_t partial_count;     /* CTAs touching this pair, at most 160           */
   int32_t cta_first;         /* first CTA touching this pair                  */
   int32_t reserved[3];
 } ucb_decode_pair;
@@ -177,9 +177,11 @@ UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, in
                          void* partials_dev, int* counters_dev, void* out_dev, int64_t out_stride,
                          float* lse_dev, void* stream);
 
-/* Diagnostics: when trace_dev (device memory, 4 uint64 per CTA) is not NULL,
- * later ucb_decode_attention calls record per CTA {start ns, end ns, SM id,
- * pairs it merged}.  NULL switches it off. */
+/* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
+ * NULL, later ucb_decode_attention calls record per CTA {start, streaming
+ * loops done, merge ticket taken, end, SM id, pairs it merged, then the loop
+ * end of each warp} (times from the global timer, ns).  NULL switches it
+ * off. */
 UCB_API int ucb_decode_set_trace(void* trace_dev);
 
 /* Launch shape of ucb_decode_attention on the current device: CTAs that run at

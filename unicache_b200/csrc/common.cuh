@@ -49,6 +49,12 @@ __device__ __forceinline__ void fence_mbarrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// 16-byte asynchronous global->shared copy through L2 only (data other SMs wrote).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -98,6 +104,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_u32(dst_smem)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// L2 policy for data read once per launch (the KV stream): evicting it first
+// keeps the kernel's code, descriptors and partials resident in L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 
@@ -157,11 +181,12 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return d;
 }
 
-// (x - 128) * s + m on bf16 pairs, where x holds 128 + code in each half (exact):
-// the subtraction is exact and the fused multiply-add rounds once to bf16.
-__device__ __forceinline__ uint32_t bf16x2_dequant(uint32_t x, uint32_t s, uint32_t m) {
+// (x - M) * s + m on bf16 pairs, where x holds M + code in each half exactly
+// and neg_m holds -M: the subtraction is exact and the fused multiply-add
+// rounds once to bf16.
+__device__ __forceinline__ uint32_t bf16x2_dequant(uint32_t x, uint32_t neg_m, uint32_t s, uint32_t m) {
   uint32_t c, d;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(c) : "r"(x), "r"(0x3F803F80u), "r"(0xC300C300u));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(c) : "r"(x), "r"(0x3F803F80u), "r"(neg_m));
   asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(c), "r"(s), "r"(m));
   return d;
 }

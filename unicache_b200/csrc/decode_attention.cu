@@ -42,6 +42,8 @@ constexpr int DT = 8;             // tokens per dense stage
 constexpr int DROW = 272;         // dense shared-memory row stride (bytes), conflict-free ldmatrix
 constexpr int DENSE_STAGE = 2 * DT * DROW;
 constexpr int MAXC = 4;           // pairs one CTA may touch
+constexpr int MAX_SPANS = 16;     // spans one CTA may touch
+constexpr int MAXP = 160;         // partials of one pair (CTAs touching it)
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr int PARTIAL_FLOATS = 16 + 8 * D;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -73,8 +75,16 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_ZERO + D * 2;                    // WARPS x 2 mbarriers
   static constexpr int OFF_TAG = OFF_BAR + WARPS * 2 * 8;             // WARPS x 2 state tags
   static constexpr int OFF_MISC = OFF_TAG + WARPS * 2 * 4;            // last-CTA flags
-  static constexpr int SMEM = OFF_MISC + 64;
+  static constexpr int OFF_SPANS = round_up(OFF_MISC + 64, 16);       // the CTA's spans
+  static constexpr int OFF_PAIRS = OFF_SPANS + MAX_SPANS * (int)sizeof(ucb_span);  // the CTA's pair records
+  static constexpr int SMEM = OFF_PAIRS + MAXC * (int)sizeof(ucb_decode_pair);
   static_assert(SLOT >= PARTIAL_FLOATS * 4, "a ring slot must hold a warp state");
+  // partials whose rows the last CTA of a pair stages in shared memory
+  static constexpr int MCAP_RAW = (WARPS * 2 * SLOT - (MAXP * 24 + 16) * 4) / (8 * D * 4);
+  static constexpr int MCAP = MCAP_RAW > 16 ? 16 : MCAP_RAW;
+  static_assert(MCAP >= 4, "the ring must hold the merge tables and a few partials");
+  static_assert(MAXC * 2 * WARPS * 9 * 4 + MAXC * 4 <= MAXC * 8 * D * 2, "merge tables must fit the query rows");
+  static_assert(2 * WARPS <= 32, "one lane per warp state");
 };
 
 // Token <-> MMA-row map inside a 16-token tile.  Row r and row r+8 of lane
@@ -105,18 +115,21 @@ __device__ __forceinline__ float warp_sum_r(float v) {
   return v;
 }
 
-// Online-softmax update for NTILE C fragments (logits in, probabilities out).
-// Returns whether any lane's running max moved (then accumulators need alpha).
+// Online-softmax update for NTILE C fragments.  `lg` holds raw q.k (or -inf
+// for masked slots) and becomes exp2(q.k * scale_log2 - running max); the max
+// is kept in the log2 domain.  Returns whether any lane's running max moved
+// (then the accumulators need the alpha factors).
 template <int NTILE>
-__device__ __forceinline__ bool softmax_update(float (&lg)[NTILE][4], WarpState& st, float& alpha0, float& alpha1) {
+__device__ __forceinline__ bool softmax_update(float (&lg)[NTILE][4], float scale_log2, WarpState& st, float& alpha0,
+                                               float& alpha1) {
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int j = 0; j < NTILE; ++j) {
     mx0 = fmaxf(mx0, fmaxf(lg[j][0], lg[j][2]));
     mx1 = fmaxf(mx1, fmaxf(lg[j][1], lg[j][3]));
   }
-  mx0 = warp_max_r(mx0);
-  mx1 = warp_max_r(mx1);
+  mx0 = warp_max_r(mx0) * scale_log2;
+  mx1 = warp_max_r(mx1) * scale_log2;
   const float n0 = fmaxf(st.mrun[0], mx0), n1 = fmaxf(st.mrun[1], mx1);
   const bool moved = __any_sync(0xffffffffu, n0 != st.mrun[0] || n1 != st.mrun[1]);
   alpha0 = fast_exp2(st.mrun[0] - n0);
@@ -124,10 +137,10 @@ __device__ __forceinline__ bool softmax_update(float (&lg)[NTILE][4], WarpState&
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
   for (int j = 0; j < NTILE; ++j) {
-    lg[j][0] = fast_exp2(lg[j][0] - n0);
-    lg[j][1] = fast_exp2(lg[j][1] - n1);
-    lg[j][2] = fast_exp2(lg[j][2] - n0);
-    lg[j][3] = fast_exp2(lg[j][3] - n1);
+    lg[j][0] = fast_exp2(fmaf(lg[j][0], scale_log2, -n0));
+    lg[j][1] = fast_exp2(fmaf(lg[j][1], scale_log2, -n1));
+    lg[j][2] = fast_exp2(fmaf(lg[j][2], scale_log2, -n0));
+    lg[j][3] = fast_exp2(fmaf(lg[j][3], scale_log2, -n1));
     s0 += lg[j][0] + lg[j][2];
     s1 += lg[j][1] + lg[j][3];
   }
@@ -158,7 +171,7 @@ struct Params {
   int64_t out_stride;
   float* lse;
   unsigned int* err;
-  uint64_t* trace;  // optional: per CTA {start ns, end ns, sm id, pairs merged}
+  uint64_t* trace;  // optional: per CTA 12 words, see ucb_decode_set_trace
 };
 
 template <int KB, int VB, int G, typename ST>
@@ -183,12 +196,13 @@ struct Kernel {
     const unsigned char* kmin = static_cast<const unsigned char*>(sp.key_minimum) + (size_t)g0 * D * sizeof(ST);
     const unsigned char* vscale = static_cast<const unsigned char*>(sp.value_scale) + (size_t)t0 * C::NG * sizeof(ST);
     const unsigned char* vmin = static_cast<const unsigned char*>(sp.value_minimum) + (size_t)t0 * C::NG * sizeof(ST);
-    bulk_g2s(slot + C::OFF_KC, kcode, kc, bar);
-    bulk_g2s(slot + C::OFF_VC, vcode, vc, bar);
-    bulk_g2s(slot + C::OFF_KS, kscale, ks, bar);
-    bulk_g2s(slot + C::OFF_KM, kmin, ks, bar);
-    bulk_g2s(slot + C::OFF_VS, vscale, vs, bar);
-    bulk_g2s(slot + C::OFF_VM, vmin, vs, bar);
+    const uint64_t pol = l2_evict_first_policy();
+    bulk_g2s_hint(slot + C::OFF_KC, kcode, kc, bar, pol);
+    bulk_g2s_hint(slot + C::OFF_VC, vcode, vc, bar, pol);
+    bulk_g2s_hint(slot + C::OFF_KS, kscale, ks, bar, pol);
+    bulk_g2s_hint(slot + C::OFF_KM, kmin, ks, bar, pol);
+    bulk_g2s_hint(slot + C::OFF_VS, vscale, vs, bar, pol);
+    bulk_g2s_hint(slot + C::OFF_VM, vmin, vs, bar, pol);
   }
 
   __device__ static void issue_dense(const ucb_span& sp, int t0, int t1, unsigned char* slot, uint64_t* bar,
@@ -204,7 +218,8 @@ struct Kernel {
       const bool is_v = lane >= 8;
       const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(is_v ? sp.value_code : sp.key_code);
       const int64_t stride = is_v ? sp.value_stride : sp.key_stride;
-      bulk_g2s(slot + (is_v ? DT * DROW : 0) + row * DROW, base + (t0 + row) * stride, D * 2, bar);
+      bulk_g2s_hint(slot + (is_v ? DT * DROW : 0) + row * DROW, base + (t0 + row) * stride, D * 2, bar,
+                    l2_evict_first_policy());
     }
   }
 
@@ -223,19 +238,21 @@ struct Kernel {
     float acc[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    uint32_t sel_lo, sel_hi, msk, sh_lo, sh_hi;
+    // 2-bit: one PRMT copies byte (r%4) of two key words into both bytes of
+    // each half, one shift by 2*pr brings the codes of rows r and r+8 to bits
+    // 0-1 and 2-3 of each half; a single AND/OR then forms 128 + code or
+    // 32 + code exactly in bf16.  4-bit: one PRMT per row.
+    uint32_t sel_lo, sel_hi, sh_lo, sh_hi;
     if constexpr (KB == 2) {
-      sel_lo = sel_hi = (r & 3) | ((4 + (r & 3)) << 8);
-      sh_lo = 2 * pr;
-      sh_hi = 2 * pr2;
-      msk = 0x00030003u;
+      const uint32_t b = r & 3;
+      sel_lo = sel_hi = b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12);
+      sh_lo = sh_hi = 2 * pr;
     } else {
       const int blo = (r & 1) * 2 + (pr >> 1), bhi = (r & 1) * 2 + (pr2 >> 1);
       sel_lo = blo | ((4 + blo) << 8);
       sel_hi = bhi | ((4 + bhi) << 8);
       sh_lo = 4 * (pr & 1);
       sh_hi = 4 * (pr2 & 1);
-      msk = 0x000F000Fu;
     }
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) {
@@ -250,14 +267,21 @@ struct Kernel {
         const int gi = (G >= NT) ? 0 : (16 * j) / G;
         const int wr = (KB == 2) ? j : 2 * j + ((r & 3) >> 1);
         const uint4 w = lds128(slot + C::OFF_KC + (wr * D + 16 * kk + 4 * c) * 4);
-        const uint32_t y0l = prmt(w.x, w.y, sel_lo), y1l = prmt(w.z, w.w, sel_lo);
-        const uint32_t y0h = (KB == 2) ? y0l : prmt(w.x, w.y, sel_hi);
-        const uint32_t y1h = (KB == 2) ? y1l : prmt(w.z, w.w, sel_hi);
         uint32_t a[4];
-        a[0] = bf16x2_dequant(((y0l >> sh_lo) & msk) | 0x43004300u, ks[gi].x, km[gi].x);
-        a[1] = bf16x2_dequant(((y0h >> sh_hi) & msk) | 0x43004300u, ks[gi].x, km[gi].x);
-        a[2] = bf16x2_dequant(((y1l >> sh_lo) & msk) | 0x43004300u, ks[gi].y, km[gi].y);
-        a[3] = bf16x2_dequant(((y1h >> sh_hi) & msk) | 0x43004300u, ks[gi].y, km[gi].y);
+        if constexpr (KB == 2) {
+          const uint32_t z0 = prmt(w.x, w.y, sel_lo) >> sh_lo, z1 = prmt(w.z, w.w, sel_lo) >> sh_lo;
+          a[0] = bf16x2_dequant((z0 & 0x00030003u) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
+          a[1] = bf16x2_dequant((z0 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, ks[gi].x, km[gi].x);
+          a[2] = bf16x2_dequant((z1 & 0x00030003u) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
+          a[3] = bf16x2_dequant((z1 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, ks[gi].y, km[gi].y);
+        } else {
+          const uint32_t y0l = prmt(w.x, w.y, sel_lo), y1l = prmt(w.z, w.w, sel_lo);
+          const uint32_t y0h = prmt(w.x, w.y, sel_hi), y1h = prmt(w.z, w.w, sel_hi);
+          a[0] = bf16x2_dequant(((y0l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
+          a[1] = bf16x2_dequant(((y0h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
+          a[2] = bf16x2_dequant(((y1l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
+          a[3] = bf16x2_dequant(((y1h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
+        }
         mma_bf16(acc[j], a, qbp[kk][0], qbp[kk][1]);
       }
     }
@@ -265,14 +289,14 @@ struct Kernel {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const bool vlo = FULL || 16 * j + tok_lo < n_valid, vhi = FULL || 16 * j + tok_hi < n_valid;
-      lg[j][0] = vlo ? acc[j][0] * scale_log2 : -INFINITY;
-      lg[j][1] = vlo ? acc[j][1] * scale_log2 : -INFINITY;
-      lg[j][2] = vhi ? acc[j][2] * scale_log2 : -INFINITY;
-      lg[j][3] = vhi ? acc[j][3] * scale_log2 : -INFINITY;
+      lg[j][0] = vlo ? acc[j][0] : -INFINITY;
+      lg[j][1] = vlo ? acc[j][1] : -INFINITY;
+      lg[j][2] = vhi ? acc[j][2] : -INFINITY;
+      lg[j][3] = vhi ? acc[j][3] : -INFINITY;
     }
 
     float alpha0, alpha1;
-    if (softmax_update<4>(lg, st, alpha0, alpha1)) {
+    if (softmax_update<4>(lg, scale_log2, st, alpha0, alpha1)) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         o[i][0] *= alpha0;
@@ -403,12 +427,12 @@ struct Kernel {
       mma_bf16(acc, a, b0, b1);
     }
     float lg[1][4];
-    lg[0][0] = tok_lo < n_valid ? acc[0] * scale_log2 : -INFINITY;
-    lg[0][1] = tok_lo < n_valid ? acc[1] * scale_log2 : -INFINITY;
-    lg[0][2] = tok_hi < n_valid ? acc[2] * scale_log2 : -INFINITY;
-    lg[0][3] = tok_hi < n_valid ? acc[3] * scale_log2 : -INFINITY;
+    lg[0][0] = tok_lo < n_valid ? acc[0] : -INFINITY;
+    lg[0][1] = tok_lo < n_valid ? acc[1] : -INFINITY;
+    lg[0][2] = tok_hi < n_valid ? acc[2] : -INFINITY;
+    lg[0][3] = tok_hi < n_valid ? acc[3] : -INFINITY;
     float alpha0, alpha1;
-    if (softmax_update<1>(lg, st, alpha0, alpha1)) {
+    if (softmax_update<1>(lg, scale_log2, st, alpha0, alpha1)) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         o[i][0] *= alpha0;
@@ -515,6 +539,14 @@ struct Kernel {
     }
     for (int i = tid; i < D * 2 / 16; i += C::THREADS)
       reinterpret_cast<uint4*>(smem + C::OFF_ZERO)[i] = make_uint4(0, 0, 0, 0);
+    ucb_span* spans = reinterpret_cast<ucb_span*>(smem + C::OFF_SPANS);
+    // Pair records are cached: under full HBM load a global round trip costs
+    // microseconds, and the epilogue would otherwise pay several in a row.
+    ucb_decode_pair* pcache = reinterpret_cast<ucb_decode_pair*>(smem + C::OFF_PAIRS);
+    if (tid < cta.num_pairs) pcache[tid] = P.pairs[cta.pair_begin + tid];
+    const int n_spans = cta.reserved[0] - cta.span_begin;  // spans [span_begin, span_end)
+    for (int i = tid; i < n_spans * (int)(sizeof(ucb_span) / 8); i += C::THREADS)
+      reinterpret_cast<uint64_t*>(spans)[i] = reinterpret_cast<const uint64_t*>(P.spans + cta.span_begin)[i];
     if (lane == 0) {
       tags[2 * warp] = tags[2 * warp + 1] = -1;
       mbar_init(&bars[0], 1);
@@ -524,10 +556,10 @@ struct Kernel {
     __syncthreads();
 
     // ---- the warp's units, in order; an issue cursor runs two units ahead.
-    int issue_u = u_begin, issue_span = cta.span_begin;
+    int issue_u = u_begin, issue_span = 0;
     auto issue_next = [&](int slot_idx) {
-      while (issue_span + 1 < P.num_spans && P.spans[issue_span + 1].unit_begin <= issue_u) ++issue_span;
-      const ucb_span& sp = P.spans[issue_span];
+      while (issue_span + 1 < n_spans && spans[issue_span + 1].unit_begin <= issue_u) ++issue_span;
+      const ucb_span& sp = spans[issue_span];
       const int stage = sp.kind == 0 ? NT : DT;
       const int t0 = (issue_u - sp.unit_begin) * stage;
       const int t1 = min(sp.tokens, t0 + stage);
@@ -553,7 +585,7 @@ struct Kernel {
     for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) qbp[kk][0] = qbp[kk][1] = 0u;
-    int cur_pl = -1, cur_kind = -1, span = cta.span_begin;
+    int cur_pl = -1, cur_kind = -1, span = 0;
     bool ok = true, stashed = false;
     int s = 0;
     for (int u = u_begin; u < u_end; ++u, ++s) {
@@ -562,8 +594,8 @@ struct Kernel {
         ok = false;
         break;
       }
-      while (span + 1 < P.num_spans && P.spans[span + 1].unit_begin <= u) ++span;
-      const ucb_span& sp = P.spans[span];
+      while (span + 1 < n_spans && spans[span + 1].unit_begin <= u) ++span;
+      const ucb_span& sp = spans[span];
       const int pl = sp.pair - cta.pair_begin;
       const int kind = sp.kind;
       if (pl != cur_pl || kind != cur_kind) {
@@ -606,6 +638,7 @@ struct Kernel {
       __syncwarp();
       if (issue_u < u_end) issue_next(slot_idx);
     }
+    if (P.trace && lane == 0) P.trace[32 * blockIdx.x + 6 + warp] = global_timer_ns();
     if (!ok) {
       // Let copies still in flight land before the shared memory is reused.
       for (int k = s; k < s + 2; ++k) {
@@ -617,85 +650,145 @@ struct Kernel {
       if (lane == 0) tags[2 * warp + 1] = cur_pl;
     }
     __syncthreads();
+    const uint64_t t_loops = P.trace ? global_timer_ns() : 0;
 
-    // ---- merge the warp states of each pair into one partial
-    for (int pl = 0; pl < cta.num_pairs; ++pl) {
-      const ucb_decode_pair pr = P.pairs[cta.pair_begin + pl];
-      float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
-      for (int hd = tid; hd < 8 * D + 8; hd += C::THREADS) {
-        const bool is_l = hd >= 8 * D;
-        const int h = is_l ? hd - 8 * D : hd / D, d = hd % D;
-        float M = -INFINITY;
-        for (int w = 0; w < C::WARPS; ++w) {
+    // ---- merge the warp states of each pair into one partial.  One warp per
+    // (pair, head) finds the states of the pair with a ballot, their common
+    // maximum and exp2 weights; then every thread sums weighted rows.  The
+    // query rows are dead by now, so the weight tables live in their place.
+    const int grp = P.grp;
+    float* mw = reinterpret_cast<float*>(qs);                  // [MAXC][2*WARPS][8] weights
+    int* mlist = reinterpret_cast<int*>(mw + MAXC * 2 * C::WARPS * 8);  // [MAXC][2*WARPS] states
+    int* mcount = mlist + MAXC * 2 * C::WARPS;                 // [MAXC]
+    auto state_ptr = [&](int sidx) -> const float* {
+      return (sidx & 1) ? reinterpret_cast<const float*>(smem + (sidx >> 1) * 2 * C::SLOT)
+                        : reinterpret_cast<const float*>(smem + C::OFF_STASH) + (sidx >> 1) * PARTIAL_FLOATS;
+    };
+    for (int combo = warp; combo < cta.num_pairs * 8; combo += C::WARPS) {
+      const int pl = combo >> 3, h = combo & 7;
+      const bool mine = lane < 2 * C::WARPS && tags[lane] == pl;
+      const float* src = mine ? state_ptr(lane) : nullptr;
+      const float m = mine ? src[h] : -INFINITY;
+      const float l = mine ? src[8 + h] : 0.f;
+      float M = m;
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            if (tags[2 * w + k] != pl) continue;
-            const float* src = k ? reinterpret_cast<const float*>(smem + w * 2 * C::SLOT)
-                                 : reinterpret_cast<const float*>(smem + C::OFF_STASH) + w * PARTIAL_FLOATS;
-            M = fmaxf(M, src[h]);
-          }
-        }
-        float acc = 0.f;
-        for (int w = 0; w < C::WARPS; ++w) {
+      for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
+      float L = w * l;
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            if (tags[2 * w + k] != pl) continue;
-            const float* src = k ? reinterpret_cast<const float*>(smem + w * 2 * C::SLOT)
-                                 : reinterpret_cast<const float*>(smem + C::OFF_STASH) + w * PARTIAL_FLOATS;
-            if (src[h] == -INFINITY) continue;
-            acc = fmaf(fast_exp2(src[h] - M), is_l ? src[8 + h] : src[16 + h * D + d], acc);
-          }
-        }
-        if (is_l) {
-          part[h] = M;
-          part[8 + h] = acc;
-        } else {
-          part[16 + h * D + d] = acc;
-        }
+      for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      const unsigned ball = __ballot_sync(0xffffffffu, mine);
+      const int rank = __popc(ball & ((1u << lane) - 1u));
+      if (mine) {
+        mw[(pl * 2 * C::WARPS + rank) * 8 + h] = w;
+        if (h == 0) mlist[pl * 2 * C::WARPS + rank] = lane;
+      }
+      if (lane == 0) {
+        if (h == 0) mcount[pl] = __popc(ball);
+        const ucb_decode_pair& pr = pcache[pl];
+        float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
+        part[h] = M;
+        part[8 + h] = L;
       }
     }
-    __threadfence();
+    __syncthreads();
+    for (int pl = 0; pl < cta.num_pairs; ++pl) {
+      const ucb_decode_pair& pr = pcache[pl];
+      float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
+      const int n = mcount[pl];
+      const float* wrow = mw + pl * 2 * C::WARPS * 8;
+      const int* lrow = mlist + pl * 2 * C::WARPS;
+      for (int e = tid; e < grp * D; e += C::THREADS) {
+        const int h = e / D;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < n; ++i) acc = fmaf(wrow[i * 8 + h], state_ptr(lrow[i])[16 + e], acc);
+        part[16 + e] = acc;
+      }
+    }
+    // Release the partials with one gpu-scope fence per arriving pair after
+    // the CTA barrier (the barrier orders every thread's stores before it).
     __syncthreads();
     if (tid < cta.num_pairs) {
-      const ucb_decode_pair pr = P.pairs[cta.pair_begin + tid];
+      const ucb_decode_pair& pr = pcache[tid];
+      __threadfence();
       const int prev = atomicAdd(&P.counters[cta.pair_begin + tid], 1);
+      __threadfence();
       last_flags[tid] = (prev == pr.partial_count - 1) ? 1 : 0;
     }
     __syncthreads();
+    const uint64_t t_ticket = P.trace ? global_timer_ns() : 0;
+
+    // ---- last CTA of a pair: merge its partials.  Headers (max, sum) of all
+    // partials and the rows of the first MCAP partials are fetched into
+    // shared memory in one round of asynchronous copies.
     int merged = 0;
+    float* hdr = reinterpret_cast<float*>(smem);  // ring space is free now: [MAXP][16]
+    float* wts = hdr + MAXP * 16;                  // [MAXP][8] weights
+    float* tot = wts + MAXP * 8;                   // [8] sum, [8] max
+    float* rows = tot + 16;                        // [MCAP][grp*D]
     for (int pl = 0; pl < cta.num_pairs; ++pl) {
       if (!last_flags[pl]) continue;
       ++merged;
-      __threadfence();
       const int pidx = cta.pair_begin + pl;
-      const ucb_decode_pair pr = P.pairs[pidx];
+      const ucb_decode_pair& pr = pcache[pl];
+      const int np = pr.partial_count;  // <= MAXP (the planner guarantees it)
+      const int cap = np < C::MCAP ? np : C::MCAP;
+      const int gd4 = grp * D / 4;
       const float* base = P.partials + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
-      for (int hd = tid; hd < P.grp * D; hd += C::THREADS) {
-        const int h = hd / D, d = hd % D;
-        float M = -INFINITY;
-        for (int p = 0; p < pr.partial_count; ++p) M = fmaxf(M, __ldcg(base + (int64_t)p * PARTIAL_FLOATS + h));
-        float sum = 0.f, lsum = 0.f;
-        for (int p = 0; p < pr.partial_count; ++p) {
-          const float* pp = base + (int64_t)p * PARTIAL_FLOATS;
-          const float mp = __ldcg(pp + h);
-          if (mp == -INFINITY) continue;
-          const float f = fast_exp2(mp - M);
-          sum = fmaf(f, __ldcg(pp + 16 + h * D + d), sum);
-          lsum = fmaf(f, __ldcg(pp + 8 + h), lsum);
-        }
-        const float val = sum / lsum;
-        const int qh = pr.kv_head * P.grp + h;
-        P.out[pr.seq * P.out_stride + (int64_t)qh * D + d] = __float2bfloat16_rn(val);
-        if (!isfinite(val)) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-        if (d == 0 && P.lse != nullptr) P.lse[(int64_t)pr.seq * P.hq + qh] = (M + __log2f(lsum)) * LN2;
+      for (int i = tid; i < np * 4; i += C::THREADS)
+        cp_async16(smem_u32(hdr + 4 * i), base + (int64_t)(i >> 2) * PARTIAL_FLOATS + 4 * (i & 3));
+      for (int i = tid; i < cap * gd4; i += C::THREADS) {
+        const int pp = i / gd4, q4 = i - pp * gd4;
+        cp_async16(smem_u32(rows + 4 * i), base + (int64_t)pp * PARTIAL_FLOATS + 16 + 4 * q4);
       }
+      cp_async_wait_all();
+      __syncthreads();
+      if (warp < 8) {
+        const int h = warp;
+        float M = -INFINITY;
+        for (int pp = lane; pp < np; pp += 32) M = fmaxf(M, hdr[pp * 16 + h]);
+#pragma unroll
+        for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int pp = lane; pp < np; pp += 32) {
+          const float m = hdr[pp * 16 + h];
+          const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
+          wts[pp * 8 + h] = w;
+          L = fmaf(w, hdr[pp * 16 + 8 + h], L);
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane == 0) {
+          tot[h] = L;
+          tot[8 + h] = M;
+        }
+      }
+      __syncthreads();
+      for (int e = tid; e < grp * D; e += C::THREADS) {
+        const int h = e / D;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int pp = 0; pp < cap; ++pp) acc = fmaf(wts[pp * 8 + h], rows[pp * grp * D + e], acc);
+        for (int pp = cap; pp < np; ++pp)
+          acc = fmaf(wts[pp * 8 + h], __ldcg(base + (int64_t)pp * PARTIAL_FLOATS + 16 + e), acc);
+        const float val = acc / tot[h];
+        P.out[pr.seq * P.out_stride + (int64_t)(pr.kv_head * grp) * D + e] = __float2bfloat16_rn(val);
+        if (!isfinite(val)) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+      }
+      if (tid < grp && P.lse != nullptr)
+        P.lse[(int64_t)pr.seq * P.hq + pr.kv_head * grp + tid] = (tot[8 + tid] + __log2f(tot[tid])) * LN2;
       if (tid == 0) P.counters[pidx] = 0;
+      __syncthreads();
     }
     if (P.trace && tid == 0) {
-      P.trace[4 * blockIdx.x + 0] = t_start;
-      P.trace[4 * blockIdx.x + 1] = global_timer_ns();
-      P.trace[4 * blockIdx.x + 2] = sm_id();
-      P.trace[4 * blockIdx.x + 3] = merged;
+      uint64_t* tr = P.trace + 32 * blockIdx.x;
+      tr[0] = t_start;
+      tr[1] = t_loops;
+      tr[2] = t_ticket;
+      tr[3] = global_timer_ns();
+      tr[4] = sm_id();
+      tr[5] = merged;
     }
   }
 };

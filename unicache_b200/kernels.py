@@ -241,6 +241,13 @@ def compact_rows(src: torch.Tensor, mask: torch.Tensor, types: torch.Tensor | No
 PACKED_STAGE = 64   # tokens per packed unit (decode kernel stage)
 DENSE_STAGE = 8     # tokens per dense unit
 MAX_PAIRS_PER_CTA = 4
+MAX_SPANS_PER_CTA = 16
+# Warp time model fitted to per-warp loop times on B200 (2-bit K/V, G32):
+# a dense 8-token stage costs 0.55 of a full packed stage (0.83 per byte of a
+# 2-bit packed stage) and entering a new segment costs 0.4 packed stages.
+DENSE_UNIT_COST = 0.83
+SEGMENT_SWITCH_STAGES = 0.4
+MAX_PARTIALS_PER_PAIR = 160
 
 
 @dataclass
@@ -399,7 +406,7 @@ def _split_warps(weights: list[float], segs: list[int], u0: int, u1: int, warps:
 
 
 def _assign_ctas(unit_weights: list[float], unit_pair: list[int], unit_seg: list[int], num_ctas: int,
-                 warps: int) -> list[list[int]]:
+                 warps: int, unit_span: list[int] | None = None) -> list[list[int]]:
     """Cut the unit sequence into about ``num_ctas`` contiguous ranges of equal
     weight, each touching at most MAX_PAIRS_PER_CTA pairs, and split every range
     into per-warp bounds.  Returns one bounds list (warps + 1 entries) per CTA."""
@@ -433,7 +440,8 @@ def _assign_ctas(unit_weights: list[float], unit_pair: list[int], unit_seg: list
     stack = list(reversed(ranges))
     while stack:
         u0, u1 = stack.pop()
-        bounds = _split_warps(unit_weights, unit_seg, u0, u1, warps)
+        too_many_spans = unit_span is not None and unit_span[u1 - 1] - unit_span[u0] + 1 > MAX_SPANS_PER_CTA
+        bounds = None if too_many_spans else _split_warps(unit_weights, unit_seg, u0, u1, warps)
         if bounds is None:
             mid = (u0 + u1) // 2
             stack.append((mid, u1))
@@ -519,25 +527,35 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
     unit_weights: list[float] = []
     unit_pair: list[int] = []
     unit_seg: list[int] = []
+    unit_span: list[int] = []
     seg_id, last_key = -1, None
+    packed_stage_bytes = packed_bytes_per_token(k_bits, v_bits, group, head_dim) * PACKED_STAGE
     for s, sp in enumerate(spans):
         stage = PACKED_STAGE if sp.kind == 0 else DENSE_STAGE
         units = math.ceil(sp.tokens / stage)
         sp.unit_begin = len(unit_weights)
-        if (sp.pair, sp.kind) != last_key:
+        new_segment = (sp.pair, sp.kind) != last_key
+        if new_segment:
             seg_id += 1
             last_key = (sp.pair, sp.kind)
         per_token = span_bytes[s] / sp.tokens
+        # Weights are time estimates in bytes of packed stream (see the model
+        # above DENSE_UNIT_COST).
+        cost = 1.0 if sp.kind == 0 else DENSE_UNIT_COST
         for k in range(units):
             n = min(stage, sp.tokens - k * stage)
-            unit_weights.append(per_token * n)
+            w = per_token * n * cost
+            if k == 0 and new_segment:
+                w += SEGMENT_SWITCH_STAGES * packed_stage_bytes
+            unit_weights.append(w)
             unit_pair.append(sp.pair)
             unit_seg.append(seg_id)
+            unit_span.append(s)
     with torch.cuda.device(device):
         slots, warps = decode_config(k_bits, v_bits, group)
     if target_ctas is None:
         target_ctas = slots
-    cta_bounds = _assign_ctas(unit_weights, unit_pair, unit_seg, target_ctas, warps)
+    cta_bounds = _assign_ctas(unit_weights, unit_pair, unit_seg, target_ctas, warps, unit_span)
 
     span_starts = [sp.unit_begin for sp in spans]
     ctas: list[UcbDecodeCta] = []
@@ -548,7 +566,8 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         flat_bounds.extend(bounds)
         rec = UcbDecodeCta()
         rec.unit_begin, rec.unit_end = u0, u1
-        rec.span_begin = max(i for i, st in enumerate(span_starts) if st <= u0)
+        rec.span_begin = unit_span[u0]
+        rec.reserved[0] = unit_span[u1 - 1] + 1
         p0, p1 = unit_pair[u0], unit_pair[u1 - 1]
         rec.pair_begin, rec.num_pairs = p0, p1 - p0 + 1
         if rec.num_pairs > MAX_PAIRS_PER_CTA:
@@ -562,6 +581,8 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         cs = touched[p]
         if cs != list(range(cs[0], cs[0] + len(cs))):
             raise AssertionError("CTAs of a pair must be consecutive")
+        if len(cs) > MAX_PARTIALS_PER_PAIR:
+            raise ValueError(f"a (sequence, KV head) pair spans {len(cs)} CTAs; at most {MAX_PARTIALS_PER_PAIR}")
         pr = UcbDecodePair()
         pr.seq, pr.kv_head = b, h
         pr.partial_begin, pr.partial_count, pr.cta_first = partial_total, len(cs), cs[0]
