@@ -177,6 +177,24 @@ UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, in
                          void* partials_dev, int* counters_dev, void* out_dev, int64_t out_stride,
                          float* lse_dev, void* stream);
 
+/* Allocation-free variant of ucb_decode_attention; no counterpart in the
+ * reference.  For callers that may not allocate device memory when they
+ * decode (an engine that owns the whole HBM pool, a host that forbids library
+ * allocations): the partials and pair counters come from one static device
+ * array of 2,131,968 bytes that the library holds on every GPU it is loaded
+ * on until exit, so the plan may use at most 512 partial slots (num_partials
+ * = sum of partial_count) and 512 pairs; larger plans get UCB_ERR_INVALID.
+ * It calls no cudaMalloc or cudaFree.  The first call on a device looks up the
+ * array's address (set-up); make that call before any stream capture.  Every
+ * call shares the one array and clears the counters in stream order first:
+ * calls that overlap on the GPU (other streams, other host threads) race. */
+UCB_API int ucb_decode_attention_noalloc(const void* query_dev, int64_t query_stride, int num_q_heads,
+                         int num_kv_heads, int head_dim, const ucb_span* spans_dev, int num_spans,
+                         const ucb_decode_cta* ctas_dev, int num_ctas, const int32_t* warp_bounds_dev,
+                         const ucb_decode_pair* pairs_dev, int num_pairs, int num_partials, int k_bits,
+                         int v_bits, int group_size, int stat_dtype, float softmax_scale, void* out_dev,
+                         int64_t out_stride, float* lse_dev, void* stream);
+
 /* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
  * NULL, later ucb_decode_attention calls record per CTA {start, streaming
  * loops done, merge ticket taken, end, SM id, pairs it merged, then the loop

@@ -29,6 +29,7 @@
 //    one (max, sum, out) partial, and the last CTA of a pair (atomic ticket,
 //    no waiting) merges the partials into out and LSE.
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -945,6 +946,81 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.trace = g_decode_trace;
   return ucb::decode::dispatch<ucb::decode::LaunchFn>(k_bits, v_bits, group_size, P, num_ctas,
                                                       static_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------- allocation-free decode
+// Some callers cannot allocate device memory at the time they decode: an
+// engine that hands the whole HBM pool to its own allocator up front, code
+// running while a CUDA graph is being captured by someone else, or a plugin
+// host that forbids the library from calling cudaMalloc.  For them the
+// partials and pair counters live in one statically sized device array that
+// the library module carries on every GPU it is loaded on, until exit.
+namespace {
+constexpr int NOALLOC_MAX_PARTIALS = 512;  // partial slots (sum of partial_count)
+constexpr int NOALLOC_MAX_PAIRS = 512;     // (sequence, KV head) pairs
+constexpr size_t NOALLOC_PARTIAL_BYTES = (size_t)NOALLOC_MAX_PARTIALS * ucb::decode::PARTIAL_FLOATS * sizeof(float);
+constexpr size_t NOALLOC_SCRATCH_BYTES = NOALLOC_PARTIAL_BYTES + (size_t)NOALLOC_MAX_PAIRS * sizeof(int);
+static_assert(NOALLOC_PARTIAL_BYTES % 256 == 0, "counters start 256-byte aligned");
+
+// Host code must not use this name as a pointer: it is only a handle from which
+// cudaGetSymbolAddress returns the array's address on the current device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the first call on a device does this set-up).
+int noalloc_scratch(unsigned char** ptr) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(UCB_ERR_CUDA, "ucb_decode_attention_noalloc: cudaGetDevice: %s",
+                                         cudaGetErrorString(e));
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
+    return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(UCB_ERR_CUDA, "ucb_decode_attention_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *ptr = static_cast<unsigned char*>(g_noalloc_ptr[dev]);
+  return UCB_OK;
+}
+}  // namespace
+
+extern "C" int ucb_decode_attention_noalloc(const void* query, int64_t query_stride, int num_q_heads,
+                                            int num_kv_heads, int head_dim, const ucb_span* spans, int num_spans,
+                                            const ucb_decode_cta* ctas, int num_ctas, const int32_t* warp_bounds,
+                                            const ucb_decode_pair* pairs, int num_pairs, int num_partials,
+                                            int k_bits, int v_bits, int group_size, int stat_dtype,
+                                            float softmax_scale, void* out, int64_t out_stride, float* lse,
+                                            void* stream) {
+  if (num_partials <= 0 || num_partials > NOALLOC_MAX_PARTIALS)
+    return set_error(UCB_ERR_INVALID,
+                     "ucb_decode_attention_noalloc: the plan needs %d partial slots; the static scratch holds 1..%d",
+                     num_partials, NOALLOC_MAX_PARTIALS);
+  if (num_pairs <= 0 || num_pairs > NOALLOC_MAX_PAIRS)
+    return set_error(UCB_ERR_INVALID,
+                     "ucb_decode_attention_noalloc: %d (sequence, KV head) pairs; the static scratch holds 1..%d",
+                     num_pairs, NOALLOC_MAX_PAIRS);
+  unsigned char* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != UCB_OK) return rc;
+  int* counters = reinterpret_cast<int*>(scratch + NOALLOC_PARTIAL_BYTES);
+  // The counters must start at zero; a call that stopped on a device error may
+  // have left some set, so clear them in stream order before every launch.
+  const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)num_pairs * sizeof(int),
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return set_error(UCB_ERR_CUDA, "ucb_decode_attention_noalloc: clearing counters: %s", cudaGetErrorString(e));
+  return ucb_decode_attention(query, query_stride, num_q_heads, num_kv_heads, head_dim, spans, num_spans, ctas,
+                              num_ctas, warp_bounds, pairs, num_pairs, k_bits, v_bits, group_size, stat_dtype,
+                              softmax_scale, scratch, counters, out, out_stride, lse, stream);
 }
 
 extern "C" int ucb_merge_partials(const void* partials, int n_parts, const ucb_decode_pair* pairs, int num_pairs,
