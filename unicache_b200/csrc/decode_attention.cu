@@ -80,6 +80,7 @@ struct Cfg {
   static constexpr int OFF_PAIRS = OFF_SPANS + MAX_SPANS * (int)sizeof(ucb_span);  // the CTA's pair records
   static constexpr int SMEM = OFF_PAIRS + MAXC * (int)sizeof(ucb_decode_pair);
   static_assert(SLOT >= PARTIAL_FLOATS * 4, "a ring slot must hold a warp state");
+  static_assert(KC >= NT * NG * 4 + 16 * NG * 8, "value tables must fit the key-code area");
   // partials whose rows the last CTA of a pair stages in shared memory
   static constexpr int MCAP_RAW = (WARPS * 2 * SLOT - (MAXP * 24 + 16) * 4) / (8 * D * 4);
   static constexpr int MCAP = MCAP_RAW > 16 ? 16 : MCAP_RAW;
@@ -227,7 +228,7 @@ struct Kernel {
   // -------------------------------------------------------------- packed stage
   template <bool FULL>
   __device__ static void packed_stage(const unsigned char* slot, int n_valid, int lane, const uint32_t (&qbp)[KCH][2],
-                                      float scale_log2, WarpState& st, float (&o)[8][4], float (&accm)[C::NG][2]) {
+                                      float scale_log2, WarpState& st, float (&o)[8][4], float (&accm)[4]) {
     const int r = lane >> 2, c = lane & 3;
     const int pr = tile_pos(r), pr2 = (pr + 1) & 3;
     const int tok_lo = 4 * (r & 3) + pr, tok_hi = 4 * (r & 3) + pr2;
@@ -255,33 +256,41 @@ struct Kernel {
       sh_lo = 4 * (pr & 1);
       sh_hi = 4 * (pr2 & 1);
     }
+    // Channel map of the QK contraction: in k-chunk kk, lane c owns channels
+    // 32*(kk/2) + 8c + 4*(kk%2) + {0..3} (k = 2c, 2c+1, 2c+8, 2c+9), so one
+    // 128-bit load brings a lane's statistics for two chunks.
+    uint4 ks4[C::GPS], km4[C::GPS];
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) {
-      uint2 ks[C::GPS], km[C::GPS];
+      const int ch = 32 * (kk >> 1) + 8 * c + 4 * (kk & 1);
+      if ((kk & 1) == 0) {
 #pragma unroll
-      for (int gi = 0; gi < C::GPS; ++gi) {
-        ks[gi] = lds64(slot + C::OFF_KS + (gi * D + 16 * kk + 4 * c) * (int)sizeof(ST));
-        km[gi] = lds64(slot + C::OFF_KM + (gi * D + 16 * kk + 4 * c) * (int)sizeof(ST));
+        for (int gi = 0; gi < C::GPS; ++gi) {
+          ks4[gi] = lds128(slot + C::OFF_KS + (gi * D + ch) * (int)sizeof(ST));
+          km4[gi] = lds128(slot + C::OFF_KM + (gi * D + ch) * (int)sizeof(ST));
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int gi = (G >= NT) ? 0 : (16 * j) / G;
+        const uint32_t s0 = (kk & 1) ? ks4[gi].z : ks4[gi].x, s1 = (kk & 1) ? ks4[gi].w : ks4[gi].y;
+        const uint32_t m0 = (kk & 1) ? km4[gi].z : km4[gi].x, m1 = (kk & 1) ? km4[gi].w : km4[gi].y;
         const int wr = (KB == 2) ? j : 2 * j + ((r & 3) >> 1);
-        const uint4 w = lds128(slot + C::OFF_KC + (wr * D + 16 * kk + 4 * c) * 4);
+        const uint4 w = lds128(slot + C::OFF_KC + (wr * D + ch) * 4);
         uint32_t a[4];
         if constexpr (KB == 2) {
           const uint32_t z0 = prmt(w.x, w.y, sel_lo) >> sh_lo, z1 = prmt(w.z, w.w, sel_lo) >> sh_lo;
-          a[0] = bf16x2_dequant((z0 & 0x00030003u) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
-          a[1] = bf16x2_dequant((z0 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, ks[gi].x, km[gi].x);
-          a[2] = bf16x2_dequant((z1 & 0x00030003u) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
-          a[3] = bf16x2_dequant((z1 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, ks[gi].y, km[gi].y);
+          a[0] = bf16x2_dequant((z0 & 0x00030003u) | 0x43004300u, 0xC300C300u, s0, m0);
+          a[1] = bf16x2_dequant((z0 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, s0, m0);
+          a[2] = bf16x2_dequant((z1 & 0x00030003u) | 0x43004300u, 0xC300C300u, s1, m1);
+          a[3] = bf16x2_dequant((z1 & 0x000C000Cu) | 0x42004200u, 0xC200C200u, s1, m1);
         } else {
           const uint32_t y0l = prmt(w.x, w.y, sel_lo), y1l = prmt(w.z, w.w, sel_lo);
           const uint32_t y0h = prmt(w.x, w.y, sel_hi), y1h = prmt(w.z, w.w, sel_hi);
-          a[0] = bf16x2_dequant(((y0l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
-          a[1] = bf16x2_dequant(((y0h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].x, km[gi].x);
-          a[2] = bf16x2_dequant(((y1l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
-          a[3] = bf16x2_dequant(((y1h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, ks[gi].y, km[gi].y);
+          a[0] = bf16x2_dequant(((y0l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, s0, m0);
+          a[1] = bf16x2_dequant(((y0h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, s0, m0);
+          a[2] = bf16x2_dequant(((y1l >> sh_lo) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, s1, m1);
+          a[3] = bf16x2_dequant(((y1h >> sh_hi) & 0x000F000Fu) | 0x43004300u, 0xC300C300u, s1, m1);
         }
         mma_bf16(acc[j], a, qbp[kk][0], qbp[kk][1]);
       }
@@ -305,54 +314,95 @@ struct Kernel {
         o[i][2] *= alpha0;
         o[i][3] *= alpha1;
       }
-#pragma unroll
-      for (int g = 0; g < C::NG; ++g) {
-        accm[g][0] *= alpha0;
-        accm[g][1] *= alpha1;
-      }
+      accm[0] *= alpha0;
+      accm[1] *= alpha1;
     }
 
-    // Values: one 16-token k-chunk per tile.
+    // Values.  Per stage the warp turns the value statistics into two small
+    // fp16 tables in the (now free) key-code area: SD[t][g] = (s, s) for the
+    // probability scaling, and MT[j][g][c] = the A fragment (minima of the
+    // lane's four k-tokens) of the minimum term, which then runs as one MMA
+    // per 16-token tile: sum_t p_th m_tg.  Tokens past the end get zeros.
+    __syncwarp();
+    unsigned char* sd_tab = const_cast<unsigned char*>(slot) + C::OFF_KC;
+    unsigned char* mt_tab = sd_tab + NT * C::NG * 4;
+    {
+      uint32_t sw[C::NG];
+      const unsigned char* src = slot + C::OFF_VS + 2 * lane * C::NG * (int)sizeof(ST);
+      if constexpr (C::NG == 4) {
+        const uint4 v = lds128(src);
+        sw[0] = v.x; sw[1] = v.y; sw[2] = v.z; sw[3] = v.w;
+      } else if constexpr (C::NG == 2) {
+        const uint2 v = lds64(src);
+        sw[0] = v.x; sw[1] = v.y;
+      } else {
+        sw[0] = *reinterpret_cast<const uint32_t*>(src);
+      }
+      uint32_t dup[2 * C::NG];
+#pragma unroll
+      for (int k = 0; k < 2 * C::NG; ++k) {
+        const float f = (k & 1) ? bf16hi(sw[k >> 1]) : bf16lo(sw[k >> 1]);
+        const bool valid = FULL || 2 * lane + k / C::NG < n_valid;
+        dup[k] = valid ? pack_f16x2(f, f) : 0u;
+      }
+      uint32_t* dst = reinterpret_cast<uint32_t*>(sd_tab) + 2 * lane * C::NG;
+#pragma unroll
+      for (int k = 0; k < 2 * C::NG; k += 4 < 2 * C::NG ? 4 : 2 * C::NG) {
+        if constexpr (2 * C::NG >= 4)
+          *reinterpret_cast<uint4*>(dst + k) = make_uint4(dup[k], dup[k + 1], dup[k + 2], dup[k + 3]);
+        else
+          *reinterpret_cast<uint2*>(dst + k) = make_uint2(dup[k], dup[k + 1]);
+      }
+    }
+#pragma unroll
+    for (int e0 = 0; e0 < 16 * C::NG; e0 += 32) {
+      const int e = e0 + lane;
+      if (16 * C::NG >= 32 || e < 16 * C::NG) {
+        const int jj = e / (4 * C::NG), g = (e >> 2) & (C::NG - 1), cc = e & 3;
+        const int tk[4] = {16 * jj + tile_tok(2 * cc), 16 * jj + tile_tok(2 * cc + 1), 16 * jj + tile_tok(2 * cc + 8),
+                           16 * jj + tile_tok(2 * cc + 9)};
+        float mv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint16_t raw = *reinterpret_cast<const uint16_t*>(slot + C::OFF_VM + (tk[q] * C::NG + g) * 2);
+          mv[q] = (FULL || tk[q] < n_valid) ? bf16lo(raw) : 0.f;
+        }
+        *reinterpret_cast<uint2*>(mt_tab + e * 8) = make_uint2(pack_f16x2(mv[0], mv[1]), pack_f16x2(mv[2], mv[3]));
+      }
+    }
+    fence_proxy_async_smem();  // the slot's next bulk copy overwrites these tables
+    __syncwarp();
     const int u0 = tile_tok(2 * c), u1 = tile_tok(2 * c + 1), u2 = tile_tok(2 * c + 8), u3 = tile_tok(2 * c + 9);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const bool vlo = FULL || 16 * j + tok_lo < n_valid, vhi = FULL || 16 * j + tok_hi < n_valid;
-      const unsigned char* vs_lo = slot + C::OFF_VS + (16 * j + tok_lo) * C::NG * (int)sizeof(ST);
-      const unsigned char* vs_hi = slot + C::OFF_VS + (16 * j + tok_hi) * C::NG * (int)sizeof(ST);
-      const int moff = C::OFF_VM - C::OFF_VS;
-      float slo[C::NG], shi[C::NG], mlo[C::NG], mhi[C::NG];
-      if constexpr (C::NG == 1) {
-        slo[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_lo));
-        shi[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_hi));
-        mlo[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_lo + moff));
-        mhi[0] = bf16lo(*reinterpret_cast<const uint16_t*>(vs_hi + moff));
-      } else {
-#pragma unroll
-        for (int g = 0; g < C::NG; g += 2) {
-          const uint32_t s_l = *reinterpret_cast<const uint32_t*>(vs_lo + 2 * g);
-          const uint32_t s_h = *reinterpret_cast<const uint32_t*>(vs_hi + 2 * g);
-          const uint32_t m_l = *reinterpret_cast<const uint32_t*>(vs_lo + moff + 2 * g);
-          const uint32_t m_h = *reinterpret_cast<const uint32_t*>(vs_hi + moff + 2 * g);
-          slo[g] = bf16lo(s_l);
-          slo[g + 1] = bf16hi(s_l);
-          shi[g] = bf16lo(s_h);
-          shi[g + 1] = bf16hi(s_h);
-          mlo[g] = bf16lo(m_l);
-          mlo[g + 1] = bf16hi(m_l);
-          mhi[g] = bf16lo(m_h);
-          mhi[g + 1] = bf16hi(m_h);
+      const uint32_t p_lo = pack_f16x2(lg[j][0], lg[j][1]), p_hi = pack_f16x2(lg[j][2], lg[j][3]);
+      {
+        const uint2 am = lds64(mt_tab + ((j * C::NG + (r & (C::NG - 1))) * 4 + c) * 8);
+        const uint32_t aa[4] = {am.x, am.x, am.y, am.y};  // rows >= NG are don't-care
+        mma_f16(accm, aa, movmatrix_trans(p_lo), movmatrix_trans(p_hi));
+      }
+      uint32_t sl[C::NG], sh[C::NG];
+      {
+        const unsigned char* rl = sd_tab + (16 * j + tok_lo) * C::NG * 4;
+        const unsigned char* rh = sd_tab + (16 * j + tok_hi) * C::NG * 4;
+        if constexpr (C::NG == 4) {
+          const uint4 x = lds128(rl), y = lds128(rh);
+          sl[0] = x.x; sl[1] = x.y; sl[2] = x.z; sl[3] = x.w;
+          sh[0] = y.x; sh[1] = y.y; sh[2] = y.z; sh[3] = y.w;
+        } else if constexpr (C::NG == 2) {
+          const uint2 x = lds64(rl), y = lds64(rh);
+          sl[0] = x.x; sl[1] = x.y;
+          sh[0] = y.x; sh[1] = y.y;
+        } else {
+          sl[0] = *reinterpret_cast<const uint32_t*>(rl);
+          sh[0] = *reinterpret_cast<const uint32_t*>(rh);
         }
       }
       uint32_t bp[C::NG][2];
 #pragma unroll
       for (int g = 0; g < C::NG; ++g) {
-        // Past the end the shared memory holds stale bytes: select, never multiply by 0.
-        const float sl = vlo ? slo[g] : 0.f, sh = vhi ? shi[g] : 0.f;
-        const float ml = vlo ? mlo[g] : 0.f, mh = vhi ? mhi[g] : 0.f;
-        bp[g][0] = movmatrix_trans(pack_f16x2(lg[j][0] * sl, lg[j][1] * sl));
-        bp[g][1] = movmatrix_trans(pack_f16x2(lg[j][2] * sh, lg[j][3] * sh));
-        accm[g][0] = fmaf(lg[j][0], ml, fmaf(lg[j][2], mh, accm[g][0]));
-        accm[g][1] = fmaf(lg[j][1], ml, fmaf(lg[j][3], mh, accm[g][1]));
+        bp[g][0] = movmatrix_trans(hmul2_f16(p_lo, sl[g]));
+        bp[g][1] = movmatrix_trans(hmul2_f16(p_hi, sh[g]));
       }
       if constexpr (VB == 2) {
         constexpr int ROW = D * 2 / 8;  // bytes per token
@@ -456,15 +506,15 @@ struct Kernel {
   // Stores (max, sum, out) of the warp's current segment, in natural channel
   // order, into a private shared-memory block [m 8][l 8][O 8 x D].
   __device__ static void store_state(float* dst, bool packed, const WarpState& st, float (&o)[8][4],
-                                     float (&accm)[C::NG][2], int lane) {
+                                     const float (&accm)[4], int lane) {
     const int r = lane >> 2, c = lane & 3;
     const float l0 = warp_sum_r(st.lrun[0]), l1 = warp_sum_r(st.lrun[1]);
-    if (packed) {
+    // Minimum-term sums: group g, heads 2c and 2c+1 live in lane 4g + c.
+    float mg0[C::NG], mg1[C::NG];
 #pragma unroll
-      for (int g = 0; g < C::NG; ++g) {
-        accm[g][0] = warp_sum_r(accm[g][0]);
-        accm[g][1] = warp_sum_r(accm[g][1]);
-      }
+    for (int g = 0; g < C::NG; ++g) {
+      mg0[g] = __shfl_sync(0xffffffffu, accm[0], 4 * g + c);
+      mg1[g] = __shfl_sync(0xffffffffu, accm[1], 4 * g + c);
     }
     if (r == 0) {
       dst[2 * c] = st.mrun[0];
@@ -490,10 +540,10 @@ struct Kernel {
           f_lo = f_hi = __int_as_float((127 + 24 - 4 * (r & 1)) << 23);
         }
         const int g = (16 * i) / G;
-        v[0] = fmaf(o[i][0], f_lo, accm[g][0]);
-        v[1] = fmaf(o[i][1], f_lo, accm[g][1]);
-        v[2] = fmaf(o[i][2], f_hi, accm[g][0]);
-        v[3] = fmaf(o[i][3], f_hi, accm[g][1]);
+        v[0] = fmaf(o[i][0], f_lo, mg0[g]);
+        v[1] = fmaf(o[i][1], f_lo, mg1[g]);
+        v[2] = fmaf(o[i][2], f_hi, mg0[g]);
+        v[3] = fmaf(o[i][3], f_hi, mg1[g]);
       } else {
         d_lo = 16 * i + r;
         d_hi = d_lo + 8;
@@ -578,12 +628,12 @@ struct Kernel {
     st.mrun[0] = st.mrun[1] = -INFINITY;
     st.lrun[0] = st.lrun[1] = 0.f;
     float o[8][4];
-    float accm[C::NG][2];
+    float accm[4];
     uint32_t qbp[KCH][2];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 #pragma unroll
-    for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
+    for (int g = 0; g < 4; ++g) accm[g] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < KCH; ++kk) qbp[kk][0] = qbp[kk][1] = 0u;
     int cur_pl = -1, cur_kind = -1, span = 0;
@@ -612,11 +662,11 @@ struct Kernel {
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 #pragma unroll
-        for (int g = 0; g < C::NG; ++g) accm[g][0] = accm[g][1] = 0.f;
+        for (int g = 0; g < 4; ++g) accm[g] = 0.f;
         if (kind == 0) {
 #pragma unroll
           for (int kk = 0; kk < KCH; ++kk) {
-            const uint2 q2 = lds64(qs + ((pl * 8 + r) * D + 16 * kk + 4 * c) * 2);
+            const uint2 q2 = lds64(qs + ((pl * 8 + r) * D + 32 * (kk >> 1) + 8 * c + 4 * (kk & 1)) * 2);
             qbp[kk][0] = q2.x;
             qbp[kk][1] = q2.y;
           }
