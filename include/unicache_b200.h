@@ -123,13 +123,18 @@ UCB_API int ucb_fake_quant(const void* x_dev, void* out_dev, int dtype, int64_t 
  * [pair_begin, pair_begin + num_pairs) (at most 4); its warp w processes units
  * [warp_bounds[i*(W+1) + w], warp_bounds[i*(W+1) + w + 1]) where W comes from
  * ucb_decode_config, and each warp range may cross at most one segment
- * boundary (a change of pair or of span kind).  CTA i writes one partial per
- * touched pair at partials[pair.partial_begin + i - pair.cta_first].  The last
- * CTA of a pair merges its partials into out_dev [seq, q_head, :] (bf16) and
+ * boundary (a change of pair or of span kind).  A warp writes the softmax state
+ * (max, sum, unnormalised rows) of each segment it processed into a state slot
+ * of ucb_decode_partial_bytes(head_dim) bytes: warp_slots_dev[2*(i*W + w)] for
+ * its first segment when it crosses a boundary, warp_slots_dev[2*(i*W + w) + 1]
+ * for its last segment (-1 where the warp has none).  The slots of pair p are
+ * [pair.partial_begin, pair.partial_begin + pair.partial_count).  A merge
+ * kernel launched after the decode grid on the same stream folds each pair's
+ * states into out_dev [seq, q_head, :] (bf16) and
  * lse_dev [seq, q_head] (natural-log LSE, fp32; may be NULL).
- * Workspaces: partials_dev >= ucb_decode_partial_bytes(head_dim) * sum of
- * partial_count bytes; counters_dev >= num_pairs int32 zeroed once before first
- * use (the kernel leaves them zero).  Calls sharing counters must not overlap. */
+ * Workspace: partials_dev >= ucb_decode_partial_bytes(head_dim) * (number of
+ * slots) bytes; every slot the merge reads is written by the same call, so
+ * nothing needs zeroing.  Calls sharing a workspace must not overlap. */
 typedef struct ucb_span {
   const void* key_code;      /* packed: int32/uint8 codes; dense: key rows    */
   const void* key_scale;     /* packed only                                   */
@@ -158,8 +163,8 @@ typedef struct ucb_decode_pair {
   int32_t seq;
   int32_t kv_head;
   int32_t partial_begin;
-  int32_t partial_count;     /* CTAs touching this pair, at most 160           */
-  int32_t cta_first;         /* first CTA touching this pair                  */
+  int32_t partial_count;     /* warp-state slots of this pair                 */
+  int32_t cta_first;         /* first CTA touching this pair (informational)  */
   int32_t reserved[3];
 } ucb_decode_pair;
 
@@ -174,32 +179,33 @@ UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, in
                          int num_ctas, const int32_t* warp_bounds_dev, const ucb_decode_pair* pairs_dev,
                          int num_pairs, int k_bits,
                          int v_bits, int group_size, int stat_dtype, float softmax_scale,
-                         void* partials_dev, int* counters_dev, void* out_dev, int64_t out_stride,
+                         void* partials_dev, const int32_t* warp_slots_dev, void* out_dev, int64_t out_stride,
                          float* lse_dev, void* stream);
 
 /* Allocation-free variant of ucb_decode_attention; no counterpart in the
  * reference.  For callers that may not allocate device memory when they
  * decode (an engine that owns the whole HBM pool, a host that forbids library
- * allocations): the partials and pair counters come from one static device
- * array of 2,131,968 bytes that the library holds on every GPU it is loaded
- * on until exit, so the plan may use at most 512 partial slots (num_partials
- * = sum of partial_count) and 512 pairs; larger plans get UCB_ERR_INVALID.
- * It calls no cudaMalloc or cudaFree.  The first call on a device looks up the
- * array's address (set-up); make that call before any stream capture.  Every
- * call shares the one array and clears the counters in stream order first:
- * calls that overlap on the GPU (other streams, other host threads) race. */
+ * allocations): the warp-state slots come from one static device array of
+ * 2,129,920 bytes that the library holds on every GPU it is loaded on until
+ * exit, so the plan may use at most 512 slots (num_partials = sum of
+ * partial_count); larger plans get UCB_ERR_INVALID.  The caller still passes
+ * the plan tables, the query and the outputs.  It calls no cudaMalloc or
+ * cudaFree.  The first call on a device looks up the array's address (set-up);
+ * make that call before any stream capture.  Every call shares the one array
+ * (each slot it reads is written earlier in the same call, so nothing needs
+ * clearing): calls that overlap on the GPU (other streams, other host
+ * threads) race. */
 UCB_API int ucb_decode_attention_noalloc(const void* query_dev, int64_t query_stride, int num_q_heads,
                          int num_kv_heads, int head_dim, const ucb_span* spans_dev, int num_spans,
                          const ucb_decode_cta* ctas_dev, int num_ctas, const int32_t* warp_bounds_dev,
-                         const ucb_decode_pair* pairs_dev, int num_pairs, int num_partials, int k_bits,
-                         int v_bits, int group_size, int stat_dtype, float softmax_scale, void* out_dev,
-                         int64_t out_stride, float* lse_dev, void* stream);
+                         const ucb_decode_pair* pairs_dev, int num_pairs, const int32_t* warp_slots_dev,
+                         int num_partials, int k_bits, int v_bits, int group_size, int stat_dtype,
+                         float softmax_scale, void* out_dev, int64_t out_stride, float* lse_dev, void* stream);
 
 /* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
- * NULL, later ucb_decode_attention calls record per CTA {start, streaming
- * loops done, merge ticket taken, end, SM id, pairs it merged, then the loop
- * end of each warp} (times from the global timer, ns).  NULL switches it
- * off. */
+ * NULL, later ucb_decode_attention calls record per CTA word 0 = start,
+ * word 4 = SM id and word 6 + w = the time warp w finished (state written),
+ * from the global timer in ns.  NULL switches it off. */
 UCB_API int ucb_decode_set_trace(void* trace_dev);
 
 /* Launch shape of ucb_decode_attention on the current device: CTAs that run at

@@ -44,7 +44,6 @@ constexpr int DROW = 272;         // dense shared-memory row stride (bytes), con
 constexpr int DENSE_STAGE = 2 * DT * DROW;
 constexpr int MAXC = 4;           // pairs one CTA may touch
 constexpr int MAX_SPANS = 16;     // spans one CTA may touch
-constexpr int MAXP = 160;         // partials of one pair (CTAs touching it)
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr int PARTIAL_FLOATS = 16 + 8 * D;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -70,23 +69,12 @@ struct Cfg {
   static constexpr int OFF_VM = OFF_VS + VS;
   static constexpr int PACKED_STAGE = OFF_VM + VS;
   static constexpr int SLOT = round_up(PACKED_STAGE > DENSE_STAGE ? PACKED_STAGE : DENSE_STAGE, 128);
-  static constexpr int OFF_STASH = WARPS * 2 * SLOT;                // WARPS first-segment states
-  static constexpr int OFF_Q = OFF_STASH + WARPS * PARTIAL_FLOATS * 4; // MAXC x 8 query rows (bf16)
+  static constexpr int OFF_Q = WARPS * 2 * SLOT;                  // MAXC x 8 query rows (bf16)
   static constexpr int OFF_ZERO = OFF_Q + MAXC * 8 * D * 2;           // one zero row
   static constexpr int OFF_BAR = OFF_ZERO + D * 2;                    // WARPS x 2 mbarriers
-  static constexpr int OFF_TAG = OFF_BAR + WARPS * 2 * 8;             // WARPS x 2 state tags
-  static constexpr int OFF_MISC = OFF_TAG + WARPS * 2 * 4;            // last-CTA flags
-  static constexpr int OFF_SPANS = round_up(OFF_MISC + 64, 16);       // the CTA's spans
-  static constexpr int OFF_PAIRS = OFF_SPANS + MAX_SPANS * (int)sizeof(ucb_span);  // the CTA's pair records
-  static constexpr int SMEM = OFF_PAIRS + MAXC * (int)sizeof(ucb_decode_pair);
-  static_assert(SLOT >= PARTIAL_FLOATS * 4, "a ring slot must hold a warp state");
+  static constexpr int OFF_SPANS = round_up(OFF_BAR + WARPS * 2 * 8, 16);  // the CTA's spans
+  static constexpr int SMEM = OFF_SPANS + MAX_SPANS * (int)sizeof(ucb_span);
   static_assert(KC >= NT * NG * 4 + 16 * NG * 8, "value tables must fit the key-code area");
-  // partials whose rows the last CTA of a pair stages in shared memory
-  static constexpr int MCAP_RAW = (WARPS * 2 * SLOT - (MAXP * 24 + 16) * 4) / (8 * D * 4);
-  static constexpr int MCAP = MCAP_RAW > 16 ? 16 : MCAP_RAW;
-  static_assert(MCAP >= 4, "the ring must hold the merge tables and a few partials");
-  static_assert(MAXC * 2 * WARPS * 9 * 4 + MAXC * 4 <= MAXC * 8 * D * 2, "merge tables must fit the query rows");
-  static_assert(2 * WARPS <= 32, "one lane per warp state");
 };
 
 // Token <-> MMA-row map inside a 16-token tile.  Row r and row r+8 of lane
@@ -166,14 +154,15 @@ struct Params {
   const ucb_decode_cta* ctas;
   const int32_t* warp_bounds;  // per CTA: WARPS+1 unit boundaries
   const ucb_decode_pair* pairs;
+  int num_pairs;
   float scale_log2;  // softmax_scale * log2(e)
-  float* partials;
-  int* counters;
+  float* partials;             // warp states, one slot each
+  const int32_t* warp_slots;   // per CTA and warp: {first-segment slot, last-segment slot}, -1 = none
   __nv_bfloat16* out;
   int64_t out_stride;
   float* lse;
   unsigned int* err;
-  uint64_t* trace;  // optional: per CTA 12 words, see ucb_decode_set_trace
+  uint64_t* trace;  // optional: per CTA 32 words, see ucb_decode_set_trace
 };
 
 template <int KB, int VB, int G, typename ST>
@@ -568,11 +557,9 @@ struct Kernel {
     const int32_t* bounds = P.warp_bounds + (int64_t)blockIdx.x * (C::WARPS + 1);
     const int u_begin = bounds[warp], u_end = bounds[warp + 1];
 
-    float* stash = reinterpret_cast<float*>(smem + C::OFF_STASH) + warp * PARTIAL_FLOATS;
+    const int2 wslot = reinterpret_cast<const int2*>(P.warp_slots)[blockIdx.x * C::WARPS + warp];
     unsigned char* qs = smem + C::OFF_Q;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR) + warp * 2;
-    int* tags = reinterpret_cast<int*>(smem + C::OFF_TAG);      // [warp][2]: pair_local or -1
-    int* last_flags = reinterpret_cast<int*>(smem + C::OFF_MISC);
     const uint32_t zero_row = smem_u32(smem + C::OFF_ZERO);
     unsigned char* ring = smem + warp * 2 * C::SLOT;
 
@@ -591,15 +578,10 @@ struct Kernel {
     for (int i = tid; i < D * 2 / 16; i += C::THREADS)
       reinterpret_cast<uint4*>(smem + C::OFF_ZERO)[i] = make_uint4(0, 0, 0, 0);
     ucb_span* spans = reinterpret_cast<ucb_span*>(smem + C::OFF_SPANS);
-    // Pair records are cached: under full HBM load a global round trip costs
-    // microseconds, and the epilogue would otherwise pay several in a row.
-    ucb_decode_pair* pcache = reinterpret_cast<ucb_decode_pair*>(smem + C::OFF_PAIRS);
-    if (tid < cta.num_pairs) pcache[tid] = P.pairs[cta.pair_begin + tid];
     const int n_spans = cta.reserved[0] - cta.span_begin;  // spans [span_begin, span_end)
     for (int i = tid; i < n_spans * (int)(sizeof(ucb_span) / 8); i += C::THREADS)
       reinterpret_cast<uint64_t*>(spans)[i] = reinterpret_cast<const uint64_t*>(P.spans + cta.span_begin)[i];
     if (lane == 0) {
-      tags[2 * warp] = tags[2 * warp + 1] = -1;
       mbar_init(&bars[0], 1);
       mbar_init(&bars[1], 1);
       fence_mbarrier_init();
@@ -652,9 +634,11 @@ struct Kernel {
       if (pl != cur_pl || kind != cur_kind) {
         if (cur_pl >= 0) {
           // At most one segment boundary per warp (the planner guarantees it).
-          if (stashed) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-          store_state(stash, cur_kind == 0, st, o, accm, lane);
-          if (lane == 0) tags[2 * warp] = cur_pl;
+          if (stashed || wslot.x < 0) {
+            atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+          } else {
+            store_state(P.partials + (int64_t)wslot.x * PARTIAL_FLOATS, cur_kind == 0, st, o, accm, lane);
+          }
           stashed = true;
         }
         st.mrun[0] = st.mrun[1] = -INFINITY;
@@ -689,157 +673,25 @@ struct Kernel {
       __syncwarp();
       if (issue_u < u_end) issue_next(slot_idx);
     }
-    if (P.trace && lane == 0) P.trace[32 * blockIdx.x + 6 + warp] = global_timer_ns();
     if (!ok) {
-      // Let copies still in flight land before the shared memory is reused.
+      // Let copies still in flight land before the shared memory is released.
       for (int k = s; k < s + 2; ++k) {
         if (u_begin + k < u_end) mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1, WAIT_LIMIT);
       }
       if (lane == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
     } else if (cur_pl >= 0) {
-      store_state(reinterpret_cast<float*>(ring), cur_kind == 0, st, o, accm, lane);
-      if (lane == 0) tags[2 * warp + 1] = cur_pl;
+      if (wslot.y < 0)
+        atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+      else
+        store_state(P.partials + (int64_t)wslot.y * PARTIAL_FLOATS, cur_kind == 0, st, o, accm, lane);
     }
-    __syncthreads();
-    const uint64_t t_loops = P.trace ? global_timer_ns() : 0;
-
-    // ---- merge the warp states of each pair into one partial.  One warp per
-    // (pair, head) finds the states of the pair with a ballot, their common
-    // maximum and exp2 weights; then every thread sums weighted rows.  The
-    // query rows are dead by now, so the weight tables live in their place.
-    const int grp = P.grp;
-    float* mw = reinterpret_cast<float*>(qs);                  // [MAXC][2*WARPS][8] weights
-    int* mlist = reinterpret_cast<int*>(mw + MAXC * 2 * C::WARPS * 8);  // [MAXC][2*WARPS] states
-    int* mcount = mlist + MAXC * 2 * C::WARPS;                 // [MAXC]
-    auto state_ptr = [&](int sidx) -> const float* {
-      return (sidx & 1) ? reinterpret_cast<const float*>(smem + (sidx >> 1) * 2 * C::SLOT)
-                        : reinterpret_cast<const float*>(smem + C::OFF_STASH) + (sidx >> 1) * PARTIAL_FLOATS;
-    };
-    for (int combo = warp; combo < cta.num_pairs * 8; combo += C::WARPS) {
-      const int pl = combo >> 3, h = combo & 7;
-      const bool mine = lane < 2 * C::WARPS && tags[lane] == pl;
-      const float* src = mine ? state_ptr(lane) : nullptr;
-      const float m = mine ? src[h] : -INFINITY;
-      const float l = mine ? src[8 + h] : 0.f;
-      float M = m;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
-      float L = w * l;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      const unsigned ball = __ballot_sync(0xffffffffu, mine);
-      const int rank = __popc(ball & ((1u << lane) - 1u));
-      if (mine) {
-        mw[(pl * 2 * C::WARPS + rank) * 8 + h] = w;
-        if (h == 0) mlist[pl * 2 * C::WARPS + rank] = lane;
-      }
-      if (lane == 0) {
-        if (h == 0) mcount[pl] = __popc(ball);
-        const ucb_decode_pair& pr = pcache[pl];
-        float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
-        part[h] = M;
-        part[8 + h] = L;
-      }
-    }
-    __syncthreads();
-    for (int pl = 0; pl < cta.num_pairs; ++pl) {
-      const ucb_decode_pair& pr = pcache[pl];
-      float* part = P.partials + (int64_t)(pr.partial_begin + (blockIdx.x - pr.cta_first)) * PARTIAL_FLOATS;
-      const int n = mcount[pl];
-      const float* wrow = mw + pl * 2 * C::WARPS * 8;
-      const int* lrow = mlist + pl * 2 * C::WARPS;
-      for (int e = tid; e < grp * D; e += C::THREADS) {
-        const int h = e / D;
-        float acc = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < n; ++i) acc = fmaf(wrow[i * 8 + h], state_ptr(lrow[i])[16 + e], acc);
-        part[16 + e] = acc;
-      }
-    }
-    // Release the partials with one gpu-scope fence per arriving pair after
-    // the CTA barrier (the barrier orders every thread's stores before it).
-    __syncthreads();
-    if (tid < cta.num_pairs) {
-      const ucb_decode_pair& pr = pcache[tid];
-      __threadfence();
-      const int prev = atomicAdd(&P.counters[cta.pair_begin + tid], 1);
-      __threadfence();
-      last_flags[tid] = (prev == pr.partial_count - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    const uint64_t t_ticket = P.trace ? global_timer_ns() : 0;
-
-    // ---- last CTA of a pair: merge its partials.  Headers (max, sum) of all
-    // partials and the rows of the first MCAP partials are fetched into
-    // shared memory in one round of asynchronous copies.
-    int merged = 0;
-    float* hdr = reinterpret_cast<float*>(smem);  // ring space is free now: [MAXP][16]
-    float* wts = hdr + MAXP * 16;                  // [MAXP][8] weights
-    float* tot = wts + MAXP * 8;                   // [8] sum, [8] max
-    float* rows = tot + 16;                        // [MCAP][grp*D]
-    for (int pl = 0; pl < cta.num_pairs; ++pl) {
-      if (!last_flags[pl]) continue;
-      ++merged;
-      const int pidx = cta.pair_begin + pl;
-      const ucb_decode_pair& pr = pcache[pl];
-      const int np = pr.partial_count;  // <= MAXP (the planner guarantees it)
-      const int cap = np < C::MCAP ? np : C::MCAP;
-      const int gd4 = grp * D / 4;
-      const float* base = P.partials + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
-      for (int i = tid; i < np * 4; i += C::THREADS)
-        cp_async16(smem_u32(hdr + 4 * i), base + (int64_t)(i >> 2) * PARTIAL_FLOATS + 4 * (i & 3));
-      for (int i = tid; i < cap * gd4; i += C::THREADS) {
-        const int pp = i / gd4, q4 = i - pp * gd4;
-        cp_async16(smem_u32(rows + 4 * i), base + (int64_t)pp * PARTIAL_FLOATS + 16 + 4 * q4);
-      }
-      cp_async_wait_all();
-      __syncthreads();
-      if (warp < 8) {
-        const int h = warp;
-        float M = -INFINITY;
-        for (int pp = lane; pp < np; pp += 32) M = fmaxf(M, hdr[pp * 16 + h]);
-#pragma unroll
-        for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float L = 0.f;
-        for (int pp = lane; pp < np; pp += 32) {
-          const float m = hdr[pp * 16 + h];
-          const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
-          wts[pp * 8 + h] = w;
-          L = fmaf(w, hdr[pp * 16 + 8 + h], L);
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-        if (lane == 0) {
-          tot[h] = L;
-          tot[8 + h] = M;
-        }
-      }
-      __syncthreads();
-      for (int e = tid; e < grp * D; e += C::THREADS) {
-        const int h = e / D;
-        float acc = 0.f;
-#pragma unroll 4
-        for (int pp = 0; pp < cap; ++pp) acc = fmaf(wts[pp * 8 + h], rows[pp * grp * D + e], acc);
-        for (int pp = cap; pp < np; ++pp)
-          acc = fmaf(wts[pp * 8 + h], __ldcg(base + (int64_t)pp * PARTIAL_FLOATS + 16 + e), acc);
-        const float val = acc / tot[h];
-        P.out[pr.seq * P.out_stride + (int64_t)(pr.kv_head * grp) * D + e] = __float2bfloat16_rn(val);
-        if (!isfinite(val)) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-      }
-      if (tid < grp && P.lse != nullptr)
-        P.lse[(int64_t)pr.seq * P.hq + pr.kv_head * grp + tid] = (tot[8 + tid] + __log2f(tot[tid])) * LN2;
-      if (tid == 0) P.counters[pidx] = 0;
-      __syncthreads();
-    }
-    if (P.trace && tid == 0) {
+    if (P.trace && lane == 0) {
       uint64_t* tr = P.trace + 32 * blockIdx.x;
-      tr[0] = t_start;
-      tr[1] = t_loops;
-      tr[2] = t_ticket;
-      tr[3] = global_timer_ns();
-      tr[4] = sm_id();
-      tr[5] = merged;
+      tr[6 + warp] = global_timer_ns();
+      if (warp == 0) {
+        tr[0] = t_start;
+        tr[4] = sm_id();
+      }
     }
   }
 };
@@ -848,6 +700,56 @@ template <int KB, int VB, int G, typename ST>
 __global__ void __launch_bounds__(Cfg<KB, VB, G, ST>::THREADS, 1) decode_kernel(Params P) {
   extern __shared__ __align__(128) unsigned char smem[];
   Kernel<KB, VB, G, ST>::run(P, smem);
+}
+
+// ---------------------------------------------------------------- state merge
+// One CTA per (pair, 32-channel chunk), warp h = query head h of the pair.  In
+// rounds of 32 states, lane k loads state k's (max, sum) for head h and every
+// lane loads its channel of all 32 rows, all in one batch; the round's weights
+// exp2(m_k - M) reach the lanes by shuffles.  Output out[seq, kv*grp + h, d]
+// in bf16 and, for d == 0, the natural-log LSE.  No shared memory, no CTA
+// barrier: each warp is independent.
+constexpr int MERGE_DCH = 32;
+
+__global__ void __launch_bounds__(256) state_merge_kernel(const float* __restrict__ states,
+                                                          const ucb_decode_pair* __restrict__ pairs, int grp,
+                                                          int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                                                          float* __restrict__ lse) {
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31, d = blockIdx.y * MERGE_DCH + lane;
+  if (h >= grp) return;
+  const ucb_decode_pair pr = pairs[blockIdx.x];
+  const float* base = states + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
+  float M = -INFINITY, L = 0.f, acc = 0.f;
+  for (int k0 = 0; k0 < pr.partial_count; k0 += 32) {
+    const int nk = min(32, pr.partial_count - k0);
+    const float* st = base + (int64_t)k0 * PARTIAL_FLOATS;
+    const float mk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + h) : -INFINITY;
+    const float lk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + 8 + h) : 0.f;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) v[q] = q < nk ? __ldcg(st + (int64_t)q * PARTIAL_FLOATS + 16 + h * D + d) : 0.f;
+    float mx = mk;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float m_new = fmaxf(M, mx);
+    const float wk = (mk == -INFINITY) ? 0.f : fast_exp2(mk - m_new);
+    float l = wk * lk;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    const float f = (M == -INFINITY) ? 0.f : fast_exp2(M - m_new);
+    float a0 = acc * f, a1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < 32; q += 2) {
+      a0 = fmaf(__shfl_sync(0xffffffffu, wk, q), v[q], a0);
+      a1 = fmaf(__shfl_sync(0xffffffffu, wk, q + 1), v[q + 1], a1);
+    }
+    acc = a0 + a1;
+    L = fmaf(L, f, l);
+    M = m_new;
+  }
+  const int qh = pr.kv_head * grp + h;
+  out[pr.seq * out_stride + (int64_t)qh * D + d] = __float2bfloat16_rn(acc / L);
+  if (d == 0 && lse != nullptr) lse[(int64_t)pr.seq * hq + qh] = (M + __log2f(L)) * LN2;
 }
 
 template <int KB, int VB, int G, typename ST>
@@ -870,7 +772,13 @@ int launch(const Params& P, int num_ctas, cudaStream_t s) {
   int rc = configure<KB, VB, G, ST>();
   if (rc) return rc;
   decode_kernel<KB, VB, G, ST><<<num_ctas, C::THREADS, C::SMEM, s>>>(P);
-  return ucb_host::check_launch("decode_kernel");
+  rc = ucb_host::check_launch("decode_kernel");
+  if (rc) return rc;
+  // Stream order makes the merge wait for every warp state.  (Launching it as
+  // a programmatic dependent measured slower: 31.7 vs 29.0 us per config-2 step.)
+  state_merge_kernel<<<dim3(P.num_pairs, D / MERGE_DCH), 256, 0, s>>>(
+      static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse);
+  return ucb_host::check_launch("state_merge_kernel");
 }
 
 template <int KB, int VB, int G, typename ST>
@@ -962,8 +870,9 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
                                     int num_ctas, const int32_t* warp_bounds, const ucb_decode_pair* pairs,
                                     int num_pairs, int k_bits, int v_bits,
                                     int group_size, int stat_dtype, float softmax_scale, void* partials,
-                                    int* counters, void* out, int64_t out_stride, float* lse, void* stream) {
-  if (!query || !spans || !ctas || !warp_bounds || !pairs || !partials || !counters || !out)
+                                    const int32_t* warp_slots, void* out, int64_t out_stride, float* lse,
+                                    void* stream) {
+  if (!query || !spans || !ctas || !warp_bounds || !pairs || !partials || !warp_slots || !out)
     return set_error(UCB_ERR_INVALID, "ucb_decode_attention: null pointer");
   if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention: head_dim must be 128");
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > 8)
@@ -986,9 +895,10 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.ctas = ctas;
   P.warp_bounds = warp_bounds;
   P.pairs = pairs;
+  P.num_pairs = num_pairs;
   P.scale_log2 = softmax_scale * ucb::decode::LOG2E;
   P.partials = static_cast<float*>(partials);
-  P.counters = counters;
+  P.warp_slots = warp_slots;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.out_stride = out_stride;
   P.lse = lse;
@@ -1003,14 +913,11 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
 // engine that hands the whole HBM pool to its own allocator up front, code
 // running while a CUDA graph is being captured by someone else, or a plugin
 // host that forbids the library from calling cudaMalloc.  For them the
-// partials and pair counters live in one statically sized device array that
+// warp-state slots live in one statically sized device array that
 // the library module carries on every GPU it is loaded on, until exit.
 namespace {
-constexpr int NOALLOC_MAX_PARTIALS = 512;  // partial slots (sum of partial_count)
-constexpr int NOALLOC_MAX_PAIRS = 512;     // (sequence, KV head) pairs
-constexpr size_t NOALLOC_PARTIAL_BYTES = (size_t)NOALLOC_MAX_PARTIALS * ucb::decode::PARTIAL_FLOATS * sizeof(float);
-constexpr size_t NOALLOC_SCRATCH_BYTES = NOALLOC_PARTIAL_BYTES + (size_t)NOALLOC_MAX_PAIRS * sizeof(int);
-static_assert(NOALLOC_PARTIAL_BYTES % 256 == 0, "counters start 256-byte aligned");
+constexpr int NOALLOC_MAX_PARTIALS = 512;  // warp-state slots (sum of partial_count)
+constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)NOALLOC_MAX_PARTIALS * ucb::decode::PARTIAL_FLOATS * sizeof(float);
 
 // Host code must not use this name as a pointer: it is only a handle from which
 // cudaGetSymbolAddress returns the array's address on the current device.
@@ -1046,31 +953,20 @@ int noalloc_scratch(unsigned char** ptr) {
 extern "C" int ucb_decode_attention_noalloc(const void* query, int64_t query_stride, int num_q_heads,
                                             int num_kv_heads, int head_dim, const ucb_span* spans, int num_spans,
                                             const ucb_decode_cta* ctas, int num_ctas, const int32_t* warp_bounds,
-                                            const ucb_decode_pair* pairs, int num_pairs, int num_partials,
-                                            int k_bits, int v_bits, int group_size, int stat_dtype,
-                                            float softmax_scale, void* out, int64_t out_stride, float* lse,
-                                            void* stream) {
+                                            const ucb_decode_pair* pairs, int num_pairs,
+                                            const int32_t* warp_slots, int num_partials, int k_bits, int v_bits,
+                                            int group_size, int stat_dtype, float softmax_scale, void* out,
+                                            int64_t out_stride, float* lse, void* stream) {
   if (num_partials <= 0 || num_partials > NOALLOC_MAX_PARTIALS)
     return set_error(UCB_ERR_INVALID,
                      "ucb_decode_attention_noalloc: the plan needs %d partial slots; the static scratch holds 1..%d",
                      num_partials, NOALLOC_MAX_PARTIALS);
-  if (num_pairs <= 0 || num_pairs > NOALLOC_MAX_PAIRS)
-    return set_error(UCB_ERR_INVALID,
-                     "ucb_decode_attention_noalloc: %d (sequence, KV head) pairs; the static scratch holds 1..%d",
-                     num_pairs, NOALLOC_MAX_PAIRS);
   unsigned char* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != UCB_OK) return rc;
-  int* counters = reinterpret_cast<int*>(scratch + NOALLOC_PARTIAL_BYTES);
-  // The counters must start at zero; a call that stopped on a device error may
-  // have left some set, so clear them in stream order before every launch.
-  const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)num_pairs * sizeof(int),
-                                        static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess)
-    return set_error(UCB_ERR_CUDA, "ucb_decode_attention_noalloc: clearing counters: %s", cudaGetErrorString(e));
   return ucb_decode_attention(query, query_stride, num_q_heads, num_kv_heads, head_dim, spans, num_spans, ctas,
                               num_ctas, warp_bounds, pairs, num_pairs, k_bits, v_bits, group_size, stat_dtype,
-                              softmax_scale, scratch, counters, out, out_stride, lse, stream);
+                              softmax_scale, scratch, warp_slots, out, out_stride, lse, stream);
 }
 
 extern "C" int ucb_merge_partials(const void* partials, int n_parts, const ucb_decode_pair* pairs, int num_pairs,

@@ -247,7 +247,6 @@ MAX_SPANS_PER_CTA = 16
 # 2-bit packed stage) and entering a new segment costs 0.4 packed stages.
 DENSE_UNIT_COST = 0.83
 SEGMENT_SWITCH_STAGES = 0.4
-MAX_PARTIALS_PER_PAIR = 160
 
 
 @dataclass
@@ -288,7 +287,8 @@ class DecodePlan:
     num_ctas: int
     num_pairs: int
     partials: torch.Tensor
-    counters: torch.Tensor
+    warp_slots: torch.Tensor
+    num_partials: int = 0
     keepalive: list = field(default_factory=list)
     bytes_per_step: int = 0
 
@@ -315,7 +315,7 @@ class DecodePlan:
              self.head_dim, self.spans.data_ptr(), self.num_spans, self.ctas.data_ptr(), self.num_ctas,
              self.warp_bounds.data_ptr(), self.pairs.data_ptr(), self.num_pairs, self.k_bits, self.v_bits,
              self.group_size, _capi.UCB_BF16,
-             scale, self.partials.data_ptr(), self.counters.data_ptr(), out.data_ptr(), out.stride(0),
+             scale, self.partials.data_ptr(), self.warp_slots.data_ptr(), out.data_ptr(), out.stride(0),
              lse.data_ptr(), stream_of(query))
         return out, lse
 
@@ -575,18 +575,34 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         ctas.append(rec)
         for p in range(p0, p1 + 1):
             touched.setdefault(p, []).append(c)
+    # Warp states: a warp writes one state per segment it processed (its first
+    # segment only when it crosses a boundary, its last segment always).  The
+    # slots of a pair are contiguous, in CTA and warp order.
+    states_by_pair: dict[int, list[int]] = {}
+    warp_slots = [-1] * (2 * warps * len(cta_bounds))
+    for c, bounds in enumerate(cta_bounds):
+        for w in range(warps):
+            a, b = bounds[w], bounds[w + 1]
+            if a == b:
+                continue
+            if unit_seg[a] != unit_seg[b - 1]:
+                states_by_pair.setdefault(unit_pair[a], []).append(2 * (c * warps + w))
+            states_by_pair.setdefault(unit_pair[b - 1], []).append(2 * (c * warps + w) + 1)
     pairs: list[UcbDecodePair] = []
     partial_total = 0
     for p, (b, h) in enumerate(pairs_info):
         cs = touched[p]
         if cs != list(range(cs[0], cs[0] + len(cs))):
             raise AssertionError("CTAs of a pair must be consecutive")
-        if len(cs) > MAX_PARTIALS_PER_PAIR:
-            raise ValueError(f"a (sequence, KV head) pair spans {len(cs)} CTAs; at most {MAX_PARTIALS_PER_PAIR}")
         pr = UcbDecodePair()
         pr.seq, pr.kv_head = b, h
-        pr.partial_begin, pr.partial_count, pr.cta_first = partial_total, len(cs), cs[0]
-        partial_total += len(cs)
+        pr.partial_begin, pr.cta_first = partial_total, cs[0]
+        for idx in states_by_pair.get(p, []):
+            warp_slots[idx] = partial_total
+            partial_total += 1
+        pr.partial_count = partial_total - pr.partial_begin
+        if pr.partial_count == 0:
+            raise AssertionError("every pair needs at least one warp state")
         pairs.append(pr)
 
     def upload(structs) -> torch.Tensor:
@@ -611,7 +627,8 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         num_ctas=len(ctas),
         num_pairs=len(pairs),
         partials=torch.empty(partial_total * partial_bytes, device=device, dtype=torch.uint8),
-        counters=torch.zeros(len(pairs), device=device, dtype=torch.int32),
+        warp_slots=torch.tensor(warp_slots, dtype=torch.int32).to(device),
+        num_partials=partial_total,
         keepalive=keepalive,
         bytes_per_step=int(sum(span_bytes)),
     )
