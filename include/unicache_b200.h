@@ -213,6 +213,22 @@ UCB_API int ucb_decode_set_trace(void* trace_dev);
 UCB_API int ucb_decode_config(int k_bits, int v_bits, int group_size, int stat_dtype, int* ctas,
                               int* warps_per_cta);
 
+/* ------------------------------------------------------------------ long-query attention
+ * Replaces the q_len > 1 branch of the fused mixed physical attention
+ * (unicache/adapters/bagel.py:1598-1858: dequantized workspace, then
+ * flash_attn_func(..., causal=False) at :1796-1801) for all KV heads at once,
+ * on the tcgen05 tensor cores.  Per KV head h (non-causal):
+ *   out[h, m, :] = softmax(q[h, m, :] . k[h, :n_tokens, :]^T * softmax_scale) v
+ *   lse[h, m]    = natural-log log-sum-exp of the scaled logits (may be NULL)
+ * q_dev bf16 [heads, m_rows, 128] (the query rows of one KV head: (position,
+ * head-in-group) pairs), k_dev bf16 [heads, n_padded, 128], vt_dev bf16
+ * [heads, 128, n_padded] (V transposed), out_dev bf16 [heads, m_rows, 128],
+ * lse_dev fp32 [heads, m_rows].  n_padded >= n_tokens, a multiple of 8; key
+ * and value padding tokens must be finite (zeros).  Operands 16-byte aligned. */
+UCB_API int ucb_prefill_attention(const void* q_dev, const void* k_dev, const void* vt_dev, int heads, int m_rows,
+                                  int n_tokens, int n_padded, float softmax_scale, void* out_dev, float* lse_dev,
+                                  void* stream);
+
 /* ------------------------------------------------------------------ LSE merge
  * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).
  * n summaries, summary i: out_ptrs[i] -> [rows, heads, head_dim] (dtype),

@@ -1,0 +1,107 @@
+"""Long-query (prefill) attention on the tcgen05 tensor cores.
+
+The kernel is floating point, so it is checked against a plain PyTorch fp32
+reference of the same non-causal attention (reference adapter
+unicache/adapters/bagel.py:1796-1801 runs flash_attn_func(..., causal=False)
+over the dequantized segments).  Tolerance: the north-star bf16 bound,
+max-abs 2e-2 and mean-abs 1e-3 on the output, 2e-2 on the natural-log LSE.
+The mixed-segment path is checked against the float64 oracle."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention, kivi
+from unicache_b200 import GQAH2OCache, PackedKIVICache, kernels
+from unicache_b200.adapters.attention import long_query_attention_summary
+from unicache_b200.synthetic import make_kv, make_query
+
+from .gpu_util import MAX_ABS, MEAN_ABS, assert_attention_close, host, need_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+def _reference(q, k, v, n):
+    qf, kf, vf = q.float(), k[:, :n].float(), v[:, :n].float()
+    logits = torch.matmul(qf, kf.transpose(1, 2)) / math.sqrt(q.shape[-1])
+    lse = torch.logsumexp(logits, dim=-1)
+    return torch.matmul(torch.softmax(logits, dim=-1), vf), lse
+
+
+def _operands(heads, m, n, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    n_pad = (n + 7) // 8 * 8
+    q = torch.randn(heads, m, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.zeros(heads, n_pad, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.zeros_like(k)
+    k[:, :n] = (torch.randn(heads, n, 128, generator=gen, device="cuda") * 1.5).to(torch.bfloat16)
+    v[:, :n] = torch.randn(heads, n, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    return q, k, v, n_pad
+
+
+@pytest.mark.parametrize("heads,m,n", [(1, 128, 128), (1, 128, 40), (2, 200, 300), (4, 448, 1000), (1, 64, 1)])
+def test_prefill_matches_fp32_reference(heads, m, n):
+    need_gpu()
+    q, k, v, n_pad = _operands(heads, m, n, seed=m + n)
+    out, lse = kernels.prefill_attention(q, k, v.transpose(1, 2).contiguous(), n)
+    torch.cuda.synchronize()
+    ref, ref_lse = _reference(q, k, v, n)
+    diff = (out.float() - ref).abs()
+    assert torch.isfinite(out.float()).all()
+    assert float(diff.max()) <= MAX_ABS and float(diff.mean()) <= MEAN_ABS, (float(diff.max()), float(diff.mean()))
+    assert float((lse - ref_lse).abs().max()) <= 2e-2
+    assert kernels.device_status() == 0
+
+
+def test_prefill_config4_shape_and_repeat():
+    """BASELINE config 4 per layer: Lq = 1024 queries x 7 heads per KV head
+    against 3095 keys, 4 KV heads; a second launch is bitwise identical."""
+    need_gpu()
+    q, k, v, n_pad = _operands(4, 1024 * 7, 3095, seed=4)
+    vt = v.transpose(1, 2).contiguous()
+    out, lse = kernels.prefill_attention(q, k, vt, 3095)
+    out2, lse2 = kernels.prefill_attention(q, k, vt, 3095)
+    torch.cuda.synchronize()
+    ref, ref_lse = _reference(q, k, v, 3095)
+    diff = (out.float() - ref).abs()
+    assert float(diff.max()) <= MAX_ABS and float(diff.mean()) <= MEAN_ABS, (float(diff.max()), float(diff.mean()))
+    assert float((lse - ref_lse).abs().max()) <= 2e-2
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
+
+
+def test_prefill_rejects_bad_arguments():
+    need_gpu()
+    q, k, v, n_pad = _operands(1, 128, 100, seed=1)
+    with pytest.raises(ValueError):
+        kernels.prefill_attention(q, k, v, 100)  # v not transposed: shape mismatch
+    with pytest.raises(ValueError):
+        kernels.prefill_attention(q, k[:, :100].contiguous(), v.transpose(1, 2)[:, :, :100].contiguous(), 100)
+
+
+def test_long_query_over_mixed_segments_matches_oracle():
+    """A 96-token query block over [dense 16 | H2O | packed KIVI + residual]."""
+    need_gpu()
+    heads, tokens = 4, 352
+    key, value = make_kv(tokens, heads, 128, seed=31, device="cuda")
+    packed = PackedKIVICache.from_dense(key, value, logical_token_ids=torch.arange(tokens, device="cuda"),
+                                        token_type_id=3, k_bits=2, v_bits=2, group_size=32, residual_length=32)
+    hk, hv = make_kv(200, heads, 128, seed=32, device="cuda")
+    scores = torch.rand(heads, 200, generator=torch.Generator().manual_seed(5)).to("cuda")
+    h2o = GQAH2OCache.from_dense(hk, hv, logical_token_ids=torch.arange(200, device="cuda"), token_type_id=1,
+                                 per_kv_head_scores=scores, target_tokens=60, recent_tokens=12)
+    dk, dv = make_kv(16, heads, 128, seed=33, device="cuda")
+    query = make_query(96, 28, 128, seed=34, device="cuda")
+    out, lse = long_query_attention_summary(query, [h2o, packed], dense_key=dk, dense_value=dv)
+    torch.cuda.synchronize()
+    ref = kivi.packed_from_dense(host(key), host(value), "bfloat16", k_bits=2, v_bits=2, group_size=32,
+                                 residual_length=32)
+    rk, rv = kivi.packed_dequantize(ref)
+    keys = [host(dk), host(h2o.key).transpose(1, 0, 2), rk]
+    vals = [host(dv), host(h2o.value).transpose(1, 0, 2), rv]
+    e_out, e_lse = attention.mixed_attention(host(query), keys, vals)
+    assert_attention_close(out, e_out, what="long-query mixed")
+    assert np.abs(host(lse) - e_lse).max() <= 2e-2

@@ -101,49 +101,69 @@ def fused_mixed_decode(query: torch.Tensor, dense_key: torch.Tensor | None, dens
                                    int(query.shape[-1]))
 
 
-def _dequantized_segments(segments, dtype, include_residual=True):
-    keys, values = [], []
+def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_residual: bool = True):
+    """Head-major bf16 key rows [H, Np, D] and transposed values [H, D, Np]
+    of all segments (packed spans restored by the bit-exact dequant kernel,
+    dense and H2O rows copied); Np is the token count rounded up to 8 and the
+    padding is zero.  Mirrors the reference's mixed-attention workspace
+    (bagel.py:1410-1450)."""
+
+    spans = []
     for seg in segments:
         if isinstance(seg, PackedKIVICache):
-            if seg.quantized_tokens:
-                k = torch.empty((seg.quantized_tokens, seg.num_kv_heads, seg.head_dim),
-                                device=seg.key_code.device, dtype=dtype)
-                v = torch.empty_like(k)
-                seg.dequantize_range(0, seg.quantized_tokens, dtype=dtype, output_key=k, output_value=v)
-                keys.append(k)
-                values.append(v)
-            if include_residual and int(seg.residual_key.shape[0]):
-                keys.append(seg.residual_key.to(dtype))
-                values.append(seg.residual_value.to(dtype))
+            spans.append((seg, seg.quantized_tokens + (int(seg.residual_key.shape[0]) if include_residual else 0)))
         elif isinstance(seg, GQAH2OCache):
-            keys.append(seg.key.transpose(0, 1).to(dtype))
-            values.append(seg.value.transpose(0, 1).to(dtype))
+            spans.append((seg, seg.retained_tokens))
         else:
-            k, v = seg
-            keys.append(k.to(dtype))
-            values.append(v.to(dtype))
-    return torch.cat(keys, dim=0), torch.cat(values, dim=0)
+            spans.append((seg, int(seg[0].shape[0])))
+    total = sum(n for _, n in spans)
+    padded = max(8, (total + 7) // 8 * 8)
+    kw = torch.zeros((num_kv_heads, padded, head_dim), device=device, dtype=torch.bfloat16)
+    vw = torch.zeros_like(kw)
+    t0 = 0
+    for seg, n in spans:
+        if isinstance(seg, PackedKIVICache):
+            q = seg.quantized_tokens
+            if q:
+                seg.dequantize_range(0, q, dtype=torch.bfloat16, output_key=kw[:, t0:t0 + q].transpose(0, 1),
+                                     output_value=vw[:, t0:t0 + q].transpose(0, 1))
+            if n > q:
+                kw[:, t0 + q:t0 + n] = seg.residual_key.transpose(0, 1)
+                vw[:, t0 + q:t0 + n] = seg.residual_value.transpose(0, 1)
+        elif isinstance(seg, GQAH2OCache):
+            kw[:, t0:t0 + n] = seg.key
+            vw[:, t0:t0 + n] = seg.value
+        else:
+            kw[:, t0:t0 + n] = seg[0].transpose(0, 1)
+            vw[:, t0:t0 + n] = seg[1].transpose(0, 1)
+        t0 += n
+    return kw, vw.transpose(1, 2).contiguous(), total
 
 
 def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_key=None, dense_value=None,
                                  include_residual: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
-    """Multi-query attention over physical segments: (out [Lq, Hq, D], lse [Hq, Lq]).
+    """Multi-query (non-causal) attention over physical segments on the tcgen05
+    tensor cores: (out [Lq, Hq, D], lse [Hq, Lq] natural log).
 
-    Restores packed segments with the bit-exact dequant kernel and contracts
-    with the library GEMM in fp32; the tensor-core long-query kernel replaces
-    this path."""
+    The query rows of each KV head ((position, head-in-group) pairs) form one
+    M x N attention problem; keys and values come from a bf16 workspace."""
 
     kernels.require_cuda(query, "query")
     segs = _segments_for(dense_key, dense_value, segments)
-    key, value = _dequantized_segments(segs, query.dtype, include_residual=include_residual)
+    if not segs:
+        raise ValueError("long-query attention needs at least one segment")
+    first = segs[0]
+    if isinstance(first, (PackedKIVICache, GQAH2OCache)):
+        hkv = first.num_kv_heads
+    else:
+        hkv = int(first[0].shape[1])
     lq, hq, d = map(int, query.shape)
-    hkv = int(key.shape[1])
+    if hq % hkv:
+        raise ValueError("Query heads must be divisible by KV heads")
     grp = hq // hkv
-    q = query.transpose(0, 1).float().reshape(hkv, grp * lq, d)
-    k = key.transpose(0, 1).float()
-    v = value.transpose(0, 1).float()
-    logits = torch.matmul(q, k.transpose(-1, -2)) / math.sqrt(d)
-    lse = torch.logsumexp(logits, dim=-1)
-    probs = torch.exp(logits - lse.unsqueeze(-1))
-    out = torch.matmul(probs, v).reshape(hq, lq, d).transpose(0, 1)
-    return out.to(query.dtype), lse.reshape(hq, lq)
+    kw, vt, total = _kv_workspace(segs, hkv, d, query.device, include_residual=include_residual)
+    q = query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, lq * grp, d).contiguous()
+    out, lse = kernels.prefill_attention(q, kw, vt, total)
+    out = out.view(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
+    lse = lse.view(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
+    return out.to(query.dtype), lse

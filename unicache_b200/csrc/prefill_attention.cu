@@ -1,0 +1,388 @@
+// Long-query attention on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces the q_len > 1 branch of the physical-cache attention of the
+// reference adapter (unicache/adapters/bagel.py:1598-1858, the fused mixed
+// path that ends in flash_attn_func(..., causal=False) over the dequantized
+// segments) for one KV head group at a time:
+//
+//   out[h, m, :] = softmax(q[h, m, :] . k[h, :, :]^T * scale) v[h, :, :]
+//   lse[h, m]    = log sum_t exp(q . k_t * scale)               (natural log)
+//
+// q rows are the (query position, head-in-group) pairs of one KV head, so the
+// grouped-query structure becomes a plain M x N attention per KV head.
+//
+// Design (one CTA of 4 warps per 128 query rows of one KV head):
+//  * Q (128 x 128 bf16), K tiles (128 tokens x 128) and V^T tiles (128 channels
+//    x 128 tokens) arrive by TMA with 128-byte swizzle, which is the canonical
+//    K-major operand layout of tcgen05.mma.  K and V^T tiles are double
+//    buffered and prefetched.
+//  * One thread issues S = Q K^T (eight K=16 steps) into tensor memory; each
+//    thread then owns one row of S (TMEM lane = row), so the row max and sum
+//    need no shuffles.  P = exp2(S*scale*log2e - m) is written in bf16 to
+//    shared memory in the same swizzled layout and O += P V^T runs on the
+//    tensor cores with the accumulator in tensor memory.
+//  * The running max is only moved (and O rescaled in TMEM) when a row's new
+//    maximum exceeds it by more than 8 (log2 units); otherwise P may exceed 1
+//    by up to 2^8, which bf16 and the fp32 accumulator absorb.
+//  * Every mbarrier wait is bounded; a timeout sets a device error flag, and
+//    the CTA still waits (bounded) for its tensor-core work and frees TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace ucb {
+namespace prefill {
+
+constexpr int D = 128;
+constexpr int BM = 128;                  // query rows per CTA (TMEM lanes)
+constexpr int BN = 128;                  // key tokens per tile
+constexpr int HALF = 64 * 128 * 2;       // one 64-column swizzled half of a 128-row tile (16 KB)
+constexpr int TILE = 2 * HALF;           // 32 KB
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE;      // 2 buffers
+constexpr int OFF_V = OFF_K + 2 * TILE;  // 2 buffers (V^T tiles)
+constexpr int OFF_P = OFF_V + 2 * TILE;
+constexpr int OFF_BAR = OFF_P + TILE;    // 8 mbarriers
+constexpr int OFF_TMEM = OFF_BAR + 8 * 8;
+constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + alignment slack
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr float RESCALE_THRESHOLD = 8.f;  // log2 units
+constexpr uint32_t TMEM_COLS = 256;       // S: columns [0, 128), O: [128, 256)
+
+// tcgen05 instruction descriptor, kind::f16: F32 accumulator, BF16 A and B,
+// both K-major, N = 128, M = 128.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled operand
+// whose 8-row atoms are 1024 bytes apart (stride byte offset), starting at
+// `addr` (16-byte units); leading byte offset unused for this layout (1).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Tiled TMA load of box {x, y, z} of a 3-D tensor map into shared memory.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+struct Params {
+  int m_rows;       // query rows per KV head
+  int n_tokens;     // valid key tokens per KV head
+  float scale_log2;  // softmax scale * log2(e)
+  __nv_bfloat16* out;  // [heads, m_rows, D]
+  float* lse;          // [heads, m_rows], may be null
+  unsigned int* err;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, Params P) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int head = blockIdx.y, m0 = blockIdx.x * BM;
+  const int n_tiles = (P.n_tokens + BN - 1) / BN;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* bar_k = bars + 1;  // [2]
+  uint64_t* bar_v = bars + 3;  // [2]
+  uint64_t* bar_s = bars + 5;
+  uint64_t* bar_o = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+
+  if (tid == 0) {
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+
+  auto load_k = [&](int j) {
+    uint64_t* bar = &bar_k[j & 1];
+    mbar_arrive_expect_tx(bar, TILE);
+    unsigned char* dst = smem + OFF_K + (j & 1) * TILE;
+    tma_load_3d(dst, &tm_k, 0, j * BN, head, bar);
+    tma_load_3d(dst + HALF, &tm_k, 64, j * BN, head, bar);
+  };
+  auto load_v = [&](int j) {
+    uint64_t* bar = &bar_v[j & 1];
+    mbar_arrive_expect_tx(bar, TILE);
+    unsigned char* dst = smem + OFF_V + (j & 1) * TILE;
+    tma_load_3d(dst, &tm_v, j * BN, 0, head, bar);
+    tma_load_3d(dst + HALF, &tm_v, j * BN + 64, 0, head, bar);
+  };
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_q, TILE);
+    tma_load_3d(smem + OFF_Q, &tm_q, 0, m0, head, bar_q);
+    tma_load_3d(smem + OFF_Q + HALF, &tm_q, 64, m0, head, bar_q);
+    load_k(0);
+    if (n_tiles > 1) load_k(1);
+    load_v(0);
+  }
+
+  const uint32_t q_addr = smem_u32(smem + OFF_Q), p_addr = smem_u32(smem + OFF_P);
+  const int row = tid;  // TMEM lane and query row within the tile
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  for (int j = 0; j < n_tiles; ++j) {
+    const int b = j & 1;
+    if (tid == 0 && ok) {
+      if (j == 0) ok = mbar_wait_bounded(bar_q, 0, WAIT_LIMIT);
+      ok = ok && mbar_wait_bounded(&bar_k[b], (j >> 1) & 1, WAIT_LIMIT);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + OFF_K + b * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc_mma(t_s, sw128_desc(q_addr + off), sw128_desc(k_addr + off), kk > 0 ? 1u : 0u);
+        }
+      }
+      tc_commit(bar_s);  // arrives once every earlier tcgen05.mma of this thread is done
+    }
+    ok = mbar_wait_bounded(bar_s, j & 1, WAIT_LIMIT) && ok;
+    tc_fence_after();
+    // S_j and O += P_{j-1} V_{j-1} are complete: K buffer b and V buffer b^1 are free.
+    if (tid == 0 && ok) {
+      if (j + 2 < n_tiles) load_k(j + 2);
+      if (j + 1 < n_tiles) load_v(j + 1);
+    }
+
+    // ---- softmax on this thread's row
+    uint32_t sv[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tc_ld32(t_s + lane_off + 32 * c, sv[c]);
+    tc_wait_ld();
+    const int valid = min(BN, P.n_tokens - j * BN);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (32 * c + i < valid) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+    mx *= P.scale_log2;
+    const bool move = mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
+    if (__any_sync(0xffffffffu, move)) {
+      const float m_new = move ? fmaxf(mx, m_run) : m_run;
+      const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+      if (j > 0) {  // O holds the sum of earlier tiles: rescale this row in TMEM
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tc_ld32(t_o + lane_off + 32 * c, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tc_st32(t_o + lane_off + 32 * c, ov);
+        }
+        tc_wait_st();
+      }
+      l_run *= alpha;
+      m_run = m_new;
+    }
+    float sum = 0.f;
+    unsigned char* prow = smem + OFF_P + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // 8 tokens = one 16-byte chunk
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t0 = 32 * c + 8 * q + 2 * e;
+          const float p0 = t0 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, -m_run)) : 0.f;
+          const float p1 =
+              t0 + 1 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, -m_run)) : 0.f;
+          const uint32_t pk = pack_bf16x2(p0, p1);
+          sum += bf16lo(pk) + bf16hi(pk);  // the sum sees the rounded weights the MMA uses
+          w[e] = pk;
+        }
+        const int chunk = 4 * c + q;  // 0..15 over the 128 tokens
+        unsigned char* dst = prow + (chunk >> 3) * HALF + (((chunk & 7) ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    l_run += sum;
+    fence_proxy_async_smem();  // P (generic stores) -> tensor-core reads (async proxy)
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && ok) {
+      tc_fence_after();
+      ok = mbar_wait_bounded(&bar_v[b], (j >> 1) & 1, WAIT_LIMIT);
+      if (ok) {
+        const uint32_t v_addr = smem_u32(smem + OFF_V + b * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc_mma(t_o, sw128_desc(p_addr + off), sw128_desc(v_addr + off), (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      }
+    }
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+  }
+  if (tid == 0) tc_commit(bar_o);
+  const bool done = mbar_wait_bounded(bar_o, 0, WAIT_LIMIT);
+  tc_fence_after();
+  if (ok && done && n_tiles > 0) {
+    const float inv = 1.f / l_run;
+    const int m = m0 + row;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tc_ld32(t_o + lane_off + 32 * c, ov);
+      tc_wait_ld();
+      if (m < P.m_rows) {
+        __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
+          v.y = pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
+          v.z = pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
+          v.w = pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + i) = v;
+        }
+      }
+    }
+    if (m < P.m_rows && P.lse) P.lse[(int64_t)head * P.m_rows + m] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
+  } else if (tid == 0) {
+    atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D bf16 tensor map {x: inner, y, z} with a {64, 128, 1} box and 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z) {
+  auto fn = encode_fn();
+  if (!fn) return ucb_host::set_error(UCB_ERR_CUDA, "prefill: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {x, y, z};
+  const cuuint64_t strides[2] = {x * 2, x * y * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return ucb_host::set_error(UCB_ERR_CUDA, "prefill: tensor map encoding failed (%d)", (int)r);
+  return UCB_OK;
+}
+
+}  // namespace prefill
+}  // namespace ucb
+
+extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* vt, int heads, int m_rows,
+                                     int n_tokens, int n_padded, float softmax_scale, void* out, float* lse,
+                                     void* stream) {
+  using namespace ucb::prefill;
+  if (!q || !k || !vt || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: null pointer");
+  if (heads <= 0 || m_rows <= 0 || n_tokens <= 0)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: empty problem");
+  if (n_padded < n_tokens || n_padded % 8)
+    return ucb_host::set_error(UCB_ERR_INVALID,
+                               "ucb_prefill_attention: n_padded must be >= n_tokens and a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(vt)) & 15)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: operands must be 16-byte aligned");
+  unsigned int* err = ucb_host::device_error_word();
+  if (!err) return ucb_host::set_error(UCB_ERR_CUDA, "ucb_prefill_attention: device error word unavailable");
+  CUtensorMap tq, tk, tv;
+  int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads);
+  if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads);
+  if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads);
+  if (rc) return rc;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+      return ucb_host::set_error(UCB_ERR_CUDA, "prefill: cannot reserve %d bytes of shared memory", SMEM);
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  Params P;
+  P.m_rows = m_rows;
+  P.n_tokens = n_tokens;
+  P.scale_log2 = softmax_scale * 1.4426950408889634f;
+  P.out = static_cast<__nv_bfloat16*>(out);
+  P.lse = lse;
+  P.err = err;
+  const dim3 grid((m_rows + BM - 1) / BM, heads);
+  prefill_kernel<<<grid, 128, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
+  return ucb_host::check_launch("prefill_kernel");
+}

@@ -634,6 +634,34 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
     )
 
 
+# ---------------------------------------------------------------- long-query attention
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, n_tokens: int, *,
+                      softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                      lse: torch.Tensor | None = None):
+    """Non-causal attention per KV head on the tcgen05 tensor cores.
+
+    q [H, M, 128] bf16, k [H, Np, 128] bf16, vt [H, 128, Np] bf16 with
+    Np >= n_tokens a multiple of 8 and finite padding -> (out [H, M, 128] bf16,
+    lse [H, M] fp32, natural log)."""
+
+    for name, t in (("q", q), ("k", k), ("vt", vt)):
+        require_cuda(t, name)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 3:
+            raise ValueError(f"{name} must be a contiguous 3-D bfloat16 tensor")
+    heads, m_rows, d = map(int, q.shape)
+    n_padded = int(k.shape[1])
+    if d != 128 or tuple(k.shape) != (heads, n_padded, d) or tuple(vt.shape) != (heads, d, n_padded):
+        raise ValueError("prefill attention expects q [H,M,128], k [H,Np,128], vt [H,128,Np]")
+    scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
+    call("ucb_prefill_attention", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, int(n_tokens),
+         n_padded, scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    return out, lse
+
+
 def device_status(device: torch.device | None = None) -> int:
     flags = ctypes.c_uint(0)
     stream = torch.cuda.current_stream(device).cuda_stream
