@@ -11,9 +11,10 @@
 // q rows are the (query position, head-in-group) pairs of one KV head, so the
 // grouped-query structure becomes a plain M x N attention per KV head.
 //
-// Design (one CTA of 4 warps per 128 query rows of one KV head):
-//  * Q (128 x 128 bf16), K tiles (128 tokens x 128) and V^T tiles (128 channels
-//    x 128 tokens) arrive by TMA with 128-byte swizzle, which is the canonical
+// Design (one CTA of 4 warps per 128 query rows of one KV head, two CTAs per
+// SM so that one CTA's softmax overlaps the other's tensor-core work):
+//  * Q (128 x 128 bf16), K tiles (64 tokens x 128) and V^T tiles (128 channels
+//    x 64 tokens) arrive by TMA with 128-byte swizzle, which is the canonical
 //    K-major operand layout of tcgen05.mma.  K and V^T tiles are double
 //    buffered and prefetched.
 //  * One thread issues S = Q K^T (eight K=16 steps) into tensor memory; each
@@ -35,25 +36,33 @@ namespace ucb {
 namespace prefill {
 
 constexpr int D = 128;
-constexpr int BM = 128;                  // query rows per CTA (TMEM lanes)
-constexpr int BN = 128;                  // key tokens per tile
-constexpr int HALF = 64 * 128 * 2;       // one 64-column swizzled half of a 128-row tile (16 KB)
-constexpr int TILE = 2 * HALF;           // 32 KB
+constexpr int BM = 128;                   // query rows per CTA (TMEM lanes)
+constexpr int BN = 64;                    // key tokens per tile
+constexpr int QTILE = BM * D * 2;         // 32 KB: two 64-channel swizzled halves
+constexpr int QHALF = QTILE / 2;          // 16 KB
+constexpr int KTILE = BN * D * 2;         // 16 KB: two 64-channel halves of 64 rows
+constexpr int KHALF = KTILE / 2;          // 8 KB
+constexpr int VTILE = D * BN * 2;         // 16 KB: 128 channel rows x 64 tokens
+constexpr int PTILE = BM * BN * 2;        // 16 KB: 128 query rows x 64 tokens
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE;      // 2 buffers
-constexpr int OFF_V = OFF_K + 2 * TILE;  // 2 buffers (V^T tiles)
-constexpr int OFF_P = OFF_V + 2 * TILE;
-constexpr int OFF_BAR = OFF_P + TILE;    // 8 mbarriers
+constexpr int OFF_K = OFF_Q + QTILE;      // 2 buffers
+constexpr int OFF_V = OFF_K + 2 * KTILE;  // 2 buffers (V^T tiles)
+constexpr int OFF_P = OFF_V + 2 * VTILE;
+constexpr int OFF_BAR = OFF_P + PTILE;    // 8 mbarriers
 constexpr int OFF_TMEM = OFF_BAR + 8 * 8;
-constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + alignment slack
+constexpr int SMEM = OFF_TMEM + 16;       // two CTAs per SM
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr float RESCALE_THRESHOLD = 8.f;  // log2 units
-constexpr uint32_t TMEM_COLS = 256;       // S: columns [0, 128), O: [128, 256)
+constexpr uint32_t TMEM_COLS = 256;       // S: columns [0, 64), O: [64, 192)
+constexpr uint32_t COL_O = 64;
 
-// tcgen05 instruction descriptor, kind::f16: F32 accumulator, BF16 A and B,
-// both K-major, N = 128, M = 128.
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+// tcgen05 instruction descriptors, kind::f16: F32 accumulator, BF16 A and B,
+// both K-major, M = 128; N = 64 for S = Q K^T and N = 128 for O += P V.
+constexpr uint32_t idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+constexpr uint32_t IDESC_S = idesc(BN);
+constexpr uint32_t IDESC_O = idesc(D);
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled operand
 // whose 8-row atoms are 1024 bytes apart (stride byte offset), starting at
@@ -66,12 +75,13 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(IDESC), "r"(accumulate)
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -124,15 +134,18 @@ struct Params {
   unsigned int* err;
 };
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5;
   const int head = blockIdx.y, m0 = blockIdx.x * BM;
   const int n_tiles = (P.n_tokens + BN - 1) / BN;
+  // The swizzled operand layout needs a 1024-byte aligned base.
+  if (smem_u32(smem) & 1023) {
+    if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_k = bars + 1;  // [2]
@@ -155,27 +168,25 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t t_s = tmem, t_o = tmem + COL_O;
   const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
 
   auto load_k = [&](int j) {
     uint64_t* bar = &bar_k[j & 1];
-    mbar_arrive_expect_tx(bar, TILE);
-    unsigned char* dst = smem + OFF_K + (j & 1) * TILE;
+    mbar_arrive_expect_tx(bar, KTILE);
+    unsigned char* dst = smem + OFF_K + (j & 1) * KTILE;
     tma_load_3d(dst, &tm_k, 0, j * BN, head, bar);
-    tma_load_3d(dst + HALF, &tm_k, 64, j * BN, head, bar);
+    tma_load_3d(dst + KHALF, &tm_k, 64, j * BN, head, bar);
   };
   auto load_v = [&](int j) {
     uint64_t* bar = &bar_v[j & 1];
-    mbar_arrive_expect_tx(bar, TILE);
-    unsigned char* dst = smem + OFF_V + (j & 1) * TILE;
-    tma_load_3d(dst, &tm_v, j * BN, 0, head, bar);
-    tma_load_3d(dst + HALF, &tm_v, j * BN + 64, 0, head, bar);
+    mbar_arrive_expect_tx(bar, VTILE);
+    tma_load_3d(smem + OFF_V + (j & 1) * VTILE, &tm_v, j * BN, 0, head, bar);
   };
   if (tid == 0) {
-    mbar_arrive_expect_tx(bar_q, TILE);
+    mbar_arrive_expect_tx(bar_q, QTILE);
     tma_load_3d(smem + OFF_Q, &tm_q, 0, m0, head, bar_q);
-    tma_load_3d(smem + OFF_Q + HALF, &tm_q, 64, m0, head, bar_q);
+    tma_load_3d(smem + OFF_Q + QHALF, &tm_q, 64, m0, head, bar_q);
     load_k(0);
     if (n_tiles > 1) load_k(1);
     load_v(0);
@@ -192,11 +203,12 @@ __global__ void __launch_bounds__(128, 1)
       ok = ok && mbar_wait_bounded(&bar_k[b], (j >> 1) & 1, WAIT_LIMIT);
       if (ok) {
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + OFF_K + b * TILE);
+        const uint32_t k_addr = smem_u32(smem + OFF_K + b * KTILE);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          tc_mma(t_s, sw128_desc(q_addr + off), sw128_desc(k_addr + off), kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {  // 8 steps over the channels
+          const uint32_t col = (kk & 3) * 32;
+          tc_mma(t_s, sw128_desc(q_addr + (kk >> 2) * QHALF + col), sw128_desc(k_addr + (kk >> 2) * KHALF + col),
+                 IDESC_S, kk > 0 ? 1u : 0u);
         }
       }
       tc_commit(bar_s);  // arrives once every earlier tcgen05.mma of this thread is done
@@ -209,15 +221,15 @@ __global__ void __launch_bounds__(128, 1)
       if (j + 1 < n_tiles) load_v(j + 1);
     }
 
-    // ---- softmax on this thread's row
-    uint32_t sv[4][32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) tc_ld32(t_s + lane_off + 32 * c, sv[c]);
+    // ---- softmax on this thread's row (64 columns)
+    uint32_t sv[2][32];
+    tc_ld32(t_s + lane_off, sv[0]);
+    tc_ld32(t_s + lane_off + 32, sv[1]);
     tc_wait_ld();
     const int valid = min(BN, P.n_tokens - j * BN);
     float mx = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < 2; ++c)
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (32 * c + i < valid) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
@@ -244,7 +256,7 @@ __global__ void __launch_bounds__(128, 1)
     float sum = 0.f;
     unsigned char* prow = smem + OFF_P + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {  // 8 tokens = one 16-byte chunk
         uint32_t w[4];
@@ -258,9 +270,8 @@ __global__ void __launch_bounds__(128, 1)
           sum += bf16lo(pk) + bf16hi(pk);  // the sum sees the rounded weights the MMA uses
           w[e] = pk;
         }
-        const int chunk = 4 * c + q;  // 0..15 over the 128 tokens
-        unsigned char* dst = prow + (chunk >> 3) * HALF + (((chunk & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        const int chunk = 4 * c + q;  // 0..7 over the 64 tokens
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     l_run += sum;
@@ -271,12 +282,11 @@ __global__ void __launch_bounds__(128, 1)
       tc_fence_after();
       ok = mbar_wait_bounded(&bar_v[b], (j >> 1) & 1, WAIT_LIMIT);
       if (ok) {
-        const uint32_t v_addr = smem_u32(smem + OFF_V + b * TILE);
+        const uint32_t v_addr = smem_u32(smem + OFF_V + b * VTILE);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          tc_mma(t_o, sw128_desc(p_addr + off), sw128_desc(v_addr + off), (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < BN / 16; ++kk)  // 4 steps over the tokens
+          tc_mma(t_o, sw128_desc(p_addr + kk * 32), sw128_desc(v_addr + kk * 32), IDESC_O,
+                 (j > 0 || kk > 0) ? 1u : 0u);
       }
     }
     ok = __syncthreads_and(ok);
@@ -330,13 +340,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map {x: inner, y, z} with a {64, 128, 1} box and 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z) {
+// 3-D bf16 tensor map {x: inner, y, z} with a {64, box_y, 1} box and 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint32_t box_y) {
   auto fn = encode_fn();
   if (!fn) return ucb_host::set_error(UCB_ERR_CUDA, "prefill: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[3] = {x, y, z};
   const cuuint64_t strides[2] = {x * 2, x * y * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t box[3] = {64, box_y, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -363,9 +373,9 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   unsigned int* err = ucb_host::device_error_word();
   if (!err) return ucb_host::set_error(UCB_ERR_CUDA, "ucb_prefill_attention: device error word unavailable");
   CUtensorMap tq, tk, tv;
-  int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads);
-  if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads);
-  if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads);
+  int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads, BM);
+  if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
+  if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
   if (rc) return rc;
   static bool configured[64] = {false};
   int dev = 0;
