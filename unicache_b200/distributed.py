@@ -1,0 +1,98 @@
+"""Multi-GPU decode over packed physical caches, one process per GPU.
+
+* Batch-partitioned decode (independent requests): ``partition_requests``
+  gives each rank a contiguous block of requests.  Ranks never communicate on
+  the data path; only timing or metrics are reduced, off the hot path.
+* Sequence split of one long context: ``split_tokens`` cuts a sequence into
+  contiguous group-aligned shards, one per rank.  Each rank packs and decodes
+  its shard locally.  ``SequenceSplitDecode`` then gathers every rank's
+  normalised output and log-sum-exp with one all-gather (NCCL over NVLink on
+  GPUs, gloo on CPU) and merges them with the LSE merge kernel.  That merge is
+  the reference's merge_attention_summaries (unicache/adapters/bagel.py:57-72)
+  applied across ranks instead of across segments.  Each rank exchanges
+  (B, Hq, D + 1) values: the output rows and their LSE.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import kernels
+
+
+def partition_requests(num_requests: int, world: int, rank: int) -> range:
+    """Contiguous block of request indices owned by ``rank`` (sizes differ by
+    at most one)."""
+
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must lie in [0, world)")
+    if num_requests < 0:
+        raise ValueError("num_requests must be non-negative")
+    base, extra = divmod(num_requests, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def split_tokens(tokens: int, world: int, group_size: int, residual_length: int = 0) -> list[tuple[int, int]]:
+    """Contiguous shards [start, stop) of a ``tokens``-long sequence, one per
+    rank.  Every boundary is a multiple of ``group_size``, so each shard packs
+    whole KIVI groups.  The last shard also holds the final ``residual_length``
+    full-precision tokens.  Raises ValueError when a rank would get no whole
+    group."""
+
+    if world <= 0 or group_size <= 0:
+        raise ValueError("world and group_size must be positive")
+    quantized = max(0, (tokens - residual_length) // group_size * group_size)
+    groups = quantized // group_size
+    if groups < world:
+        raise ValueError(f"{tokens} tokens give {groups} groups of {group_size}; need at least one per rank")
+    shards = []
+    for r in range(world):
+        g = partition_requests(groups, world, r)
+        shards.append((g.start * group_size, g.stop * group_size))
+    shards[-1] = (shards[-1][0], tokens)
+    return shards
+
+
+def exchange_summaries(out: torch.Tensor, lse: torch.Tensor, group=None) -> tuple[list, list]:
+    """All-gather every rank's (out [B, Hq, D], lse [B, Hq]).  Without an
+    initialised process group the local pair is returned alone."""
+
+    if not dist.is_available() or not dist.is_initialized():
+        return [out], [lse]
+    world = dist.get_world_size(group)
+    outs = [torch.empty_like(out) for _ in range(world)]
+    lses = [torch.empty_like(lse) for _ in range(world)]
+    dist.all_gather(outs, out.contiguous(), group=group)
+    dist.all_gather(lses, lse.contiguous(), group=group)
+    return outs, lses
+
+
+def merge_rank_summaries(outs: list, lses: list) -> tuple[torch.Tensor, torch.Tensor]:
+    """Merge per-rank decode results (out [B, Hq, D], lse [B, Hq]) on the GPU."""
+
+    if len(outs) == 1:
+        return outs[0], lses[0]
+    merged, total = kernels.lse_merge([(o, l.t()) for o, l in zip(outs, lses)])
+    return merged, total.t().contiguous()
+
+
+class SequenceSplitDecode:
+    """Decode of sequences whose tokens are split across ranks.
+
+    ``local_sequences`` holds, for each sequence of the batch, this rank's
+    segments (its shard of the packed cache, plus dense or H2O segments it
+    owns).  Every rank calls it with the same query; every rank gets the
+    merged result."""
+
+    def __init__(self, local_sequences: list[list], *, num_kv_heads: int, head_dim: int = 128, group=None):
+        self.plan = kernels.build_decode_plan(local_sequences, num_kv_heads=num_kv_heads, head_dim=head_dim)
+        self.group = group
+
+    def __call__(self, query: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """query [B, Hq, D] bf16 -> (out [B, Hq, D] bf16, lse [B, Hq] fp32)."""
+
+        out, lse = self.plan.run(query)
+        outs, lses = exchange_summaries(out, lse, self.group)
+        return merge_rank_summaries(outs, lses)
