@@ -68,6 +68,58 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def measured_bf16_peak() -> tuple[float, str]:
+    """Dense bf16 tensor throughput (TFLOP/s, burst) of this pool's B200s."""
+
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as handle:
+            return float(json.load(handle)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def long_query_leg(device) -> dict:
+    """BASELINE config 4, one layer: a 1024-token query block (28 query / 4 KV
+    heads) against 3095 cached tokens per KV head (51 + 980 H2O, 992 packed +
+    32 residual, 16 boundary, 1024 current-latent), non-causal, on the tcgen05
+    kernel with the operands resident; FLOPs = 4 * Lq * Hq * D * N."""
+
+    import torch
+
+    from unicache_b200 import kernels
+
+    heads, grp, lq, n = KV_HEADS, Q_HEADS // KV_HEADS, 1024, 3095
+    n_pad = (n + 7) // 8 * 8
+    gen = torch.Generator(device=device).manual_seed(1)
+    q = torch.randn(heads, lq * grp, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.zeros(heads, n_pad, HEAD_DIM, device=device, dtype=torch.bfloat16)
+    vt = torch.zeros(heads, HEAD_DIM, n_pad, device=device, dtype=torch.bfloat16)
+    k[:, :n] = torch.randn(heads, n, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
+    vt[:, :, :n] = torch.randn(heads, HEAD_DIM, n, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lse = torch.empty(heads, lq * grp, device=device, dtype=torch.float32)
+    for _ in range(3):
+        kernels.prefill_attention(q, k, vt, n, out=out, lse=lse)
+    torch.cuda.synchronize()
+    reps = 20
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        kernels.prefill_attention(q, k, vt, n, out=out, lse=lse)
+    t1.record()
+    torch.cuda.synchronize()
+    seconds = t0.elapsed_time(t1) / 1000.0 / reps
+    flops = 4.0 * lq * Q_HEADS * HEAD_DIM * n
+    peak, kind = measured_bf16_peak()
+    achieved = flops / seconds / 1e12
+    return {"workload": "config4 layer: Lq=1024 x 28/4 heads over 3095 keys, D=128, bf16, non-causal",
+            "us_per_layer": seconds * 1e6, "tflops": achieved,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": kind}}
+
+
 def ncu_traffic() -> float | None:
     """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
 
@@ -379,6 +431,7 @@ def run_b200(args) -> None:
                     "h2d_bytes_per_step": query.numel() * query.element_size(),
                     "d2h_bytes_per_step": out.numel() * out.element_size() + lse.numel() * lse.element_size()},
             "gpu_launches": 2 * args.steps,
+            "long_query": long_query_leg(device) if world == 1 else None,
             "clocks": clocks.summary(),
             "device_status": status,
             "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
