@@ -204,8 +204,9 @@ UCB_API int ucb_decode_attention_noalloc(const void* query_dev, int64_t query_st
 
 /* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
  * NULL, later ucb_decode_attention calls record per CTA word 0 = start,
- * word 4 = SM id and word 6 + w = the time warp w finished (state written),
- * from the global timer in ns.  NULL switches it off. */
+ * word 4 = SM id, word 6 + w = the time warp w finished (state written) and
+ * word 18 + w = the time warp w spent waiting for its copies (global timer,
+ * ns).  NULL switches it off. */
 UCB_API int ucb_decode_set_trace(void* trace_dev);
 
 /* Launch shape of ucb_decode_attention on the current device: CTAs that run at

@@ -621,12 +621,15 @@ struct Kernel {
     int cur_pl = -1, cur_kind = -1, span = 0;
     bool ok = true, stashed = false;
     int s = 0;
+    uint64_t waited = 0;  // diagnostics: time blocked on this warp's copies
     for (int u = u_begin; u < u_end; ++u, ++s) {
       const int slot_idx = s & 1;
+      const uint64_t w0 = P.trace ? global_timer_ns() : 0;
       if (!mbar_wait_bounded(&bars[slot_idx], (s >> 1) & 1, WAIT_LIMIT)) {
         ok = false;
         break;
       }
+      if (P.trace) waited += global_timer_ns() - w0;
       while (span + 1 < n_spans && spans[span + 1].unit_begin <= u) ++span;
       const ucb_span& sp = spans[span];
       const int pl = sp.pair - cta.pair_begin;
@@ -687,7 +690,9 @@ struct Kernel {
     }
     if (P.trace && lane == 0) {
       uint64_t* tr = P.trace + 32 * blockIdx.x;
+      static_assert(C::WARPS <= 12, "the trace record holds 12 warps");
       tr[6 + warp] = global_timer_ns();
+      tr[18 + warp] = waited;
       if (warp == 0) {
         tr[0] = t_start;
         tr[4] = sm_id();
