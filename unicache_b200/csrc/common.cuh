@@ -16,20 +16,30 @@ namespace ucb {
 
 // ---------------------------------------------------------------- dtypes
 template <typename T> struct Dtype;
+// vec2: two adjacent elements loaded at once; lo/hi convert them to fp32.
 template <> struct Dtype<__nv_bfloat16> {
   static constexpr int code = UCB_BF16;
+  using vec2 = uint32_t;
   __device__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  __device__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
+  __device__ static float hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 };
 template <> struct Dtype<__half> {
   static constexpr int code = UCB_F16;
+  using vec2 = uint32_t;
   __device__ static float to_f(__half x) { return __half2float(x); }
   __device__ static __half from_f(float x) { return __float2half_rn(x); }
+  __device__ static float lo(uint32_t v) { return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu))); }
+  __device__ static float hi(uint32_t v) { return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16))); }
 };
 template <> struct Dtype<float> {
   static constexpr int code = UCB_F32;
+  using vec2 = float2;
   __device__ static float to_f(float x) { return x; }
   __device__ static float from_f(float x) { return x; }
+  __device__ static float lo(float2 v) { return v.x; }
+  __device__ static float hi(float2 v) { return v.y; }
 };
 
 // bf16 bit pattern (low or high half of a 32-bit word) -> fp32, exact.

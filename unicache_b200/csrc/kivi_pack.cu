@@ -28,106 +28,169 @@ __device__ __forceinline__ uint32_t quant_code(float v, float mn, float scale, f
   return static_cast<uint32_t>(q);
 }
 
+// Same result as quant_code.  |d * RN(1/scale) - RN(d/scale)| < 2^-22 * q,
+// which is below 2^-14 for q < 2^8, so a product more than 2^-12 away from a
+// half-integer rounds to the same integer; the rare products closer than that
+// (or q >= 2^8) take the exact division.
+__device__ __forceinline__ uint32_t quant_code_fast(float v, float mn, float scale, float inv_scale, float max_code) {
+  const float d = __fsub_rn(v, mn);
+  const float q = __fmul_rn(d, inv_scale);
+  float c = rintf(q);
+  if (!(0.5f - fabsf(q - c) > 0x1p-12f) || q >= 256.0f) c = rintf(__fdiv_rn(d, scale));
+  c = fminf(fmaxf(c, 0.0f), max_code);
+  return static_cast<uint32_t>(c);
+}
+
 // ---------------------------------------------------------------- key pack
-// One CTA per (token group, head); one thread per channel.  Groups run along
-// tokens, so a thread reduces a column of `group` values and emits
-// group*bits/32 words for its channel.
-template <typename T, int BITS>
-__global__ void __launch_bounds__(128) pack_key_kernel(const T* __restrict__ x, int64_t stride_t,
-                                                       int64_t stride_h, int tokens, int head_dim,
-                                                       int group, uint32_t* __restrict__ codes32,
-                                                       uint8_t* __restrict__ codes8,
-                                                       T* __restrict__ scale, T* __restrict__ minimum) {
-  const int g = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+// One CTA per (token group, head); one thread per pair of adjacent channels,
+// so a warp reads 64 channels (a full 128-byte line for 16-bit inputs) per
+// token row.  Groups run along tokens: a thread reduces two columns of G
+// values and emits G*bits/32 words per channel.  Loads are issued 32 rows at
+// a time before any reduction; for G = 32 the values stay in registers for
+// the code pass, larger groups re-read them from L1.
+template <typename T, int BITS, int G>
+__global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, int64_t stride_t,
+                                                      int64_t stride_h, int tokens, int head_dim,
+                                                      uint32_t* __restrict__ codes32,
+                                                      uint8_t* __restrict__ codes8,
+                                                      T* __restrict__ scale, T* __restrict__ minimum) {
+  constexpr int CH = 32;
+  using V2 = typename Dtype<T>::vec2;
+  const int g = blockIdx.x, h = blockIdx.y, d = 2 * threadIdx.x;
   if (d >= head_dim) return;
-  const int groups = tokens / group;
-  const T* col = x + static_cast<int64_t>(g) * group * stride_t + h * stride_h + d;
-  float mn = INFINITY, mx = -INFINITY;
-  for (int i = 0; i < group; ++i) {
-    const float v = ld(col + i * stride_t);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
+  const int groups = tokens / G;
+  const T* col = x + static_cast<int64_t>(g) * G * stride_t + h * stride_h + d;
+  float a[CH], b[CH];
+  float mna = INFINITY, mxa = -INFINITY, mnb = INFINITY, mxb = -INFINITY;
+#pragma unroll
+  for (int c0 = 0; c0 < G; c0 += CH) {
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const V2 pr = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
+      a[i] = Dtype<T>::lo(pr);
+      b[i] = Dtype<T>::hi(pr);
+    }
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      mna = fminf(mna, a[i]);
+      mxa = fmaxf(mxa, a[i]);
+      mnb = fminf(mnb, b[i]);
+      mxb = fmaxf(mxb, b[i]);
+    }
   }
   constexpr float kMax = static_cast<float>((1 << BITS) - 1);
-  const float sc = quant_scale(mn, mx, kMax);
+  const float sca = quant_scale(mna, mxa, kMax), scb = quant_scale(mnb, mxb, kMax);
+  const float inva = __frcp_rn(sca), invb = __frcp_rn(scb);
   const int64_t stat = (static_cast<int64_t>(h) * groups + g) * head_dim + d;
-  scale[stat] = Dtype<T>::from_f(sc);
-  minimum[stat] = Dtype<T>::from_f(mn);
-  if constexpr (BITS == 8) {
-    uint8_t* out = codes8 + (static_cast<int64_t>(h) * tokens + static_cast<int64_t>(g) * group) * head_dim + d;
-    for (int i = 0; i < group; ++i) {
-      out[static_cast<int64_t>(i) * head_dim] =
-          static_cast<uint8_t>(quant_code(ld(col + i * stride_t), mn, sc, kMax));
-    }
-  } else {
-    constexpr int F = 32 / BITS;
-    const int words = group / F;
-    uint32_t* out = codes32 + (static_cast<int64_t>(h) * (tokens / F) + static_cast<int64_t>(g) * words) * head_dim + d;
-    for (int w = 0; w < words; ++w) {
-      uint32_t word = 0;
+  scale[stat] = Dtype<T>::from_f(sca);
+  scale[stat + 1] = Dtype<T>::from_f(scb);
+  minimum[stat] = Dtype<T>::from_f(mna);
+  minimum[stat + 1] = Dtype<T>::from_f(mnb);
 #pragma unroll
-      for (int j = 0; j < F; ++j) {
-        word |= quant_code(ld(col + (w * F + j) * stride_t), mn, sc, kMax) << (j * BITS);
+  for (int c0 = 0; c0 < G; c0 += CH) {
+    if (G > CH) {
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        const V2 pr = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
+        a[i] = Dtype<T>::lo(pr);
+        b[i] = Dtype<T>::hi(pr);
       }
-      out[static_cast<int64_t>(w) * head_dim] = word;
+    }
+    if constexpr (BITS == 8) {
+      uint8_t* out = codes8 + (static_cast<int64_t>(h) * tokens + static_cast<int64_t>(g) * G + c0) * head_dim + d;
+#pragma unroll
+      for (int i = 0; i < CH; ++i)
+        *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) = static_cast<uint16_t>(
+            quant_code_fast(a[i], mna, sca, inva, kMax) | (quant_code_fast(b[i], mnb, scb, invb, kMax) << 8));
+    } else {
+      constexpr int F = 32 / BITS;
+      uint32_t* out = codes32 + (static_cast<int64_t>(h) * (tokens / F) + (static_cast<int64_t>(g) * G + c0) / F) *
+                                    head_dim + d;
+#pragma unroll
+      for (int w = 0; w < CH / F; ++w) {
+        uint32_t wa = 0, wb = 0;
+#pragma unroll
+        for (int j = 0; j < F; ++j) {
+          wa |= quant_code_fast(a[w * F + j], mna, sca, inva, kMax) << (j * BITS);
+          wb |= quant_code_fast(b[w * F + j], mnb, scb, invb, kMax) << (j * BITS);
+        }
+        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(w) * head_dim) = make_uint2(wa, wb);
+      }
     }
   }
 }
 
 // ---------------------------------------------------------------- value pack
-// One warp per (token, head) row of D channels; lane l holds VPL = D/32
-// consecutive channels.  A group of G channels spans G/VPL lanes.
-template <typename T, int BITS, int D, int G>
+// One thread per (token row, channel group): it reads the group's G channels
+// with 16-byte loads, reduces them locally and writes G*bits/32 words and its
+// two statistics.  Consecutive threads take consecutive groups of consecutive
+// rows, so a warp reads one contiguous span of the input.
+template <typename T, int BITS, int D, int G, bool VEC>
 __global__ void __launch_bounds__(256) pack_value_kernel(const T* __restrict__ x, int64_t stride_t,
                                                          int64_t stride_h, int tokens, int heads,
                                                          uint32_t* __restrict__ codes32,
                                                          uint8_t* __restrict__ codes8,
                                                          T* __restrict__ scale, T* __restrict__ minimum) {
-  constexpr int VPL = D / 32;
-  constexpr int LPG = G / VPL;  // lanes per group
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= static_cast<int64_t>(tokens) * heads) return;
+  constexpr int NG = D / G;                     // groups per row
+  constexpr int EPV = 16 / (int)sizeof(T);      // elements per 16-byte load
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n_items = static_cast<int64_t>(tokens) * heads * NG;
+  if (item >= n_items) return;
+  const int gi = static_cast<int>(item % NG);
+  const int64_t row = item / NG;
   const int t = static_cast<int>(row / heads), h = static_cast<int>(row % heads);
-  const T* src = x + t * stride_t + h * stride_h + lane * VPL;
-  float v[VPL];
+  const T* src = x + t * stride_t + h * stride_h + gi * G;
+  float v[G];
+  if constexpr (VEC) {  // 16-byte aligned rows
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) v[j] = ld(src + j);
+    for (int c = 0; c < G; c += EPV) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + c);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) v[c + j] = Dtype<T>::to_f(e[j]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < G; ++c) v[c] = ld(src + c);
+  }
   float mn = v[0], mx = v[0];
 #pragma unroll
-  for (int j = 1; j < VPL; ++j) {
+  for (int j = 1; j < G; ++j) {
     mn = fminf(mn, v[j]);
     mx = fmaxf(mx, v[j]);
   }
-#pragma unroll
-  for (int off = 1; off < LPG; off <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  }
   constexpr float kMax = static_cast<float>((1 << BITS) - 1);
   const float sc = quant_scale(mn, mx, kMax);
+  const float inv = __frcp_rn(sc);
   const int64_t out_row = static_cast<int64_t>(h) * tokens + t;
-  if (lane % LPG == 0) {
-    const int gd = lane / LPG;
-    scale[out_row * (D / G) + gd] = Dtype<T>::from_f(sc);
-    minimum[out_row * (D / G) + gd] = Dtype<T>::from_f(mn);
-  }
-  uint32_t code[VPL];
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) code[j] = quant_code(v[j], mn, sc, kMax);
+  scale[out_row * NG + gi] = Dtype<T>::from_f(sc);
+  minimum[out_row * NG + gi] = Dtype<T>::from_f(mn);
   if constexpr (BITS == 8) {
-    uint8_t* out = codes8 + out_row * D + lane * VPL;
+    uint8_t* out = codes8 + out_row * D + gi * G;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) out[j] = static_cast<uint8_t>(code[j]);
+    for (int c = 0; c < G; c += 16) {
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        w[q] = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[q] |= quant_code_fast(v[c + 4 * q + j], mn, sc, inv, kMax) << (8 * j);
+      }
+      *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   } else {
     constexpr int F = 32 / BITS;
-    constexpr int LPW = F / VPL;  // lanes per word
-    uint32_t word = 0;
+    constexpr int W = G / F;  // words per group: 2-bit 2/4/8, 4-bit 4/8/16
+    uint32_t w[W];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) word |= code[j] << (((lane * VPL + j) % F) * BITS);
+    for (int k = 0; k < W; ++k) {
+      w[k] = 0;
 #pragma unroll
-    for (int off = 1; off < LPW; off <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, off);
-    if (lane % LPW == 0) codes32[out_row * (D / F) + lane / LPW] = word;
+      for (int j = 0; j < F; ++j) w[k] |= quant_code_fast(v[k * F + j], mn, sc, inv, kMax) << (j * BITS);
+    }
+    uint32_t* out = codes32 + out_row * (D / F) + gi * W;
+#pragma unroll
+    for (int k = 0; k < W; k += 2) *reinterpret_cast<uint2*>(out + k) = make_uint2(w[k], w[k + 1]);
   }
 }
 
@@ -259,32 +322,43 @@ int launch_pack_key(const void* x, int64_t T_, int64_t H, int64_t D, int64_t st,
   auto* c8 = static_cast<uint8_t*>(codes);
   T* sp = static_cast<T*>(scale);
   T* mp = static_cast<T*>(minimum);
-  if (bits == 2)
-    ucb::pack_key_kernel<T, 2><<<grid, 128, 0, s>>>(xp, st, sh, (int)T_, (int)D, group, c32, c8, sp, mp);
-  else if (bits == 4)
-    ucb::pack_key_kernel<T, 4><<<grid, 128, 0, s>>>(xp, st, sh, (int)T_, (int)D, group, c32, c8, sp, mp);
-  else
-    ucb::pack_key_kernel<T, 8><<<grid, 128, 0, s>>>(xp, st, sh, (int)T_, (int)D, group, c32, c8, sp, mp);
-  return check_launch("pack_key_kernel");
+#define UCB_PACK_KEY(B_, G_) \
+  if (bits == B_ && group == G_) { \
+    ucb::pack_key_kernel<T, B_, G_><<<grid, (unsigned)(D / 2), 0, s>>>(xp, st, sh, (int)T_, (int)D, c32, c8, sp, mp); \
+    return check_launch("pack_key_kernel"); \
+  }
+  UCB_PACK_KEY(2, 32) UCB_PACK_KEY(2, 64) UCB_PACK_KEY(2, 128)
+  UCB_PACK_KEY(4, 32) UCB_PACK_KEY(4, 64) UCB_PACK_KEY(4, 128)
+  UCB_PACK_KEY(8, 32) UCB_PACK_KEY(8, 64) UCB_PACK_KEY(8, 128)
+#undef UCB_PACK_KEY
+  return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_key: unsupported (bits=%d, group=%d)", bits, group);
 }
 
 template <typename T, int BITS, int D>
 int launch_pack_value_g(const void* x, int64_t T_, int64_t H, int64_t st, int64_t sh, int group, void* codes,
                         void* scale, void* minimum, cudaStream_t s) {
-  const int64_t rows = T_ * H;
-  dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  const int64_t items = T_ * H * (D / group);  // one thread per (row, channel group)
+  dim3 grid(static_cast<unsigned>((items + 255) / 256));
   const T* xp = static_cast<const T*>(x);
   auto* c32 = static_cast<uint32_t*>(codes);
   auto* c8 = static_cast<uint8_t*>(codes);
   T* sp = static_cast<T*>(scale);
   T* mp = static_cast<T*>(minimum);
-  if (group == 32)
-    ucb::pack_value_kernel<T, BITS, D, 32><<<grid, 256, 0, s>>>(xp, st, sh, (int)T_, (int)H, c32, c8, sp, mp);
-  else if (group == 64)
-    ucb::pack_value_kernel<T, BITS, D, 64><<<grid, 256, 0, s>>>(xp, st, sh, (int)T_, (int)H, c32, c8, sp, mp);
-  else
-    ucb::pack_value_kernel<T, BITS, D, 128><<<grid, 256, 0, s>>>(xp, st, sh, (int)T_, (int)H, c32, c8, sp, mp);
-  return check_launch("pack_value_kernel");
+  constexpr int EPV = 16 / (int)sizeof(T);
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && st % EPV == 0 && sh % EPV == 0;
+#define UCB_PACK_VALUE(G_)                                                                                 \
+  if (group == G_) {                                                                                       \
+    if constexpr (G_ <= D) {                                                                               \
+      if (vec)                                                                                             \
+        ucb::pack_value_kernel<T, BITS, D, G_, true><<<grid, 256, 0, s>>>(xp, st, sh, (int)T_, (int)H, c32, c8, sp, mp); \
+      else                                                                                                 \
+        ucb::pack_value_kernel<T, BITS, D, G_, false><<<grid, 256, 0, s>>>(xp, st, sh, (int)T_, (int)H, c32, c8, sp, mp); \
+      return check_launch("pack_value_kernel");                                                            \
+    }                                                                                                      \
+  }
+  UCB_PACK_VALUE(32) UCB_PACK_VALUE(64) UCB_PACK_VALUE(128)
+#undef UCB_PACK_VALUE
+  return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_value: unsupported (head_dim=%d, group=%d)", D, group);
 }
 
 template <typename T, int D>
