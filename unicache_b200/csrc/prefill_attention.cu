@@ -11,22 +11,24 @@
 // q rows are the (query position, head-in-group) pairs of one KV head, so the
 // grouped-query structure becomes a plain M x N attention per KV head.
 //
-// Design (one CTA of 4 warps per 128 query rows of one KV head, two CTAs per
-// SM so that one CTA's softmax overlaps the other's tensor-core work):
-//  * Q (128 x 128 bf16), K tiles (64 tokens x 128) and V^T tiles (128 channels
-//    x 64 tokens) arrive by TMA with 128-byte swizzle, which is the canonical
-//    K-major operand layout of tcgen05.mma.  K and V^T tiles are double
-//    buffered and prefetched.
-//  * One thread issues S = Q K^T (eight K=16 steps) into tensor memory; each
-//    thread then owns one row of S (TMEM lane = row), so the row max and sum
-//    need no shuffles.  P = exp2(S*scale*log2e - m) is written in bf16 to
-//    shared memory in the same swizzled layout and O += P V^T runs on the
-//    tensor cores with the accumulator in tensor memory.
-//  * The running max is only moved (and O rescaled in TMEM) when a row's new
-//    maximum exceeds it by more than 8 (log2 units); otherwise P may exceed 1
-//    by up to 2^8, which bf16 and the fp32 accumulator absorb.
-//  * Every mbarrier wait is bounded; a timeout sets a device error flag, and
-//    the CTA still waits (bounded) for its tensor-core work and frees TMEM.
+// Design: one CTA per 256 query rows (two 128-row tiles A and B) of one KV
+// head, warp-specialised so that the tensor core works on one tile while the
+// other tile's softmax runs:
+//  * warp 8 (one lane) loads Q_A, Q_B once and streams K tiles (64 tokens x
+//    128 channels) and V^T tiles (128 channels x 64 tokens) by TMA with
+//    128-byte swizzle (the canonical K-major tcgen05 operand layout) through a
+//    three-stage ring of full/empty mbarriers;
+//  * warp 9 (one lane) issues tcgen05.mma (bf16 operands from shared-memory
+//    descriptors, fp32 accumulators in tensor memory): S_A = Q_A K^T,
+//    S_B = Q_B K^T, then O_A += P_A V^T and O_B += P_B V^T as the softmax
+//    warpgroups hand over P;
+//  * warps 0-3 (tile A) and 4-7 (tile B): each thread owns one query row
+//    (one TMEM lane), so the row max and sum need no shuffles.  P =
+//    exp2(S*scale*log2e - m) goes to shared memory in bf16 in the swizzled
+//    layout.  The running max only moves (and O is rescaled in TMEM) when a
+//    row's maximum grows by more than 8 (log2 units).
+//  * Every wait has a time budget; on expiry the CTA sets the device error
+//    word, drains its tensor-core work (bounded) and frees TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -36,25 +38,27 @@ namespace ucb {
 namespace prefill {
 
 constexpr int D = 128;
-constexpr int BM = 128;                   // query rows per CTA (TMEM lanes)
-constexpr int BN = 64;                    // key tokens per tile
+constexpr int BM = 128;                   // query rows per tile (TMEM lanes)
+constexpr int BN = 64;                    // key tokens per K/V tile
+constexpr int STAGES = 3;                 // K/V ring depth
 constexpr int QTILE = BM * D * 2;         // 32 KB: two 64-channel swizzled halves
 constexpr int QHALF = QTILE / 2;          // 16 KB
 constexpr int KTILE = BN * D * 2;         // 16 KB: two 64-channel halves of 64 rows
 constexpr int KHALF = KTILE / 2;          // 8 KB
 constexpr int VTILE = D * BN * 2;         // 16 KB: 128 channel rows x 64 tokens
 constexpr int PTILE = BM * BN * 2;        // 16 KB: 128 query rows x 64 tokens
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + QTILE;      // 2 buffers
-constexpr int OFF_V = OFF_K + 2 * KTILE;  // 2 buffers (V^T tiles)
-constexpr int OFF_P = OFF_V + 2 * VTILE;
-constexpr int OFF_BAR = OFF_P + PTILE;    // 8 mbarriers
-constexpr int OFF_TMEM = OFF_BAR + 8 * 8;
-constexpr int SMEM = OFF_TMEM + 16;       // two CTAs per SM
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int OFF_Q = 0;                  // Q_A, Q_B
+constexpr int OFF_K = OFF_Q + 2 * QTILE;
+constexpr int OFF_V = OFF_K + STAGES * KTILE;
+constexpr int OFF_P = OFF_V + STAGES * VTILE;  // P_A, P_B
+constexpr int OFF_BAR = OFF_P + 2 * PTILE;
+constexpr int NBAR = 1 + 4 * STAGES + 7;  // q_full, k/v full/empty, s_full[2], p_full[2], o_done[2], drain
+constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+constexpr int SMEM = OFF_TMEM + 16;
+constexpr int THREADS = 384;              // warps 0-7 softmax, 8 loader, 9 MMA, 10-11 idle
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
 constexpr float RESCALE_THRESHOLD = 8.f;  // log2 units
-constexpr uint32_t TMEM_COLS = 256;       // S: columns [0, 64), O: [64, 192)
-constexpr uint32_t COL_O = 64;
+constexpr uint32_t TMEM_COLS = 512;       // S_A [0,64) S_B [64,128) O_A [128,256) O_B [256,384)
 
 // tcgen05 instruction descriptors, kind::f16: F32 accumulator, BF16 A and B,
 // both K-major, M = 128; N = 64 for S = Q K^T and N = 128 for O += P V.
@@ -134,12 +138,12 @@ struct Params {
   unsigned int* err;
 };
 
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int head = blockIdx.y, m0 = blockIdx.x * BM;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int head = blockIdx.y, m0 = blockIdx.x * 2 * BM;
   const int n_tiles = (P.n_tokens + BN - 1) / BN;
   // The swizzled operand layout needs a 1024-byte aligned base.
   if (smem_u32(smem) & 1023) {
@@ -147,15 +151,33 @@ __global__ void __launch_bounds__(128, 2)
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* bar_q = bars + 0;
-  uint64_t* bar_k = bars + 1;  // [2]
-  uint64_t* bar_v = bars + 3;  // [2]
-  uint64_t* bar_s = bars + 5;
-  uint64_t* bar_o = bars + 6;
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + STAGES;
+  uint64_t* v_full = k_empty + STAGES;
+  uint64_t* v_empty = v_full + STAGES;
+  uint64_t* s_full = v_empty + STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* o_done = p_full + 2;        // [2]
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+  __shared__ int failed;
 
   if (tid == 0) {
-    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
+    failed = 0;
+    mbar_init(q_full, 1);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], BM);
+      mbar_init(&o_done[x], 1);
+    }
+    mbar_init(drain, 1);
     fence_mbarrier_init();
   }
   if (warp == 0) {
@@ -168,160 +190,206 @@ __global__ void __launch_bounds__(128, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + COL_O;
-  const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+  auto fail = [&]() { atomicOr(&failed, 1); };
 
-  auto load_k = [&](int j) {
-    uint64_t* bar = &bar_k[j & 1];
-    mbar_arrive_expect_tx(bar, KTILE);
-    unsigned char* dst = smem + OFF_K + (j & 1) * KTILE;
-    tma_load_3d(dst, &tm_k, 0, j * BN, head, bar);
-    tma_load_3d(dst + KHALF, &tm_k, 64, j * BN, head, bar);
-  };
-  auto load_v = [&](int j) {
-    uint64_t* bar = &bar_v[j & 1];
-    mbar_arrive_expect_tx(bar, VTILE);
-    tma_load_3d(smem + OFF_V + (j & 1) * VTILE, &tm_v, j * BN, 0, head, bar);
-  };
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_q, QTILE);
-    tma_load_3d(smem + OFF_Q, &tm_q, 0, m0, head, bar_q);
-    tma_load_3d(smem + OFF_Q + QHALF, &tm_q, 64, m0, head, bar_q);
-    load_k(0);
-    if (n_tiles > 1) load_k(1);
-    load_v(0);
-  }
-
-  const uint32_t q_addr = smem_u32(smem + OFF_Q), p_addr = smem_u32(smem + OFF_P);
-  const int row = tid;  // TMEM lane and query row within the tile
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;
-  for (int j = 0; j < n_tiles; ++j) {
-    const int b = j & 1;
-    if (tid == 0 && ok) {
-      if (j == 0) ok = mbar_wait_bounded(bar_q, 0, WAIT_LIMIT);
-      ok = ok && mbar_wait_bounded(&bar_k[b], (j >> 1) & 1, WAIT_LIMIT);
+  if (warp == 8) {
+    // ---------------- loader
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * QTILE);
+      for (int x = 0; x < 2; ++x) {
+        tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
+        tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++j) {
+        const int st = j % STAGES;
+        const uint32_t ph = ((j / STAGES) - 1) & 1;
+        if (j >= STAGES && (!mbar_wait_for(&k_empty[st], ph, WAIT_NS) || !mbar_wait_for(&v_empty[st], ph, WAIT_NS))) {
+          fail();
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], KTILE);
+        tma_load_3d(smem + OFF_K + st * KTILE, &tm_k, 0, j * BN, head, &k_full[st]);
+        tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, j * BN, head, &k_full[st]);
+        mbar_arrive_expect_tx(&v_full[st], VTILE);
+        tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, j * BN, 0, head, &v_full[st]);
+        issued = j + 1;
+      }
+      // Copies still in flight must land before the shared memory is released.
+      mbar_wait_for(q_full, 0, WAIT_NS);
+      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j) {
+        mbar_wait_for(&k_full[j % STAGES], (j / STAGES) & 1, WAIT_NS);
+        mbar_wait_for(&v_full[j % STAGES], (j / STAGES) & 1, WAIT_NS);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer.  Order on the tensor core: S_A(0) S_B(0) |
+    // PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ..., so that while one tile's
+    // softmax runs the other tile's products are in flight.
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(smem + OFF_Q), p_addr = smem_u32(smem + OFF_P);
+      auto issue_s = [&](int j, int x) {
+        const uint32_t k_addr = smem_u32(smem + OFF_K + (j % STAGES) * KTILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t col = (kk & 3) * 32;
+          tc_mma(tmem + 64 * x, sw128_desc(q_addr + x * QTILE + (kk >> 2) * QHALF + col),
+                 sw128_desc(k_addr + (kk >> 2) * KHALF + col), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int j, int x) {
+        const uint32_t v_addr = smem_u32(smem + OFF_V + (j % STAGES) * VTILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma(tmem + 128 + 128 * x, sw128_desc(p_addr + x * PTILE + kk * 32), sw128_desc(v_addr + kk * 32),
+                 IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[x]);
+      };
+      bool ok = mbar_wait_for(q_full, 0, WAIT_NS) && mbar_wait_for(&k_full[0], 0, WAIT_NS);
       if (ok) {
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + OFF_K + b * KTILE);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {  // 8 steps over the channels
-          const uint32_t col = (kk & 3) * 32;
-          tc_mma(t_s, sw128_desc(q_addr + (kk >> 2) * QHALF + col), sw128_desc(k_addr + (kk >> 2) * KHALF + col),
-                 IDESC_S, kk > 0 ? 1u : 0u);
+        issue_s(0, 0);
+        issue_s(0, 1);
+        tc_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % STAGES, st1 = (j + 1) % STAGES;
+        const bool more = j + 1 < n_tiles;
+        ok = mbar_wait_for(&v_full[st], (j / STAGES) & 1, WAIT_NS) && mbar_wait_for(&p_full[0], j & 1, WAIT_NS);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(j, 0);
+        if (more) {
+          ok = mbar_wait_for(&k_full[st1], ((j + 1) / STAGES) & 1, WAIT_NS);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(j + 1, 0);
+        }
+        ok = mbar_wait_for(&p_full[1], j & 1, WAIT_NS);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(j, 1);
+        tc_commit(&v_empty[st]);
+        if (more) {
+          issue_s(j + 1, 1);
+          tc_commit(&k_empty[st1]);
         }
       }
-      tc_commit(bar_s);  // arrives once every earlier tcgen05.mma of this thread is done
+      if (!ok) fail();
+      // Everything issued has finished before TMEM can be released.
+      tc_commit(drain);
+      mbar_wait_for(drain, 0, WAIT_NS);
     }
-    ok = mbar_wait_bounded(bar_s, j & 1, WAIT_LIMIT) && ok;
-    tc_fence_after();
-    // S_j and O += P_{j-1} V_{j-1} are complete: K buffer b and V buffer b^1 are free.
-    if (tid == 0 && ok) {
-      if (j + 2 < n_tiles) load_k(j + 2);
-      if (j + 1 < n_tiles) load_v(j + 1);
-    }
-
-    // ---- softmax on this thread's row (64 columns)
-    uint32_t sv[2][32];
-    tc_ld32(t_s + lane_off, sv[0]);
-    tc_ld32(t_s + lane_off + 32, sv[1]);
-    tc_wait_ld();
-    const int valid = min(BN, P.n_tokens - j * BN);
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (32 * c + i < valid) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
-    mx *= P.scale_log2;
-    const bool move = mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
-    if (__any_sync(0xffffffffu, move)) {
-      const float m_new = move ? fmaxf(mx, m_run) : m_run;
-      const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
-      if (j > 0) {  // O holds the sum of earlier tiles: rescale this row in TMEM
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc_ld32(t_o + lane_off + 32 * c, ov);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tc_st32(t_o + lane_off + 32 * c, ov);
-        }
-        tc_wait_st();
-      }
-      l_run *= alpha;
-      m_run = m_new;
-    }
-    float sum = 0.f;
-    unsigned char* prow = smem + OFF_P + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // 8 tokens = one 16-byte chunk
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t0 = 32 * c + 8 * q + 2 * e;
-          const float p0 = t0 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, -m_run)) : 0.f;
-          const float p1 =
-              t0 + 1 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, -m_run)) : 0.f;
-          const uint32_t pk = pack_bf16x2(p0, p1);
-          sum += bf16lo(pk) + bf16hi(pk);  // the sum sees the rounded weights the MMA uses
-          w[e] = pk;
-        }
-        const int chunk = 4 * c + q;  // 0..7 over the 64 tokens
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-    l_run += sum;
-    fence_proxy_async_smem();  // P (generic stores) -> tensor-core reads (async proxy)
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && ok) {
+  } else if (warp < 8) {
+    // ---------------- softmax warpgroups
+    const int x = warp >> 2;             // tile
+    const int row = tid & (BM - 1);      // query row in the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t t_s = tmem + 64 * x + lane_off, t_o = tmem + 128 + 128 * x + lane_off;
+    unsigned char* prow = smem + OFF_P + x * PTILE + (row >> 3) * 1024 + (row & 7) * 128;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      ok = mbar_wait_for(&s_full[x], j & 1, WAIT_NS);
+      if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      ok = mbar_wait_bounded(&bar_v[b], (j >> 1) & 1, WAIT_LIMIT);
-      if (ok) {
-        const uint32_t v_addr = smem_u32(smem + OFF_V + b * VTILE);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)  // 4 steps over the tokens
-          tc_mma(t_o, sw128_desc(p_addr + kk * 32), sw128_desc(v_addr + kk * 32), IDESC_O,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-      }
-    }
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-  }
-  if (tid == 0) tc_commit(bar_o);
-  const bool done = mbar_wait_bounded(bar_o, 0, WAIT_LIMIT);
-  tc_fence_after();
-  if (ok && done && n_tiles > 0) {
-    const float inv = 1.f / l_run;
-    const int m = m0 + row;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t ov[32];
-      tc_ld32(t_o + lane_off + 32 * c, ov);
+      uint32_t sv[2][32];
+      tc_ld32(t_s, sv[0]);
+      tc_ld32(t_s + 32, sv[1]);
       tc_wait_ld();
-      if (m < P.m_rows) {
-        __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
+      const int valid = min(BN, P.n_tokens - j * BN);
+      float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
-          v.y = pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
-          v.z = pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
-          v.w = pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
-          *reinterpret_cast<uint4*>(dst + i) = v;
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c + i < valid) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+      mx *= P.scale_log2;
+      // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
+      if (j > 0) {
+        ok = mbar_wait_for(&o_done[x], (j - 1) & 1, WAIT_NS);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+      }
+      const bool move = mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
+      if (__any_sync(0xffffffffu, move)) {
+        const float m_new = move ? fmaxf(mx, m_run) : m_run;
+        const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+        if (j > 0) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            tc_ld32(t_o + 32 * c, ov);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tc_st32(t_o + 32 * c, ov);
+          }
+          tc_wait_st();
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t0 = 32 * c + 8 * q + 2 * e;
+            const float p0 =
+                t0 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, -m_run)) : 0.f;
+            const float p1 = t0 + 1 < valid
+                                 ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, -m_run))
+                                 : 0.f;
+            const uint32_t pk = pack_bf16x2(p0, p1);
+            sum += bf16lo(pk) + bf16hi(pk);  // the sum sees the rounded weights the MMA uses
+            w[e] = pk;
+          }
+          const int chunk = 4 * c + q;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      l_run += sum;
+      fence_proxy_async_smem();  // P (generic stores) -> tensor-core reads (async proxy)
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
     }
-    if (m < P.m_rows && P.lse) P.lse[(int64_t)head * P.m_rows + m] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
-  } else if (tid == 0) {
-    atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
+    if (ok && n_tiles > 0) ok = mbar_wait_for(&o_done[x], (n_tiles - 1) & 1, WAIT_NS);
+    tc_fence_after();
+    if (__all_sync(0xffffffffu, ok)) {
+      const float inv = 1.f / l_run;
+      const int m = m0 + x * BM + row;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ov[32];
+        tc_ld32(t_o + 32 * c, ov);
+        tc_wait_ld();
+        if (m < P.m_rows) {
+          __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + i) = v;
+          }
+        }
+      }
+      if (m < P.m_rows && P.lse)
+        P.lse[(int64_t)head * P.m_rows + m] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
+    } else if (lane == 0) {
+      fail();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (failed && tid == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
@@ -392,7 +460,7 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   P.err = err;
-  const dim3 grid((m_rows + BM - 1) / BM, heads);
-  prefill_kernel<<<grid, 128, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
+  const dim3 grid((m_rows + 2 * BM - 1) / (2 * BM), heads);
+  prefill_kernel<<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
   return ucb_host::check_launch("prefill_kernel");
 }
