@@ -25,7 +25,8 @@
 //  * warps 0-3 (tile A) and 4-7 (tile B): each thread owns one query row
 //    (one TMEM lane), so the row max and sum need no shuffles.  P =
 //    exp2(S*scale*log2e - m) goes to shared memory in bf16 in the swizzled
-//    layout.  The running max only moves (and O is rescaled in TMEM) when a
+//    layout; the row sum accumulates the fp32 weights, as FlashAttention's
+//    does.  The running max only moves (and O is rescaled in TMEM) when a
 //    row's maximum grows by more than 8 (log2 units).
 //  * Every wait has a time budget; on expiry the CTA sets the device error
 //    word, drains its tensor-core work (bounded) and frees TMEM.
@@ -299,13 +300,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_ld32(t_s + 32, sv[1]);
       tc_wait_ld();
       const int valid = min(BN, P.n_tokens - j * BN);
-      float mx = -INFINITY;
+      if (valid < BN) {  // ragged last tile: masked columns never win the max and get weight 0
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i < valid) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
-      mx *= P.scale_log2;
+          for (int i = 0; i < 32; ++i)
+            if (32 * c + i >= valid) sv[c][i] = __float_as_uint(-INFINITY);
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        mx0 = fmaxf(mx0, fmaxf(__uint_as_float(sv[0][i]), __uint_as_float(sv[0][i + 1])));
+        mx1 = fmaxf(mx1, fmaxf(__uint_as_float(sv[1][i]), __uint_as_float(sv[1][i + 1])));
+      }
+      const float mx = fmaxf(mx0, mx1) * P.scale_log2;
       // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
       if (j > 0) {
         ok = mbar_wait_for(&o_done[x], (j - 1) & 1, WAIT_NS);
@@ -331,7 +339,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         l_run *= alpha;
         m_run = m_new;
       }
-      float sum = 0.f;
+      const float neg_m = -m_run;
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -339,20 +348,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int t0 = 32 * c + 8 * q + 2 * e;
-            const float p0 =
-                t0 < valid ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, -m_run)) : 0.f;
-            const float p1 = t0 + 1 < valid
-                                 ? fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, -m_run))
-                                 : 0.f;
-            const uint32_t pk = pack_bf16x2(p0, p1);
-            sum += bf16lo(pk) + bf16hi(pk);  // the sum sees the rounded weights the MMA uses
-            w[e] = pk;
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, neg_m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, neg_m));
+            sum0 += p0;
+            sum1 += p1;
+            w[e] = pack_bf16x2(p0, p1);
           }
           const int chunk = 4 * c + q;
           *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      const float sum = sum0 + sum1;
       l_run += sum;
       fence_proxy_async_smem();  // P (generic stores) -> tensor-core reads (async proxy)
       tc_fence_before();
