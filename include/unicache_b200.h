@@ -302,6 +302,20 @@ UCB_API int ucb_compact_rows(const void* src_dev, int64_t row_bytes, const uint8
  * *max_abs_err receives the largest deviation from an fp32 reference. */
 UCB_API int ucb_selftest_mma_subnormal(float* max_abs_err, void* stream);
 
+/* ------------------------------------------------------------------ host transfers
+ * No counterpart in the reference (its engine copies with torch).  Per-step
+ * host <-> device transfers of small buffers (a decode query, its output and
+ * LSE) done by a kernel over mapped pinned host memory instead of a DMA copy.
+ * ucb_host_device_pointer: device-visible address of pinned host memory
+ * (cudaHostGetDevicePointer); UCB_ERR_INVALID when the memory is not mapped.
+ * ucb_copy_ranges: one kernel copies n (1..8) ranges, bytes[i] from src[i]
+ * to dst[i], all device-visible (device memory or such mapped host
+ * addresses) and 16-byte aligned, on `stream`; the pointer and size arrays
+ * are host arrays. */
+UCB_API int ucb_host_device_pointer(const void* host, void** dev);
+UCB_API int ucb_copy_ranges(int n, void* const* dst_dev, const void* const* src_dev, const int64_t* bytes,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -207,3 +207,30 @@ def test_decode_rejects_cpu_and_bad_query():
         batch(torch.zeros(2, 28, 128, dtype=torch.bfloat16, device="cuda"))
     with pytest.raises(ValueError):
         batch(torch.zeros(1, 28, 128, dtype=torch.float32, device="cuda"))
+
+
+def test_decode_step_graph_matches_eager_calls_with_host_buffers():
+    """DecodeStepGraph: per-step host->device query copy, decode, merge and
+    device->host output/LSE copy replayed as one CUDA graph."""
+    need_gpu()
+    from unicache_b200 import DecodeStepGraph
+
+    seqs = []
+    for b in range(3):
+        cache, _ = _packed(640 + 64 * b, 32, 2, 2, 32, seed=300 + b)
+        seqs.append([cache])
+    batch = PhysicalDecodeBatch(seqs, num_kv_heads=4)
+    host_q = torch.empty(3, 28, 128, dtype=torch.bfloat16).pin_memory()
+    host_o = torch.empty(3, 28, 128, dtype=torch.bfloat16).pin_memory()
+    host_l = torch.empty(3, 28, dtype=torch.float32).pin_memory()
+    step = DecodeStepGraph(batch, host_q, host_o, host_l)
+    for seed in (11, 12):
+        q = make_query(3, 28, 128, seed=seed)
+        host_q.copy_(q)
+        step()
+        torch.cuda.synchronize()
+        ref_o, ref_l = batch(q.cuda())
+        torch.cuda.synchronize()
+        assert torch.equal(host_o, ref_o.cpu()) and torch.equal(host_l, ref_l.cpu())
+    with pytest.raises(ValueError):
+        DecodeStepGraph(batch, torch.empty(3, 28, 128, dtype=torch.bfloat16), host_o, host_l)

@@ -7,6 +7,7 @@ reference's storage / operator API on top.
 """
 
 from .adapters import (
+    DecodeStepGraph,
     PhysicalDecodeBatch,
     fused_h2o_decode,
     fused_mixed_decode,

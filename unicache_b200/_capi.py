@@ -113,6 +113,9 @@ SIGNATURES = {
     "ucb_compact_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  ctypes.POINTER(c_int64), c_void_p]),
     "ucb_selftest_mma_subnormal": (c_int, [ctypes.POINTER(c_float), c_void_p]),
+    "ucb_host_device_pointer": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "ucb_copy_ranges": (c_int, [c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64),
+                                c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -1,6 +1,7 @@
 """Attention fast paths over physical segments (counterpart of unicache/adapters)."""
 
 from .attention import (
+    DecodeStepGraph,
     PhysicalDecodeBatch,
     fused_h2o_decode,
     fused_mixed_decode,
@@ -9,6 +10,7 @@ from .attention import (
 )
 
 __all__ = [
+    "DecodeStepGraph",
     "PhysicalDecodeBatch",
     "fused_h2o_decode",
     "fused_mixed_decode",

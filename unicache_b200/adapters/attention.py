@@ -11,6 +11,8 @@ unicache/adapters/bagel.py):
 * ``PhysicalDecodeBatch``         batched decode over many sequences (the
                                   shape of ``apply_static_physical_attention_batch``,
                                   bagel.py:773-980, for decoding)
+* ``DecodeStepGraph``             one such decode step with its host transfers
+                                  captured as a CUDA graph
 * ``long_query_attention_summary`` multi-query attention over the same
                                   segments (bagel.py:1598-1858 with q_len > 1)
 """
@@ -59,6 +61,52 @@ class PhysicalDecodeBatch:
         """query [B, Hq, D] bf16 -> (out [B, Hq, D] bf16, lse [B, Hq] fp32 natural log)."""
 
         return self.plan.run(query, out=out, lse=lse)
+
+
+class DecodeStepGraph:
+    """One decode step of a ``PhysicalDecodeBatch`` with its host transfers,
+    captured as a CUDA graph: every replay reads the query from
+    ``host_query``, decodes, and writes the output and LSE to ``host_out`` /
+    ``host_lse`` (all three pinned host tensors).  The transfers ride inside
+    the two kernels over the mapped pinned buffers.  The decode kernel loads
+    the query rows across PCIe, and the state merge stores the results
+    across PCIe.  So one step is one graph of two kernels instead of five
+    operations.  Capture once, then call it every step after writing the
+    next query into ``host_query``.  The call is asynchronous on the current
+    stream: synchronize before reading the host outputs."""
+
+    def __init__(self, batch: PhysicalDecodeBatch, host_query: torch.Tensor, host_out: torch.Tensor,
+                 host_lse: torch.Tensor):
+        for name, t in (("host_query", host_query), ("host_out", host_out), ("host_lse", host_lse)):
+            if t.is_cuda or not t.is_pinned() or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous pinned host tensor")
+        plan = batch.plan
+        b, hq, d = map(int, host_query.shape)
+        if host_query.dtype != torch.bfloat16 or host_out.dtype != torch.bfloat16 or host_lse.dtype != torch.float32:
+            raise ValueError("host_query/host_out must be bfloat16 and host_lse float32")
+        if (b, d) != (plan.num_seqs, plan.head_dim) or tuple(host_out.shape) != (b, hq, d) or \
+                tuple(host_lse.shape) != (b, hq):
+            raise ValueError("host buffers must be [B, Hq, D], [B, Hq, D] and [B, Hq] for this batch")
+        self.host_query, self.host_out, self.host_lse = host_query, host_out, host_lse
+        q_ptr = kernels.host_device_pointer(host_query)
+        o_ptr = kernels.host_device_pointer(host_out)
+        l_ptr = kernels.host_device_pointer(host_lse)
+        device = plan.device
+        stream = torch.cuda.Stream(device=device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        launch = lambda: plan.launch(q_ptr, hq * d, hq, o_ptr, hq * d, l_ptr, stream.cuda_stream)
+        launch()  # first-call set-up outside the capture
+        stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(self.graph, stream=stream):
+                launch()
+        torch.cuda.current_stream(device).wait_stream(stream)
+        self.h2d_bytes = host_query.numel() * host_query.element_size()
+        self.d2h_bytes = host_out.numel() * host_out.element_size() + host_lse.numel() * host_lse.element_size()
+
+    def __call__(self) -> None:
+        self.graph.replay()
 
 
 def _single_sequence_decode(query, segments, num_kv_heads, head_dim, owner=None, key=None):

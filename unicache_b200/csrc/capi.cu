@@ -124,3 +124,63 @@ extern "C" int ucb_selftest_mma_subnormal(float* max_abs_err, void* stream) {
   if (max_abs_err) *max_abs_err = h;
   return rc;
 }
+
+// ---------------------------------------------------------------- host transfers
+namespace {
+constexpr int MAX_RANGES = 8;
+struct CopyRanges {
+  unsigned char* dst[MAX_RANGES];
+  const unsigned char* src[MAX_RANGES];
+  int64_t bytes[MAX_RANGES];
+  int n;
+};
+
+// Grid-stride copy in 16-byte chunks of every range, then the tail bytes.
+// Either side may be device memory or pinned host memory mapped into the
+// device address space.
+__global__ void copy_ranges_kernel(const CopyRanges R) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int r = 0; r < R.n; ++r) {
+    const int64_t n16 = R.bytes[r] / 16;
+    for (int64_t i = first; i < n16; i += stride)
+      reinterpret_cast<uint4*>(R.dst[r])[i] = reinterpret_cast<const uint4*>(R.src[r])[i];
+    const int64_t tail = R.bytes[r] - n16 * 16;
+    if (first < tail) R.dst[r][n16 * 16 + first] = R.src[r][n16 * 16 + first];
+  }
+}
+}  // namespace
+
+extern "C" int ucb_host_device_pointer(const void* host, void** dev) {
+  if (!host || !dev) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_host_device_pointer: null pointer");
+  void* d = nullptr;
+  const cudaError_t e = cudaHostGetDevicePointer(&d, const_cast<void*>(host), 0);
+  if (e != cudaSuccess || d == nullptr) {
+    cudaGetLastError();  // clear the (non-sticky) error the failed query left behind
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_host_device_pointer: memory is not mapped pinned host memory (%s)",
+                               cudaGetErrorString(e));
+  }
+  *dev = d;
+  return UCB_OK;
+}
+
+extern "C" int ucb_copy_ranges(int n, void* const* dst, const void* const* src, const int64_t* bytes, void* stream) {
+  if (n < 1 || n > MAX_RANGES || !dst || !src || !bytes)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_copy_ranges: need 1..%d ranges", MAX_RANGES);
+  CopyRanges R;
+  R.n = n;
+  int64_t most = 0;
+  for (int r = 0; r < n; ++r) {
+    if (!dst[r] || !src[r] || bytes[r] < 0) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_copy_ranges: bad range %d", r);
+    if ((reinterpret_cast<uintptr_t>(dst[r]) | reinterpret_cast<uintptr_t>(src[r])) & 15)
+      return ucb_host::set_error(UCB_ERR_INVALID, "ucb_copy_ranges: range %d is not 16-byte aligned", r);
+    R.dst[r] = static_cast<unsigned char*>(dst[r]);
+    R.src[r] = static_cast<const unsigned char*>(src[r]);
+    R.bytes[r] = bytes[r];
+    most = bytes[r] > most ? bytes[r] : most;
+  }
+  const int64_t chunks = (most + 15) / 16;
+  const int blocks = (int)((chunks + 255) / 256 < 148 ? (chunks + 255) / 256 : 148);
+  copy_ranges_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(R);
+  return ucb_host::check_launch("copy_ranges_kernel");
+}

@@ -292,6 +292,19 @@ class DecodePlan:
     keepalive: list = field(default_factory=list)
     bytes_per_step: int = 0
 
+    def launch(self, query_ptr: int, query_stride: int, q_heads: int, out_ptr: int, out_stride: int, lse_ptr: int,
+               stream: int, softmax_scale: float | None = None) -> None:
+        """Launch on raw device-visible addresses (device memory or mapped
+        pinned host memory): query rows [B, q_heads, D] bf16 with row stride
+        ``query_stride`` elements, out likewise, lse fp32 [B, q_heads] or 0."""
+
+        scale = (1.0 / math.sqrt(self.head_dim)) if softmax_scale is None else float(softmax_scale)
+        call("ucb_decode_attention", query_ptr, query_stride, q_heads, self.num_kv_heads, self.head_dim,
+             self.spans.data_ptr(), self.num_spans, self.ctas.data_ptr(), self.num_ctas, self.warp_bounds.data_ptr(),
+             self.pairs.data_ptr(), self.num_pairs, self.k_bits, self.v_bits, self.group_size, _capi.UCB_BF16,
+             scale, self.partials.data_ptr(), self.warp_slots.data_ptr(), out_ptr, out_stride, lse_ptr or None,
+             stream)
+
     def run(self, query: torch.Tensor, *, softmax_scale: float | None = None, out: torch.Tensor | None = None,
             lse: torch.Tensor | None = None):
         """query [B, Hq, D] bf16 -> (out [B, Hq, D] bf16, lse [B, Hq] fp32)."""
@@ -660,6 +673,28 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, n_toke
     call("ucb_prefill_attention", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, int(n_tokens),
          n_padded, scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
     return out, lse
+
+
+# ---------------------------------------------------------------- host transfers
+def host_device_pointer(host: torch.Tensor) -> int:
+    """Device-visible address of a pinned host tensor (mapped pinned memory)."""
+
+    if host.is_cuda or not host.is_pinned():
+        raise ValueError("expected a pinned host tensor")
+    dev = ctypes.c_void_p()
+    call("ucb_host_device_pointer", host.data_ptr(), ctypes.byref(dev))
+    return int(dev.value)
+
+
+def copy_ranges(ranges: list[tuple[int, int, int]], stream: int) -> None:
+    """One kernel copies every (dst, src, nbytes) range between device-visible
+    addresses (device memory or mapped pinned host memory), 16-byte aligned."""
+
+    n = len(ranges)
+    dst = (ctypes.c_void_p * n)(*[r[0] for r in ranges])
+    src = (ctypes.c_void_p * n)(*[r[1] for r in ranges])
+    size = (ctypes.c_int64 * n)(*[int(r[2]) for r in ranges])
+    call("ucb_copy_ranges", n, dst, src, size, stream)
 
 
 def device_status(device: torch.device | None = None) -> int:
