@@ -197,6 +197,33 @@ def test_full_size_config2_batch_decode():
     assert kernels.device_status() == 0
 
 
+def test_full_size_config3_per_gpu_batch_decode():
+    """Config 3 per GPU (batch 64 over 8 GPUs): 8 sequences x (32768 packed
+    4-bit G64 + 128 bf16 residual), 28/4 heads; sequences 0, 3 and 7 are
+    checked against the oracle (the packing of all eight is checked against
+    the oracle for sequence 0 bit for bit)."""
+
+    need_gpu()
+    caches, refs = [], []
+    for b in range(8):
+        c, r = _packed(32768 + 128, 128, 4, 4, 64, seed=2000 + b)
+        caches.append([c])
+        refs.append(r)
+    layout = caches[0][0].reference_layout()
+    assert np.array_equal(host(layout["key_code"]), refs[0]["key_code"])
+    assert np.array_equal(host(layout["value_code"]), refs[0]["value_code"])
+    batch = PhysicalDecodeBatch(caches, num_kv_heads=4)
+    queries = make_query(8, 28, 128, seed=98, device="cuda")
+    out, lse = batch(queries)
+    qh = host(queries)
+    for b in (0, 3, 7):
+        rk, rv = kivi.packed_dequantize(refs[b])
+        eo, el = _oracle_decode(qh[b], [rk], [rv])
+        assert_attention_close(out[b], eo, what=f"seq{b}")
+        assert np.abs(host(lse)[b] - el).max() < LSE_ABS
+    assert kernels.device_status() == 0
+
+
 def test_decode_rejects_cpu_and_bad_query():
     need_gpu()
     cache, _ = _packed(256, 0, 2, 2, 32, seed=1)
