@@ -240,13 +240,6 @@ UCB_API int ucb_lse_merge(int n, const void* const* out_ptrs, const float* const
                   int64_t rows, int64_t heads, int64_t head_dim, void* out_dev, float* lse_out_dev,
                   void* stream);
 
-/* Merge per-rank decode partials gathered from several GPUs (sequence split):
- * partials_dev holds n_parts blocks of ucb_decode_partial_bytes(head_dim) bytes per
- * (pair); layout [part][pair].  Writes out/lse like ucb_decode_attention. */
-UCB_API int ucb_merge_partials(const void* partials_dev, int n_parts, const ucb_decode_pair* pairs_dev,
-                       int num_pairs, int num_q_heads, int num_kv_heads, int head_dim, void* out_dev,
-                       int64_t out_stride, float* lse_dev, void* stream);
-
 /* ------------------------------------------------------------------ H2O
  * Per-KV-head heavy-hitter selection (GQAH2OCache.from_dense / trim,
  * unicache/storage/physical.py:508-532 and :624-649): for each of `heads` rows

@@ -101,8 +101,6 @@ SIGNATURES = {
                                       c_void_p, c_void_p]),
     "ucb_lse_merge": (c_int, [c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int, c_int64, c_int64,
                               c_int64, c_void_p, c_void_p, c_void_p]),
-    "ucb_merge_partials": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,
-                                   c_void_p, c_void_p]),
     "ucb_h2o_select": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "ucb_gather_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_int, c_int64, c_void_p,
                                 c_void_p]),

@@ -823,29 +823,6 @@ struct SlotsFn {
   static int call(int* out, int* warps) { return slots<KB, VB, G, ST>(out, warps); }
 };
 
-// ---------------------------------------------------------------- partial merge (cross-GPU)
-// Merge n_parts partial blocks per pair (layout [part][pair]) into the output.
-__global__ void merge_partials_kernel(const float* __restrict__ parts, int n_parts, const ucb_decode_pair* pairs,
-                                      int num_pairs, int grp, int num_kv_heads, __nv_bfloat16* out,
-                                      int64_t out_stride, float* lse) {
-  const int pidx = blockIdx.x, tid = threadIdx.x;
-  const ucb_decode_pair pair = pairs[pidx];
-  for (int h = 0; h < grp; ++h) {
-    float M = -INFINITY;
-    for (int p = 0; p < n_parts; ++p) M = fmaxf(M, parts[((int64_t)p * num_pairs + pidx) * PARTIAL_FLOATS + h]);
-    float acc = 0.f, lsum = 0.f;
-    for (int p = 0; p < n_parts; ++p) {
-      const float* pp = parts + ((int64_t)p * num_pairs + pidx) * PARTIAL_FLOATS;
-      if (pp[h] == -INFINITY) continue;
-      const float f = fast_exp2(pp[h] - M);
-      acc = fmaf(f, pp[16 + h * D + tid], acc);
-      lsum = fmaf(f, pp[8 + h], lsum);
-    }
-    const int qh = pair.kv_head * grp + h;
-    out[pair.seq * out_stride + (int64_t)qh * D + tid] = __float2bfloat16_rn(acc / lsum);
-    if (tid == 0 && lse != nullptr) lse[(int64_t)pair.seq * (grp * num_kv_heads) + qh] = (M + __log2f(lsum)) * LN2;
-  }
-}
 
 }  // namespace decode
 }  // namespace ucb
@@ -974,16 +951,3 @@ extern "C" int ucb_decode_attention_noalloc(const void* query, int64_t query_str
                               softmax_scale, scratch, warp_slots, out, out_stride, lse, stream);
 }
 
-extern "C" int ucb_merge_partials(const void* partials, int n_parts, const ucb_decode_pair* pairs, int num_pairs,
-                                  int num_q_heads, int num_kv_heads, int head_dim, void* out, int64_t out_stride,
-                                  float* lse, void* stream) {
-  if (!partials || !pairs || !out || n_parts <= 0 || num_pairs <= 0)
-    return set_error(UCB_ERR_INVALID, "ucb_merge_partials: bad arguments");
-  if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_merge_partials: head_dim must be 128");
-  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > 8)
-    return set_error(UCB_ERR_UNSUPPORTED, "ucb_merge_partials: need q_heads/kv_heads in [1, 8]");
-  ucb::decode::merge_partials_kernel<<<num_pairs, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const float*>(partials), n_parts, pairs, num_pairs, num_q_heads / num_kv_heads, num_kv_heads,
-      static_cast<__nv_bfloat16*>(out), out_stride, lse);
-  return ucb_host::check_launch("merge_partials_kernel");
-}
