@@ -230,6 +230,25 @@ UCB_API int ucb_prefill_attention(const void* q_dev, const void* k_dev, const vo
                                   int n_tokens, int n_padded, float softmax_scale, void* out_dev, float* lse_dev,
                                   void* stream);
 
+/* Batched variant: one launch over several problems (samples) that share the
+ * tensors q_dev [heads, m_rows, 128], k_dev [heads, n_padded, 128],
+ * vt_dev [heads, 128, n_padded], out_dev, lse_dev.  items_dev: device array of
+ * num_items ucb_prefill_item records, one per CTA; CTA i computes query rows
+ * [q_row0, q_row0 + q_rows) (q_rows <= 256) of KV head `head` against keys
+ * [k_row0, k_row0 + n_tokens) of that head.  k_row0 must be a multiple of 64
+ * and key rows k_row0 + n_tokens .. k_row0 + 64*ceil(n_tokens/64) - 1 must
+ * exist and be finite (zeros); query rows q_row0 .. q_row0 + 255 must exist.
+ * Replaces the single flash_attn_varlen_func(causal=False) call of
+ * apply_static_physical_attention_batch (unicache/adapters/bagel.py:773-980)
+ * for query blocks. */
+typedef struct ucb_prefill_item {
+  int32_t head, q_row0, q_rows, k_row0, n_tokens, reserved[3];
+} ucb_prefill_item;
+
+UCB_API int ucb_prefill_attention_batched(const void* q_dev, const void* k_dev, const void* vt_dev, int heads,
+                                          int m_rows, int n_padded, const void* items_dev, int num_items,
+                                          float softmax_scale, void* out_dev, float* lse_dev, void* stream);
+
 /* ------------------------------------------------------------------ LSE merge
  * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).
  * n summaries, summary i: out_ptrs[i] -> [rows, heads, head_dim] (dtype),

@@ -105,3 +105,42 @@ def test_long_query_over_mixed_segments_matches_oracle():
     e_out, e_lse = attention.mixed_attention(host(query), keys, vals)
     assert_attention_close(out, e_out, what="long-query mixed")
     assert np.abs(host(lse) - e_lse).max() <= 2e-2
+
+
+def test_batched_long_query_matches_per_sample_launches():
+    """bagel.py:773-980 (varlen, non-causal): three samples with different
+    query lengths and segment mixes in one launch equal three single
+    launches bit for bit; sample 1 is also checked against the oracle."""
+    need_gpu()
+    from unicache_b200 import batched_long_query_attention
+
+    heads = 4
+    samples, queries, dense = [], [], []
+    for i, (tokens, lq, n_dense) in enumerate([(352, 40, 16), (1088, 300, 0), (200, 7, 70)]):
+        key, value = make_kv(tokens, heads, 128, seed=60 + i, device="cuda")
+        packed = PackedKIVICache.from_dense(key, value, logical_token_ids=torch.arange(tokens, device="cuda"),
+                                            token_type_id=3, k_bits=2, v_bits=4, group_size=32, residual_length=32)
+        segs = [packed]
+        if i != 1:
+            hk, hv = make_kv(150, heads, 128, seed=70 + i, device="cuda")
+            sc = torch.rand(heads, 150, generator=torch.Generator().manual_seed(i)).to("cuda")
+            segs.insert(0, GQAH2OCache.from_dense(hk, hv, logical_token_ids=torch.arange(150, device="cuda"),
+                                                  token_type_id=1, per_kv_head_scores=sc, target_tokens=45,
+                                                  recent_tokens=9))
+        samples.append(segs)
+        queries.append(make_query(lq, 28, 128, seed=80 + i, device="cuda"))
+        dense.append(make_kv(n_dense, heads, 128, seed=90 + i, device="cuda") if n_dense else None)
+    results = batched_long_query_attention(queries, samples, dense_by_sample=dense)
+    for q, segs, dn, (out, lse) in zip(queries, samples, dense, results):
+        single_out, single_lse = long_query_attention_summary(q, segs, dense_key=dn[0] if dn else None,
+                                                              dense_value=dn[1] if dn else None)
+        torch.cuda.synchronize()
+        assert torch.equal(out, single_out) and torch.equal(lse, single_lse)
+    key, value = make_kv(1088, heads, 128, seed=61, device="cuda")
+    ref = kivi.packed_from_dense(host(key), host(value), "bfloat16", k_bits=2, v_bits=4, group_size=32,
+                                 residual_length=32)
+    rk, rv = kivi.packed_dequantize(ref)
+    e_out, e_lse = attention.mixed_attention(host(queries[1]), [rk], [rv])
+    assert_attention_close(results[1][0], e_out, what="batched sample 1")
+    assert np.abs(host(results[1][1]) - e_lse).max() <= 2e-2
+    assert kernels.device_status() == 0

@@ -9,6 +9,7 @@ reference's storage / operator API on top.
 from .adapters import (
     DecodeStepGraph,
     PhysicalDecodeBatch,
+    batched_long_query_attention,
     fused_h2o_decode,
     fused_mixed_decode,
     long_query_attention_summary,

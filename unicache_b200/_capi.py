@@ -99,6 +99,8 @@ SIGNATURES = {
     "ucb_decode_set_trace": (c_int, [c_void_p]),
     "ucb_prefill_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p,
                                       c_void_p, c_void_p]),
+    "ucb_prefill_attention_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int,
+                                              c_float, c_void_p, c_void_p, c_void_p]),
     "ucb_lse_merge": (c_int, [c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int, c_int64, c_int64,
                               c_int64, c_void_p, c_void_p, c_void_p]),
     "ucb_h2o_select": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),

@@ -3,6 +3,7 @@
 from .attention import (
     DecodeStepGraph,
     PhysicalDecodeBatch,
+    batched_long_query_attention,
     fused_h2o_decode,
     fused_mixed_decode,
     long_query_attention_summary,
@@ -12,6 +13,7 @@ from .attention import (
 __all__ = [
     "DecodeStepGraph",
     "PhysicalDecodeBatch",
+    "batched_long_query_attention",
     "fused_h2o_decode",
     "fused_mixed_decode",
     "long_query_attention_summary",

@@ -15,6 +15,8 @@ unicache/adapters/bagel.py):
                                   captured as a CUDA graph
 * ``long_query_attention_summary`` multi-query attention over the same
                                   segments (bagel.py:1598-1858 with q_len > 1)
+* ``batched_long_query_attention`` several samples' query blocks in one
+                                  launch (bagel.py:773-980, varlen)
 """
 
 from __future__ import annotations
@@ -149,13 +151,7 @@ def fused_mixed_decode(query: torch.Tensor, dense_key: torch.Tensor | None, dens
                                    int(query.shape[-1]))
 
 
-def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_residual: bool = True):
-    """Head-major bf16 key rows [H, Np, D] and transposed values [H, D, Np]
-    of all segments (packed spans restored by the bit-exact dequant kernel,
-    dense and H2O rows copied); Np is the token count rounded up to 8 and the
-    padding is zero.  Mirrors the reference's mixed-attention workspace
-    (bagel.py:1410-1450)."""
-
+def _span_tokens(segments, include_residual: bool) -> list:
     spans = []
     for seg in segments:
         if isinstance(seg, PackedKIVICache):
@@ -164,11 +160,13 @@ def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_re
             spans.append((seg, seg.retained_tokens))
         else:
             spans.append((seg, int(seg[0].shape[0])))
-    total = sum(n for _, n in spans)
-    padded = max(8, (total + 7) // 8 * 8)
-    kw = torch.zeros((num_kv_heads, padded, head_dim), device=device, dtype=torch.bfloat16)
-    vw = torch.zeros_like(kw)
-    t0 = 0
+    return spans
+
+
+def _fill_kv(spans, kw: torch.Tensor, vw: torch.Tensor, t0: int) -> None:
+    """Write the segments' key/value rows into head-major workspaces [H, N, D]
+    from row t0 on (packed spans restored by the bit-exact dequant kernel)."""
+
     for seg, n in spans:
         if isinstance(seg, PackedKIVICache):
             q = seg.quantized_tokens
@@ -176,8 +174,8 @@ def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_re
                 seg.dequantize_range(0, q, dtype=torch.bfloat16, output_key=kw[:, t0:t0 + q].transpose(0, 1),
                                      output_value=vw[:, t0:t0 + q].transpose(0, 1))
             if n > q:
-                kw[:, t0 + q:t0 + n] = seg.residual_key.transpose(0, 1)
-                vw[:, t0 + q:t0 + n] = seg.residual_value.transpose(0, 1)
+                kw[:, t0 + q:t0 + n] = seg.residual_key[:n - q].transpose(0, 1)
+                vw[:, t0 + q:t0 + n] = seg.residual_value[:n - q].transpose(0, 1)
         elif isinstance(seg, GQAH2OCache):
             kw[:, t0:t0 + n] = seg.key
             vw[:, t0:t0 + n] = seg.value
@@ -185,7 +183,91 @@ def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_re
             kw[:, t0:t0 + n] = seg[0].transpose(0, 1)
             vw[:, t0:t0 + n] = seg[1].transpose(0, 1)
         t0 += n
+
+
+def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_residual: bool = True):
+    """Head-major bf16 key rows [H, Np, D] and transposed values [H, D, Np]
+    of all segments; Np is the token count rounded up to 8 and the padding is
+    zero.  Mirrors the reference's mixed-attention workspace
+    (bagel.py:1410-1450)."""
+
+    spans = _span_tokens(segments, include_residual)
+    total = sum(n for _, n in spans)
+    padded = max(8, (total + 7) // 8 * 8)
+    kw = torch.zeros((num_kv_heads, padded, head_dim), device=device, dtype=torch.bfloat16)
+    vw = torch.zeros_like(kw)
+    _fill_kv(spans, kw, vw, 0)
     return kw, vw.transpose(1, 2).contiguous(), total
+
+
+def _kv_heads_of(segs) -> int:
+    first = segs[0]
+    if isinstance(first, (PackedKIVICache, GQAH2OCache)):
+        return first.num_kv_heads
+    return int(first[0].shape[1])
+
+
+def batched_long_query_attention(queries: list, segments_by_sample: list, *, dense_by_sample: list | None = None,
+                                 include_residual: bool = True) -> list:
+    """Non-causal attention of several samples' query blocks over their own
+    physical segments in one tcgen05 launch, the counterpart of the varlen
+    launch of apply_static_physical_attention_batch (bagel.py:773-980).
+
+    queries[i] [Lq_i, Hq, D]; segments_by_sample[i] the sample's segments;
+    dense_by_sample[i] an optional (key, value) [N, Hkv, D] pair of the
+    sample's own current tokens.  Returns [(out_i [Lq_i, Hq, D],
+    lse_i [Hq, Lq_i] natural log)]."""
+
+    if not queries or len(queries) != len(segments_by_sample):
+        raise ValueError("one segment list per query block is required")
+    dense_by_sample = dense_by_sample or [None] * len(queries)
+    samples = []
+    for query, segs, dense in zip(queries, segments_by_sample, dense_by_sample):
+        kernels.require_cuda(query, "query")
+        all_segs = _segments_for(dense[0] if dense else None, dense[1] if dense else None, segs)
+        if not all_segs:
+            raise ValueError("every sample needs at least one segment")
+        samples.append((query, all_segs))
+    hkv = _kv_heads_of(samples[0][1])
+    d = int(samples[0][0].shape[-1])
+    device = samples[0][0].device
+    q_rows, k_rows, metas = 0, 0, []
+    for query, segs in samples:
+        if _kv_heads_of(segs) != hkv or int(query.shape[-1]) != d:
+            raise ValueError("all samples must share KV heads and head_dim")
+        lq, hq = int(query.shape[0]), int(query.shape[1])
+        if hq % hkv:
+            raise ValueError("Query heads must be divisible by KV heads")
+        spans = _span_tokens(segs, include_residual)
+        total = sum(n for _, n in spans)
+        if total == 0:
+            raise ValueError("every sample needs at least one key token")
+        rows = lq * (hq // hkv)
+        metas.append((q_rows, rows, k_rows, total, spans))
+        q_rows += (rows + 255) // 256 * 256
+        k_rows += (total + 63) // 64 * 64
+    qp = torch.zeros((hkv, q_rows, d), device=device, dtype=torch.bfloat16)
+    kw = torch.zeros((hkv, k_rows, d), device=device, dtype=torch.bfloat16)
+    vw = torch.zeros_like(kw)
+    items = []
+    for (query, _), (q0, rows, k0, total, spans) in zip(samples, metas):
+        lq, hq = int(query.shape[0]), int(query.shape[1])
+        grp = hq // hkv
+        qp[:, q0:q0 + rows] = query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, rows, d)
+        _fill_kv(spans, kw, vw, k0)
+        for h in range(hkv):
+            for r in range(0, rows, 256):
+                items.append([h, q0 + r, min(256, rows - r), k0, total, 0, 0, 0])
+    table = torch.tensor(items, dtype=torch.int32).to(device)
+    out, lse = kernels.prefill_attention_batched(qp, kw, vw.transpose(1, 2).contiguous(), table)
+    results = []
+    for (query, _), (q0, rows, _, _, _) in zip(samples, metas):
+        lq, hq = int(query.shape[0]), int(query.shape[1])
+        grp = hq // hkv
+        o = out[:, q0:q0 + rows].reshape(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
+        l = lse[:, q0:q0 + rows].reshape(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
+        results.append((o.to(query.dtype), l))
+    return results
 
 
 def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_key=None, dense_value=None,
@@ -200,11 +282,7 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
     segs = _segments_for(dense_key, dense_value, segments)
     if not segs:
         raise ValueError("long-query attention needs at least one segment")
-    first = segs[0]
-    if isinstance(first, (PackedKIVICache, GQAH2OCache)):
-        hkv = first.num_kv_heads
-    else:
-        hkv = int(first[0].shape[1])
+    hkv = _kv_heads_of(segs)
     lq, hq, d = map(int, query.shape)
     if hq % hkv:
         raise ValueError("Query heads must be divisible by KV heads")

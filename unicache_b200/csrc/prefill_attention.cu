@@ -130,10 +130,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// One CTA's problem: query rows [q_row0, q_row0 + q_rows) of KV head `head`
+// (at most 2*BM rows) against keys [k_row0, k_row0 + n_tokens) of that head.
+struct WorkItem {
+  int head, q_row0, q_rows, k_row0, n_tokens, pad[3];
+};
+
 struct Params {
-  int m_rows;       // query rows per KV head
-  int n_tokens;     // valid key tokens per KV head
+  int m_rows;        // query rows per head in q / out / lse (row stride of the head)
+  int n_tokens;      // key tokens per head (single-problem launches)
   float scale_log2;  // softmax scale * log2(e)
+  const WorkItem* items;  // per-CTA problems (batched launches), or null: CTA (x, y) = rows 2*BM*x.. of head y
   __nv_bfloat16* out;  // [heads, m_rows, D]
   float* lse;          // [heads, m_rows], may be null
   unsigned int* err;
@@ -144,8 +151,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int head = blockIdx.y, m0 = blockIdx.x * 2 * BM;
-  const int n_tiles = (P.n_tokens + BN - 1) / BN;
+  int head, m0, m_end, k0, n_tokens;
+  if (P.items) {
+    const WorkItem it = P.items[blockIdx.x];
+    head = it.head;
+    m0 = it.q_row0;
+    m_end = it.q_row0 + it.q_rows;
+    k0 = it.k_row0;
+    n_tokens = it.n_tokens;
+  } else {
+    head = blockIdx.y;
+    m0 = blockIdx.x * 2 * BM;
+    m_end = P.m_rows;
+    k0 = 0;
+    n_tokens = P.n_tokens;
+  }
+  const int n_tiles = (n_tokens + BN - 1) / BN;
   // The swizzled operand layout needs a 1024-byte aligned base.
   if (smem_u32(smem) & 1023) {
     if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
@@ -210,10 +231,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         mbar_arrive_expect_tx(&k_full[st], KTILE);
-        tma_load_3d(smem + OFF_K + st * KTILE, &tm_k, 0, j * BN, head, &k_full[st]);
-        tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, j * BN, head, &k_full[st]);
+        tma_load_3d(smem + OFF_K + st * KTILE, &tm_k, 0, k0 + j * BN, head, &k_full[st]);
+        tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, k0 + j * BN, head, &k_full[st]);
         mbar_arrive_expect_tx(&v_full[st], VTILE);
-        tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, j * BN, 0, head, &v_full[st]);
+        tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, k0 + j * BN, 0, head, &v_full[st]);
         issued = j + 1;
       }
       // Copies still in flight must land before the shared memory is released.
@@ -299,7 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_ld32(t_s, sv[0]);
       tc_ld32(t_s + 32, sv[1]);
       tc_wait_ld();
-      const int valid = min(BN, P.n_tokens - j * BN);
+      const int valid = min(BN, n_tokens - j * BN);
       if (valid < BN) {  // ragged last tile: masked columns never win the max and get weight 0
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -374,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t ov[32];
         tc_ld32(t_o + 32 * c, ov);
         tc_wait_ld();
-        if (m < P.m_rows) {
+        if (m < m_end) {
           __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -387,7 +408,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (m < P.m_rows && P.lse)
+      if (m < m_end && P.lse)
         P.lse[(int64_t)head * P.m_rows + m] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
     } else if (lane == 0) {
       fail();
@@ -432,18 +453,13 @@ int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_
 }  // namespace prefill
 }  // namespace ucb
 
-extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* vt, int heads, int m_rows,
-                                     int n_tokens, int n_padded, float softmax_scale, void* out, float* lse,
-                                     void* stream) {
+namespace {
+int launch_prefill(const void* q, const void* k, const void* vt, int heads, int m_rows, int n_padded,
+                   ucb::prefill::Params P, dim3 grid, void* stream) {
   using namespace ucb::prefill;
-  if (!q || !k || !vt || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: null pointer");
-  if (heads <= 0 || m_rows <= 0 || n_tokens <= 0)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: empty problem");
-  if (n_padded < n_tokens || n_padded % 8)
-    return ucb_host::set_error(UCB_ERR_INVALID,
-                               "ucb_prefill_attention: n_padded must be >= n_tokens and a multiple of 8");
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(vt)) & 15)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: operands must be 16-byte aligned");
+  if (n_padded % 8) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: n_padded must be a multiple of 8");
   unsigned int* err = ucb_host::device_error_word();
   if (!err) return ucb_host::set_error(UCB_ERR_CUDA, "ucb_prefill_attention: device error word unavailable");
   CUtensorMap tq, tk, tv;
@@ -459,14 +475,45 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
       return ucb_host::set_error(UCB_ERR_CUDA, "prefill: cannot reserve %d bytes of shared memory", SMEM);
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
+  P.err = err;
+  prefill_kernel<<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
+  return ucb_host::check_launch("prefill_kernel");
+}
+}  // namespace
+
+extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* vt, int heads, int m_rows,
+                                     int n_tokens, int n_padded, float softmax_scale, void* out, float* lse,
+                                     void* stream) {
+  using namespace ucb::prefill;
+  if (!q || !k || !vt || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: null pointer");
+  if (heads <= 0 || m_rows <= 0 || n_tokens <= 0)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: empty problem");
+  if (n_padded < n_tokens)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: n_padded must be >= n_tokens");
   Params P;
   P.m_rows = m_rows;
   P.n_tokens = n_tokens;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
+  P.items = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
-  P.err = err;
-  const dim3 grid((m_rows + 2 * BM - 1) / (2 * BM), heads);
-  prefill_kernel<<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
-  return ucb_host::check_launch("prefill_kernel");
+  return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3((m_rows + 2 * BM - 1) / (2 * BM), heads), stream);
+}
+
+extern "C" int ucb_prefill_attention_batched(const void* q, const void* k, const void* vt, int heads, int m_rows,
+                                             int n_padded, const void* items, int num_items, float softmax_scale,
+                                             void* out, float* lse, void* stream) {
+  using namespace ucb::prefill;
+  if (!q || !k || !vt || !out || !items)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_batched: null pointer");
+  if (heads <= 0 || m_rows <= 0 || n_padded <= 0 || num_items <= 0)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_batched: empty problem");
+  Params P;
+  P.m_rows = m_rows;
+  P.n_tokens = 0;
+  P.scale_log2 = softmax_scale * 1.4426950408889634f;
+  P.items = static_cast<const WorkItem*>(items);
+  P.out = static_cast<__nv_bfloat16*>(out);
+  P.lse = lse;
+  return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3(num_items), stream);
 }

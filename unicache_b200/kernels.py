@@ -675,6 +675,38 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, n_toke
     return out, lse
 
 
+def prefill_attention_batched(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, items: torch.Tensor, *,
+                              softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                              lse: torch.Tensor | None = None):
+    """One launch over several non-causal attention problems sharing the
+    tensors q [H, M, 128], k [H, Np, 128], vt [H, 128, Np] (bf16):
+    ``items`` is an int32 device tensor [num_items, 8] of (head, q_row0,
+    q_rows <= 256, k_row0 (multiple of 64), n_tokens, 0, 0, 0), one per CTA.
+    Returns (out [H, M, 128] bf16, lse [H, M] fp32); rows no item covers are
+    left unwritten."""
+
+    for name, t in (("q", q), ("k", k), ("vt", vt), ("items", items)):
+        require_cuda(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or vt.dtype != torch.bfloat16:
+        raise ValueError("q, k and vt must be bfloat16")
+    if items.dtype != torch.int32 or items.dim() != 2 or int(items.shape[1]) != 8:
+        raise ValueError("items must be int32 [num_items, 8]")
+    heads, m_rows, d = map(int, q.shape)
+    n_padded = int(k.shape[1])
+    if d != 128 or tuple(k.shape) != (heads, n_padded, d) or tuple(vt.shape) != (heads, d, n_padded):
+        raise ValueError("batched prefill expects q [H,M,128], k [H,Np,128], vt [H,128,Np]")
+    scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
+    call("ucb_prefill_attention_batched", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, n_padded,
+         items.data_ptr(), int(items.shape[0]), scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    return out, lse
+
+
 # ---------------------------------------------------------------- host transfers
 def host_device_pointer(host: torch.Tensor) -> int:
     """Device-visible address of a pinned host tensor (mapped pinned memory)."""
