@@ -103,6 +103,7 @@ class PackedKIVICache:
     backend: str = "b200"
     kernel_native_layout: bool = True
     budget_shortfall_events: int = 0
+    residual_length: int = 0  # requested full-precision window (streaming append keeps it)
 
     @classmethod
     def from_dense(
@@ -170,7 +171,55 @@ class PackedKIVICache:
             num_kv_heads=heads,
             backend=backend,
             kernel_native_layout=True,
+            residual_length=max(0, int(residual_length)),
         )
+
+    # ---------------------------------------------------------------- streaming append
+    def append(self, key: torch.Tensor, value: torch.Tensor, *, logical_token_ids: torch.Tensor) -> int:
+        """Append decoded tokens [n, H, D] at the end of the segment.
+
+        The full-precision residual keeps between ``residual_length`` and
+        ``residual_length + group_size - 1`` tokens; every whole group that
+        leaves it is quantized and packed on the GPU and appended to the packed
+        tensors, oldest first, so the cache stays equal, bit for bit, to
+        ``from_dense`` over the whole sequence with the same residual length.
+        Returns the number of tokens packed.  Decode plans built on this cache
+        must be rebuilt (its tensors move)."""
+
+        if key.shape != value.shape or key.dim() != 3 or tuple(key.shape[1:]) != (self.num_kv_heads, self.head_dim):
+            raise ValueError("appended key/value must be [tokens, kv_heads, head_dim] matching the cache")
+        if key.dtype != self.residual_key.dtype or value.dtype != self.residual_value.dtype:
+            raise ValueError("appended key/value must have the residual's dtype")
+        n = int(key.shape[0])
+        if int(logical_token_ids.numel()) != n:
+            raise ValueError("one logical token id per appended token is required")
+        kernels.require_cuda(key, "key")
+        kernels.require_cuda(value, "value")
+        total = self.token_count + n
+        target = max(0, (total - self.residual_length) // self.group_size * self.group_size)
+        flush = target - self.quantized_tokens
+        res_key = torch.cat([self.residual_key, key], dim=0)
+        res_value = torch.cat([self.residual_value, value], dim=0)
+        if flush > 0:
+            kc, ks, km = kernels.kivi_pack_key(res_key[:flush].contiguous(), bits=self.k_bits,
+                                               group_size=self.group_size)
+            vc, vs, vm = kernels.kivi_pack_value(res_value[:flush].contiguous(), bits=self.v_bits,
+                                                 group_size=self.group_size)
+            new = (kc, ks, km, vc, vs, vm)
+            names = ("key_code", "key_scale", "key_minimum", "value_code", "value_scale", "value_minimum")
+            for name, tensor in zip(names, new):
+                old = getattr(self, name)
+                # b200 layout: tokens (or token groups, or packed words) run along dim 1
+                setattr(self, name, tensor if old is None else torch.cat([old, tensor], dim=1))
+            self.quantized_tokens = target
+            res_key = res_key[flush:].clone()
+            res_value = res_value[flush:].clone()
+        self.residual_key, self.residual_value = res_key, res_value
+        self.logical_token_ids = torch.cat(
+            [self.logical_token_ids, logical_token_ids.to(self.logical_token_ids.device,
+                                                          self.logical_token_ids.dtype)])
+        self.__dict__.pop("_decode_plans", None)
+        return max(0, flush)
 
     # ---------------------------------------------------------------- accounting
     @property
