@@ -235,9 +235,10 @@ UCB_API int ucb_prefill_attention(const void* q_dev, const void* k_dev, const vo
  * vt_dev [heads, 128, n_padded], out_dev, lse_dev.  items_dev: device array of
  * num_items ucb_prefill_item records, one per CTA; CTA i computes query rows
  * [q_row0, q_row0 + q_rows) (q_rows <= 256) of KV head `head` against keys
- * [k_row0, k_row0 + n_tokens) of that head.  k_row0 must be a multiple of 64
- * and key rows k_row0 + n_tokens .. k_row0 + 64*ceil(n_tokens/64) - 1 must
- * exist and be finite (zeros); query rows q_row0 .. q_row0 + 255 must exist.
+ * [k_row0, k_row0 + n_tokens) of that head.  k_row0 must be a multiple of 64;
+ * key rows k_row0 + n_tokens .. k_row0 + 128*ceil(n_tokens/128) - 1 that lie
+ * inside n_padded must be finite (zeros or another problem's keys); rows past
+ * n_padded read as zeros.  Query rows q_row0 .. q_row0 + 255 must exist.
  * Replaces the single flash_attn_varlen_func(causal=False) call of
  * apply_static_physical_attention_batch (unicache/adapters/bagel.py:773-980)
  * for query blocks. */

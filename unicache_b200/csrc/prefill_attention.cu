@@ -14,20 +14,24 @@
 // Design: one CTA per 256 query rows (two 128-row tiles A and B) of one KV
 // head, warp-specialised so that the tensor core works on one tile while the
 // other tile's softmax runs:
-//  * warp 8 (one lane) loads Q_A, Q_B once and streams K tiles (64 tokens x
-//    128 channels) and V^T tiles (128 channels x 64 tokens) by TMA with
+//  * warp 8 (one lane) loads Q_A, Q_B once and streams K tiles (128 tokens x
+//    128 channels) and V^T tiles (128 channels x 128 tokens) by TMA with
 //    128-byte swizzle (the canonical K-major tcgen05 operand layout) through a
-//    three-stage ring of full/empty mbarriers;
-//  * warp 9 (one lane) issues tcgen05.mma (bf16 operands from shared-memory
-//    descriptors, fp32 accumulators in tensor memory): S_A = Q_A K^T,
-//    S_B = Q_B K^T, then O_A += P_A V^T and O_B += P_B V^T as the softmax
-//    warpgroups hand over P;
+//    two-stage ring of full/empty mbarriers;
+//  * warp 9 (one lane) issues tcgen05.mma (fp32 accumulators in tensor
+//    memory): S_A = Q_A K^T and S_B = Q_B K^T from shared-memory operands,
+//    then O_A += P_A V^T and O_B += P_B V^T with P read from tensor memory
+//    as the softmax warpgroups hand it over;
 //  * warps 0-3 (tile A) and 4-7 (tile B): each thread owns one query row
 //    (one TMEM lane), so the row max and sum need no shuffles.  P =
-//    exp2(S*scale*log2e - m) goes to shared memory in bf16 in the swizzled
-//    layout; the row sum accumulates the fp32 weights, as FlashAttention's
-//    does.  The running max only moves (and O is rescaled in TMEM) when a
-//    row's maximum grows by more than 8 (log2 units).
+//    exp2(S*scale*log2e - m) is written in bf16 over the first half of its
+//    own S columns in tensor memory (no shared-memory round trip); the row
+//    sum accumulates the fp32 weights, as FlashAttention's does.  The running
+//    max only moves (and O is rescaled in TMEM) when a row's maximum grows by
+//    more than 8 (log2 units).
+//  * tcgen05.mma operations of one thread execute in issue order, so the
+//    PV product that reads P_x(j) completes its reads before S_x(j+1),
+//    issued after it, overwrites those columns.
 //  * Every wait has a time budget; on expiry the CTA sets the device error
 //    word, drains its tensor-core work (bounded) and frees TMEM.
 #include <cuda.h>
@@ -40,29 +44,29 @@ namespace prefill {
 
 constexpr int D = 128;
 constexpr int BM = 128;                   // query rows per tile (TMEM lanes)
-constexpr int BN = 64;                    // key tokens per K/V tile
-constexpr int STAGES = 3;                 // K/V ring depth
+constexpr int BN = 128;                   // key tokens per K/V tile
+constexpr int STAGES = 2;                 // K/V ring depth
 constexpr int QTILE = BM * D * 2;         // 32 KB: two 64-channel swizzled halves
 constexpr int QHALF = QTILE / 2;          // 16 KB
-constexpr int KTILE = BN * D * 2;         // 16 KB: two 64-channel halves of 64 rows
-constexpr int KHALF = KTILE / 2;          // 8 KB
-constexpr int VTILE = D * BN * 2;         // 16 KB: 128 channel rows x 64 tokens
-constexpr int PTILE = BM * BN * 2;        // 16 KB: 128 query rows x 64 tokens
+constexpr int KTILE = BN * D * 2;         // 32 KB: two 64-channel halves of 128 rows
+constexpr int KHALF = KTILE / 2;          // 16 KB
+constexpr int VTILE = D * BN * 2;         // 32 KB: two 64-token halves of 128 channel rows
+constexpr int VHALF = VTILE / 2;          // 16 KB
 constexpr int OFF_Q = 0;                  // Q_A, Q_B
 constexpr int OFF_K = OFF_Q + 2 * QTILE;
 constexpr int OFF_V = OFF_K + STAGES * KTILE;
-constexpr int OFF_P = OFF_V + STAGES * VTILE;  // P_A, P_B
-constexpr int OFF_BAR = OFF_P + 2 * PTILE;
+constexpr int OFF_BAR = OFF_V + STAGES * VTILE;
 constexpr int NBAR = 1 + 4 * STAGES + 7;  // q_full, k/v full/empty, s_full[2], p_full[2], o_done[2], drain
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM = OFF_TMEM + 16;
 constexpr int THREADS = 384;              // warps 0-7 softmax, 8 loader, 9 MMA, 10-11 idle
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
 constexpr float RESCALE_THRESHOLD = 8.f;  // log2 units
-constexpr uint32_t TMEM_COLS = 512;       // S_A [0,64) S_B [64,128) O_A [128,256) O_B [256,384)
+constexpr uint32_t TMEM_COLS = 512;       // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
+constexpr uint32_t S_COL = 0, O_COL = 256; // tile x: S at S_COL + 128x (P_x in its first 64), O at O_COL + 128x
 
 // tcgen05 instruction descriptors, kind::f16: F32 accumulator, BF16 A and B,
-// both K-major, M = 128; N = 64 for S = Q K^T and N = 128 for O += P V.
+// both K-major, M = 128; N = 128 for S = Q K^T and for O += P V.
 constexpr uint32_t idesc(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
@@ -87,6 +91,17 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (TMEM) += A (TMEM, M rows x 16 bf16 in 8 columns) * B (shared memory).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -120,6 +135,69 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32])
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Row maximum of a 128-column S tile (this thread's TMEM lane), 64 columns
+// per load batch; RAGGED masks columns >= valid.
+template <bool RAGGED>
+__device__ __forceinline__ float row_max(uint32_t t_s, int valid) {
+  float mx = -INFINITY;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t sv[2][32];
+    tc_ld32(t_s + 64 * h, sv[0]);
+    tc_ld32(t_s + 64 * h + 32, sv[1]);
+    tc_wait_ld();
+    float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int col = 64 * h + 32 * c + i;
+        m0 = fmaxf(m0, (!RAGGED || col < valid) ? __uint_as_float(sv[c][i]) : -INFINITY);
+        m1 = fmaxf(m1, (!RAGGED || col + 1 < valid) ? __uint_as_float(sv[c][i + 1]) : -INFINITY);
+      }
+    mx = fmaxf(mx, fmaxf(m0, m1));
+  }
+  return mx;
+}
+
+// P = 2^(S * scale_log2 - m) in bf16 pairs over the first 64 columns of the
+// S tile (column c holds tokens 2c, 2c+1); each 64-column half of S is read
+// before the P columns it feeds overwrite any S column.  Returns the fp32
+// row sum of the weights.  The scaling and the sums run as packed fp32 pairs
+// (one FFMA2 and one FADD2 per two columns), the exponentials on the MUFU.
+template <bool RAGGED>
+__device__ __forceinline__ float write_p(uint32_t t_s, int valid, float scale_log2, float neg_m) {
+  const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
+  float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t sv[2][32];
+    tc_ld32(t_s + 64 * h, sv[0]);
+    tc_ld32(t_s + 64 * h + 32, sv[1]);
+    tc_wait_ld();
+    uint32_t pw[32];
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int col = 64 * h + 32 * c + i;
+        const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1])), sc, nm);
+        float2 p;
+        if constexpr (RAGGED) {
+          p.x = col < valid ? fast_exp2(x.x) : 0.f;
+          p.y = col + 1 < valid ? fast_exp2(x.y) : 0.f;
+        } else {
+          p.x = fast_exp2(x.x);
+          p.y = fast_exp2(x.y);
+        }
+        sum = __fadd2_rn(sum, p);
+        pw[16 * c + i / 2] = pack_bf16x2(p.x, p.y);
+      }
+    tc_st32(t_s + 32 * h, pw);
+  }
+  return sum.x + sum.y;
+}
 
 // Tiled TMA load of box {x, y, z} of a 3-D tensor map into shared memory.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
@@ -235,6 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, k0 + j * BN, head, &k_full[st]);
         mbar_arrive_expect_tx(&v_full[st], VTILE);
         tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, k0 + j * BN, 0, head, &v_full[st]);
+        tma_load_3d(smem + OFF_V + st * VTILE + VHALF, &tm_v, k0 + j * BN + 64, 0, head, &v_full[st]);
         issued = j + 1;
       }
       // Copies still in flight must land before the shared memory is released.
@@ -249,13 +328,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     // PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ..., so that while one tile's
     // softmax runs the other tile's products are in flight.
     if (lane == 0) {
-      const uint32_t q_addr = smem_u32(smem + OFF_Q), p_addr = smem_u32(smem + OFF_P);
+      const uint32_t q_addr = smem_u32(smem + OFF_Q);
       auto issue_s = [&](int j, int x) {
         const uint32_t k_addr = smem_u32(smem + OFF_K + (j % STAGES) * KTILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t col = (kk & 3) * 32;
-          tc_mma(tmem + 64 * x, sw128_desc(q_addr + x * QTILE + (kk >> 2) * QHALF + col),
+          tc_mma(tmem + S_COL + 128 * x, sw128_desc(q_addr + x * QTILE + (kk >> 2) * QHALF + col),
                  sw128_desc(k_addr + (kk >> 2) * KHALF + col), IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[x]);
@@ -263,9 +342,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto issue_pv = [&](int j, int x) {
         const uint32_t v_addr = smem_u32(smem + OFF_V + (j % STAGES) * VTILE);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma(tmem + 128 + 128 * x, sw128_desc(p_addr + x * PTILE + kk * 32), sw128_desc(v_addr + kk * 32),
-                 IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BN / 16; ++kk)  // P_x: 8 TMEM columns (16 tokens) per step
+          tc_mma_ts(tmem + O_COL + 128 * x, tmem + S_COL + 128 * x + 8 * kk,
+                    sw128_desc(v_addr + (kk >> 2) * VHALF + (kk & 3) * 32), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&o_done[x]);
       };
       bool ok = mbar_wait_for(q_full, 0, WAIT_NS) && mbar_wait_for(&k_full[0], 0, WAIT_NS);
@@ -308,33 +387,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int x = warp >> 2;             // tile
     const int row = tid & (BM - 1);      // query row in the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const uint32_t t_s = tmem + 64 * x + lane_off, t_o = tmem + 128 + 128 * x + lane_off;
-    unsigned char* prow = smem + OFF_P + x * PTILE + (row >> 3) * 1024 + (row & 7) * 128;
+    const uint32_t t_s = tmem + S_COL + 128 * x + lane_off, t_o = tmem + O_COL + 128 * x + lane_off;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       ok = mbar_wait_for(&s_full[x], j & 1, WAIT_NS);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      uint32_t sv[2][32];
-      tc_ld32(t_s, sv[0]);
-      tc_ld32(t_s + 32, sv[1]);
-      tc_wait_ld();
       const int valid = min(BN, n_tokens - j * BN);
-      if (valid < BN) {  // ragged last tile: masked columns never win the max and get weight 0
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * c + i >= valid) sv[c][i] = __float_as_uint(-INFINITY);
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        mx0 = fmaxf(mx0, fmaxf(__uint_as_float(sv[0][i]), __uint_as_float(sv[0][i + 1])));
-        mx1 = fmaxf(mx1, fmaxf(__uint_as_float(sv[1][i]), __uint_as_float(sv[1][i + 1])));
-      }
-      const float mx = fmaxf(mx0, mx1) * P.scale_log2;
+      const float mx = (valid < BN ? row_max<true>(t_s, valid) : row_max<false>(t_s, valid)) * P.scale_log2;
       // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
       if (j > 0) {
         ok = mbar_wait_for(&o_done[x], (j - 1) & 1, WAIT_NS);
@@ -352,7 +413,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_ld32(t_o + 32 * c, ov);
             tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            for (int i = 0; i < 32; i += 2) {
+              const float2 v = __fmul2_rn(make_float2(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])),
+                                          make_float2(alpha, alpha));
+              ov[i] = __float_as_uint(v.x);
+              ov[i + 1] = __float_as_uint(v.y);
+            }
             tc_st32(t_o + 32 * c, ov);
           }
           tc_wait_st();
@@ -360,28 +426,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         l_run *= alpha;
         m_run = m_new;
       }
-      const float neg_m = -m_run;
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e]), P.scale_log2, neg_m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][8 * q + 2 * e + 1]), P.scale_log2, neg_m));
-            sum0 += p0;
-            sum1 += p1;
-            w[e] = pack_bf16x2(p0, p1);
-          }
-          const int chunk = 4 * c + q;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      const float sum = sum0 + sum1;
-      l_run += sum;
-      fence_proxy_async_smem();  // P (generic stores) -> tensor-core reads (async proxy)
+      l_run += valid < BN ? write_p<true>(t_s, valid, P.scale_log2, -m_run)
+                          : write_p<false>(t_s, valid, P.scale_log2, -m_run);
+      tc_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
     }
