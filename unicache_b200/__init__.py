@@ -26,9 +26,11 @@ from .operators import (
 from .storage import (
     CacheMutationResult,
     GQAH2OCache,
+    HostPackedKIVI,
     PackedKIVICache,
     PhysicalLayerCache,
     PhysicalSegment,
+    QuantizedHostArchive,
     TensorCacheStorageBackend,
     dequantize_kivi_chunk,
     gqa_probability_value,

@@ -1,5 +1,6 @@
 """Physical storage layouts and their B200 kernels (counterpart of unicache/storage)."""
 
+from .hierarchy import HostPackedKIVI, QuantizedHostArchive, QuantizedWorkingSetTransition, to_host
 from .kivi_b200 import (
     dequantize_kivi_chunk,
     packed_kivi_attention_parts,
@@ -20,6 +21,9 @@ from .tensor_backend import CacheMutationResult, TensorCacheStorageBackend
 __all__ = [
     "CacheMutationResult",
     "GQAH2OCache",
+    "HostPackedKIVI",
+    "QuantizedHostArchive",
+    "QuantizedWorkingSetTransition",
     "PackedKIVICache",
     "PhysicalLayerCache",
     "PhysicalSegment",
@@ -31,4 +35,5 @@ __all__ = [
     "packed_kivi_quantized_attention_summary",
     "quantize_kivi_b200",
     "tensor_bytes",
+    "to_host",
 ]

@@ -221,6 +221,13 @@ class PackedKIVICache:
         self.__dict__.pop("_decode_plans", None)
         return max(0, flush)
 
+    def to_host(self):
+        """A contiguous host replica of this cache (``storage.hierarchy``)."""
+
+        from .hierarchy import HostPackedKIVI
+
+        return HostPackedKIVI.from_cache(self)
+
     # ---------------------------------------------------------------- accounting
     @property
     def token_count(self) -> int:
