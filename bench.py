@@ -216,7 +216,7 @@ class ClockSampler:
                     for name, bit in self.REASONS.items():
                         if mask & bit:
                             self.reasons.add(name)
-                    time.sleep(0.02)
+                    time.sleep(0.0005)  # the timed replay lasts milliseconds: sample densely
 
             self._thread = threading.Thread(target=loop, daemon=True)
             self._thread.start()
@@ -540,12 +540,172 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+def shard_bytes(tokens: int, residual: int) -> int:
+    """Bytes one decode step moves for one sequence shard of ``tokens`` packed
+    + ``residual`` bf16 tokens, over all KV heads (query and output included)."""
+
+    codes = 2 * tokens * HEAD_DIM * BITS // 8
+    key_stats = (tokens // GROUP) * HEAD_DIM * 2 * 2
+    value_stats = tokens * (HEAD_DIM // GROUP) * 2 * 2
+    res = residual * HEAD_DIM * 2 * 2
+    q_and_o = (Q_HEADS // KV_HEADS) * HEAD_DIM * 2 * 2
+    return KV_HEADS * (codes + key_stats + value_stats + res + q_and_o)
+
+
+def run_split(args) -> None:
+    """BASELINE config 3, long-context half: ONE sequence of TOKENS packed
+    (4-bit, group 64) + RESIDUAL bf16 tokens split over the ranks in
+    contiguous group-aligned shards (the last rank also holds the residual).
+    A step = every rank decodes its shard (decode + state merge), one NCCL
+    all-gather of every rank's (out, LSE), and the LSE merge; the step time is
+    the max over ranks (strong scaling: the sequence is fixed).  Steps rotate
+    over enough shard replicas to exceed the 126 MB L2."""
+
+    import torch
+    import torch.distributed as dist
+
+    from unicache_b200 import PackedKIVICache, kernels
+    from unicache_b200.distributed import SequenceSplitDecode, split_tokens
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    start, stop = split_tokens(TOKENS + RESIDUAL, world, GROUP, RESIDUAL)[rank]
+    n_local = stop - start
+    residual = RESIDUAL if rank == world - 1 else 0
+    local_bytes = shard_bytes(n_local - residual, residual)
+    replicas_n = max(2, math.ceil(256e6 / local_bytes))
+    gen = torch.Generator(device=device).manual_seed(4321 + 7919 * rank)
+    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(device)
+    decoders = []
+    for _ in range(replicas_n):
+        k = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=device)
+        k[:, :, outlier] *= 10.0
+        v = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=device)
+        cache = PackedKIVICache.from_dense(k.to(torch.bfloat16), v.to(torch.bfloat16),
+                                           logical_token_ids=torch.arange(start, stop, device=device),
+                                           token_type_id=3, k_bits=BITS, v_bits=BITS, group_size=GROUP,
+                                           residual_length=residual)
+        del k, v
+        decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group))
+    torch.cuda.empty_cache()
+    qgen = torch.Generator(device=device).manual_seed(99)  # every rank decodes the same query
+    query = torch.randn(1, Q_HEADS, HEAD_DIM, generator=qgen, device=device).to(torch.bfloat16)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(step_fn) -> float:
+        for i in range(args.warmup):
+            step_fn(i)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            step_fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / 1000.0
+
+    with ClockSampler(local_rank) as clocks:
+        elapsed = timed(lambda i: decoders[i % replicas_n](query))
+    local_elapsed = timed(lambda i: decoders[i % replicas_n].plan.run(query))
+    host_q = query.cpu().pin_memory()
+    host_o = torch.empty(query.shape, dtype=query.dtype).pin_memory()
+    host_l = torch.empty((1, Q_HEADS), dtype=torch.float32).pin_memory()
+    dev_q = torch.empty_like(query)
+
+    def e2e_step(i):
+        dev_q.copy_(host_q, non_blocking=True)
+        o, l = decoders[i % replicas_n](dev_q)
+        host_o.copy_(o, non_blocking=True)
+        host_l.copy_(l, non_blocking=True)
+
+    e2e_elapsed = timed(e2e_step)
+    status = kernels.device_status()
+    if world > 1:
+        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, float(status)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, local_elapsed, e2e_elapsed, status = float(t[0]), float(t[1]), float(t[2]), int(t[3])
+    total_bytes = shard_bytes(TOKENS, RESIDUAL)
+    if rank == 0:
+        step_s = elapsed / args.steps
+        peak, peak_kind = measured_peaks()
+        achieved = total_bytes / world / step_s / 1e9  # per GPU
+        cpu_s, cpu_tokens = cpu_oracle_sample(4242)
+        line = {
+            "metric": METRIC,
+            "value": args.steps / elapsed,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": 1000.0 * step_s,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": (f"config3split: one sequence of {TOKENS} packed KIVI {BITS}-bit G{GROUP} + {RESIDUAL} bf16 "
+                             f"tokens split over {world} GPU(s), 28/4 heads, D=128"),
+                "global_batch": 1,
+                "seq_len": TOKENS + RESIDUAL,
+                "parallelism": f"sequence-split x{world} + NCCL all-gather of (out, LSE) + LSE merge",
+                "l2": f"steps rotate over {replicas_n} shard replicas ({replicas_n * local_bytes / 1e6:.0f} MB per GPU > 126 MB L2)",
+            },
+            "hbm_gbs": achieved,
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "peak_source": peak_kind,
+                "traffic": None,
+                "algorithmic_bytes_per_launch": total_bytes // world,
+                "kernel_ms": 1000.0 * step_s,
+                "kernel": "per GPU: shard decode + state merge + all-gather + LSE merge, eager per step",
+            },
+            "local_decode_ms_per_step": 1000.0 * local_elapsed / args.steps,
+            "e2e": {"value": args.steps / e2e_elapsed, "unit": "tokens/s",
+                    "h2d_bytes_per_step": query.numel() * query.element_size(),
+                    "d2h_bytes_per_step": host_o.numel() * host_o.element_size() + host_l.numel() * 4,
+                    "api": "SequenceSplitDecode.__call__ with the query copied from and the result copied to pinned host memory"},
+            "gpu_launches": (3 if world > 1 else 2) * args.steps,
+            "clocks": clocks.summary(),
+            "device_status": status,
+            "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+                             "sample": f"the whole {TOKENS}+{RESIDUAL}-token sequence, one decode token (dequantize + "
+                                       f"float64 attention), timed on one of the {KV_HEADS} KV heads and scaled x{KV_HEADS}"},
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 WORKLOADS = {
     # BASELINE config 2: 16 sequences per GPU, 8192 + 128 tokens, 2-bit, group 32
     "config2": dict(BATCH=16, TOKENS=8192, RESIDUAL=128, BITS=2, GROUP=32, REPLICAS=8),
     # BASELINE config 3 per GPU (batch 64 over 8 GPUs): 8 sequences, 32768 + 128
     # tokens, 4-bit, group 64
     "config3": dict(BATCH=8, TOKENS=32768, RESIDUAL=128, BITS=4, GROUP=64, REPLICAS=2),
+    # BASELINE config 3, long-context half: one 131072 + 128 token sequence,
+    # 4-bit, group 64, split over the GPUs (strong scaling)
+    "config3split": dict(BATCH=1, TOKENS=131072, RESIDUAL=128, BITS=4, GROUP=64, REPLICAS=0),
 }
 
 
@@ -569,6 +729,8 @@ def main() -> None:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif WORKLOAD == "config3split":
+        run_split(args)
     else:
         run_b200(args)
 

@@ -224,6 +224,28 @@ def test_full_size_config3_per_gpu_batch_decode():
     assert kernels.device_status() == 0
 
 
+def test_full_size_config3_long_sequence_decode():
+    """Config 3, long-context half, on one GPU: ONE sequence of 131072 packed
+    4-bit G64 + 128 bf16 residual tokens (4 pairs spread over every SM, so
+    each pair carries hundreds of warp states and the wide state merge runs),
+    checked against the oracle."""
+
+    need_gpu()
+    cache, ref = _packed(131072 + 128, 128, 4, 4, 64, seed=3100)
+    query = make_query(1, 28, 128, seed=31, device="cuda")
+    batch = PhysicalDecodeBatch([[cache]], num_kv_heads=4)
+    assert batch.plan.num_partials > 64 * 4  # the wide merge's regime
+    out, lse = batch(query)
+    out2, lse2 = batch(query)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
+    rk, rv = kivi.packed_dequantize(ref)
+    eo, el = _oracle_decode(host(query)[0], [rk], [rv])
+    assert_attention_close(out[0], eo, what="131072-token sequence")
+    assert np.abs(host(lse)[0] - el).max() < LSE_ABS
+    assert kernels.device_status() == 0
+
+
 def test_decode_rejects_cpu_and_bad_query():
     need_gpu()
     cache, _ = _packed(256, 0, 2, 2, 32, seed=1)

@@ -716,6 +716,46 @@ __global__ void __launch_bounds__(Cfg<KB, VB, G, ST>::THREADS, 1) decode_kernel(
 // barrier: each warp is independent.
 constexpr int MERGE_DCH = 32;
 
+// One round of the merge: up to 32 states starting at `st` folded into the
+// running (M, L, acc) of query head h, channel d (this lane).  Lane k loads
+// state k's (max, sum); every lane loads its channel of all rows in one batch.
+__device__ __forceinline__ void merge_round(const float* st, int nk, int h, int d, int lane, float& M, float& L,
+                                            float& acc) {
+  const float mk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + h) : -INFINITY;
+  const float lk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + 8 + h) : 0.f;
+  float v[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) v[q] = q < nk ? __ldcg(st + (int64_t)q * PARTIAL_FLOATS + 16 + h * D + d) : 0.f;
+  float mx = mk;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float m_new = fmaxf(M, mx);
+  if (m_new == -INFINITY) return;  // nothing seen yet (empty states)
+  const float wk = (mk == -INFINITY) ? 0.f : fast_exp2(mk - m_new);
+  float l = wk * lk;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+  const float f = (M == -INFINITY) ? 0.f : fast_exp2(M - m_new);
+  float a0 = acc * f, a1 = 0.f;
+#pragma unroll
+  for (int q = 0; q < 32; q += 2) {
+    a0 = fmaf(__shfl_sync(0xffffffffu, wk, q), v[q], a0);
+    a1 = fmaf(__shfl_sync(0xffffffffu, wk, q + 1), v[q + 1], a1);
+  }
+  acc = a0 + a1;
+  L = fmaf(L, f, l);
+  M = m_new;
+}
+
+__device__ __forceinline__ void merge_store(const ucb_decode_pair& pr, int grp, int hq, int h, int d, float M, float L,
+                                            float acc, __nv_bfloat16* out, int64_t out_stride, float* lse) {
+  const int qh = pr.kv_head * grp + h;
+  out[pr.seq * out_stride + (int64_t)qh * D + d] = __float2bfloat16_rn(acc / L);
+  if (d == 0 && lse != nullptr) lse[(int64_t)pr.seq * hq + qh] = (M + __log2f(L)) * LN2;
+}
+
+// Few states per pair (many pairs): CTA per (pair, 32-channel chunk), warp h =
+// query head h walks all the pair's states.
 __global__ void __launch_bounds__(256) state_merge_kernel(const float* __restrict__ states,
                                                           const ucb_decode_pair* __restrict__ pairs, int grp,
                                                           int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride,
@@ -725,36 +765,44 @@ __global__ void __launch_bounds__(256) state_merge_kernel(const float* __restric
   const ucb_decode_pair pr = pairs[blockIdx.x];
   const float* base = states + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
   float M = -INFINITY, L = 0.f, acc = 0.f;
-  for (int k0 = 0; k0 < pr.partial_count; k0 += 32) {
-    const int nk = min(32, pr.partial_count - k0);
-    const float* st = base + (int64_t)k0 * PARTIAL_FLOATS;
-    const float mk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + h) : -INFINITY;
-    const float lk = lane < nk ? __ldcg(st + (int64_t)lane * PARTIAL_FLOATS + 8 + h) : 0.f;
-    float v[32];
-#pragma unroll
-    for (int q = 0; q < 32; ++q) v[q] = q < nk ? __ldcg(st + (int64_t)q * PARTIAL_FLOATS + 16 + h * D + d) : 0.f;
-    float mx = mk;
-#pragma unroll
-    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    const float m_new = fmaxf(M, mx);
-    const float wk = (mk == -INFINITY) ? 0.f : fast_exp2(mk - m_new);
-    float l = wk * lk;
-#pragma unroll
-    for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    const float f = (M == -INFINITY) ? 0.f : fast_exp2(M - m_new);
-    float a0 = acc * f, a1 = 0.f;
-#pragma unroll
-    for (int q = 0; q < 32; q += 2) {
-      a0 = fmaf(__shfl_sync(0xffffffffu, wk, q), v[q], a0);
-      a1 = fmaf(__shfl_sync(0xffffffffu, wk, q + 1), v[q + 1], a1);
-    }
-    acc = a0 + a1;
-    L = fmaf(L, f, l);
-    M = m_new;
+  for (int k0 = 0; k0 < pr.partial_count; k0 += 32)
+    merge_round(base + (int64_t)k0 * PARTIAL_FLOATS, min(32, pr.partial_count - k0), h, d, lane, M, L, acc);
+  merge_store(pr, grp, hq, h, d, M, L, acc, out, out_stride, lse);
+}
+
+// Many states per pair (few long sequences): CTA per (pair, query head,
+// 32-channel chunk); its 8 warps take every 8th block of 32 states and fold
+// their partial results through shared memory.
+constexpr int WIDE_MERGE_WARPS = 8;
+__global__ void __launch_bounds__(WIDE_MERGE_WARPS * 32)
+    state_merge_wide_kernel(const float* __restrict__ states, const ucb_decode_pair* __restrict__ pairs, int grp,
+                            int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride, float* __restrict__ lse) {
+  __shared__ float sm_m[WIDE_MERGE_WARPS], sm_l[WIDE_MERGE_WARPS], sm_acc[WIDE_MERGE_WARPS][32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, d = blockIdx.y * MERGE_DCH + lane;
+  const int pi = blockIdx.x / grp, h = blockIdx.x % grp;
+  const ucb_decode_pair pr = pairs[pi];
+  const float* base = states + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
+  float M = -INFINITY, L = 0.f, acc = 0.f;
+  for (int k0 = 32 * w; k0 < pr.partial_count; k0 += 32 * WIDE_MERGE_WARPS)
+    merge_round(base + (int64_t)k0 * PARTIAL_FLOATS, min(32, pr.partial_count - k0), h, d, lane, M, L, acc);
+  if (lane == 0) {
+    sm_m[w] = M;
+    sm_l[w] = L;
   }
-  const int qh = pr.kv_head * grp + h;
-  out[pr.seq * out_stride + (int64_t)qh * D + d] = __float2bfloat16_rn(acc / L);
-  if (d == 0 && lse != nullptr) lse[(int64_t)pr.seq * hq + qh] = (M + __log2f(L)) * LN2;
+  sm_acc[w][lane] = acc;
+  __syncthreads();
+  if (w != 0) return;
+  float Mt = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < WIDE_MERGE_WARPS; ++k) Mt = fmaxf(Mt, sm_m[k]);
+  float Lt = 0.f, At = 0.f;
+#pragma unroll
+  for (int k = 0; k < WIDE_MERGE_WARPS; ++k) {
+    const float f = (sm_m[k] == -INFINITY) ? 0.f : fast_exp2(sm_m[k] - Mt);
+    Lt = fmaf(sm_l[k], f, Lt);
+    At = fmaf(sm_acc[k][lane], f, At);
+  }
+  merge_store(pr, grp, hq, h, d, Mt, Lt, At, out, out_stride, lse);
 }
 
 template <int KB, int VB, int G, typename ST>
@@ -781,6 +829,13 @@ int launch(const Params& P, int num_ctas, cudaStream_t s) {
   if (rc) return rc;
   // Stream order makes the merge wait for every warp state.  (Launching it as
   // a programmatic dependent measured slower: 31.7 vs 29.0 us per config-2 step.)
+  // Pairs hold about num_ctas * WARPS / num_pairs warp states each: above 64
+  // the per-head walk over them gets long, so 8 warps share each head.
+  if ((int64_t)num_ctas * C::WARPS > 64LL * P.num_pairs) {
+    state_merge_wide_kernel<<<dim3(P.num_pairs * P.grp, D / MERGE_DCH), WIDE_MERGE_WARPS * 32, 0, s>>>(
+        static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse);
+    return ucb_host::check_launch("state_merge_wide_kernel");
+  }
   state_merge_kernel<<<dim3(P.num_pairs, D / MERGE_DCH), 256, 0, s>>>(
       static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse);
   return ucb_host::check_launch("state_merge_kernel");

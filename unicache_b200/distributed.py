@@ -10,7 +10,8 @@
   GPUs, gloo on CPU) and merges them with the LSE merge kernel.  That merge is
   the reference's merge_attention_summaries (unicache/adapters/bagel.py:57-72)
   applied across ranks instead of across segments.  Each rank exchanges
-  (B, Hq, D + 1) values: the output rows and their LSE.
+  its output rows (bf16) and their LSE (fp32) as one buffer in one
+  all-gather.
 """
 
 from __future__ import annotations
@@ -56,16 +57,23 @@ def split_tokens(tokens: int, world: int, group_size: int, residual_length: int 
 
 
 def exchange_summaries(out: torch.Tensor, lse: torch.Tensor, group=None) -> tuple[list, list]:
-    """All-gather every rank's (out [B, Hq, D], lse [B, Hq]).  Without an
-    initialised process group the local pair is returned alone."""
+    """All-gather every rank's (out [B, Hq, D], lse [B, Hq]) in ONE collective:
+    both travel as the bytes of one buffer (out first; its byte size is a
+    multiple of 4, so the fp32 LSE stays aligned).  Without an initialised
+    process group the local pair is returned alone."""
 
     if not dist.is_available() or not dist.is_initialized():
         return [out], [lse]
     world = dist.get_world_size(group)
-    outs = [torch.empty_like(out) for _ in range(world)]
-    lses = [torch.empty_like(lse) for _ in range(world)]
-    dist.all_gather(outs, out.contiguous(), group=group)
-    dist.all_gather(lses, lse.contiguous(), group=group)
+    ob = out.contiguous().view(torch.uint8).reshape(-1)
+    lb = lse.contiguous().view(torch.uint8).reshape(-1)
+    if ob.numel() % 4:
+        raise ValueError("out must span a multiple of 4 bytes")
+    send = torch.cat([ob, lb])
+    parts = [torch.empty_like(send) for _ in range(world)]
+    dist.all_gather(parts, send, group=group)
+    outs = [p[:ob.numel()].view(out.dtype).view(out.shape) for p in parts]
+    lses = [p[ob.numel():].view(lse.dtype).view(lse.shape) for p in parts]
     return outs, lses
 
 
