@@ -619,9 +619,33 @@ def run_split(args) -> None:
         barrier()
         return e0.elapsed_time(e1) / 1000.0
 
-    with ClockSampler(local_rank) as clocks:
-        elapsed = timed(lambda i: decoders[i % replicas_n](query))
+    # eager per-call steps (also warm the NCCL communicator before capture)
+    eager_elapsed = timed(lambda i: decoders[i % replicas_n](query))
     local_elapsed = timed(lambda i: decoders[i % replicas_n].plan.run(query))
+    # device-timed region: the K steps (decode, state merge, all-gather, LSE
+    # merge each) captured once in a CUDA graph, NCCL included
+    capture_stream = torch.cuda.Stream(device=device)
+    capture_stream.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(capture_stream):
+        with torch.cuda.graph(graph, stream=capture_stream):
+            for i in range(args.steps):
+                decoders[i % replicas_n](query)
+    torch.cuda.current_stream(device).wait_stream(capture_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        g0.record()
+        graph.replay()
+        g1.record()
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = g0.elapsed_time(g1) / 1000.0
+    del graph  # released before the process group is destroyed
     host_q = query.cpu().pin_memory()
     host_o = torch.empty(query.shape, dtype=query.dtype).pin_memory()
     host_l = torch.empty((1, Q_HEADS), dtype=torch.float32).pin_memory()
@@ -636,9 +660,11 @@ def run_split(args) -> None:
     e2e_elapsed = timed(e2e_step)
     status = kernels.device_status()
     if world > 1:
-        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, float(status)], device=device, dtype=torch.float64)
+        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, eager_elapsed, float(status)], device=device,
+                         dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, local_elapsed, e2e_elapsed, status = float(t[0]), float(t[1]), float(t[2]), int(t[3])
+        elapsed, local_elapsed, e2e_elapsed, eager_elapsed, status = (float(t[0]), float(t[1]), float(t[2]),
+                                                                      float(t[3]), int(t[4]))
     total_bytes = shard_bytes(TOKENS, RESIDUAL)
     if rank == 0:
         step_s = elapsed / args.steps
@@ -677,9 +703,10 @@ def run_split(args) -> None:
                 "traffic": None,
                 "algorithmic_bytes_per_launch": total_bytes // world,
                 "kernel_ms": 1000.0 * step_s,
-                "kernel": "per GPU: shard decode + state merge + all-gather + LSE merge, eager per step",
+                "kernel": "per GPU: shard decode + state merge + all-gather + LSE merge, one graph replay of K steps",
             },
             "local_decode_ms_per_step": 1000.0 * local_elapsed / args.steps,
+            "eager_ms_per_step": 1000.0 * eager_elapsed / args.steps,
             "e2e": {"value": args.steps / e2e_elapsed, "unit": "tokens/s",
                     "h2d_bytes_per_step": query.numel() * query.element_size(),
                     "d2h_bytes_per_step": host_o.numel() * host_o.element_size() + host_l.numel() * 4,

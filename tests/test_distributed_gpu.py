@@ -81,13 +81,18 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
-        key, value = make_kv(TOKENS, HEADS, 128, seed=91, device="cuda")
-        query = make_query(1, 28, 128, seed=92, device="cuda")
+        # two sequences split the same way; two calls reuse the step buffers
+        kvs = [make_kv(TOKENS, HEADS, 128, seed=91 + 10 * b, device="cuda") for b in range(2)]
+        query = make_query(2, 28, 128, seed=92, device="cuda")
         start, stop = split_tokens(TOKENS, world, GROUP, RESIDUAL)[rank]
-        decode = SequenceSplitDecode([[_shard_cache(key, value, start, stop, rank == world - 1)]], num_kv_heads=HEADS)
+        decode = SequenceSplitDecode([[_shard_cache(k, v, start, stop, rank == world - 1)] for k, v in kvs],
+                                     num_kv_heads=HEADS)
         out, lse = decode(query)
+        out2, lse2 = decode(query)
         torch.cuda.synchronize()
-        _check(out, lse, _oracle(key, value, query, world))
+        assert torch.equal(out, out2) and torch.equal(lse, lse2)
+        for b, (k, v) in enumerate(kvs):
+            _check(out[b:b + 1], lse[b:b + 1], _oracle(k, v, query[b:b + 1], world))
         open(os.path.join(result_dir, f"ok{rank}"), "w").close()
     finally:
         dist.destroy_process_group()

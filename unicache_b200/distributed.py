@@ -16,6 +16,8 @@
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -92,15 +94,51 @@ class SequenceSplitDecode:
     ``local_sequences`` holds, for each sequence of the batch, this rank's
     segments (its shard of the packed cache, plus dense or H2O segments it
     owns).  Every rank calls it with the same query; every rank gets the
-    merged result."""
+    merged result.
+
+    One step is three operations on the current stream: the local decode
+    writes its output rows (bf16) and LSE (fp32) straight into a preallocated
+    send buffer, ONE ``all_gather_into_tensor`` fills a preallocated receive
+    buffer with every rank's buffer, and the LSE merge kernel folds the
+    ranks' summaries in place (out viewed as [1, B*Hq, D] and LSE as
+    [B*Hq, 1], so no transposes are needed).  A second call reuses the
+    buffers: steps are ordered on the stream, so a step's merge has read the
+    receive buffer before the next step's all-gather overwrites it."""
 
     def __init__(self, local_sequences: list[list], *, num_kv_heads: int, head_dim: int = 128, group=None):
         self.plan = kernels.build_decode_plan(local_sequences, num_kv_heads=num_kv_heads, head_dim=head_dim)
         self.group = group
+        self._buffers = None  # (q_heads, send, recv, out view, lse view, out pointers, lse pointers, world)
+
+    def _setup(self, query: torch.Tensor):
+        b, hq, d = map(int, query.shape)
+        world = dist.get_world_size(self.group)
+        ob, lb = b * hq * d * 2, b * hq * 4
+        send = torch.empty(ob + lb, dtype=torch.uint8, device=query.device)
+        recv = torch.empty(world * (ob + lb), dtype=torch.uint8, device=query.device)
+        out_view = send[:ob].view(torch.bfloat16).view(b, hq, d)
+        lse_view = send[ob:].view(torch.float32).view(b, hq)
+        base = recv.data_ptr()
+        optrs = (ctypes.c_void_p * world)(*[base + r * (ob + lb) for r in range(world)])
+        lptrs = (ctypes.c_void_p * world)(*[base + r * (ob + lb) + ob for r in range(world)])
+        self._buffers = (hq, send, recv, out_view, lse_view, optrs, lptrs, world)
 
     def __call__(self, query: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """query [B, Hq, D] bf16 -> (out [B, Hq, D] bf16, lse [B, Hq] fp32)."""
 
-        out, lse = self.plan.run(query)
-        outs, lses = exchange_summaries(out, lse, self.group)
-        return merge_rank_summaries(outs, lses)
+        if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return self.plan.run(query)
+        if query.dtype != torch.bfloat16 or query.dim() != 3:
+            raise ValueError("query must be bfloat16 [B, Hq, D]")
+        if self._buffers is None or self._buffers[0] != int(query.shape[1]) or \
+                self._buffers[1].device != query.device:
+            self._setup(query)
+        hq, send, recv, out_view, lse_view, optrs, lptrs, world = self._buffers
+        b, _, d = map(int, query.shape)
+        self.plan.run(query, out=out_view, lse=lse_view)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        merged = torch.empty_like(out_view)
+        total = torch.empty_like(lse_view)
+        kernels.call("ucb_lse_merge", world, optrs, lptrs, kernels.dtype_code(torch.bfloat16), 1, b * hq, d,
+                     merged.data_ptr(), total.data_ptr(), kernels.stream_of(query))
+        return merged, total
