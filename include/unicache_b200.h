@@ -78,6 +78,19 @@ UCB_API int ucb_kivi_pack_value(const void* x_dev, int dtype, int64_t tokens, in
                         int64_t stride_token, int64_t stride_head, int bits, int group_size,
                         void* codes_dev, void* scale_dev, void* minimum_dev, void* stream);
 
+/* Keys and values of one segment in ONE launch (the whole pack step of
+ * PackedKIVICache.from_dense, unicache/storage/physical.py:291-304), with
+ * results identical to ucb_kivi_pack_key + ucb_kivi_pack_value on the same
+ * inputs.  Built for dtype UCB_BF16, head_dim 128 and group_size 32 with
+ * 16-byte-aligned value rows; any other case returns UCB_ERR_UNSUPPORTED and
+ * the caller uses the two separate entries.  Key and value inputs may have
+ * different strides; both are [tokens, heads, 128]. */
+UCB_API int ucb_kivi_pack_kv(const void* key_dev, const void* value_dev, int dtype, int64_t tokens, int64_t heads,
+                             int64_t head_dim, int64_t key_stride_token, int64_t key_stride_head,
+                             int64_t value_stride_token, int64_t value_stride_head, int k_bits, int v_bits,
+                             int group_size, void* key_codes_dev, void* key_scale_dev, void* key_minimum_dev,
+                             void* value_codes_dev, void* value_scale_dev, void* value_minimum_dev, void* stream);
+
 /* ------------------------------------------------------------------ KIVI dequantize
  * Replaces PackedKIVICache.dequantize (physical.py:379-423 -> _dequantize_grouped
  * :178-201) and dequantize_kivi_chunk (unicache/storage/kivi_cuda.py:58-93 ->

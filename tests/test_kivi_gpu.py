@@ -231,3 +231,34 @@ def test_fake_quant_bf16_and_partial_groups_vs_oracle():
         np.testing.assert_array_equal(host(got), kivi.fake_quant_key(host(key), "bfloat16", bits=bits, group_size=32))
         got = kivi_fake_quant_value(key, bits=bits, group_size=48)
         np.testing.assert_array_equal(host(got), kivi.fake_quant_value(host(key), "bfloat16", bits=bits, group_size=48))
+
+
+@pytest.mark.parametrize("kb,vb", [(2, 2), (2, 4), (4, 2), (4, 4), (8, 2), (2, 8), (8, 8)])
+@pytest.mark.parametrize("tokens", [32, 96, 8192])
+def test_fused_key_value_pack_equals_separate_kernels(kb, vb, tokens):
+    """ucb_kivi_pack_kv (one launch) writes exactly what ucb_kivi_pack_key +
+    ucb_kivi_pack_value write, including for a key view with a padded head
+    stride and a value view with a padded token stride."""
+    need_gpu()
+    gen = torch.Generator(device="cuda").manual_seed(tokens + 10 * kb + vb)
+    big_k = (torch.randn(tokens, 4, 136, generator=gen, device="cuda") * 3).to(torch.bfloat16)
+    big_v = torch.randn(tokens, 5, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    key, value = big_k[:, :, :128], big_v[:, :4]
+    fused = kernels.kivi_pack_kv(key, value, k_bits=kb, v_bits=vb, group_size=32)
+    separate = (*kernels.kivi_pack_key(key, bits=kb, group_size=32),
+                *kernels.kivi_pack_value(value, bits=vb, group_size=32))
+    torch.cuda.synchronize()
+    for a, b in zip(fused, separate):
+        assert a.dtype == b.dtype and a.shape == b.shape and torch.equal(a, b)
+    assert kernels.device_status() == 0
+
+
+def test_fused_pack_other_groups_use_the_separate_kernels():
+    need_gpu()
+    key, value = make_kv(256, 4, 128, seed=12, device="cuda")
+    for g in (64, 128):
+        fused = kernels.kivi_pack_kv(key, value, k_bits=4, v_bits=2, group_size=g)
+        separate = (*kernels.kivi_pack_key(key, bits=4, group_size=g),
+                    *kernels.kivi_pack_value(value, bits=2, group_size=g))
+        for a, b in zip(fused, separate):
+            assert torch.equal(a, b)

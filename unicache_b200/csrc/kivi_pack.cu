@@ -49,14 +49,13 @@ __device__ __forceinline__ uint32_t quant_code_fast(float v, float mn, float sca
 // a time before any reduction; for G = 32 the values stay in registers for
 // the code pass, larger groups re-read them from L1.
 template <typename T, int BITS, int G>
-__global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, int64_t stride_t,
-                                                      int64_t stride_h, int tokens, int head_dim,
-                                                      uint32_t* __restrict__ codes32,
-                                                      uint8_t* __restrict__ codes8,
-                                                      T* __restrict__ scale, T* __restrict__ minimum) {
+__device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t stride_t, int64_t stride_h, int tokens,
+                                              int head_dim, uint32_t* __restrict__ codes32,
+                                              uint8_t* __restrict__ codes8, T* __restrict__ scale,
+                                              T* __restrict__ minimum, int g, int h, int pair) {
   constexpr int CH = 32;
   using V2 = typename Dtype<T>::vec2;
-  const int g = blockIdx.x, h = blockIdx.y, d = 2 * threadIdx.x;
+  const int d = 2 * pair;
   if (d >= head_dim) return;
   const int groups = tokens / G;
   const T* col = x + static_cast<int64_t>(g) * G * stride_t + h * stride_h + d;
@@ -120,20 +119,28 @@ __global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, i
   }
 }
 
+template <typename T, int BITS, int G>
+__global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, int64_t stride_t,
+                                                      int64_t stride_h, int tokens, int head_dim,
+                                                      uint32_t* __restrict__ codes32,
+                                                      uint8_t* __restrict__ codes8,
+                                                      T* __restrict__ scale, T* __restrict__ minimum) {
+  pack_key_item<T, BITS, G>(x, stride_t, stride_h, tokens, head_dim, codes32, codes8, scale, minimum, blockIdx.x,
+                            blockIdx.y, threadIdx.x);
+}
+
 // ---------------------------------------------------------------- value pack
 // One thread per (token row, channel group): it reads the group's G channels
 // with 16-byte loads, reduces them locally and writes G*bits/32 words and its
 // two statistics.  Consecutive threads take consecutive groups of consecutive
 // rows, so a warp reads one contiguous span of the input.
 template <typename T, int BITS, int D, int G, bool VEC>
-__global__ void __launch_bounds__(256) pack_value_kernel(const T* __restrict__ x, int64_t stride_t,
-                                                         int64_t stride_h, int tokens, int heads,
-                                                         uint32_t* __restrict__ codes32,
-                                                         uint8_t* __restrict__ codes8,
-                                                         T* __restrict__ scale, T* __restrict__ minimum) {
+__device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t stride_t, int64_t stride_h,
+                                                int tokens, int heads, uint32_t* __restrict__ codes32,
+                                                uint8_t* __restrict__ codes8, T* __restrict__ scale,
+                                                T* __restrict__ minimum, int64_t item) {
   constexpr int NG = D / G;                     // groups per row
   constexpr int EPV = 16 / (int)sizeof(T);      // elements per 16-byte load
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n_items = static_cast<int64_t>(tokens) * heads * NG;
   if (item >= n_items) return;
   const int gi = static_cast<int>(item % NG);
@@ -191,6 +198,53 @@ __global__ void __launch_bounds__(256) pack_value_kernel(const T* __restrict__ x
     uint32_t* out = codes32 + out_row * (D / F) + gi * W;
 #pragma unroll
     for (int k = 0; k < W; k += 2) *reinterpret_cast<uint2*>(out + k) = make_uint2(w[k], w[k + 1]);
+  }
+}
+
+template <typename T, int BITS, int D, int G, bool VEC>
+__global__ void __launch_bounds__(256) pack_value_kernel(const T* __restrict__ x, int64_t stride_t,
+                                                         int64_t stride_h, int tokens, int heads,
+                                                         uint32_t* __restrict__ codes32,
+                                                         uint8_t* __restrict__ codes8,
+                                                         T* __restrict__ scale, T* __restrict__ minimum) {
+  pack_value_item<T, BITS, D, G, VEC>(x, stride_t, stride_h, tokens, heads, codes32, codes8, scale, minimum,
+                                      static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x);
+}
+
+// ---------------------------------------------------------------- fused key + value pack
+// One launch for both halves of PackedKIVICache.from_dense's pack step: blocks
+// [0, key_blocks) quantize keys, four (token group, head) items of 64 channel
+// pairs per 256-thread block; the remaining blocks quantize values, one
+// (token row, channel group) per thread.  Each item runs the same code as the
+// separate kernels, so the results are identical; one launch instead of two
+// saves one launch and one memory ramp per sequence.  Built for group 32
+// only: two 256-thread blocks per SM hold both paths without spilling there
+// (groups 64 and 128 would spill, so they keep the separate kernels).
+struct PackSide {
+  const void* x;
+  int64_t stride_t, stride_h;
+  void* codes;
+  void* scale;
+  void* minimum;
+};
+
+template <int KB, int VB, int G>
+__global__ void __launch_bounds__(256, 2) pack_kv_kernel(PackSide k, PackSide v, int tokens, int heads, int key_blocks) {
+  using T = __nv_bfloat16;
+  constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
+  if (static_cast<int>(blockIdx.x) < key_blocks) {
+    const int groups = tokens / G;
+    const int item = blockIdx.x * ITEMS + threadIdx.x / PAIRS;
+    if (item >= groups * heads) return;
+    pack_key_item<T, KB, G>(static_cast<const T*>(k.x), k.stride_t, k.stride_h, tokens, D,
+                            static_cast<uint32_t*>(k.codes), static_cast<uint8_t*>(k.codes),
+                            static_cast<T*>(k.scale), static_cast<T*>(k.minimum), item % groups, item / groups,
+                            threadIdx.x % PAIRS);
+  } else {
+    const int64_t item = static_cast<int64_t>(blockIdx.x - key_blocks) * 256 + threadIdx.x;
+    pack_value_item<T, VB, D, G, true>(static_cast<const T*>(v.x), v.stride_t, v.stride_h, tokens, heads,
+                                       static_cast<uint32_t*>(v.codes), static_cast<uint8_t*>(v.codes),
+                                       static_cast<T*>(v.scale), static_cast<T*>(v.minimum), item);
   }
 }
 
@@ -486,6 +540,50 @@ extern "C" int ucb_kivi_pack_value(const void* x, int dtype, int64_t tokens, int
     default:
       return launch_pack_value<float>(x, tokens, heads, head_dim, stride_token, stride_head, bits, group_size, codes, scale, minimum, s);
   }
+}
+
+extern "C" int ucb_kivi_pack_kv(const void* key, const void* value, int dtype, int64_t tokens, int64_t heads,
+                                int64_t head_dim, int64_t key_stride_token, int64_t key_stride_head,
+                                int64_t value_stride_token, int64_t value_stride_head, int k_bits, int v_bits,
+                                int group_size, void* key_codes, void* key_scale, void* key_minimum,
+                                void* value_codes, void* value_scale, void* value_minimum, void* stream) {
+  int rc = validate_pack("ucb_kivi_pack_kv", key, dtype, tokens, heads, head_dim, k_bits, group_size, key_codes,
+                         key_scale, key_minimum);
+  if (rc) return rc;
+  rc = validate_pack("ucb_kivi_pack_kv", value, dtype, tokens, heads, head_dim, v_bits, group_size, value_codes,
+                     value_scale, value_minimum);
+  if (rc) return rc;
+  if (tokens % group_size)
+    return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv: tokens (%lld) must be a multiple of group_size (%d)",
+                     (long long)tokens, group_size);
+  if (dtype != UCB_BF16 || head_dim != 128 || group_size != 32)
+    return set_error(UCB_ERR_UNSUPPORTED,
+                     "ucb_kivi_pack_kv: bf16, head_dim 128, group 32 only (use the separate entries)");
+  if (!aligned(value, 16) || value_stride_token % 8 || value_stride_head % 8)
+    return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_kv: value rows must be 16-byte aligned");
+  if ((tokens / group_size) * heads > (1LL << 31) - 1 || tokens * heads * (head_dim / group_size) > (1LL << 40))
+    return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv: problem too large");
+  const ucb::PackSide k{key, key_stride_token, key_stride_head, key_codes, key_scale, key_minimum};
+  const ucb::PackSide v{value, value_stride_token, value_stride_head, value_codes, value_scale, value_minimum};
+  const int key_blocks = static_cast<int>(((tokens / group_size) * heads + 3) / 4);
+  const int64_t value_items = tokens * heads * (head_dim / group_size);
+  const int64_t blocks = key_blocks + (value_items + 255) / 256;
+  if (blocks > 0x7fffffffLL) return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv: problem too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define UCB_PACK_KV(KB_, VB_, G_)                                                                             \
+  if (k_bits == KB_ && v_bits == VB_ && group_size == G_) {                                                   \
+    ucb::pack_kv_kernel<KB_, VB_, G_><<<static_cast<unsigned>(blocks), 256, 0, s>>>(k, v, (int)tokens, (int)heads, \
+                                                                                     key_blocks);              \
+    return check_launch("pack_kv_kernel");                                                                    \
+  }
+#define UCB_PACK_KV_G(KB_, VB_) UCB_PACK_KV(KB_, VB_, 32)
+  UCB_PACK_KV_G(2, 2) UCB_PACK_KV_G(2, 4) UCB_PACK_KV_G(2, 8)
+  UCB_PACK_KV_G(4, 2) UCB_PACK_KV_G(4, 4) UCB_PACK_KV_G(4, 8)
+  UCB_PACK_KV_G(8, 2) UCB_PACK_KV_G(8, 4) UCB_PACK_KV_G(8, 8)
+#undef UCB_PACK_KV_G
+#undef UCB_PACK_KV
+  return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_kv: unsupported (bits %d/%d, group %d)", k_bits, v_bits,
+                   group_size);
 }
 
 extern "C" int ucb_kivi_dequant_key(const void* codes, const void* scale, const void* minimum, int stat_dtype,

@@ -90,6 +90,39 @@ def kivi_pack_value(value: torch.Tensor, *, bits: int, group_size: int):
     return codes, scale, minimum
 
 
+def kivi_pack_kv(key: torch.Tensor, value: torch.Tensor, *, k_bits: int, v_bits: int, group_size: int):
+    """Quantize and pack keys and values [T, H, D] of one segment: (key codes,
+    key scale, key min, value codes, value scale, value min) in the b200
+    layout, identical to ``kivi_pack_key`` + ``kivi_pack_value``.  bf16 inputs
+    with head_dim 128 and group 32 take one fused launch; other shapes the two
+    separate kernels."""
+
+    require_cuda(key, "key")
+    require_cuda(value, "value")
+    if key.shape != value.shape or key.dim() != 3 or key.stride(2) != 1 or value.stride(2) != 1:
+        raise ValueError("key and value must be matching [tokens, heads, head_dim] with unit channel stride")
+    tokens, heads, head_dim = map(int, key.shape)
+    fused = (key.dtype == torch.bfloat16 and value.dtype == torch.bfloat16 and head_dim == 128 and group_size == 32
+             and value.data_ptr() % 16 == 0 and value.stride(0) % 8 == 0 and value.stride(1) % 8 == 0
+             and tokens > 0 and tokens % group_size == 0)
+    if not fused:
+        return (*kivi_pack_key(key, bits=k_bits, group_size=group_size),
+                *kivi_pack_value(value, bits=v_bits, group_size=group_size))
+    dev = key.device
+    kc = (torch.empty((heads, tokens, head_dim), device=dev, dtype=torch.uint8) if k_bits == 8 else
+          torch.empty((heads, tokens // codes_per_word(k_bits), head_dim), device=dev, dtype=torch.int32))
+    vc = (torch.empty((heads, tokens, head_dim), device=dev, dtype=torch.uint8) if v_bits == 8 else
+          torch.empty((heads, tokens, head_dim // codes_per_word(v_bits)), device=dev, dtype=torch.int32))
+    ks = torch.empty((heads, tokens // group_size, head_dim), device=dev, dtype=key.dtype)
+    km = torch.empty_like(ks)
+    vs = torch.empty((heads, tokens, head_dim // group_size), device=dev, dtype=value.dtype)
+    vm = torch.empty_like(vs)
+    call("ucb_kivi_pack_kv", key.data_ptr(), value.data_ptr(), dtype_code(key.dtype), tokens, heads, head_dim,
+         key.stride(0), key.stride(1), value.stride(0), value.stride(1), k_bits, v_bits, group_size,
+         kc.data_ptr(), ks.data_ptr(), km.data_ptr(), vc.data_ptr(), vs.data_ptr(), vm.data_ptr(), stream_of(key))
+    return kc, ks, km, vc, vs, vm
+
+
 def kivi_dequant(which: str, codes, scale, minimum, *, bits: int, group_size: int, quantized_tokens: int,
                  heads: int, head_dim: int, start: int, stop: int, out: torch.Tensor) -> torch.Tensor:
     """Dequantize tokens [start, stop) into ``out`` rows [0, stop-start) ([N, H, D] view)."""

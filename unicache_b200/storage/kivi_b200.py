@@ -35,9 +35,7 @@ def quantize_kivi_b200(key: torch.Tensor, value: torch.Tensor, *, k_bits: int, v
 
     if key.shape != value.shape or key.dim() != 3:
         raise ValueError("KIVI packing expects matching [tokens, heads, dim] KV")
-    kc, ks, km = kernels.kivi_pack_key(key, bits=k_bits, group_size=group_size)
-    vc, vs, vm = kernels.kivi_pack_value(value, bits=v_bits, group_size=group_size)
-    return kc, ks, km, vc, vs, vm
+    return kernels.kivi_pack_kv(key, value, k_bits=k_bits, v_bits=v_bits, group_size=group_size)
 
 
 def dequantize_kivi_chunk(

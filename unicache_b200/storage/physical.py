@@ -145,10 +145,9 @@ class PackedKIVICache:
                 q_key = q_key.contiguous()
             if q_value.stride(2) != 1:
                 q_value = q_value.contiguous()
-            key_code, key_scale, key_minimum = kernels.kivi_pack_key(q_key, bits=k_bits, group_size=group_size)
-            value_code, value_scale, value_minimum = kernels.kivi_pack_value(
-                q_value, bits=v_bits, group_size=group_size
-            )
+            (key_code, key_scale, key_minimum, value_code, value_scale,
+             value_minimum) = kernels.kivi_pack_kv(q_key, q_value, k_bits=k_bits, v_bits=v_bits,
+                                                   group_size=group_size)
         else:
             key_code = key_scale = key_minimum = None
             value_code = value_scale = value_minimum = None
@@ -201,11 +200,8 @@ class PackedKIVICache:
         res_key = torch.cat([self.residual_key, key], dim=0)
         res_value = torch.cat([self.residual_value, value], dim=0)
         if flush > 0:
-            kc, ks, km = kernels.kivi_pack_key(res_key[:flush].contiguous(), bits=self.k_bits,
-                                               group_size=self.group_size)
-            vc, vs, vm = kernels.kivi_pack_value(res_value[:flush].contiguous(), bits=self.v_bits,
-                                                 group_size=self.group_size)
-            new = (kc, ks, km, vc, vs, vm)
+            new = kernels.kivi_pack_kv(res_key[:flush].contiguous(), res_value[:flush].contiguous(),
+                                       k_bits=self.k_bits, v_bits=self.v_bits, group_size=self.group_size)
             names = ("key_code", "key_scale", "key_minimum", "value_code", "value_scale", "value_minimum")
             for name, tensor in zip(names, new):
                 old = getattr(self, name)
