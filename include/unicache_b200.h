@@ -256,12 +256,34 @@ UCB_API int ucb_prefill_attention(const void* q_dev, const void* k_dev, const vo
  * apply_static_physical_attention_batch (unicache/adapters/bagel.py:773-980)
  * for query blocks. */
 typedef struct ucb_prefill_item {
-  int32_t head, q_row0, q_rows, k_row0, n_tokens, reserved[3];
+  int32_t head, q_row0, q_rows, k_row0, n_tokens;
+  int32_t mode; /* 0: write out/lse; 1: partial (see ucb_prefill_attention_items); 2: merge */
+  int32_t slot; /* partial slot and flag index for modes 1 and 2 */
+  int32_t reserved;
 } ucb_prefill_item;
 
 UCB_API int ucb_prefill_attention_batched(const void* q_dev, const void* k_dev, const void* vt_dev, int heads,
                                           int m_rows, int n_padded, const void* items_dev, int num_items,
                                           float softmax_scale, void* out_dev, float* lse_dev, void* stream);
+
+/* Batched variant whose items may split a row block's keys in two, to fill
+ * every SM when a problem has fewer row blocks than SMs (no counterpart in
+ * the reference, whose varlen FlashAttention call schedules itself).  The
+ * mode-1 item (keys [k_row0, k_row0 + n_tokens) of the second part) writes
+ * its normalised fp32 rows and log2 LSE to partials_dev slot `slot`
+ * (ucb_prefill_partial_bytes() each) and then sets flags_dev[slot]; the
+ * mode-2 item of the same rows (the first part) waits for that flag (bounded:
+ * on expiry it sets the device error word), merges the two results by LSE
+ * into out/lse and clears the flag.  flags_dev must be zero before the first
+ * launch and is zero again after every complete launch.  Mode-2 items must be
+ * fewer than the SMs, so that their partners always find an SM; list them
+ * first so they start first.  partials_dev and flags_dev may be NULL when no
+ * item uses modes 1 or 2. */
+UCB_API int ucb_prefill_attention_items(const void* q_dev, const void* k_dev, const void* vt_dev, int heads,
+                                        int m_rows, int n_padded, const void* items_dev, int num_items,
+                                        float softmax_scale, void* out_dev, float* lse_dev, float* partials_dev,
+                                        unsigned int* flags_dev, void* stream);
+UCB_API int64_t ucb_prefill_partial_bytes(void);
 
 /* ------------------------------------------------------------------ LSE merge
  * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).

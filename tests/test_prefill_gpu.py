@@ -109,8 +109,10 @@ def test_long_query_over_mixed_segments_matches_oracle():
 
 def test_batched_long_query_matches_per_sample_launches():
     """bagel.py:773-980 (varlen, non-causal): three samples with different
-    query lengths and segment mixes in one launch equal three single
-    launches bit for bit; sample 1 is also checked against the oracle."""
+    query lengths and segment mixes in one launch agree with three single
+    launches (which may split their keys across CTAs, so within the bf16
+    tolerance rather than bitwise); sample 1 is also checked against the
+    oracle."""
     need_gpu()
     from unicache_b200 import batched_long_query_attention
 
@@ -135,7 +137,9 @@ def test_batched_long_query_matches_per_sample_launches():
         single_out, single_lse = long_query_attention_summary(q, segs, dense_key=dn[0] if dn else None,
                                                               dense_value=dn[1] if dn else None)
         torch.cuda.synchronize()
-        assert torch.equal(out, single_out) and torch.equal(lse, single_lse)
+        diff = (out.float() - single_out.float()).abs()
+        assert float(diff.max()) <= MAX_ABS and float(diff.mean()) <= MEAN_ABS, (float(diff.max()), float(diff.mean()))
+        assert float((lse - single_lse).abs().max()) <= 2e-2
     key, value = make_kv(1088, heads, 128, seed=61, device="cuda")
     ref = kivi.packed_from_dense(host(key), host(value), "bfloat16", k_bits=2, v_bits=4, group_size=32,
                                  residual_length=32)
@@ -143,4 +147,29 @@ def test_batched_long_query_matches_per_sample_launches():
     e_out, e_lse = attention.mixed_attention(host(queries[1]), [rk], [rv])
     assert_attention_close(results[1][0], e_out, what="batched sample 1")
     assert np.abs(host(results[1][1]) - e_lse).max() <= 2e-2
+    assert kernels.device_status() == 0
+
+
+def test_key_split_fills_the_gpu_and_cleans_up():
+    """Config 4 has 112 row blocks for 148 SMs: every row block's keys are
+    split (the first 23 tiles merge the last 2 tiles' partial by LSE).  Three
+    launches in a row agree bitwise with each other and with the fp32
+    reference, and the flags are zero after each launch."""
+    need_gpu()
+    q, k, v, n_pad = _operands(4, 1024 * 7, 3095, seed=14)
+    vt = v.transpose(1, 2).contiguous()
+    first, _ = kernels.prefill_attention(q, k, vt, 3095)
+    split = kernels._KEY_SPLITS[(q.device.index, 4, 7168, 3095, n_pad, kernels.stream_of(q))]
+    assert split is not None
+    items, _, flags = split
+    assert int(items.shape[0]) == 2 * 112 and int(items[0, 4]) == kernels.plan_key_split(112, 25, 148) * 128
+    results = [kernels.prefill_attention(q, k, vt, 3095) for _ in range(2)]
+    torch.cuda.synchronize()
+    assert int(flags.abs().sum()) == 0
+    for out, lse in results:
+        assert torch.equal(out, first)
+    ref, ref_lse = _reference(q, k, v, 3095)
+    diff = (first.float() - ref).abs()
+    assert float(diff.max()) <= MAX_ABS and float(diff.mean()) <= MEAN_ABS, (float(diff.max()), float(diff.mean()))
+    assert float((results[0][1] - ref_lse).abs().max()) <= 2e-2
     assert kernels.device_status() == 0

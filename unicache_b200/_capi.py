@@ -104,6 +104,9 @@ SIGNATURES = {
                                       c_void_p, c_void_p]),
     "ucb_prefill_attention_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int,
                                               c_float, c_void_p, c_void_p, c_void_p]),
+    "ucb_prefill_attention_items": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int,
+                                            c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ucb_prefill_partial_bytes": (ctypes.c_int64, []),
     "ucb_lse_merge": (c_int, [c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int, c_int64, c_int64,
                               c_int64, c_void_p, c_void_p, c_void_p]),
     "ucb_h2o_select": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),

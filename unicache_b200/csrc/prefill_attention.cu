@@ -210,15 +210,35 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 
 // One CTA's problem: query rows [q_row0, q_row0 + q_rows) of KV head `head`
 // (at most 2*BM rows) against keys [k_row0, k_row0 + n_tokens) of that head.
+// mode ITEM_FINAL writes out/lse; a row block whose keys are split in two
+// runs as an ITEM_PARTIAL item (writes its normalised fp32 rows and log2 LSE
+// to partial slot `slot`, then sets flags[slot]) and an ITEM_MERGE item (waits
+// for flags[slot], merges that partial with its own result by LSE, writes
+// out/lse and clears the flag for the next launch).
 struct WorkItem {
-  int head, q_row0, q_rows, k_row0, n_tokens, pad[3];
+  int head, q_row0, q_rows, k_row0, n_tokens, mode, slot, pad;
 };
+constexpr int ITEM_FINAL = 0, ITEM_PARTIAL = 1, ITEM_MERGE = 2;
+constexpr int PARTIAL_SLOT_FLOATS = 2 * BM * D + 2 * BM;  // O [D][256 rows], then log2 LSE [256]
+
+__device__ __forceinline__ bool wait_flag(const unsigned int* flag, uint64_t budget_ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v != 0) return true;
+    if (global_timer_ns() - t0 > budget_ns) return false;
+    __nanosleep(256);
+  }
+}
 
 struct Params {
   int m_rows;        // query rows per head in q / out / lse (row stride of the head)
   int n_tokens;      // key tokens per head (single-problem launches)
   float scale_log2;  // softmax scale * log2(e)
   const WorkItem* items;  // per-CTA problems (batched launches), or null: CTA (x, y) = rows 2*BM*x.. of head y
+  float* partials;        // PARTIAL_SLOT_FLOATS per slot (split row blocks), or null
+  unsigned int* flags;    // one per slot, zero between launches, or null
   __nv_bfloat16* out;  // [heads, m_rows, D]
   float* lse;          // [heads, m_rows], may be null
   unsigned int* err;
@@ -229,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int head, m0, m_end, k0, n_tokens;
+  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0;
   if (P.items) {
     const WorkItem it = P.items[blockIdx.x];
     head = it.head;
@@ -237,6 +257,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     m_end = it.q_row0 + it.q_rows;
     k0 = it.k_row0;
     n_tokens = it.n_tokens;
+    mode = it.mode;
+    slot = it.slot;
+    if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
+      if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+      mode = ITEM_FINAL;
+    }
   } else {
     head = blockIdx.y;
     m0 = blockIdx.x * 2 * BM;
@@ -434,31 +460,78 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok && n_tiles > 0) ok = mbar_wait_for(&o_done[x], (n_tiles - 1) & 1, WAIT_NS);
     tc_fence_after();
-    if (__all_sync(0xffffffffu, ok)) {
+    const bool good = __all_sync(0xffffffffu, ok);
+    const int r_blk = x * BM + row;  // row within the item's 2*BM-row block
+    const int m = m0 + r_blk;
+    float* part = P.partials + (int64_t)slot * PARTIAL_SLOT_FLOATS;
+    bool merged = false;
+    if (!good) {
+      if (lane == 0) fail();
+    } else if (mode == ITEM_PARTIAL) {
       const float inv = 1.f / l_run;
-      const int m = m0 + x * BM + row;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ov[32];
+        tc_ld32(t_o + 32 * c, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) part[(32 * c + i) * (2 * BM) + r_blk] = __uint_as_float(ov[i]) * inv;
+      }
+      part[D * 2 * BM + r_blk] = m_run + __log2f(l_run);
+      __threadfence();
+    } else {
+      // ITEM_FINAL, or ITEM_MERGE: fold in the partner's rows once published.
+      float w_own = 1.f, w_p = 0.f, lse2 = m_run + __log2f(l_run);
+      if (mode == ITEM_MERGE) {
+        merged = __all_sync(0xffffffffu, wait_flag(P.flags + slot, WAIT_NS));
+        if (!merged) {
+          if (lane == 0) fail();
+        } else {
+          const float lp = __ldcg(part + D * 2 * BM + r_blk);
+          const float mx = fmaxf(lse2, lp);
+          w_own = fast_exp2(lse2 - mx);
+          w_p = fast_exp2(lp - mx);
+          const float sum = w_own + w_p;
+          lse2 = mx + __log2f(sum);
+          w_own /= sum;
+          w_p /= sum;
+        }
+      }
+      const float inv = w_own / l_run;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t ov[32];
         tc_ld32(t_o + 32 * c, ov);
         tc_wait_ld();
         if (m < m_end) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __uint_as_float(ov[i]) * inv;
+            if (merged) v[i] = fmaf(w_p, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
+          }
           __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
-            v.y = pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
-            v.z = pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
-            v.w = pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + i) = v;
+            uint4 w4;
+            w4.x = pack_bf16x2(v[i], v[i + 1]);
+            w4.y = pack_bf16x2(v[i + 2], v[i + 3]);
+            w4.z = pack_bf16x2(v[i + 4], v[i + 5]);
+            w4.w = pack_bf16x2(v[i + 6], v[i + 7]);
+            *reinterpret_cast<uint4*>(dst + i) = w4;
           }
         }
       }
-      if (m < m_end && P.lse)
-        P.lse[(int64_t)head * P.m_rows + m] = (m_run + __log2f(l_run)) * 0.6931471805599453f;
-    } else if (lane == 0) {
-      fail();
+      if (m < m_end && P.lse) P.lse[(int64_t)head * P.m_rows + m] = lse2 * 0.6931471805599453f;
+    }
+    // The softmax warps meet once: a partial is published after every row
+    // is written; a consumed partial's flag is cleared after every row read.
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (tid == 0) {
+      if (mode == ITEM_PARTIAL && good)
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(P.flags + slot), "r"(1u) : "memory");
+      else if (mode == ITEM_MERGE && merged)
+        P.flags[slot] = 0u;
     }
   }
   tc_fence_before();
@@ -542,25 +615,43 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   P.n_tokens = n_tokens;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
   P.items = nullptr;
+  P.partials = nullptr;
+  P.flags = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3((m_rows + 2 * BM - 1) / (2 * BM), heads), stream);
 }
 
-extern "C" int ucb_prefill_attention_batched(const void* q, const void* k, const void* vt, int heads, int m_rows,
-                                             int n_padded, const void* items, int num_items, float softmax_scale,
-                                             void* out, float* lse, void* stream) {
+extern "C" int ucb_prefill_attention_items(const void* q, const void* k, const void* vt, int heads, int m_rows,
+                                           int n_padded, const void* items, int num_items, float softmax_scale,
+                                           void* out, float* lse, float* partials, unsigned int* flags,
+                                           void* stream) {
   using namespace ucb::prefill;
   if (!q || !k || !vt || !out || !items)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_batched: null pointer");
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_items: null pointer");
   if (heads <= 0 || m_rows <= 0 || n_padded <= 0 || num_items <= 0)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_batched: empty problem");
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_items: empty problem");
+  if ((partials == nullptr) != (flags == nullptr))
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention_items: partials and flags go together");
   Params P;
   P.m_rows = m_rows;
   P.n_tokens = 0;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
   P.items = static_cast<const WorkItem*>(items);
+  P.partials = partials;
+  P.flags = flags;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3(num_items), stream);
+}
+
+extern "C" int ucb_prefill_attention_batched(const void* q, const void* k, const void* vt, int heads, int m_rows,
+                                             int n_padded, const void* items, int num_items, float softmax_scale,
+                                             void* out, float* lse, void* stream) {
+  return ucb_prefill_attention_items(q, k, vt, heads, m_rows, n_padded, items, num_items, softmax_scale, out, lse,
+                                     nullptr, nullptr, stream);
+}
+
+extern "C" int64_t ucb_prefill_partial_bytes() {
+  return (int64_t)ucb::prefill::PARTIAL_SLOT_FLOATS * (int64_t)sizeof(float);
 }

@@ -703,9 +703,81 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, n_toke
         out = torch.empty_like(q)
     if lse is None:
         lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
-    call("ucb_prefill_attention", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, int(n_tokens),
-         n_padded, scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    split = _key_split_launch(q.device, heads, m_rows, int(n_tokens), n_padded, stream_of(q))
+    if split is None:
+        call("ucb_prefill_attention", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, int(n_tokens),
+             n_padded, scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    else:
+        items, partials, flags = split
+        call("ucb_prefill_attention_items", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, n_padded,
+             items.data_ptr(), int(items.shape[0]), scale, out.data_ptr(), lse.data_ptr(), partials.data_ptr(),
+             flags.data_ptr(), stream_of(q))
     return out, lse
+
+
+PREFILL_ROWS_PER_CTA = 256
+PREFILL_KEY_TILE = 128
+_KEY_SPLITS: dict = {}
+
+
+PREFILL_CTA_FIXED_TILES = 4.0  # a CTA's set-up, pipeline fill and epilogue, in key-tile times (measured)
+
+
+def plan_key_split(row_blocks: int, key_tiles: int, sms: int) -> int | None:
+    """Key tiles of the first part when splitting every row block's keys in
+    two fills the GPU better than one CTA per row block, else None.
+
+    With R < SMs row blocks of T key tiles, one CTA each leaves SMs idle for
+    its whole F + T tile times (F: a CTA's fixed cost, about 4 tile times on
+    B200).  Split, the R first parts (L tiles) start at once and the R second
+    parts (T - L tiles) run on the SMs - R others in ceil(R / (SMs - R))
+    rounds; the first parts then merge their partner's result (about half a
+    tile).  The plan minimises max(F + L + 1/2, rounds * (F + T - L)) and is
+    kept only if it saves at least one tile time."""
+
+    free = sms - row_blocks
+    if free <= 0 or key_tiles < 2 or row_blocks <= 0:
+        return None
+    rounds = -(-row_blocks // free)
+    fixed = PREFILL_CTA_FIXED_TILES
+    whole = fixed + key_tiles
+    best_l, best = None, whole
+    for first in range(1, key_tiles):
+        cost = max(fixed + first + 0.5, rounds * (fixed + key_tiles - first))
+        if cost < best:
+            best, best_l = cost, first
+    return best_l if best_l is not None and best <= whole - 1 else None
+
+
+def _key_split_launch(device, heads: int, m_rows: int, n_tokens: int, n_padded: int, stream: int):
+    """(items, partials, flags) of a key-split launch, cached per shape and
+    stream (the flags return to zero after every launch), or None."""
+
+    key = (device.index, heads, m_rows, n_tokens, n_padded, stream)
+    if key in _KEY_SPLITS:
+        return _KEY_SPLITS[key]
+    blocks_per_head = -(-m_rows // PREFILL_ROWS_PER_CTA)
+    row_blocks = heads * blocks_per_head
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    first = plan_key_split(row_blocks, -(-n_tokens // PREFILL_KEY_TILE), sms)
+    if first is None:
+        _KEY_SPLITS[key] = None
+        return None
+    split_at = first * PREFILL_KEY_TILE
+    merge_items, partial_items = [], []
+    for h in range(heads):
+        for b in range(blocks_per_head):
+            slot = len(merge_items)
+            q0 = b * PREFILL_ROWS_PER_CTA
+            rows = min(PREFILL_ROWS_PER_CTA, m_rows - q0)
+            merge_items.append([h, q0, rows, 0, split_at, 2, slot, 0])
+            partial_items.append([h, q0, rows, split_at, n_tokens - split_at, 1, slot, 0])
+    items = torch.tensor(merge_items + partial_items, dtype=torch.int32).to(device)
+    slot_floats = int(_capi.load().ucb_prefill_partial_bytes()) // 4
+    partials = torch.empty(row_blocks * slot_floats, device=device, dtype=torch.float32)
+    flags = torch.zeros(row_blocks, device=device, dtype=torch.int32)
+    _KEY_SPLITS[key] = (items, partials, flags)
+    return _KEY_SPLITS[key]
 
 
 def prefill_attention_batched(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, items: torch.Tensor, *,
