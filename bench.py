@@ -326,7 +326,7 @@ def run_reference(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * total / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if WORKLOAD == "config3split" else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
@@ -565,7 +565,7 @@ def run_split(args) -> None:
     import torch.distributed as dist
 
     from unicache_b200 import PackedKIVICache, kernels
-    from unicache_b200.distributed import SequenceSplitDecode, split_tokens
+    from unicache_b200.distributed import PeerExchange, SequenceSplitDecode, split_tokens
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -584,7 +584,8 @@ def run_split(args) -> None:
     replicas_n = max(2, math.ceil(256e6 / local_bytes))
     gen = torch.Generator(device=device).manual_seed(4321 + 7919 * rank)
     outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(device)
-    decoders = []
+    decoders, nccl_decoders = [], []
+    peer = PeerExchange(Q_HEADS, device) if world > 1 else None
     for _ in range(replicas_n):
         k = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=device)
         k[:, :, outlier] *= 10.0
@@ -594,7 +595,9 @@ def run_split(args) -> None:
                                            token_type_id=3, k_bits=BITS, v_bits=BITS, group_size=GROUP,
                                            residual_length=residual)
         del k, v
-        decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group))
+        decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group,
+                                            exchange="peer", peer_exchange=peer))
+        nccl_decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group))
     torch.cuda.empty_cache()
     qgen = torch.Generator(device=device).manual_seed(99)  # every rank decodes the same query
     query = torch.randn(1, Q_HEADS, HEAD_DIM, generator=qgen, device=device).to(torch.bfloat16)
@@ -621,31 +624,39 @@ def run_split(args) -> None:
 
     # eager per-call steps (also warm the NCCL communicator before capture)
     eager_elapsed = timed(lambda i: decoders[i % replicas_n](query))
+    timed(lambda i: nccl_decoders[i % replicas_n](query))
     local_elapsed = timed(lambda i: decoders[i % replicas_n].plan.run(query))
-    # device-timed region: the K steps (decode, state merge, all-gather, LSE
-    # merge each) captured once in a CUDA graph, NCCL included
-    capture_stream = torch.cuda.Stream(device=device)
-    capture_stream.wait_stream(torch.cuda.current_stream(device))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(capture_stream):
-        with torch.cuda.graph(graph, stream=capture_stream):
-            for i in range(args.steps):
-                decoders[i % replicas_n](query)
-    torch.cuda.current_stream(device).wait_stream(capture_stream)
-    graph.replay()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    g0 = torch.cuda.Event(enable_timing=True)
-    g1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        g0.record()
+
+    def graph_timed(decs):
+        # the K steps captured once in a CUDA graph (the exchange included)
+        capture_stream = torch.cuda.Stream(device=device)
+        capture_stream.wait_stream(torch.cuda.current_stream(device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(capture_stream):
+            with torch.cuda.graph(graph, stream=capture_stream):
+                for i in range(args.steps):
+                    decs[i % replicas_n](query)
+        torch.cuda.current_stream(device).wait_stream(capture_stream)
         graph.replay()
-        g1.record()
         torch.cuda.synchronize()
-    barrier()
-    elapsed = g0.elapsed_time(g1) / 1000.0
-    del graph  # released before the process group is destroyed
+        barrier()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as sampler:
+            g0.record()
+            graph.replay()
+            g1.record()
+            torch.cuda.synchronize()
+        barrier()
+        del graph  # released before the process group is destroyed
+        return g0.elapsed_time(g1) / 1000.0, sampler
+
+    # device-timed region: decode, state merge and the peer-memory exchange +
+    # merge kernel per step; the NCCL exchange is timed the same way for
+    # comparison
+    elapsed, clocks = graph_timed(decoders)
+    nccl_elapsed, _ = graph_timed(nccl_decoders)
     host_q = query.cpu().pin_memory()
     host_o = torch.empty(query.shape, dtype=query.dtype).pin_memory()
     host_l = torch.empty((1, Q_HEADS), dtype=torch.float32).pin_memory()
@@ -660,11 +671,11 @@ def run_split(args) -> None:
     e2e_elapsed = timed(e2e_step)
     status = kernels.device_status()
     if world > 1:
-        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, eager_elapsed, float(status)], device=device,
-                         dtype=torch.float64)
+        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, eager_elapsed, nccl_elapsed, float(status)],
+                         device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, local_elapsed, e2e_elapsed, eager_elapsed, status = (float(t[0]), float(t[1]), float(t[2]),
-                                                                      float(t[3]), int(t[4]))
+        elapsed, local_elapsed, e2e_elapsed, eager_elapsed, nccl_elapsed, status = (
+            float(t[0]), float(t[1]), float(t[2]), float(t[3]), float(t[4]), int(t[5]))
     total_bytes = shard_bytes(TOKENS, RESIDUAL)
     if rank == 0:
         step_s = elapsed / args.steps
@@ -689,7 +700,8 @@ def run_split(args) -> None:
                              f"tokens split over {world} GPU(s), 28/4 heads, D=128"),
                 "global_batch": 1,
                 "seq_len": TOKENS + RESIDUAL,
-                "parallelism": f"sequence-split x{world} + NCCL all-gather of (out, LSE) + LSE merge",
+                "parallelism": (f"sequence-split x{world} + one kernel: epoch-tagged peer stores of (out, LSE) "
+                                f"over NVLink + LSE merge" if world > 1 else "one GPU"),
                 "l2": f"steps rotate over {replicas_n} shard replicas ({replicas_n * local_bytes / 1e6:.0f} MB per GPU > 126 MB L2)",
             },
             "hbm_gbs": achieved,
@@ -703,10 +715,11 @@ def run_split(args) -> None:
                 "traffic": None,
                 "algorithmic_bytes_per_launch": total_bytes // world,
                 "kernel_ms": 1000.0 * step_s,
-                "kernel": "per GPU: shard decode + state merge + all-gather + LSE merge, one graph replay of K steps",
+                "kernel": "per GPU: shard decode + state merge + peer exchange/merge, one graph replay of K steps",
             },
             "local_decode_ms_per_step": 1000.0 * local_elapsed / args.steps,
             "eager_ms_per_step": 1000.0 * eager_elapsed / args.steps,
+            "nccl_exchange_ms_per_step": 1000.0 * nccl_elapsed / args.steps,
             "e2e": {"value": args.steps / e2e_elapsed, "unit": "tokens/s",
                     "h2d_bytes_per_step": query.numel() * query.element_size(),
                     "d2h_bytes_per_step": host_o.numel() * host_o.element_size() + host_l.numel() * 4,
@@ -719,6 +732,9 @@ def run_split(args) -> None:
                                        f"float64 attention), timed on one of the {KV_HEADS} KV heads and scaled x{KV_HEADS}"},
         }
         print(json.dumps(line))
+    if peer is not None:
+        torch.cuda.synchronize()
+        peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -737,6 +753,9 @@ WORKLOADS = {
 
 
 def workload_name() -> str:
+    if WORKLOAD == "config3split":
+        return (f"{WORKLOAD}: one sequence of {TOKENS} packed KIVI {BITS}-bit G{GROUP} + {RESIDUAL} bf16 tokens "
+                f"split over the GPUs, 28/4 heads, D=128")
     return (f"{WORKLOAD}: packed KIVI {BITS}-bit G{GROUP} decode, {BATCH} seqs/GPU, T={TOKENS}+{RESIDUAL} "
             f"bf16 residual, 28/4 heads, D=128")
 

@@ -285,6 +285,31 @@ UCB_API int ucb_prefill_attention_items(const void* q_dev, const void* k_dev, co
                                         unsigned int* flags_dev, void* stream);
 UCB_API int64_t ucb_prefill_partial_bytes(void);
 
+/* ---- sequence-split merge over NVLink peer memory (no counterpart in the
+ * reference, which decodes one sequence on one device).  Each rank allocates
+ * one exchange buffer of ucb_peer_buffer_bytes(rows) bytes
+ * (ucb_peer_buffer_alloc: cudaMalloc'd, zeroed, with a 64-byte CUDA IPC
+ * handle), shares the handle with its peers (for example through the process
+ * group) and maps theirs with ucb_peer_buffer_open.  ucb_split_merge_peer then
+ * replaces the all-gather + ucb_lse_merge of a split decode step: rank `rank`
+ * sends its summary (out_local [rows, 128] bf16, lse_local [rows] fp32,
+ * natural log; rows = B * Hq) into every peer's buffer as 8-byte peer stores
+ * that each carry 4 data bytes and the step's epoch, reads the peers' words
+ * from its own buffer as their epochs arrive (at most 1 s; on expiry it sets
+ * the device error word and leaves out/lse unwritten) and merges the world
+ * summaries in rank order as ucb_lse_merge does into out/lse.
+ * bufs: host array of `world` buffer addresses as mapped in this process
+ * (bufs[rank] is the local one); world <= 8.  Every rank must make the same
+ * sequence of calls; one call per buffer at a time. */
+UCB_API int64_t ucb_peer_buffer_bytes(int64_t rows);
+UCB_API int ucb_peer_buffer_alloc(int64_t bytes, void** ptr, void* handle_out);
+UCB_API int ucb_peer_buffer_open(const void* handle, void** ptr);
+UCB_API int ucb_peer_buffer_close(void* ptr);
+UCB_API int ucb_peer_buffer_free(void* ptr);
+UCB_API int ucb_split_merge_peer(int rank, int world, void* const* bufs, const void* out_local,
+                                 const float* lse_local, int64_t rows, int head_dim, void* out, float* lse,
+                                 void* stream);
+
 /* ------------------------------------------------------------------ LSE merge
  * Replaces merge_attention_summaries (unicache/adapters/bagel.py:57-72).
  * n summaries, summary i: out_ptrs[i] -> [rows, heads, head_dim] (dtype),

@@ -93,6 +93,19 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
         assert torch.equal(out, out2) and torch.equal(lse, lse2)
         for b, (k, v) in enumerate(kvs):
             _check(out[b:b + 1], lse[b:b + 1], _oracle(k, v, query[b:b + 1], world))
+        # the same step through the peer-memory exchange (one kernel:
+        # epoch-tagged peer stores, then the merge) equals the NCCL exchange
+        # bit for bit, call after call (epochs advance, slot parities alternate)
+        peer = SequenceSplitDecode([[_shard_cache(k, v, start, stop, rank == world - 1)] for k, v in kvs],
+                                   num_kv_heads=HEADS, exchange="peer")
+        for _ in range(4):
+            po, pl = peer(query)
+            torch.cuda.synchronize()
+            assert torch.equal(po, out) and torch.equal(pl, lse)
+        from unicache_b200 import kernels
+
+        assert kernels.device_status() == 0
+        peer.close()
         open(os.path.join(result_dir, f"ok{rank}"), "w").close()
     finally:
         dist.destroy_process_group()

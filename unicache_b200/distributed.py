@@ -88,6 +88,71 @@ def merge_rank_summaries(outs: list, lses: list) -> tuple[torch.Tensor, torch.Te
     return merged, total.t().contiguous()
 
 
+class PeerExchange:
+    """This rank's exchange buffer for ``ucb_split_merge_peer``, mapped on
+    every rank of ``group`` through CUDA IPC handles.
+
+    Construction and ``close`` are collective (every rank calls them in the
+    same order).  ``merge(out, lse)`` exchanges and merges one decode step's
+    summaries (out [B, Hq, 128] bf16, lse [B, Hq] fp32) in one kernel on the
+    current stream: epoch-tagged peer stores over NVLink, a bounded wait and
+    the LSE merge."""
+
+    def __init__(self, rows: int, device: torch.device, group=None):
+        from . import _capi
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the peer exchange serves at most 8 ranks")
+        self.rows = int(rows)
+        nbytes = int(_capi.load().ucb_peer_buffer_bytes(self.rows))
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            kernels.call("ucb_peer_buffer_alloc", nbytes, ctypes.byref(own), handle)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._own = own.value
+            self._opened = []
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                kernels.call("ucb_peer_buffer_open", ctypes.create_string_buffer(h, 64), ctypes.byref(peer))
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+            dist.barrier(group=group)  # every mapping exists before the first exchange
+        self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+
+    def merge(self, out: torch.Tensor, lse: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        b, hq, d = map(int, out.shape)
+        if b * hq != self.rows or d != 128 or out.dtype != torch.bfloat16 or lse.dtype != torch.float32:
+            raise ValueError("summary shape differs from the exchange buffer's")
+        out = out.contiguous()
+        lse = lse.contiguous()
+        merged = torch.empty_like(out)
+        total = torch.empty_like(lse)
+        kernels.call("ucb_split_merge_peer", self.rank, self.world, self._bufs, out.data_ptr(), lse.data_ptr(),
+                     self.rows, d, merged.data_ptr(), total.data_ptr(), kernels.stream_of(out))
+        return merged, total
+
+    def close(self) -> None:
+        """Collective: every rank unmaps its peers' buffers, then frees its own."""
+
+        if self._bufs is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            kernels.call("ucb_peer_buffer_close", ctypes.c_void_p(p))
+        dist.barrier(group=self.group)
+        kernels.call("ucb_peer_buffer_free", ctypes.c_void_p(self._own))
+        self._bufs = None
+
+
 class SequenceSplitDecode:
     """Decode of sequences whose tokens are split across ranks.
 
@@ -105,10 +170,16 @@ class SequenceSplitDecode:
     buffers: steps are ordered on the stream, so a step's merge has read the
     receive buffer before the next step's all-gather overwrites it."""
 
-    def __init__(self, local_sequences: list[list], *, num_kv_heads: int, head_dim: int = 128, group=None):
+    def __init__(self, local_sequences: list[list], *, num_kv_heads: int, head_dim: int = 128, group=None,
+                 exchange: str = "nccl", peer_exchange: "PeerExchange | None" = None):
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
         self.plan = kernels.build_decode_plan(local_sequences, num_kv_heads=num_kv_heads, head_dim=head_dim)
         self.group = group
+        self.exchange = exchange
         self._buffers = None  # (q_heads, send, recv, out view, lse view, out pointers, lse pointers, world)
+        self._peer = peer_exchange  # may be shared by decoders that run in order on one stream
+        self._owns_peer = peer_exchange is None
 
     def _setup(self, query: torch.Tensor):
         b, hq, d = map(int, query.shape)
@@ -130,6 +201,12 @@ class SequenceSplitDecode:
             return self.plan.run(query)
         if query.dtype != torch.bfloat16 or query.dim() != 3:
             raise ValueError("query must be bfloat16 [B, Hq, D]")
+        if self.exchange == "peer":
+            # one kernel: epoch-tagged peer stores of this rank's summary + merge
+            if self._peer is None:
+                self._peer = PeerExchange(int(query.shape[0]) * int(query.shape[1]), query.device, self.group)
+            out, lse = self.plan.run(query)
+            return self._peer.merge(out, lse)
         if self._buffers is None or self._buffers[0] != int(query.shape[1]) or \
                 self._buffers[1].device != query.device:
             self._setup(query)
@@ -142,3 +219,10 @@ class SequenceSplitDecode:
         kernels.call("ucb_lse_merge", world, optrs, lptrs, kernels.dtype_code(torch.bfloat16), 1, b * hq, d,
                      merged.data_ptr(), total.data_ptr(), kernels.stream_of(query))
         return merged, total
+
+    def close(self) -> None:
+        """Collective when this decoder created a peer exchange: releases it."""
+
+        if self._peer is not None and self._owns_peer:
+            self._peer.close()
+        self._peer = None
