@@ -16,6 +16,12 @@ Multi-GPU (torchrun): requests are batch-partitioned -- every rank decodes its
 own 16 sequences, no collective in the timed loop (weak scaling); the step time
 is the max over ranks.
 
+--workload config3 is config 3's per-GPU batch (8 sequences of 32768 + 128
+tokens, 4-bit, group 64); --workload config3split is its long-context half:
+ONE 131072 + 128-token sequence split over the ranks (strong scaling), each
+step ending with the exchange of every rank's (out, LSE) over NVLink peer
+memory and the LSE merge (the NCCL all-gather variant is timed beside it).
+
 Reported: value = decode tokens/s (whole job); e2e = the same through the
 public API (DecodeStepGraph) with the query copied from pinned host memory and
 the output and LSE read back every step (e2e_eager: the same through per-call
