@@ -28,17 +28,22 @@ __device__ __forceinline__ uint32_t quant_code(float v, float mn, float scale, f
   return static_cast<uint32_t>(q);
 }
 
-// Same result as quant_code.  |d * RN(1/scale) - RN(d/scale)| < 2^-22 * q,
-// which is below 2^-14 for q < 2^8, so a product more than 2^-12 away from a
-// half-integer rounds to the same integer; the rare products closer than that
-// (or q >= 2^8) take the exact division.
-__device__ __forceinline__ uint32_t quant_code_fast(float v, float mn, float scale, float inv_scale, float max_code) {
-  const float d = __fsub_rn(v, mn);
-  const float q = __fmul_rn(d, inv_scale);
-  float c = rintf(q);
-  if (!(0.5f - fabsf(q - c) > 0x1p-12f) || q >= 256.0f) c = rintf(__fdiv_rn(d, scale));
-  c = fminf(fmaxf(c, 0.0f), max_code);
-  return static_cast<uint32_t>(c);
+// Two codes with the same results as quant_code, without a division per
+// element: |d * RN(1/scale) - RN(d/scale)| < 2^-22 * q, below 2^-14 for
+// q < 2^8, so a product more than 2^-12 away from a half-integer rounds to the
+// same integer; the rare products closer than that (or q >= 2^8) take the
+// exact division.  The subtraction and the product run as packed fp32 pairs
+// (each lane rounds like the scalar operation).
+__device__ __forceinline__ uint2 quant_code_fast2(float va, float vb, float mna, float mnb, float sca, float scb,
+                                                  float inva, float invb, float max_code) {
+  const float2 d = __fadd2_rn(make_float2(va, vb), make_float2(-mna, -mnb));
+  const float2 q = __fmul2_rn(d, make_float2(inva, invb));
+  float ca = rintf(q.x), cb = rintf(q.y);
+  if (!(0.5f - fabsf(q.x - ca) > 0x1p-12f) || q.x >= 256.0f) ca = rintf(__fdiv_rn(d.x, sca));
+  if (!(0.5f - fabsf(q.y - cb) > 0x1p-12f) || q.y >= 256.0f) cb = rintf(__fdiv_rn(d.y, scb));
+  ca = fminf(fmaxf(ca, 0.0f), max_code);
+  cb = fminf(fmaxf(cb, 0.0f), max_code);
+  return make_uint2(static_cast<uint32_t>(ca), static_cast<uint32_t>(cb));
 }
 
 // ---------------------------------------------------------------- key pack
@@ -99,8 +104,10 @@ __device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t s
       uint8_t* out = codes8 + (static_cast<int64_t>(h) * tokens + static_cast<int64_t>(g) * G + c0) * head_dim + d;
 #pragma unroll
       for (int i = 0; i < CH; ++i)
-        *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) = static_cast<uint16_t>(
-            quant_code_fast(a[i], mna, sca, inva, kMax) | (quant_code_fast(b[i], mnb, scb, invb, kMax) << 8));
+      {
+        const uint2 c = quant_code_fast2(a[i], b[i], mna, mnb, sca, scb, inva, invb, kMax);
+        *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) = static_cast<uint16_t>(c.x | (c.y << 8));
+      }
     } else {
       constexpr int F = 32 / BITS;
       uint32_t* out = codes32 + (static_cast<int64_t>(h) * (tokens / F) + (static_cast<int64_t>(g) * G + c0) / F) *
@@ -110,8 +117,9 @@ __device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t s
         uint32_t wa = 0, wb = 0;
 #pragma unroll
         for (int j = 0; j < F; ++j) {
-          wa |= quant_code_fast(a[w * F + j], mna, sca, inva, kMax) << (j * BITS);
-          wb |= quant_code_fast(b[w * F + j], mnb, scb, invb, kMax) << (j * BITS);
+          const uint2 c = quant_code_fast2(a[w * F + j], b[w * F + j], mna, mnb, sca, scb, inva, invb, kMax);
+          wa |= c.x << (j * BITS);
+          wb |= c.y << (j * BITS);
         }
         *reinterpret_cast<uint2*>(out + static_cast<int64_t>(w) * head_dim) = make_uint2(wa, wb);
       }
@@ -181,7 +189,10 @@ __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t
       for (int q = 0; q < 4; ++q) {
         w[q] = 0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) w[q] |= quant_code_fast(v[c + 4 * q + j], mn, sc, inv, kMax) << (8 * j);
+        for (int j = 0; j < 4; j += 2) {
+          const uint2 cc = quant_code_fast2(v[c + 4 * q + j], v[c + 4 * q + j + 1], mn, mn, sc, sc, inv, inv, kMax);
+          w[q] |= (cc.x << (8 * j)) | (cc.y << (8 * (j + 1)));
+        }
       }
       *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -193,7 +204,10 @@ __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t
     for (int k = 0; k < W; ++k) {
       w[k] = 0;
 #pragma unroll
-      for (int j = 0; j < F; ++j) w[k] |= quant_code_fast(v[k * F + j], mn, sc, inv, kMax) << (j * BITS);
+      for (int j = 0; j < F; j += 2) {
+        const uint2 cc = quant_code_fast2(v[k * F + j], v[k * F + j + 1], mn, mn, sc, sc, inv, inv, kMax);
+        w[k] |= (cc.x << (j * BITS)) | (cc.y << ((j + 1) * BITS));
+      }
     }
     uint32_t* out = codes32 + out_row * (D / F) + gi * W;
 #pragma unroll
