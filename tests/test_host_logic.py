@@ -105,3 +105,26 @@ def test_backend_names():
         normalize_backend("reference")
     with pytest.raises(ValueError):
         normalize_backend("triton")
+
+
+def test_key_split_plan():
+    """plan_key_split: no split once row blocks fill the SMs or when it saves
+    less than a tile time; otherwise the first part leaves room for the
+    second parts on the free SMs (config 4: 112 row blocks of 25 tiles on
+    148 SMs -> 23 + 2; a single 4-block problem -> 12 + 13)."""
+    from unicache_b200.kernels import PREFILL_CTA_FIXED_TILES as F
+    from unicache_b200.kernels import plan_key_split
+
+    assert plan_key_split(148, 25, 148) is None
+    assert plan_key_split(200, 25, 148) is None
+    assert plan_key_split(10, 1, 148) is None
+    assert plan_key_split(112, 25, 148) == 23
+    assert plan_key_split(4, 25, 148) == 12
+    for rows, tiles in [(1, 8), (8, 8), (40, 64), (112, 128), (147, 30)]:
+        first = plan_key_split(rows, tiles, 148)
+        if first is None:
+            continue
+        assert 1 <= first < tiles
+        rounds = -(-rows // (148 - rows))
+        cost = max(F + first + 0.5, rounds * (F + tiles - first))
+        assert cost <= F + tiles - 1
