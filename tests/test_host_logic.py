@@ -128,3 +128,20 @@ def test_key_split_plan():
         rounds = -(-rows // (148 - rows))
         cost = max(F + first + 0.5, rounds * (F + tiles - first))
         assert cost <= F + tiles - 1
+
+
+def test_split_prefill_items_layout():
+    """Split rows: merge parts first, then unsplit rows, then partial parts;
+    each pair shares a slot and covers its row block's keys exactly once."""
+    from unicache_b200.kernels import split_prefill_items
+
+    rows = [[h, 256 * b, 256, 0, 3095, 0, 0, 0] for h in range(2) for b in range(3)] + [[0, 768, 49, 3136, 16, 0, 0, 0]]
+    out, slots = split_prefill_items(rows, 148)
+    assert slots == 6 and len(out) == 6 + 1 + 6
+    merges, whole, parts = out[:6], out[6:7], out[7:]
+    assert all(r[5] == 2 for r in merges) and all(r[5] == 1 for r in parts) and whole[0][5] == 0
+    for m, p in zip(merges, parts):
+        assert m[6] == p[6] and m[:3] == p[:3]
+        assert p[3] == m[3] + m[4] and m[4] + p[4] == 3095 and m[4] % 128 == 0
+    same, none = split_prefill_items(rows * 30, 148)
+    assert none == 0 and all(r[5] == 0 for r in same)

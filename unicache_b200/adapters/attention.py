@@ -258,8 +258,12 @@ def batched_long_query_attention(queries: list, segments_by_sample: list, *, den
         for h in range(hkv):
             for r in range(0, rows, 256):
                 items.append([h, q0 + r, min(256, rows - r), k0, total, 0, 0, 0])
+    # fewer row blocks than SMs: split keys so the idle SMs take second parts
+    items, slots = kernels.split_prefill_items(items, torch.cuda.get_device_properties(device).multi_processor_count)
     table = torch.tensor(items, dtype=torch.int32).to(device)
-    out, lse = kernels.prefill_attention_batched(qp, kw, vw.transpose(1, 2).contiguous(), table)
+    workspace = kernels.prefill_split_workspace(device, slots, kernels.stream_of(qp)) if slots else None
+    out, lse = kernels.prefill_attention_batched(qp, kw, vw.transpose(1, 2).contiguous(), table,
+                                                 split_workspace=workspace)
     results = []
     for (query, _), (q0, rows, _, _, _) in zip(samples, metas):
         lq, hq = int(query.shape[0]), int(query.shape[1])

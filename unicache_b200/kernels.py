@@ -780,15 +780,56 @@ def _key_split_launch(device, heads: int, m_rows: int, n_tokens: int, n_padded: 
     return _KEY_SPLITS[key]
 
 
+def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
+    """Item rows (head, q_row0, q_rows, k_row0, n_tokens, 0, 0, 0) with each
+    row block's keys split in two where ``plan_key_split`` says it pays
+    (fewer row blocks than SMs): the first parts as merge items (mode 2)
+    first, then the unsplit items, then the second parts as partial items
+    (mode 1), slot i shared by the i-th pair.  Returns (rows, slots)."""
+
+    if len(items) >= sms:
+        return [list(r) for r in items], 0
+    merges, whole, partials = [], [], []
+    for row in items:
+        h, q0, rows, k0, n = (int(x) for x in row[:5])
+        first = plan_key_split(len(items), -(-n // PREFILL_KEY_TILE), sms)
+        if first is None:
+            whole.append([h, q0, rows, k0, n, 0, 0, 0])
+            continue
+        cut = first * PREFILL_KEY_TILE
+        slot = len(merges)
+        merges.append([h, q0, rows, k0, cut, 2, slot, 0])
+        partials.append([h, q0, rows, k0 + cut, n - cut, 1, slot, 0])
+    return merges + whole + partials, len(merges)
+
+
+_SPLIT_WORKSPACES: dict = {}
+
+
+def prefill_split_workspace(device, slots: int, stream: int):
+    """(partials, flags) for ``slots`` split row blocks, cached per device and
+    stream (the flags return to zero after every complete launch)."""
+
+    key = (device.index, stream)
+    ws = _SPLIT_WORKSPACES.get(key)
+    if ws is None or int(ws[1].numel()) < slots:
+        slot_floats = int(_capi.load().ucb_prefill_partial_bytes()) // 4
+        ws = (torch.empty(slots * slot_floats, device=device, dtype=torch.float32),
+              torch.zeros(slots, device=device, dtype=torch.int32))
+        _SPLIT_WORKSPACES[key] = ws
+    return ws
+
+
 def prefill_attention_batched(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, items: torch.Tensor, *,
                               softmax_scale: float | None = None, out: torch.Tensor | None = None,
-                              lse: torch.Tensor | None = None):
+                              lse: torch.Tensor | None = None, split_workspace=None):
     """One launch over several non-causal attention problems sharing the
     tensors q [H, M, 128], k [H, Np, 128], vt [H, 128, Np] (bf16):
     ``items`` is an int32 device tensor [num_items, 8] of (head, q_row0,
-    q_rows <= 256, k_row0 (multiple of 64), n_tokens, 0, 0, 0), one per CTA.
-    Returns (out [H, M, 128] bf16, lse [H, M] fp32); rows no item covers are
-    left unwritten."""
+    q_rows <= 256, k_row0 (multiple of 64), n_tokens, mode, slot, 0), one per
+    CTA; items of modes 1 and 2 (see ``split_prefill_items``) need
+    ``split_workspace`` = (partials, flags).  Returns (out [H, M, 128] bf16,
+    lse [H, M] fp32); rows no item covers are left unwritten."""
 
     for name, t in (("q", q), ("k", k), ("vt", vt), ("items", items)):
         require_cuda(t, name)
@@ -807,8 +848,14 @@ def prefill_attention_batched(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor
         out = torch.empty_like(q)
     if lse is None:
         lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
-    call("ucb_prefill_attention_batched", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, n_padded,
-         items.data_ptr(), int(items.shape[0]), scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    if split_workspace is None:
+        call("ucb_prefill_attention_batched", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, n_padded,
+             items.data_ptr(), int(items.shape[0]), scale, out.data_ptr(), lse.data_ptr(), stream_of(q))
+    else:
+        partials, flags = split_workspace
+        call("ucb_prefill_attention_items", q.data_ptr(), k.data_ptr(), vt.data_ptr(), heads, m_rows, n_padded,
+             items.data_ptr(), int(items.shape[0]), scale, out.data_ptr(), lse.data_ptr(), partials.data_ptr(),
+             flags.data_ptr(), stream_of(q))
     return out, lse
 
 
