@@ -201,8 +201,12 @@ UCB_API int ucb_decode_attention(const void* query_dev, int64_t query_stride, in
  * allocations): the warp-state slots come from one static device array of
  * 2,129,920 bytes that the library holds on every GPU it is loaded on until
  * exit, so the plan may use at most 512 slots (num_partials = sum of
- * partial_count); larger plans get UCB_ERR_INVALID.  The caller still passes
- * the plan tables, the query and the outputs.  It calls no cudaMalloc or
+ * partial_count); larger plans get UCB_ERR_INVALID.  Every slot index in
+ * warp_slots_dev and every pair's [partial_begin, partial_begin +
+ * partial_count) must lie below num_partials: the kernels check each index
+ * against it, and one that does not is skipped and sets flag 2 (an invalid
+ * descriptor, read with ucb_device_status) instead of writing past the array.  The caller
+ * still passes the plan tables, the query and the outputs.  It calls no cudaMalloc or
  * cudaFree.  The first call on a device looks up the array's address (set-up);
  * make that call before any stream capture.  Every call shares the one array
  * (each slot it reads is written earlier in the same call, so nothing needs
@@ -271,11 +275,14 @@ UCB_API int ucb_prefill_attention_batched(const void* q_dev, const void* k_dev, 
  * the reference, whose varlen FlashAttention call schedules itself).  The
  * mode-1 item (keys [k_row0, k_row0 + n_tokens) of the second part) writes
  * its normalised fp32 rows and log2 LSE to partials_dev slot `slot`
- * (ucb_prefill_partial_bytes() each) and then sets flags_dev[slot]; the
- * mode-2 item of the same rows (the first part) waits for that flag (bounded:
- * on expiry it sets the device error word), merges the two results by LSE
- * into out/lse and clears the flag.  flags_dev must be zero before the first
- * launch and is zero again after every complete launch.  Mode-2 items must be
+ * (ucb_prefill_partial_bytes() each) and then adds 1 to flags_dev[slot]
+ * (making it odd); the mode-2 item of the same rows (the first part) waits
+ * for the flag to be odd (bounded: on expiry it sets the device error word),
+ * merges the two results by LSE into out/lse and adds 1 again.  Both items add
+ * exactly once per launch, a timed-out one included, so flags_dev must be even
+ * (e.g. zero) before the first launch and is even again after every launch,
+ * and a partial that lands late in a failed launch is never mistaken for the
+ * next launch's.  Mode-2 items must be
  * fewer than the SMs, so that their partners always find an SM; list them
  * first so they start first.  partials_dev and flags_dev may be NULL when no
  * item uses modes 1 or 2. */
@@ -297,7 +304,8 @@ UCB_API int64_t ucb_prefill_partial_bytes(void);
  * that each carry 4 data bytes and the step's epoch, reads the peers' words
  * from its own buffer as their epochs arrive (at most 1 s; on expiry it sets
  * the device error word and leaves out/lse unwritten) and merges the world
- * summaries in rank order as ucb_lse_merge does into out/lse.
+ * summaries in rank order as ucb_lse_merge does into out/lse, which must not
+ * alias out_local/lse_local (UCB_ERR_INVALID).
  * bufs: host array of `world` buffer addresses as mapped in this process
  * (bufs[rank] is the local one); world <= 8.  Every rank must make the same
  * sequence of calls; one call per buffer at a time. */

@@ -154,18 +154,21 @@ def test_key_split_fills_the_gpu_and_cleans_up():
     """Config 4 has 112 row blocks for 148 SMs: every row block's keys are
     split (the first 23 tiles merge the last 2 tiles' partial by LSE).  Three
     launches in a row agree bitwise with each other and with the fp32
-    reference, and the flags are zero after each launch."""
+    reference, and every flag is even (each split item adds 1 per launch)
+    after each launch."""
     need_gpu()
     q, k, v, n_pad = _operands(4, 1024 * 7, 3095, seed=14)
     vt = v.transpose(1, 2).contiguous()
     first, _ = kernels.prefill_attention(q, k, vt, 3095)
-    split = kernels._KEY_SPLITS[(q.device.index, 4, 7168, 3095, n_pad, kernels.stream_of(q))]
-    assert split is not None
-    items, _, flags = split
+    items = kernels._KEY_SPLITS[(q.device.index, 4, 7168, 3095, n_pad)]
+    assert items is not None
+    _, flags = kernels.prefill_split_workspace(q.device, 112, kernels.stream_of(q))
     assert int(items.shape[0]) == 2 * 112 and int(items[0, 4]) == kernels.plan_key_split(112, 25, 148) * 128
+    before = flags.clone()
     results = [kernels.prefill_attention(q, k, vt, 3095) for _ in range(2)]
     torch.cuda.synchronize()
-    assert int(flags.abs().sum()) == 0
+    assert int((flags % 2).abs().sum()) == 0
+    assert torch.equal(flags[:112] - before[:112], torch.full_like(flags[:112], 4))
     for out, lse in results:
         assert torch.equal(out, first)
     ref, ref_lse = _reference(q, k, v, 3095)

@@ -23,12 +23,13 @@
 //    *subnormal* (code * 2^(p-24), multiplied exactly by the tensor core) and
 //    the per-token group scale is folded into the probabilities:
 //       sum_t p_t v_td = sum_t (p_t s_tg) c_td + sum_t p_t m_tg.
-//  * Online softmax in the log2 domain per warp.  A warp that crosses a
-//    segment boundary parks its first state in a private shared-memory block;
-//    at the end the CTA merges the warp states of each pair it touched into
-//    one (max, sum, out) partial, and the last CTA of a pair (atomic ticket,
-//    no waiting) merges the partials into out and LSE.
+//  * Online softmax in the log2 domain per warp.  A warp writes the state
+//    (max, sum, unnormalised rows) of each segment it processed to a
+//    planner-assigned slot in global memory and exits (no CTA barrier, no
+//    atomics); a second, stream-ordered kernel (state_merge_kernel or
+//    state_merge_wide_kernel) folds each pair's slots into out and LSE.
 #include <cfloat>
+#include <cstdint>
 #include <mutex>
 
 #include "common.cuh"
@@ -157,6 +158,7 @@ struct Params {
   int num_pairs;
   float scale_log2;  // softmax_scale * log2(e)
   float* partials;             // warp states, one slot each
+  int max_partials;            // slots the partials buffer holds; larger slot indices are rejected
   const int32_t* warp_slots;   // per CTA and warp: {first-segment slot, last-segment slot}, -1 = none
   __nv_bfloat16* out;
   int64_t out_stride;
@@ -637,7 +639,7 @@ struct Kernel {
       if (pl != cur_pl || kind != cur_kind) {
         if (cur_pl >= 0) {
           // At most one segment boundary per warp (the planner guarantees it).
-          if (stashed || wslot.x < 0) {
+          if (stashed || wslot.x < 0 || wslot.x >= P.max_partials) {
             atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
           } else {
             store_state(P.partials + (int64_t)wslot.x * PARTIAL_FLOATS, cur_kind == 0, st, o, accm, lane);
@@ -683,7 +685,7 @@ struct Kernel {
       }
       if (lane == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
     } else if (cur_pl >= 0) {
-      if (wslot.y < 0)
+      if (wslot.y < 0 || wslot.y >= P.max_partials)
         atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
       else
         store_state(P.partials + (int64_t)wslot.y * PARTIAL_FLOATS, cur_kind == 0, st, o, accm, lane);
@@ -756,13 +758,23 @@ __device__ __forceinline__ void merge_store(const ucb_decode_pair& pr, int grp, 
 
 // Few states per pair (many pairs): CTA per (pair, 32-channel chunk), warp h =
 // query head h walks all the pair's states.
+// A pair whose slot range does not lie inside [0, max_partials) is a bad
+// descriptor: it sets the error word and writes nothing.
+__device__ __forceinline__ bool slots_in_range(const ucb_decode_pair& pr, int max_partials, unsigned int* err) {
+  if (pr.partial_begin >= 0 && pr.partial_count >= 0 && pr.partial_count <= max_partials - pr.partial_begin)
+    return true;
+  if (threadIdx.x == 0) atomicOr(err, DEVERR_BAD_DESCRIPTOR);
+  return false;
+}
+
 __global__ void __launch_bounds__(256) state_merge_kernel(const float* __restrict__ states,
                                                           const ucb_decode_pair* __restrict__ pairs, int grp,
                                                           int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride,
-                                                          float* __restrict__ lse) {
+                                                          float* __restrict__ lse, int max_partials,
+                                                          unsigned int* err) {
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31, d = blockIdx.y * MERGE_DCH + lane;
-  if (h >= grp) return;
   const ucb_decode_pair pr = pairs[blockIdx.x];
+  if (!slots_in_range(pr, max_partials, err) || h >= grp) return;
   const float* base = states + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
   float M = -INFINITY, L = 0.f, acc = 0.f;
   for (int k0 = 0; k0 < pr.partial_count; k0 += 32)
@@ -776,11 +788,13 @@ __global__ void __launch_bounds__(256) state_merge_kernel(const float* __restric
 constexpr int WIDE_MERGE_WARPS = 8;
 __global__ void __launch_bounds__(WIDE_MERGE_WARPS * 32)
     state_merge_wide_kernel(const float* __restrict__ states, const ucb_decode_pair* __restrict__ pairs, int grp,
-                            int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride, float* __restrict__ lse) {
+                            int hq, __nv_bfloat16* __restrict__ out, int64_t out_stride, float* __restrict__ lse,
+                            int max_partials, unsigned int* err) {
   __shared__ float sm_m[WIDE_MERGE_WARPS], sm_l[WIDE_MERGE_WARPS], sm_acc[WIDE_MERGE_WARPS][32];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, d = blockIdx.y * MERGE_DCH + lane;
   const int pi = blockIdx.x / grp, h = blockIdx.x % grp;
   const ucb_decode_pair pr = pairs[pi];
+  if (!slots_in_range(pr, max_partials, err)) return;  // uniform over the CTA: no barrier is skipped by part of it
   const float* base = states + (int64_t)pr.partial_begin * PARTIAL_FLOATS;
   float M = -INFINITY, L = 0.f, acc = 0.f;
   for (int k0 = 32 * w; k0 < pr.partial_count; k0 += 32 * WIDE_MERGE_WARPS)
@@ -833,11 +847,13 @@ int launch(const Params& P, int num_ctas, cudaStream_t s) {
   // the per-head walk over them gets long, so 8 warps share each head.
   if ((int64_t)num_ctas * C::WARPS > 64LL * P.num_pairs) {
     state_merge_wide_kernel<<<dim3(P.num_pairs * P.grp, D / MERGE_DCH), WIDE_MERGE_WARPS * 32, 0, s>>>(
-        static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse);
+        static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse, P.max_partials,
+        P.err);
     return ucb_host::check_launch("state_merge_wide_kernel");
   }
   state_merge_kernel<<<dim3(P.num_pairs, D / MERGE_DCH), 256, 0, s>>>(
-      static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse);
+      static_cast<const float*>(P.partials), P.pairs, P.grp, P.hq, P.out, P.out_stride, P.lse, P.max_partials,
+      P.err);
   return ucb_host::check_launch("state_merge_kernel");
 }
 
@@ -902,13 +918,16 @@ extern "C" int ucb_decode_config(int k_bits, int v_bits, int group_size, int sta
   return ucb::decode::dispatch<ucb::decode::SlotsFn>(k_bits, v_bits, group_size, ctas, warps_per_cta);
 }
 
-extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int num_q_heads, int num_kv_heads,
-                                    int head_dim, const ucb_span* spans, int num_spans, const ucb_decode_cta* ctas,
-                                    int num_ctas, const int32_t* warp_bounds, const ucb_decode_pair* pairs,
-                                    int num_pairs, int k_bits, int v_bits,
-                                    int group_size, int stat_dtype, float softmax_scale, void* partials,
-                                    const int32_t* warp_slots, void* out, int64_t out_stride, float* lse,
-                                    void* stream) {
+namespace {
+// Shared body of the two decode entry points.  max_partials bounds every slot
+// index the kernels may touch (the allocating entry trusts the plan and passes
+// INT32_MAX; the allocation-free one passes the static array's slot count).
+int decode_attention_impl(const void* query, int64_t query_stride, int num_q_heads, int num_kv_heads, int head_dim,
+                          const ucb_span* spans, int num_spans, const ucb_decode_cta* ctas, int num_ctas,
+                          const int32_t* warp_bounds, const ucb_decode_pair* pairs, int num_pairs, int k_bits,
+                          int v_bits, int group_size, int stat_dtype, float softmax_scale, void* partials,
+                          int max_partials, const int32_t* warp_slots, void* out, int64_t out_stride, float* lse,
+                          void* stream) {
   if (!query || !spans || !ctas || !warp_bounds || !pairs || !partials || !warp_slots || !out)
     return set_error(UCB_ERR_INVALID, "ucb_decode_attention: null pointer");
   if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_decode_attention: head_dim must be 128");
@@ -935,6 +954,7 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.num_pairs = num_pairs;
   P.scale_log2 = softmax_scale * ucb::decode::LOG2E;
   P.partials = static_cast<float*>(partials);
+  P.max_partials = max_partials;
   P.warp_slots = warp_slots;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.out_stride = out_stride;
@@ -943,6 +963,19 @@ extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int
   P.trace = g_decode_trace;
   return ucb::decode::dispatch<ucb::decode::LaunchFn>(k_bits, v_bits, group_size, P, num_ctas,
                                                       static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" int ucb_decode_attention(const void* query, int64_t query_stride, int num_q_heads, int num_kv_heads,
+                                    int head_dim, const ucb_span* spans, int num_spans, const ucb_decode_cta* ctas,
+                                    int num_ctas, const int32_t* warp_bounds, const ucb_decode_pair* pairs,
+                                    int num_pairs, int k_bits, int v_bits,
+                                    int group_size, int stat_dtype, float softmax_scale, void* partials,
+                                    const int32_t* warp_slots, void* out, int64_t out_stride, float* lse,
+                                    void* stream) {
+  return decode_attention_impl(query, query_stride, num_q_heads, num_kv_heads, head_dim, spans, num_spans, ctas,
+                               num_ctas, warp_bounds, pairs, num_pairs, k_bits, v_bits, group_size, stat_dtype,
+                               softmax_scale, partials, INT32_MAX, warp_slots, out, out_stride, lse, stream);
 }
 
 // ----------------------------------------------------- allocation-free decode
@@ -1001,8 +1034,11 @@ extern "C" int ucb_decode_attention_noalloc(const void* query, int64_t query_str
   unsigned char* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != UCB_OK) return rc;
-  return ucb_decode_attention(query, query_stride, num_q_heads, num_kv_heads, head_dim, spans, num_spans, ctas,
-                              num_ctas, warp_bounds, pairs, num_pairs, k_bits, v_bits, group_size, stat_dtype,
-                              softmax_scale, scratch, warp_slots, out, out_stride, lse, stream);
+  // Slot indices come from device tables the library cannot read on the host,
+  // so the kernels check each one against the array's size (a bad index sets
+  // DEVERR_BAD_DESCRIPTOR and writes nothing).
+  return decode_attention_impl(query, query_stride, num_q_heads, num_kv_heads, head_dim, spans, num_spans, ctas,
+                               num_ctas, warp_bounds, pairs, num_pairs, k_bits, v_bits, group_size, stat_dtype,
+                               softmax_scale, scratch, num_partials, warp_slots, out, out_stride, lse, stream);
 }
 

@@ -203,6 +203,10 @@ extern "C" int ucb_split_merge_peer(int rank, int world, void* const* bufs, cons
     return set_error(UCB_ERR_INVALID, "ucb_split_merge_peer: null pointer");
   if ((reinterpret_cast<uintptr_t>(out_local) | reinterpret_cast<uintptr_t>(out)) & 15)
     return set_error(UCB_ERR_INVALID, "ucb_split_merge_peer: out rows must be 16-byte aligned");
+  // The kernel sends a row's words to the peers and merges without a barrier
+  // in between, so the merged result must not overwrite the rank's own summary.
+  if (out == out_local || (lse != nullptr && lse == lse_local))
+    return set_error(UCB_ERR_INVALID, "ucb_split_merge_peer: out/lse must not alias out_local/lse_local");
   ucb::peer::PeerArgs a;
   for (int i = 0; i < ucb::peer::MAX_RANKS; ++i) a.bufs[i] = nullptr;
   for (int i = 0; i < world; ++i) {

@@ -212,9 +212,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 // (at most 2*BM rows) against keys [k_row0, k_row0 + n_tokens) of that head.
 // mode ITEM_FINAL writes out/lse; a row block whose keys are split in two
 // runs as an ITEM_PARTIAL item (writes its normalised fp32 rows and log2 LSE
-// to partial slot `slot`, then sets flags[slot]) and an ITEM_MERGE item (waits
-// for flags[slot], merges that partial with its own result by LSE, writes
-// out/lse and clears the flag for the next launch).
+// to partial slot `slot`, then adds 1 to flags[slot], making it odd) and an
+// ITEM_MERGE item (waits for flags[slot] to be odd, merges that partial with
+// its own result by LSE, writes out/lse and adds 1 again).  Each item adds
+// exactly 1 per launch whatever happens (a timed-out wait included), so every
+// flag is even again when a launch ends and a late partial from a failed
+// launch can never be taken for the next launch's: kernels on one stream run
+// one after the other, and CUDA-graph replays keep the same rule.
 struct WorkItem {
   int head, q_row0, q_rows, k_row0, n_tokens, mode, slot, pad;
 };
@@ -226,7 +230,7 @@ __device__ __forceinline__ bool wait_flag(const unsigned int* flag, uint64_t bud
   while (true) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v != 0) return true;
+    if (v & 1u) return true;
     if (global_timer_ns() - t0 > budget_ns) return false;
     __nanosleep(256);
   }
@@ -238,7 +242,7 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   const WorkItem* items;  // per-CTA problems (batched launches), or null: CTA (x, y) = rows 2*BM*x.. of head y
   float* partials;        // PARTIAL_SLOT_FLOATS per slot (split row blocks), or null
-  unsigned int* flags;    // one per slot, zero between launches, or null
+  unsigned int* flags;    // one per slot, even between launches, or null
   __nv_bfloat16* out;  // [heads, m_rows, D]
   float* lse;          // [heads, m_rows], may be null
   unsigned int* err;
@@ -273,7 +277,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_tiles = (n_tokens + BN - 1) / BN;
   // The swizzled operand layout needs a 1024-byte aligned base.
   if (smem_u32(smem) & 1023) {
-    if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+    if (tid == 0) {
+      atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+      if (mode != ITEM_FINAL) atomicAdd(P.flags + slot, 1u);  // keep the flag's parity rule
+    }
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -525,14 +532,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (m < m_end && P.lse) P.lse[(int64_t)head * P.m_rows + m] = lse2 * 0.6931471805599453f;
     }
     // The softmax warps meet once: a partial is published after every row
-    // is written; a consumed partial's flag is cleared after every row read.
+    // is written; a consumed partial's flag advances after every row read.
+    // A failed partial still publishes (its CTA has set the error word), so
+    // the parity stays in step.
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (tid == 0) {
-      if (mode == ITEM_PARTIAL && good)
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(P.flags + slot), "r"(1u) : "memory");
-      else if (mode == ITEM_MERGE && merged)
-        P.flags[slot] = 0u;
-    }
+    if (tid == 0 && mode != ITEM_FINAL)
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.flags + slot), "r"(1u) : "memory");
   }
   tc_fence_before();
   __syncthreads();

@@ -749,35 +749,45 @@ def plan_key_split(row_blocks: int, key_tiles: int, sms: int) -> int | None:
     return best_l if best_l is not None and best <= whole - 1 else None
 
 
-def _key_split_launch(device, heads: int, m_rows: int, n_tokens: int, n_padded: int, stream: int):
-    """(items, partials, flags) of a key-split launch, cached per shape and
-    stream (the flags return to zero after every launch), or None."""
+_KEY_SPLITS_MAX = 64  # item tables kept; the workspace itself is shared per (device, stream)
 
-    key = (device.index, heads, m_rows, n_tokens, n_padded, stream)
+
+def _key_split_launch(device, heads: int, m_rows: int, n_tokens: int, n_padded: int, stream: int):
+    """(items, partials, flags) of a key-split launch, or None.
+
+    Only the item table (a few hundred bytes) is cached per shape, and at most
+    ``_KEY_SPLITS_MAX`` of them; partials and flags come from the per-(device,
+    stream) workspace of ``prefill_split_workspace``, which only grows to the
+    largest row-block count seen, so a session whose key count changes every
+    call does not accumulate device memory."""
+
+    key = (device.index, heads, m_rows, n_tokens, n_padded)
     if key in _KEY_SPLITS:
-        return _KEY_SPLITS[key]
-    blocks_per_head = -(-m_rows // PREFILL_ROWS_PER_CTA)
-    row_blocks = heads * blocks_per_head
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
-    first = plan_key_split(row_blocks, -(-n_tokens // PREFILL_KEY_TILE), sms)
-    if first is None:
-        _KEY_SPLITS[key] = None
+        items = _KEY_SPLITS[key]
+    else:
+        blocks_per_head = -(-m_rows // PREFILL_ROWS_PER_CTA)
+        row_blocks = heads * blocks_per_head
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        first = plan_key_split(row_blocks, -(-n_tokens // PREFILL_KEY_TILE), sms)
+        items = None
+        if first is not None:
+            split_at = first * PREFILL_KEY_TILE
+            merge_items, partial_items = [], []
+            for h in range(heads):
+                for b in range(blocks_per_head):
+                    slot = len(merge_items)
+                    q0 = b * PREFILL_ROWS_PER_CTA
+                    rows = min(PREFILL_ROWS_PER_CTA, m_rows - q0)
+                    merge_items.append([h, q0, rows, 0, split_at, 2, slot, 0])
+                    partial_items.append([h, q0, rows, split_at, n_tokens - split_at, 1, slot, 0])
+            items = torch.tensor(merge_items + partial_items, dtype=torch.int32).to(device)
+        if len(_KEY_SPLITS) >= _KEY_SPLITS_MAX:
+            _KEY_SPLITS.pop(next(iter(_KEY_SPLITS)))
+        _KEY_SPLITS[key] = items
+    if items is None:
         return None
-    split_at = first * PREFILL_KEY_TILE
-    merge_items, partial_items = [], []
-    for h in range(heads):
-        for b in range(blocks_per_head):
-            slot = len(merge_items)
-            q0 = b * PREFILL_ROWS_PER_CTA
-            rows = min(PREFILL_ROWS_PER_CTA, m_rows - q0)
-            merge_items.append([h, q0, rows, 0, split_at, 2, slot, 0])
-            partial_items.append([h, q0, rows, split_at, n_tokens - split_at, 1, slot, 0])
-    items = torch.tensor(merge_items + partial_items, dtype=torch.int32).to(device)
-    slot_floats = int(_capi.load().ucb_prefill_partial_bytes()) // 4
-    partials = torch.empty(row_blocks * slot_floats, device=device, dtype=torch.float32)
-    flags = torch.zeros(row_blocks, device=device, dtype=torch.int32)
-    _KEY_SPLITS[key] = (items, partials, flags)
-    return _KEY_SPLITS[key]
+    partials, flags = prefill_split_workspace(device, int(items.shape[0]) // 2, stream)
+    return items, partials, flags
 
 
 def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
@@ -804,15 +814,19 @@ def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
 
 
 _SPLIT_WORKSPACES: dict = {}
+_RETIRED_WORKSPACES: list = []  # outgrown workspaces stay alive: a captured CUDA graph may still use them
 
 
 def prefill_split_workspace(device, slots: int, stream: int):
     """(partials, flags) for ``slots`` split row blocks, cached per device and
-    stream (the flags return to zero after every complete launch)."""
+    stream.  Every launch leaves each flag even (each split item adds 1), so
+    one workspace serves every later launch on that stream."""
 
     key = (device.index, stream)
     ws = _SPLIT_WORKSPACES.get(key)
     if ws is None or int(ws[1].numel()) < slots:
+        if ws is not None:
+            _RETIRED_WORKSPACES.append(ws)
         slot_floats = int(_capi.load().ucb_prefill_partial_bytes()) // 4
         ws = (torch.empty(slots * slot_floats, device=device, dtype=torch.float32),
               torch.zeros(slots, device=device, dtype=torch.int32))
