@@ -366,6 +366,17 @@ UCB_API int ucb_h2o_scores_from_lse(const void* query_dev, int64_t queries, int 
                             int kv_heads, int head_dim, const float* lse_dev, float softmax_scale,
                             float* scores_dev, int accumulate, void* stream);
 
+/* The same reduction (operators/physical.py:51-101 and GQAH2OCache.update_scores,
+ * storage/physical.py:598-610, without the [Hq, Lq, T] probabilities) for
+ * bf16 (tensor cores, mma.sync) or fp32 (CUDA cores) query and keys of one
+ * dtype.  lse_dev NULL: the attention covers exactly these keys and the LSE of
+ * every row is computed first into lse_workspace_dev (fp32 [q_heads, queries]).
+ * bf16 needs a 16-byte aligned query and 4-byte aligned key rows. */
+UCB_API int ucb_h2o_scores(const void* query_dev, int dtype, int64_t queries, int q_heads, const void* key_dev,
+                           int64_t key_stride_token, int64_t key_stride_head, int64_t tokens, int kv_heads,
+                           int head_dim, const float* lse_dev, float* lse_workspace_dev, float softmax_scale,
+                           float* scores_dev, int accumulate, void* stream);
+
 /* ------------------------------------------------------------------ dense compaction
  * Replaces TensorCacheStorageBackend.compact's per-sample boolean gather
  * (unicache/storage/tensor_backend.py:54-100).  mask_dev uint8 [rows];

@@ -123,6 +123,8 @@ SIGNATURES = {
                                          c_void_p]),
     "ucb_h2o_scores_from_lse": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int,
                                         c_int, c_void_p, c_float, c_void_p, c_int, c_void_p]),
+    "ucb_h2o_scores": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
+                               c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p]),
     "ucb_compact_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  ctypes.POINTER(c_int64), c_void_p]),
     "ucb_selftest_mma_subnormal": (c_int, [ctypes.POINTER(c_float), c_void_p]),

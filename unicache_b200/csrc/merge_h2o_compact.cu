@@ -190,17 +190,121 @@ __global__ void accumulate_probs_kernel(const T* __restrict__ probs, int grp, in
   *o = accumulate ? *o + total : total;
 }
 
-constexpr int kScoreQ = 32;  // query rows staged per round
+// ---------------------------------------------------------------- H2O scoring
+// Received attention per KV head without materialised probabilities
+// (operators/physical.py:63-65 sums softmax probabilities over queries and
+// the heads of a GQA group): scores[kv, t] (+)= sum over the kv head's rows
+// (query head h = kv*grp + g, query i) of exp(scale * q_{i,h} . k_t - lse_{h,i}),
+// with lse the natural-log normaliser of each row over ALL keys of the
+// attention (the attention kernels return it), so the terms are exactly the
+// probabilities the reference reduces.
 
-// scores[kv, t] (+)= sum over the kv head's (head, query) rows of
-// exp(scale * q.k_t - lse).  One thread per token, query rows from shared memory.
-__global__ void __launch_bounds__(128) scores_from_lse_kernel(const __nv_bfloat16* __restrict__ query,
-                                                              int64_t queries, int q_heads,
-                                                              const __nv_bfloat16* __restrict__ key,
-                                                              int64_t ks_t, int64_t ks_h, int64_t tokens,
-                                                              int grp, const float* __restrict__ lse,
-                                                              float scale, float* __restrict__ scores,
-                                                              int accumulate) {
+// bf16 keys and queries on the tensor cores (mma.sync m16n8k16, fp32
+// accumulate: bf16 products are exact).  A CTA of 4 warps takes 128 tokens of
+// one KV head (each warp 2 tiles of 16 tokens, A fragments held in registers
+// for the whole launch) and streams the head's query rows through shared
+// memory in chunks of 64; every 8 rows are one MMA column block.
+constexpr int kScoreRows = 64;    // query rows per shared-memory chunk
+constexpr int kScoreRowB = 272;   // row stride (bytes): 256 + 16, conflict-free ldmatrix
+__global__ void __launch_bounds__(128) scores_mma_kernel(const __nv_bfloat16* __restrict__ query, int64_t queries,
+                                                         int q_heads, const __nv_bfloat16* __restrict__ key,
+                                                         int64_t ks_t, int64_t ks_h, int64_t tokens, int grp,
+                                                         const float* __restrict__ lse, float scale_log2,
+                                                         float* __restrict__ scores, int accumulate) {
+  constexpr int D = 128;
+  constexpr float LOG2E_F = 1.4426950408889634f;
+  __shared__ __align__(16) unsigned char qs[kScoreRows * kScoreRowB];
+  __shared__ float ls[kScoreRows];
+  const int kv = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int64_t tok_base = (int64_t)blockIdx.x * 128 + warp * 32;
+  // A fragments: lane holds tokens (r, r+8) of each 16-token tile, channels
+  // 16kk + {2c, 2c+1, 2c+8, 2c+9}.
+  uint32_t a[2][8][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const int64_t t0 = tok_base + 16 * mt + r, t1 = t0 + 8;
+    const __nv_bfloat16* k0 = key + t0 * ks_t + (int64_t)kv * ks_h;
+    const __nv_bfloat16* k1 = key + t1 * ks_t + (int64_t)kv * ks_h;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int ch = 16 * kk + 2 * c;
+      a[mt][kk][0] = t0 < tokens ? *reinterpret_cast<const uint32_t*>(k0 + ch) : 0u;
+      a[mt][kk][1] = t1 < tokens ? *reinterpret_cast<const uint32_t*>(k1 + ch) : 0u;
+      a[mt][kk][2] = t0 < tokens ? *reinterpret_cast<const uint32_t*>(k0 + ch + 8) : 0u;
+      a[mt][kk][3] = t1 < tokens ? *reinterpret_cast<const uint32_t*>(k1 + ch + 8) : 0u;
+    }
+  }
+  float sum[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [tile][token r / r+8], this lane's columns
+  const int64_t rows = (int64_t)grp * queries;
+  const uint32_t qbase = smem_u32(qs);
+  // ldmatrix x4 row addresses: matrix m = lane / 8 covers channels 8m..8m+7 of
+  // a 32-channel block (two k-chunks), row = query row (lane % 8).
+  const uint32_t lm_off = (lane & 7) * kScoreRowB + (lane >> 3) * 16;
+  for (int64_t base = 0; base < rows; base += kScoreRows) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kScoreRows * (D / 8); i += blockDim.x) {
+      const int rr = i / (D / 8), chunk = i % (D / 8);
+      const int64_t row = base + rr;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row < rows) {
+        const int g = (int)(row / queries);
+        const int64_t qi = row % queries;
+        v = reinterpret_cast<const uint4*>(query + (qi * q_heads + kv * grp + g) * D)[chunk];
+      }
+      *reinterpret_cast<uint4*>(qs + rr * kScoreRowB + chunk * 16) = v;
+    }
+    for (int i = threadIdx.x; i < kScoreRows; i += blockDim.x) {
+      const int64_t row = base + i;
+      ls[i] = row < rows ? lse[(int64_t)(kv * grp + row / queries) * queries + row % queries] * LOG2E_F : INFINITY;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int nb = 0; nb < kScoreRows / 8; ++nb) {
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kp = 0; kp < 4; ++kp) {  // pairs of k-chunks
+        uint32_t b[4];
+        ldmatrix_x4(b, qbase + nb * 8 * kScoreRowB + kp * 64 + lm_off);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          mma_bf16(acc[mt], a[mt][2 * kp], b[0], b[1]);
+          mma_bf16(acc[mt], a[mt][2 * kp + 1], b[2], b[3]);
+        }
+      }
+      const float l0 = ls[nb * 8 + 2 * c], l1 = ls[nb * 8 + 2 * c + 1];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        sum[mt][0] += fast_exp2(fmaf(acc[mt][0], scale_log2, -l0)) + fast_exp2(fmaf(acc[mt][1], scale_log2, -l1));
+        sum[mt][1] += fast_exp2(fmaf(acc[mt][2], scale_log2, -l0)) + fast_exp2(fmaf(acc[mt][3], scale_log2, -l1));
+      }
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float v = sum[mt][h];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      const int64_t t = tok_base + 16 * mt + r + 8 * h;
+      if (c == 0 && t < tokens) {
+        float* o = scores + (int64_t)kv * tokens + t;
+        *o = accumulate ? *o + v : v;
+      }
+    }
+  }
+}
+
+// fp32 (or any dtype) on the CUDA cores, for fp32 caches: one thread per
+// token holds its key row; query rows are staged in shared memory.
+constexpr int kScoreQ = 32;  // query rows staged per round
+template <typename T>
+__global__ void __launch_bounds__(128) scores_cuda_core_kernel(const T* __restrict__ query, int64_t queries,
+                                                               int q_heads, const T* __restrict__ key, int64_t ks_t,
+                                                               int64_t ks_h, int64_t tokens, int grp,
+                                                               const float* __restrict__ lse, float scale,
+                                                               float* __restrict__ scores, int accumulate) {
   constexpr int D = 128;
   const int kv = blockIdx.y;
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -208,9 +312,9 @@ __global__ void __launch_bounds__(128) scores_from_lse_kernel(const __nv_bfloat1
   __shared__ float ls[kScoreQ];
   float k[D];
   if (t < tokens) {
-    const __nv_bfloat16* kr = key + t * ks_t + kv * ks_h;
+    const T* kr = key + t * ks_t + kv * ks_h;
 #pragma unroll
-    for (int d = 0; d < D; ++d) k[d] = __bfloat162float(kr[d]);
+    for (int d = 0; d < D; ++d) k[d] = Dtype<T>::to_f(kr[d]);
   }
   float total = 0.f;
   const int64_t rows = (int64_t)grp * queries;
@@ -222,7 +326,7 @@ __global__ void __launch_bounds__(128) scores_from_lse_kernel(const __nv_bfloat1
       if (rr < rows) {
         const int g = (int)(rr / queries);
         const int64_t q = rr % queries;
-        v = __bfloat162float(query[(q * q_heads + kv * grp + g) * D + i % D]);
+        v = Dtype<T>::to_f(query[(q * q_heads + kv * grp + g) * D + i % D]);
       }
       qs[i / D][i % D] = v;
     }
@@ -244,6 +348,38 @@ __global__ void __launch_bounds__(128) scores_from_lse_kernel(const __nv_bfloat1
     float* o = scores + (int64_t)kv * tokens + t;
     *o = accumulate ? *o + total : total;
   }
+}
+
+// Natural-log normaliser of every (query head, query) row over the given keys
+// (for callers whose attention covers exactly these keys): one warp per row,
+// the lanes split the 128 channels, online max/sum over the tokens in fp32.
+template <typename T>
+__global__ void __launch_bounds__(128) row_lse_kernel(const T* __restrict__ query, int64_t queries, int q_heads,
+                                                      const T* __restrict__ key, int64_t ks_t, int64_t ks_h,
+                                                      int64_t tokens, int grp, float scale, float* __restrict__ lse) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;  // row = h * queries + i
+  if (row >= (int64_t)q_heads * queries) return;
+  const int h = (int)(row / queries);
+  const int64_t qi = row % queries;
+  const int kv = h / grp;
+  float q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q[j] = Dtype<T>::to_f(query[(qi * q_heads + h) * 128 + 4 * lane + j]);
+  float m = -INFINITY, l = 0.f;
+  for (int64_t t = 0; t < tokens; ++t) {
+    const T* kr = key + t * ks_t + (int64_t)kv * ks_h + 4 * lane;
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dot = fmaf(q[j], Dtype<T>::to_f(kr[j]), dot);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float s = dot * scale;
+    const float mn = fmaxf(m, s);
+    l = l * expf(m - mn) + expf(s - mn);
+    m = mn;
+  }
+  if (lane == 0) lse[row] = m + logf(l);
 }
 
 // ---------------------------------------------------------------- compaction
@@ -381,20 +517,59 @@ extern "C" int ucb_h2o_accumulate_probs(const void* probs, int dtype, int q_head
   return check_launch("accumulate_probs_kernel");
 }
 
+extern "C" int ucb_h2o_scores(const void* query, int dtype, int64_t queries, int q_heads, const void* key,
+                              int64_t key_stride_token, int64_t key_stride_head, int64_t tokens, int kv_heads,
+                              int head_dim, const float* lse, float* lse_workspace, float softmax_scale,
+                              float* scores, int accumulate, void* stream) {
+  if (!query || !key || !scores || (!lse && !lse_workspace))
+    return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: null pointer");
+  if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_h2o_scores: head_dim must be 128");
+  if (kv_heads <= 0 || q_heads % kv_heads)
+    return set_error(UCB_ERR_INVALID, "Query heads must be divisible by KV heads for GQA H2O");
+  if (dtype != UCB_BF16 && dtype != UCB_F32)
+    return set_error(UCB_ERR_UNSUPPORTED, "ucb_h2o_scores: bfloat16 or float32 query and keys");
+  if (tokens <= 0 || queries <= 0) return UCB_OK;
+  const int grp = q_heads / kv_heads;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (lse == nullptr) {
+    const unsigned blocks = static_cast<unsigned>(((int64_t)q_heads * queries + 3) / 4);
+    if (dtype == UCB_BF16)
+      ucb::row_lse_kernel<__nv_bfloat16><<<blocks, 128, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(query), queries, q_heads, static_cast<const __nv_bfloat16*>(key),
+          key_stride_token, key_stride_head, tokens, grp, softmax_scale, lse_workspace);
+    else
+      ucb::row_lse_kernel<float><<<blocks, 128, 0, s>>>(static_cast<const float*>(query), queries, q_heads,
+                                                        static_cast<const float*>(key), key_stride_token,
+                                                        key_stride_head, tokens, grp, softmax_scale, lse_workspace);
+    const int rc = check_launch("row_lse_kernel");
+    if (rc) return rc;
+    lse = lse_workspace;
+  }
+  dim3 grid(static_cast<unsigned>((tokens + 127) / 128), static_cast<unsigned>(kv_heads));
+  if (dtype == UCB_BF16) {
+    if ((reinterpret_cast<uintptr_t>(query) & 15) || (reinterpret_cast<uintptr_t>(key) & 3) ||
+        (key_stride_token & 1) || (key_stride_head & 1))
+      return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: bf16 query must be 16-byte and key rows 4-byte aligned");
+    ucb::scores_mma_kernel<<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(query), queries, q_heads,
+                                                static_cast<const __nv_bfloat16*>(key), key_stride_token,
+                                                key_stride_head, tokens, grp, lse,
+                                                softmax_scale * 1.4426950408889634f, scores, accumulate);
+    return check_launch("scores_mma_kernel");
+  }
+  ucb::scores_cuda_core_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(query), queries, q_heads,
+                                                           static_cast<const float*>(key), key_stride_token,
+                                                           key_stride_head, tokens, grp, lse, softmax_scale, scores,
+                                                           accumulate);
+  return check_launch("scores_cuda_core_kernel");
+}
+
 extern "C" int ucb_h2o_scores_from_lse(const void* query, int64_t queries, int q_heads, const void* key,
                                        int64_t key_stride_token, int64_t key_stride_head, int64_t tokens,
                                        int kv_heads, int head_dim, const float* lse, float softmax_scale,
                                        float* scores, int accumulate, void* stream) {
-  if (!query || !key || !lse || !scores) return set_error(UCB_ERR_INVALID, "ucb_h2o_scores_from_lse: null pointer");
-  if (head_dim != 128) return set_error(UCB_ERR_UNSUPPORTED, "ucb_h2o_scores_from_lse: head_dim must be 128");
-  if (kv_heads <= 0 || q_heads % kv_heads)
-    return set_error(UCB_ERR_INVALID, "Query heads must be divisible by KV heads for GQA H2O");
-  if (tokens <= 0 || queries <= 0) return UCB_OK;
-  dim3 grid(static_cast<unsigned>((tokens + 127) / 128), static_cast<unsigned>(kv_heads));
-  ucb::scores_from_lse_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(query), queries, q_heads, static_cast<const __nv_bfloat16*>(key),
-      key_stride_token, key_stride_head, tokens, q_heads / kv_heads, lse, softmax_scale, scores, accumulate);
-  return check_launch("scores_from_lse_kernel");
+  if (!lse) return set_error(UCB_ERR_INVALID, "ucb_h2o_scores_from_lse: null pointer");
+  return ucb_h2o_scores(query, UCB_BF16, queries, q_heads, key, key_stride_token, key_stride_head, tokens, kv_heads,
+                        head_dim, lse, nullptr, softmax_scale, scores, accumulate, stream);
 }
 
 extern "C" int ucb_compact_rows(const void* src, int64_t row_bytes, const uint8_t* mask, int64_t rows,

@@ -230,22 +230,54 @@ def accumulate_probs(probs: torch.Tensor, kv_heads: int, scores: torch.Tensor | 
     return scores
 
 
-def scores_from_lse(query: torch.Tensor, key: torch.Tensor, lse: torch.Tensor, *, kv_heads: int,
-                    softmax_scale: float, scores: torch.Tensor | None = None) -> torch.Tensor:
-    """H2O scores without materialised probabilities: query [Lq, Hq, D] bf16,
-    key [N, Hkv, D] (any token/head strides), lse fp32 [Hq, Lq]."""
+def h2o_scores(query: torch.Tensor, key: torch.Tensor, lse: torch.Tensor | None, *, kv_heads: int,
+               softmax_scale: float, scores: torch.Tensor | None = None, head_major: bool = False) -> torch.Tensor:
+    """Per-KV-head received attention without materialised probabilities
+    (operators/physical.py:63-65 and storage/physical.py:598-610 reduce the
+    softmax probabilities; here each probability is recomputed from the
+    row's LSE): scores[kv, t] (+)= sum over the kv head's query heads h and
+    queries i of exp(scale * q[i, h] . key[t, kv] - lse[h, i]).
+
+    query [Lq, Hq, D] and key rows share a dtype (bf16: tensor cores; fp32:
+    CUDA cores).  key is [N, Hkv, D] (token-major, any strides) or, with
+    ``head_major``, [Hkv, N, D].  lse fp32 [Hq, Lq] (natural log) is the
+    normaliser over every key of the attention; None means the attention
+    covers exactly ``key`` and the LSE is computed first.  Adds into
+    ``scores`` (fp32 [Hkv, N]) when it is given."""
 
     require_cuda(query, "query")
+    require_cuda(key, "key")
+    if query.dtype != key.dtype or query.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("H2O scoring takes bfloat16 or float32 query and keys of one dtype")
     q = query.contiguous()
     queries, q_heads, head_dim = map(int, q.shape)
-    tokens = int(key.shape[0])
+    if head_major:
+        tokens, stride_t, stride_h = int(key.shape[1]), key.stride(1), key.stride(0)
+    else:
+        tokens, stride_t, stride_h = int(key.shape[0]), key.stride(0), key.stride(1)
+    if key.stride(-1) != 1 or int(key.shape[-1]) != head_dim:
+        raise ValueError("key rows must have a unit channel stride and the query's head_dim")
     accumulate = scores is not None
     if scores is None:
         scores = torch.empty((kv_heads, tokens), device=q.device, dtype=torch.float32)
-    call("ucb_h2o_scores_from_lse", q.data_ptr(), queries, q_heads, key.data_ptr(), key.stride(0), key.stride(1),
-         tokens, kv_heads, head_dim, lse.contiguous().data_ptr(), float(softmax_scale), scores.data_ptr(),
+    elif scores.dtype != torch.float32 or tuple(scores.shape) != (kv_heads, tokens) or not scores.is_contiguous():
+        raise ValueError("scores must be contiguous float32 [kv_heads, tokens]")
+    workspace = None
+    if lse is None:
+        workspace = torch.empty((q_heads, queries), device=q.device, dtype=torch.float32)
+    else:
+        lse = lse.float().contiguous()
+    call("ucb_h2o_scores", q.data_ptr(), dtype_code(q.dtype), queries, q_heads, key.data_ptr(), stride_t, stride_h,
+         tokens, kv_heads, head_dim, ptr(lse), ptr(workspace), float(softmax_scale), scores.data_ptr(),
          int(accumulate), stream_of(q))
     return scores
+
+
+def scores_from_lse(query: torch.Tensor, key: torch.Tensor, lse: torch.Tensor, *, kv_heads: int,
+                    softmax_scale: float, scores: torch.Tensor | None = None) -> torch.Tensor:
+    """``h2o_scores`` for token-major keys [N, Hkv, D] and a given LSE."""
+
+    return h2o_scores(query, key, lse, kv_heads=kv_heads, softmax_scale=softmax_scale, scores=scores)
 
 
 # ---------------------------------------------------------------- dense compaction

@@ -53,8 +53,30 @@ class H2OPhysicalGQAOperator:
         query_heads = int(attention_probs.shape[0])
         if query_heads % kv_heads != 0:
             raise ValueError("BAGEL query heads must be divisible by KV heads")
+        return self._request(ctx, kernels.accumulate_probs(attention_probs, kv_heads), query_heads, kv_heads)
+
+    def update_after_attention_lse(self, ctx, query: torch.Tensor, lse: torch.Tensor | None,
+                                   softmax_scale: float | None = None):
+        """``update_after_attention`` without materialised probabilities: the
+        per-KV-head received attention of the dense keys ``ctx.k`` [T, Hkv, D]
+        is recomputed on the tensor cores from ``query`` [Lq, Hq, D] and the
+        attention's natural-log LSE [Hq, Lq] (None: the attention covered
+        exactly ``ctx.k``), then the same physical request is queued."""
+
+        if ctx.storage_num_kv_heads is None:
+            raise RuntimeError("Physical H2O requires native KV-head metadata")
+        kv_heads = int(ctx.storage_num_kv_heads)
+        query_heads = int(query.shape[1])
+        if query_heads % kv_heads != 0:
+            raise ValueError("BAGEL query heads must be divisible by KV heads")
+        scale = (1.0 / float(int(query.shape[-1])) ** 0.5) if softmax_scale is None else float(softmax_scale)
+        scores = kernels.h2o_scores(query.to(ctx.k.dtype), ctx.k, lse, kv_heads=kv_heads, softmax_scale=scale)
+        return self._request(ctx, scores, query_heads, kv_heads)
+
+    def _request(self, ctx, per_kv_head_scores: torch.Tensor, query_heads: int, kv_heads: int):
+        """Queue the physical request and record the budget (physical.py:66-101)."""
+
         groups = query_heads // kv_heads
-        per_kv_head_scores = kernels.accumulate_probs(attention_probs, kv_heads)
         ctx.physical_request = PhysicalCacheRequest(
             operator=self.name,
             segment_id=ctx.step.segment_id,

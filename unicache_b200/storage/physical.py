@@ -451,6 +451,20 @@ class GQAH2OCache:
         kernels.accumulate_probs(probabilities, self.num_kv_heads, scores)
         self.cumulative_scores = scores
 
+    def update_scores_from_lse(self, query: torch.Tensor, lse: torch.Tensor,
+                               softmax_scale: float | None = None) -> None:
+        """``update_scores`` without the [Hq, Lq, T] probabilities: each
+        probability of the retained rows is recomputed on the tensor cores from
+        the query [Lq, Hq, D] and the attention's natural-log LSE [Hq, Lq]
+        (the decode and long-query kernels return it), and the per-KV-head sums
+        are added to ``cumulative_scores``."""
+
+        scale = (1.0 / math.sqrt(int(query.shape[-1]))) if softmax_scale is None else float(softmax_scale)
+        scores = self.cumulative_scores.float().contiguous().clone()
+        kernels.h2o_scores(query.to(self.key.dtype), self.key, lse, kv_heads=self.num_kv_heads, softmax_scale=scale,
+                           scores=scores, head_major=True)
+        self.cumulative_scores = scores
+
     def enforce_budget(self) -> None:
         self.trim(self.heavy_tokens + self.recent_tokens, self.recent_tokens)
 
