@@ -1,33 +1,37 @@
-"""Benchmark: packed 2-bit KIVI decode attention on B200.
+"""Benchmark: packed KIVI decode attention (BASELINE configs 2 and 3) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload config2|config3|config3split]
 
-Workload per GPU (config 2): 16 sequences, 28 query / 4 KV heads, head_dim 128,
-8192 KIVI 2-bit (group 32) packed tokens + 128 bf16 residual tokens, K,V ~ N(0,1)
-with 4 key outlier channels x10 (seeded synthetic data).  One step = one decode
-token for every sequence = one launch of the decode kernel plus one launch of
-the state-merge kernel.  Inputs (the packed caches) are 55 MB per replica, below
-the 126 MB L2, so steps rotate over 8 independent cache replicas (438 MB) and no
-step finds its cache in L2.  The device-timed region is one replay of a CUDA
-graph holding exactly K steps (captured once, warmed by W eager steps and one
-untimed replay); the e2e leg calls the public API eagerly every step.
+Headline (default, config 2) per GPU: 16 sequences, 28 query / 4 KV heads,
+head_dim 128, 8192 KIVI 2-bit (group 32) packed tokens + 128 bf16 residual
+tokens, K,V ~ N(0,1) with 4 key outlier channels x10 (seeded synthetic data:
+no dataset is involved).  One step = one decode token for every sequence = one
+launch of the decode kernel plus one launch of the state-merge kernel.  A
+replica of the packed caches is 55 MB, below the 126 MB L2, so steps rotate
+over 8 independent replicas (438 MB) and no step finds its cache in L2.  The
+device-timed region is one replay of a CUDA graph holding exactly K steps
+(captured once, warmed by W eager steps and one untimed replay), max over
+ranks.
 
 Multi-GPU (torchrun): requests are batch-partitioned -- every rank decodes its
-own 16 sequences, no collective in the timed loop (weak scaling); the step time
-is the max over ranks.
+own sequences, no collective in the timed loop (weak scaling).
 
---workload config3 is config 3's per-GPU batch (8 sequences of 32768 + 128
-tokens, 4-bit, group 64); --workload config3split is its long-context half:
-ONE 131072 + 128-token sequence split over the ranks (strong scaling), each
-step ending with the exchange of every rank's (out, LSE) over NVLink peer
-memory and the LSE merge (the NCCL all-gather variant is timed beside it).
+The same JSON line carries, at every N:
+* ``config3``: BASELINE config 3's batch half, 8 sequences per GPU of 32768 +
+  128 tokens, 4-bit, group 64 (weak scaling; 64 sequences at N = 8);
+* ``config3split``: its long-context half, ONE 131072 + 128-token sequence
+  split over the ranks (strong scaling), each step ending with the exchange of
+  every rank's (out, LSE) over NVLink peer memory and the LSE merge (the NCCL
+  all-gather variant timed beside it);
+and at N = 1: ``long_query`` (config 4: the tcgen05 kernel alone and the whole
+``long_query_attention_summary`` call over the real segment mix), ``config1``
+(the GPU pipeline and its CPU port), ``pack`` and the CPU baseline.
 
-Reported: value = decode tokens/s (whole job); e2e = the same through the
-public API (DecodeStepGraph) with the query copied from pinned host memory and
-the output and LSE read back every step (e2e_eager: the same through per-call
-PhysicalDecodeBatch and copy_ calls); the roofline of the decode step against
-the measured HBM copy bandwidth; and the CPU baseline (the oracle port of the
-reference algorithm).
+``e2e`` = the headline metric through the public API (DecodeStepGraph) with
+the query read from pinned host memory and the output and LSE written back
+every step.  ``--impl reference`` times the reference's own CPU path (a torch
+restatement in oracle/reference_cpu.py, all host cores) on the same workload.
 """
 
 from __future__ import annotations
@@ -40,164 +44,90 @@ import statistics
 import sys
 import threading
 import time
+from dataclasses import dataclass
+
+import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BATCH = 16
-TOKENS = 8192
-RESIDUAL = 128
-WORKLOAD = "config2"
-
 Q_HEADS = 28
 KV_HEADS = 4
 HEAD_DIM = 128
-BITS = 2
-GROUP = 32
-REPLICAS = 8
 METRIC = "packed-KV attention HBM GB/s & decode tokens/s/GPU at 1/2/4/8 B200"
 
 
-def algorithmic_bytes_per_pair() -> int:
-    """Bytes one decode step must move per (sequence, KV head)."""
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    batch: int      # sequences per GPU (1 for the split: one sequence over all GPUs)
+    tokens: int     # packed tokens per sequence
+    residual: int   # bf16 residual tokens per sequence
+    bits: int
+    group: int
+    replicas: int   # cache replicas the steps rotate over (beyond L2)
 
-    codes = 2 * TOKENS * HEAD_DIM * BITS // 8
-    key_stats = (TOKENS // GROUP) * HEAD_DIM * 2 * 2
-    value_stats = TOKENS * (HEAD_DIM // GROUP) * 2 * 2
-    residual = RESIDUAL * HEAD_DIM * 2 * 2
-    q_and_o = (Q_HEADS // KV_HEADS) * HEAD_DIM * 2 * 2
-    return codes + key_stats + value_stats + residual + q_and_o
+    def pair_bytes(self, tokens: int | None = None, residual: int | None = None) -> int:
+        """Bytes one decode step must move per (sequence, KV head)."""
+
+        t = self.tokens if tokens is None else tokens
+        r = self.residual if residual is None else residual
+        codes = 2 * t * HEAD_DIM * self.bits // 8
+        key_stats = (t // self.group) * HEAD_DIM * 2 * 2
+        value_stats = t * (HEAD_DIM // self.group) * 2 * 2
+        return codes + key_stats + value_stats + r * HEAD_DIM * 2 * 2 + (Q_HEADS // KV_HEADS) * HEAD_DIM * 2 * 2
+
+    def step_bytes(self) -> int:
+        return self.pair_bytes() * self.batch * KV_HEADS
+
+    def describe(self) -> str:
+        if self.name == "config3split":
+            return (f"config3split: one sequence of {self.tokens} packed KIVI {self.bits}-bit G{self.group} + "
+                    f"{self.residual} bf16 tokens split over the GPUs, 28/4 heads, D=128")
+        return (f"{self.name}: packed KIVI {self.bits}-bit G{self.group} decode, {self.batch} seqs/GPU, "
+                f"T={self.tokens}+{self.residual} bf16 residual, 28/4 heads, D=128")
 
 
-def measured_peaks() -> tuple[float, str]:
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+WORKLOADS = {
+    # BASELINE config 2: 16 sequences per GPU, 8192 + 128 tokens, 2-bit, group 32
+    "config2": Workload("config2", 16, 8192, 128, 2, 32, 8),
+    # BASELINE config 3 per GPU (batch 64 over 8 GPUs): 8 sequences, 32768 + 128 tokens, 4-bit, group 64
+    "config3": Workload("config3", 8, 32768, 128, 4, 64, 2),
+    # BASELINE config 3, long-context half: one 131072 + 128-token sequence split over the GPUs
+    "config3split": Workload("config3split", 1, 131072, 128, 4, 64, 0),
+}
+
+
+def measured_peak(key: str, fallback: float) -> tuple[float, str]:
     try:
-        with open(path) as handle:
-            return float(json.load(handle)["hbm_gbs"]), "measured"
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as handle:
+            return float(json.load(handle)[key]), "measured"
     except (OSError, KeyError, ValueError):
-        return 6650.0, "fallback"
+        return fallback, "fallback"
 
 
-def measured_bf16_peak() -> tuple[float, str]:
-    """Dense bf16 tensor throughput (TFLOP/s, burst) of this pool's B200s."""
-
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    try:
-        with open(path) as handle:
-            return float(json.load(handle)["bf16_tflops"]), "measured"
-    except (OSError, KeyError, ValueError):
-        return 1590.0, "fallback"
-
-
-def pack_leg(device, dense_kv) -> dict:
-    """Quantize + pack (KIVI, the workload's bits and group) of the sequences' quantized
-    tokens: one fused key+value pack launch per sequence (group 32; the key
-    and value kernels separately for other groups), captured in a CUDA graph
-    and timed with CUDA events.  Algorithmic bytes = bf16 K and V read +
-    codes and statistics written."""
-
-    import torch
-
-    from unicache_b200 import kernels
-
-    keys = [k[:TOKENS] for k, _ in dense_kv]
-    vals = [v[:TOKENS] for _, v in dense_kv]
-    def run():
-        for k, v in zip(keys, vals):
-            kernels.kivi_pack_kv(k, v, k_bits=BITS, v_bits=BITS, group_size=GROUP)
-    run()
-    torch.cuda.synchronize()
-    stream = torch.cuda.Stream(device=device)
-    stream.wait_stream(torch.cuda.current_stream(device))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(graph, stream=stream):
-            run()
-    torch.cuda.current_stream(device).wait_stream(stream)
-    graph.replay()
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    reps = 5
-    t0.record()
-    for _ in range(reps):
-        graph.replay()
-    t1.record()
-    torch.cuda.synchronize()
-    seconds = t0.elapsed_time(t1) / 1000.0 / reps / len(keys)
-    per_seq = (2 * TOKENS * KV_HEADS * HEAD_DIM * 2                       # bf16 K and V read
-               + 2 * TOKENS * KV_HEADS * HEAD_DIM * BITS // 8               # codes written
-               + 2 * 2 * TOKENS * KV_HEADS * HEAD_DIM // GROUP * 2)         # scale + min, K and V
-    peak, kind = measured_peaks()
-    gbs = per_seq / seconds / 1e9
-    del graph
-    return {"us_per_sequence": seconds * 1e6, "algorithmic_bytes_per_sequence": per_seq,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "peak_source": kind}}
-
-
-def long_query_leg(device) -> dict:
-    """BASELINE config 4, one layer: a 1024-token query block (28 query / 4 KV
-    heads) against 3095 cached tokens per KV head (51 + 980 H2O, 992 packed +
-    32 residual, 16 boundary, 1024 current-latent), non-causal, on the tcgen05
-    kernel with the operands resident; FLOPs = 4 * Lq * Hq * D * N."""
-
-    import torch
-
-    from unicache_b200 import kernels
-
-    heads, grp, lq, n = KV_HEADS, Q_HEADS // KV_HEADS, 1024, 3095
-    n_pad = (n + 7) // 8 * 8
-    gen = torch.Generator(device=device).manual_seed(1)
-    q = torch.randn(heads, lq * grp, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
-    k = torch.zeros(heads, n_pad, HEAD_DIM, device=device, dtype=torch.bfloat16)
-    vt = torch.zeros(heads, HEAD_DIM, n_pad, device=device, dtype=torch.bfloat16)
-    k[:, :n] = torch.randn(heads, n, HEAD_DIM, generator=gen, device=device).to(torch.bfloat16)
-    vt[:, :, :n] = torch.randn(heads, HEAD_DIM, n, generator=gen, device=device).to(torch.bfloat16)
-    out = torch.empty_like(q)
-    lse = torch.empty(heads, lq * grp, device=device, dtype=torch.float32)
-    for _ in range(3):
-        kernels.prefill_attention(q, k, vt, n, out=out, lse=lse)
-    torch.cuda.synchronize()
-    reps = 20
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(reps):
-        kernels.prefill_attention(q, k, vt, n, out=out, lse=lse)
-    t1.record()
-    torch.cuda.synchronize()
-    seconds = t0.elapsed_time(t1) / 1000.0 / reps
-    flops = 4.0 * lq * Q_HEADS * HEAD_DIM * n
-    peak, kind = measured_bf16_peak()
-    achieved = flops / seconds / 1e12
-    return {"workload": "config4 layer: Lq=1024 x 28/4 heads over 3095 keys, D=128, bf16, non-causal",
-            "us_per_layer": seconds * 1e6, "tflops": achieved,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_source": kind}}
+def hbm_roofline(step_bytes: float, seconds: float) -> dict:
+    peak, kind = measured_peak("hbm_gbs", 6650.0)
+    achieved = step_bytes / seconds / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": kind}
 
 
 def ncu_traffic() -> float | None:
-    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+    """Per-launch DRAM bytes of the config-2 decode kernel from the committed ncu summary."""
 
-    path = os.path.join(ROOT, "profiles", "decode_config2_traffic.json")
     try:
-        with open(path) as handle:
+        with open(os.path.join(ROOT, "profiles", "decode_config2_traffic.json")) as handle:
             return float(json.load(handle)["dram_bytes_per_launch"])
     except (OSError, KeyError, ValueError):
         return None
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons through NVML while running."""
+    """Samples SM clocks and throttle reasons through NVML while running (reads only)."""
 
-    REASONS = {
-        "sw_power_cap": 0x4,
-        "hw_slowdown": 0x8,
-        "sw_thermal_slowdown": 0x20,
-        "hw_thermal_slowdown": 0x40,
-        "hw_power_brake_slowdown": 0x80,
-    }
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index: int):
         self.index = index
@@ -236,92 +166,465 @@ class ClockSampler:
             self._thread.join()
 
     def summary(self) -> dict:
-        return {
-            "sm_mhz": statistics.median(self.samples) if self.samples else None,
-            "sm_max_mhz": self.max_mhz,
-            "reasons": sorted(self.reasons),
-            "samples": len(self.samples),
-        }
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-_ORACLE_CACHES: dict = {}
+# ------------------------------------------------------------------ run context
+class Run:
+    """Process-group plumbing shared by the legs: every rank runs the same legs
+    in the same order, so every collective below is matched."""
+
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local_rank)
+        self.device = torch.device("cuda", self.local_rank)
+        self.dist = dist
+        if self.world > 1:
+            import datetime
+
+            dist.init_process_group("nccl", device_id=self.device, timeout=datetime.timedelta(seconds=120))
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, values: list[float]) -> list[float]:
+        if self.world == 1:
+            return values
+        import torch
+
+        t = torch.tensor(values, device=self.device, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(x) for x in t]
+
+    def graph_seconds(self, step_fn, steps: int, sampler: bool = False):
+        """Device time of ``steps`` calls of step_fn(i) captured in one CUDA graph
+        (barrier + synchronize on both sides of the replay)."""
+
+        import torch
+
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(steps):
+                    step_fn(i)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        clocks = ClockSampler(self.local_rank) if sampler else None
+        if clocks:
+            clocks.__enter__()
+        t0.record()
+        graph.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        if clocks:
+            clocks.__exit__(None, None, None)
+        self.barrier()
+        del graph  # released before the process group is destroyed
+        return t0.elapsed_time(t1) / 1000.0, clocks
+
+    def eager_seconds(self, step_fn, steps: int, warmup: int) -> float:
+        import torch
+
+        for i in range(warmup):
+            step_fn(i)
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(steps):
+            step_fn(i)
+        t1.record()
+        torch.cuda.synchronize()
+        self.barrier()
+        return t0.elapsed_time(t1) / 1000.0
+
+    def close(self) -> None:
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
 
 
-SAMPLE_KV_HEADS = 1  # the CPU sample decodes one of the KV_HEADS heads of a sequence
+# ------------------------------------------------------------------ batch-partitioned decode
+def build_batches(run: Run, wl: Workload, seed: int):
+    """``wl.replicas`` decode batches of ``wl.batch`` packed sequences each
+    (generated on the GPU, seeded per rank); returns (batches, pack seconds per
+    replica, the first replica's dense K/V)."""
 
-
-def cpu_oracle_sample(seq_seed: int) -> tuple[float, int]:
-    """Decode one token of one sequence with the oracle port of the reference
-    algorithm (dequantize the packed cache, float64 attention) on one core,
-    on a bounded sample: one KV head with its 7 query heads, a quarter of the
-    sequence's work.  Returns (seconds scaled to the whole sequence, tokens
-    decoded).  The packed cache of a seed is built once per process and
-    reused, as a decode loop reuses its cache; only the decode is timed."""
-
-    from oracle import attention, kivi
-    from unicache_b200.synthetic import make_kv, make_query
-
-    try:
-        from threadpoolctl import threadpool_limits
-    except ImportError:  # pragma: no cover
-        threadpool_limits = None
-    if seq_seed not in _ORACLE_CACHES:
-        key, value = make_kv(TOKENS + RESIDUAL, SAMPLE_KV_HEADS, HEAD_DIM, seed=seq_seed)
-        query = make_query(1, Q_HEADS // KV_HEADS * SAMPLE_KV_HEADS, HEAD_DIM, seed=seq_seed)
-        cache = kivi.packed_from_dense(key.float().numpy(), value.float().numpy(), "bfloat16", k_bits=BITS,
-                                       v_bits=BITS, group_size=GROUP, residual_length=RESIDUAL)
-        _ORACLE_CACHES[seq_seed] = (cache, query.float().numpy())
-    cache, q = _ORACLE_CACHES[seq_seed]
-    ctx = threadpool_limits(limits=1) if threadpool_limits else None
-    if ctx:
-        ctx.__enter__()
-    try:
-        start = time.perf_counter()
-        rk, rv = kivi.packed_dequantize(cache)
-        attention.attention_summary(q, rk, rv)
-        elapsed = (time.perf_counter() - start) * (KV_HEADS / SAMPLE_KV_HEADS)
-    finally:
-        if ctx:
-            ctx.__exit__(None, None, None)
-    return elapsed, 1
-
-
-def _set_workload(name: str) -> None:
-    """Pool workers start fresh (spawn): give them the parent's workload and
-    one thread each."""
-
-    global WORKLOAD
-    WORKLOAD = name
-    globals().update(WORKLOADS[name])
     import torch
 
-    torch.set_num_threads(1)
+    from unicache_b200 import PackedKIVICache, PhysicalDecodeBatch
+
+    dev = run.device
+    gen = torch.Generator(device=dev).manual_seed(seed + 7919 * run.rank)
+    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(dev)
+    batches, pack_times, first_dense = [], [], None
+    n = wl.tokens + wl.residual
+    for r in range(wl.replicas):
+        dense = []
+        for _ in range(wl.batch):
+            k = torch.randn(n, KV_HEADS, HEAD_DIM, generator=gen, device=dev)
+            k[:, :, outlier] *= 10.0
+            v = torch.randn(n, KV_HEADS, HEAD_DIM, generator=gen, device=dev)
+            dense.append((k.to(torch.bfloat16), v.to(torch.bfloat16)))
+            del k, v
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record()
+        seqs = [[PackedKIVICache.from_dense(k, v, logical_token_ids=torch.arange(n, device=dev), token_type_id=3,
+                                            k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group,
+                                            residual_length=wl.residual)] for k, v in dense]
+        stop.record()
+        torch.cuda.synchronize()
+        pack_times.append(start.elapsed_time(stop) / 1000.0)
+        if r == 0:
+            first_dense = dense
+        del dense
+        batches.append(PhysicalDecodeBatch(seqs, num_kv_heads=KV_HEADS, head_dim=HEAD_DIM))
+    torch.cuda.empty_cache()
+    return batches, pack_times, first_dense
+
+
+def decode_leg(run: Run, wl: Workload, *, headline: bool) -> dict:
+    """Batch-partitioned decode of ``wl``: device-timed graph of K steps, and
+    for the headline also the end-to-end legs through the public API."""
+
+    import torch
+
+    from unicache_b200 import DecodeStepGraph, kernels
+
+    args = run.args
+    batches, pack_times, first_dense = build_batches(run, wl, seed=1234 if wl.name == "config2" else 4321)
+    dev = run.device
+    gen = torch.Generator(device=dev).manual_seed(77 + run.rank)
+    query = torch.randn(wl.batch, Q_HEADS, HEAD_DIM, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(query)
+    lse = torch.empty(wl.batch, Q_HEADS, device=dev, dtype=torch.float32)
+    for i in range(args.warmup):
+        batches[i % wl.replicas](query, out=out, lse=lse)
+    elapsed, clocks = run.graph_seconds(lambda i: batches[i % wl.replicas](query, out=out, lse=lse), args.steps,
+                                        sampler=headline)
+    result = {}
+    e2e_elapsed = eager_elapsed = 0.0
+    if headline:
+        # end to end through the public API with host buffers: DecodeStepGraph
+        # (H2D query, decode, merge, D2H out + LSE as one graph per step), and
+        # the eager per-call path with copy_ calls
+        host_q = torch.empty_like(query, device="cpu").pin_memory()
+        host_q.copy_(query.cpu())
+        host_o = torch.empty_like(out, device="cpu").pin_memory()
+        host_l = torch.empty_like(lse, device="cpu").pin_memory()
+        steps = [DecodeStepGraph(b, host_q, host_o, host_l) for b in batches]
+        for step in steps:  # first replays upload each graph
+            step()
+            step()
+        e2e_elapsed = run.eager_seconds(lambda i: steps[i % wl.replicas](), args.steps, args.warmup)
+        del steps
+        dev_q = torch.empty_like(query)
+
+        def eager_step(i):
+            dev_q.copy_(host_q, non_blocking=True)
+            o, l = batches[i % wl.replicas](dev_q)
+            host_o.copy_(o, non_blocking=True)
+            host_l.copy_(l, non_blocking=True)
+
+        eager_elapsed = run.eager_seconds(eager_step, args.steps, args.warmup)
+        result["h2d"] = query.numel() * query.element_size()
+        result["d2h"] = out.numel() * out.element_size() + lse.numel() * lse.element_size()
+    status = kernels.device_status()
+    elapsed, e2e_elapsed, eager_elapsed, status = run.max_over_ranks(
+        [elapsed, e2e_elapsed, eager_elapsed, float(status)])
+    tokens = wl.batch * run.world * args.steps
+    step_s = elapsed / args.steps
+    result.update({
+        "value": tokens / elapsed,
+        "ms_per_step": 1000.0 * step_s,
+        "roofline": dict(hbm_roofline(wl.step_bytes(), step_s), algorithmic_bytes_per_launch=wl.step_bytes(),
+                         kernel_ms=1000.0 * step_s,
+                         kernel="decode step = decode_kernel + state_merge_kernel, timed over a graph replay"),
+        "device_status": int(status),
+        "clocks": clocks.summary() if clocks else None,
+        "pack_seconds": statistics.median(pack_times),
+        "first_dense": first_dense,
+    })
+    if headline:
+        result["e2e_value"] = tokens / e2e_elapsed
+        result["eager_value"] = tokens / eager_elapsed
+    return result
+
+
+# ------------------------------------------------------------------ sequence split
+def shard_bytes(wl: Workload, tokens: int, residual: int) -> int:
+    return KV_HEADS * wl.pair_bytes(tokens, residual)
+
+
+def split_leg(run: Run) -> dict:
+    """BASELINE config 3, long-context half: one sequence split over the ranks
+    in contiguous group-aligned shards (the last rank also holds the residual).
+    A step = every rank decodes its shard, then the peer-memory exchange of
+    every rank's (out, LSE) and the LSE merge in one kernel (NCCL all-gather +
+    merge kernel timed the same way); strong scaling, max over ranks."""
+
+    import torch
+
+    from unicache_b200 import PackedKIVICache, kernels
+    from unicache_b200.distributed import PeerExchange, SequenceSplitDecode, split_tokens
+
+    wl = WORKLOADS["config3split"]
+    args, dev, world, rank = run.args, run.device, run.world, run.rank
+    start, stop = split_tokens(wl.tokens + wl.residual, world, wl.group, wl.residual)[rank]
+    n_local = stop - start
+    residual = wl.residual if rank == world - 1 else 0
+    local_bytes = shard_bytes(wl, n_local - residual, residual)
+    replicas = max(2, math.ceil(256e6 / local_bytes))
+    gen = torch.Generator(device=dev).manual_seed(4321 + 7919 * rank)
+    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(dev)
+    peer = PeerExchange(Q_HEADS, dev) if world > 1 else None
+    decoders, nccl_decoders = [], []
+    for _ in range(replicas):
+        k = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=dev)
+        k[:, :, outlier] *= 10.0
+        v = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=dev)
+        cache = PackedKIVICache.from_dense(k.to(torch.bfloat16), v.to(torch.bfloat16),
+                                           logical_token_ids=torch.arange(start, stop, device=dev), token_type_id=3,
+                                           k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group,
+                                           residual_length=residual)
+        del k, v
+        decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                                            exchange="peer" if world > 1 else "nccl", peer_exchange=peer))
+        nccl_decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM))
+    torch.cuda.empty_cache()
+    qgen = torch.Generator(device=dev).manual_seed(99)  # every rank decodes the same query
+    query = torch.randn(1, Q_HEADS, HEAD_DIM, generator=qgen, device=dev).to(torch.bfloat16)
+    # eager per-call steps (they also warm the NCCL communicator before capture)
+    eager = run.eager_seconds(lambda i: decoders[i % replicas](query), args.steps, args.warmup)
+    run.eager_seconds(lambda i: nccl_decoders[i % replicas](query), args.steps, args.warmup)
+    local = run.eager_seconds(lambda i: decoders[i % replicas].plan.run(query), args.steps, args.warmup)
+    elapsed, _ = run.graph_seconds(lambda i: decoders[i % replicas](query), args.steps)
+    nccl, _ = run.graph_seconds(lambda i: nccl_decoders[i % replicas](query), args.steps)
+    status = kernels.device_status()
+    elapsed, nccl, eager, local, status = run.max_over_ranks([elapsed, nccl, eager, local, float(status)])
+    if peer is not None:
+        torch.cuda.synchronize()
+        peer.close()
+    step_s = elapsed / args.steps
+    total = shard_bytes(wl, wl.tokens, wl.residual)
+    return {
+        "workload": wl.describe(),
+        "n_gpus": world,
+        "scaling": "strong",
+        "value": args.steps / elapsed,
+        "unit": "tokens/s",
+        "ms_per_step": 1000.0 * step_s,
+        "exchange": "peer-memory kernel (epoch-tagged NVLink peer stores + LSE merge)" if world > 1 else "none",
+        "nccl_exchange_ms_per_step": 1000.0 * nccl / args.steps,
+        "local_decode_ms_per_step_eager": 1000.0 * local / args.steps,
+        "eager_ms_per_step": 1000.0 * eager / args.steps,
+        "roofline_per_gpu": dict(hbm_roofline(total / world, step_s), algorithmic_bytes_per_gpu=total // world),
+        "l2": f"steps rotate over {replicas} shard replicas ({replicas * local_bytes / 1e6:.0f} MB per GPU)",
+        "device_status": int(status),
+    }
+
+
+# ------------------------------------------------------------------ N = 1 legs
+def pack_leg(run: Run, wl: Workload, dense_kv) -> dict:
+    """Quantize + pack of the sequences' quantized tokens, one fused key+value
+    launch per sequence, captured in a CUDA graph.  Algorithmic bytes = bf16 K
+    and V read + codes and statistics written."""
+
+    from unicache_b200 import kernels
+
+    keys = [k[:wl.tokens] for k, _ in dense_kv]
+    vals = [v[:wl.tokens] for _, v in dense_kv]
+
+    def step(_i):
+        for k, v in zip(keys, vals):
+            kernels.kivi_pack_kv(k, v, k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group)
+
+    step(0)
+    reps = 5
+    elapsed, _ = run.graph_seconds(step, reps)
+    seconds = elapsed / reps / len(keys)
+    per_seq = (2 * wl.tokens * KV_HEADS * HEAD_DIM * 2
+               + 2 * wl.tokens * KV_HEADS * HEAD_DIM * wl.bits // 8
+               + 2 * 2 * wl.tokens * KV_HEADS * HEAD_DIM // wl.group * 2)
+    return {"us_per_sequence": seconds * 1e6, "algorithmic_bytes_per_sequence": per_seq,
+            "roofline": hbm_roofline(per_seq, seconds)}
+
+
+def long_query_leg(run: Run) -> dict:
+    """BASELINE config 4, one layer: the 1024-token latent block (28 query / 4
+    KV heads) over 3095 cached tokens per KV head, non-causal.  ``kernel``:
+    the tcgen05 kernel alone on resident dense operands; ``e2e``: the whole
+    ``long_query_attention_summary`` call over the real segment mix (H2O
+    instruction and ViT rows, packed VAE tokens, residual, boundary and latent
+    rows).  FLOPs = 4 * Lq * Hq * D * N."""
+
+    import torch
+
+    from unicache_b200 import kernels
+    from unicache_b200.adapters.attention import long_query_attention_summary
+    from unicache_b200.workloads import config4_layer
+
+    dev = run.device
+    heads, grp, lq, n = KV_HEADS, Q_HEADS // KV_HEADS, 1024, 3095
+    n_pad = (n + 7) // 8 * 8
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(heads, lq * grp, HEAD_DIM, generator=gen, device=dev).to(torch.bfloat16)
+    k = torch.zeros(heads, n_pad, HEAD_DIM, device=dev, dtype=torch.bfloat16)
+    vt = torch.zeros(heads, HEAD_DIM, n_pad, device=dev, dtype=torch.bfloat16)
+    k[:, :n] = torch.randn(heads, n, HEAD_DIM, generator=gen, device=dev).to(torch.bfloat16)
+    vt[:, :, :n] = torch.randn(heads, HEAD_DIM, n, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lse = torch.empty(heads, lq * grp, device=dev, dtype=torch.float32)
+    reps = 20
+    kernel_s = run.eager_seconds(lambda i: kernels.prefill_attention(q, k, vt, n, out=out, lse=lse), reps, 3) / reps
+    layer = config4_layer(dev, seed=1)
+    assert layer.key_tokens == n
+    e2e_s = run.eager_seconds(lambda i: long_query_attention_summary(layer.query, layer.segments,
+                                                                     dense_key=layer.dense_key,
+                                                                     dense_value=layer.dense_value), reps, 3) / reps
+    flops = 4.0 * lq * Q_HEADS * HEAD_DIM * n
+    peak, kind = measured_peak("bf16_tflops", 1590.0)
+
+    def roof(seconds):
+        achieved = flops / seconds / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": kind}
+
+    return {"workload": "config4 layer: Lq=1024 x 28/4 heads over 3095 keys (51+980 H2O, 992 packed 2-bit G32 + "
+                        "32 residual, 16 boundary, 1024 latent), D=128, bf16, non-causal",
+            "us_per_layer": kernel_s * 1e6, "tflops": flops / kernel_s / 1e12, "roofline": roof(kernel_s),
+            "e2e_us_per_layer": e2e_s * 1e6, "e2e_roofline": roof(e2e_s),
+            "e2e_api": "long_query_attention_summary over the segment list"}
+
+
+def config1_leg(run: Run) -> dict:
+    """BASELINE config 1 (one fp32 layer, 2048 tokens): KIVI fake quantization
+    of the first 1920 tokens (2-bit, group 32), H2O scores of 64 decode queries
+    (LSE pass + scoring kernel), top-k selection and compaction to 410 tokens
+    per KV head, then one decode step; timed on the GPU (CUDA events) and as
+    the CPU port of the reference algorithm (numpy oracle, one core)."""
+
+    import numpy as np
+    import torch
+
+    from oracle import attention, h2o, kivi
+    from unicache_b200 import GQAH2OCache, kernels
+    from unicache_b200.adapters.attention import fused_h2o_decode
+    from unicache_b200.operators.physical import kivi_fake_quant_key, kivi_fake_quant_value
+    from unicache_b200.synthetic import make_kv, make_query
+
+    dev = run.device
+    key, value = make_kv(2048, KV_HEADS, HEAD_DIM, seed=0, dtype=torch.float32, device=dev)
+    queries = make_query(64, Q_HEADS, HEAD_DIM, seed=100, dtype=torch.float32, device=dev)
+    query = make_query(1, Q_HEADS, HEAD_DIM, seed=0, device=dev)
+    ids = torch.arange(2048, device=dev)
+    scale = 1.0 / math.sqrt(HEAD_DIM)
+
+    def pipeline(_i):
+        fk = kivi_fake_quant_key(key[:1920], bits=2, group_size=32)
+        fv = kivi_fake_quant_value(value[:1920], bits=2, group_size=32)
+        k_all = torch.cat([fk, key[1920:]])
+        v_all = torch.cat([fv, value[1920:]])
+        scores = kernels.h2o_scores(queries, k_all, None, kv_heads=KV_HEADS, softmax_scale=scale)
+        cache = GQAH2OCache.from_dense(k_all.to(torch.bfloat16), v_all.to(torch.bfloat16), logical_token_ids=ids,
+                                       token_type_id=1, per_kv_head_scores=scores, target_tokens=410,
+                                       recent_tokens=102, selection_frozen=True)
+        return fused_h2o_decode(query, None, None, [cache])
+
+    reps = 10
+    gpu_s = run.eager_seconds(pipeline, reps, 3) / reps
+    hk, hv, hq, hq1 = (t.float().cpu().numpy() for t in (key, value, queries, query))
+    cpu_times = []
+    for _ in range(2):
+        t0 = time.perf_counter()
+        ek = kivi.fake_quant_key(hk[:1920], "float32", bits=2, group_size=32)
+        ev = kivi.fake_quant_value(hv[:1920], "float32", bits=2, group_size=32)
+        ok, ov = np.concatenate([ek, hk[1920:]]), np.concatenate([ev, hv[1920:]])
+        sc = h2o.reduce_probabilities(attention.attention_probabilities(hq, ok), KV_HEADS)
+        kept = h2o.h2o_from_dense(ok, ov, np.arange(2048), sc, 410, 102)
+        attention.attention_summary(hq1, kept["key"].transpose(1, 0, 2), kept["value"].transpose(1, 0, 2))
+        cpu_times.append(time.perf_counter() - t0)
+    return {"workload": "config1: fp32 layer, 2048 tokens (1920 fake-quantized 2-bit G32 + 128 fp32), H2O scores "
+                        "of 64 queries, keep 410/KV head (308 heavy + 102 recent), one decode step",
+            "gpu_ms_per_layer": gpu_s * 1e3,
+            "cpu_port_ms_per_layer": min(cpu_times) * 1e3, "cpu_cores": 1,
+            "cpu_kind": "port (numpy restatement of the reference algorithm, float64 attention)"}
+
+
+# ------------------------------------------------------------------ CPU reference path
+_CPU_CACHES: dict = {}
+
+
+def cpu_reference_steps(wl: Workload, steps: int, warmup: int, seqs_per_step: int) -> tuple[float, str, int]:
+    """Times the reference's own CPU decode path (oracle/reference_cpu.py: its
+    unpack, grouped dequantization, fp32 logits, softmax and bf16 AV product,
+    every KV head) with torch using every host core.  A step decodes one token
+    of ``seqs_per_step`` sequences of the workload, one after the other;
+    returns (tokens/s, sample description, cores)."""
+
+    import torch
+
+    from oracle import kivi, reference_cpu
+    from unicache_b200.synthetic import make_kv, make_query
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    seeds = [10_000 + i for i in range(seqs_per_step)]
+    for s in seeds:
+        if (wl.name, s) not in _CPU_CACHES:
+            key, value = make_kv(wl.tokens + wl.residual, KV_HEADS, HEAD_DIM, seed=s)
+            ref = kivi.packed_from_dense(key.float().numpy(), value.float().numpy(), "bfloat16", k_bits=wl.bits,
+                                         v_bits=wl.bits, group_size=wl.group, residual_length=wl.residual)
+            layout = {}
+            for name in ("key_code", "value_code"):
+                layout[name] = torch.from_numpy(np.ascontiguousarray(ref[name]).astype(np.int32))
+            for name in ("key_scale", "key_minimum", "value_scale", "value_minimum", "residual_key",
+                         "residual_value"):
+                layout[name] = torch.from_numpy(np.ascontiguousarray(ref[name], dtype=np.float32)).to(torch.bfloat16)
+            cache = reference_cpu.cache_from_layout(layout, k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group,
+                                                    quantized_tokens=wl.tokens, head_dim=HEAD_DIM)
+            _CPU_CACHES[(wl.name, s)] = (cache, make_query(1, Q_HEADS, HEAD_DIM, seed=s))
+    for _ in range(warmup):
+        for s in seeds:
+            reference_cpu.decode(*_CPU_CACHES[(wl.name, s)])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for s in seeds:
+            reference_cpu.decode(*_CPU_CACHES[(wl.name, s)])
+    elapsed = time.perf_counter() - t0
+    sample = (f"{seqs_per_step} of the workload's sequences per step ({wl.tokens}+{wl.residual} tokens, all "
+              f"{KV_HEADS} KV heads), one decode token each, through the reference's CPU path (unpack, grouped "
+              f"dequantization, fp32 logits, softmax, bf16 AV) in torch with {cores} threads")
+    return seqs_per_step * steps / elapsed, sample, cores
 
 
 def run_reference(args) -> None:
-    """The reference algorithm's CPU path (the oracle port) on the host cores."""
+    """``--impl reference``: the reference's CPU path on the host cores, rank 0 only."""
 
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    import multiprocessing as mp
-
-    cores = os.cpu_count() or 1
-    per_step = cores
-    seeds = [10_000 + i for i in range(per_step)]
-    ctx = mp.get_context("spawn")
-    times = []
-    with ctx.Pool(processes=cores, initializer=_set_workload, initargs=(WORKLOAD,)) as pool:
-        for _ in range(args.warmup):
-            pool.map(cpu_oracle_sample, seeds)
-        for _ in range(args.steps):
-            # the step's sequences decode in parallel: the step takes as long as its slowest
-            results = pool.map(cpu_oracle_sample, seeds)
-            times.append(max(r[0] for r in results))
-    total = sum(times)
-    value = per_step * args.steps / total
-    sample = (f"{per_step} {WORKLOAD} sequences per step ({TOKENS}+{RESIDUAL} tokens), one decode token each, timed on "
-              f"one of the {KV_HEADS} KV heads (7 query heads) and scaled x{KV_HEADS}")
+    wl = WORKLOADS[args.workload]
+    per_step = 4 if wl.tokens <= 8192 else 1
+    value, sample, cores = cpu_reference_steps(wl, args.steps, args.warmup, per_step)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -330,444 +633,110 @@ def run_reference(args) -> None:
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": 1000.0 * total / args.steps,
+        "ms_per_step": 1000.0 * per_step / value,
         "higher_is_better": True,
-        "scaling": "strong" if WORKLOAD == "config3split" else "weak",
+        "scaling": "strong" if wl.name == "config3split" else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": workload_name(),
-                   "sample": sample},
+        "config": headline_config(wl, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
 
 
+def headline_config(wl: Workload, world: int) -> dict:
+    step_bytes = wl.step_bytes()
+    return {
+        "workload": wl.describe(),
+        "global_batch": wl.batch * world,
+        "seq_len": wl.tokens + wl.residual,
+        "parallelism": f"batch-partitioned x{world}",
+        "l2": f"steps rotate over {wl.replicas} cache replicas ({wl.replicas * step_bytes / 1e6:.0f} MB > 126 MB L2)",
+    }
+
+
 def run_b200(args) -> None:
-    import torch
-    import torch.distributed as dist
-
-    from unicache_b200 import PackedKIVICache, PhysicalDecodeBatch, kernels
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
-
-    # ---- build REPLICAS x BATCH packed caches (generated on the GPU, seeded per rank)
-    gen = torch.Generator(device=device).manual_seed(1234 + 7919 * rank)
-    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(device)
-    replicas = []
-    pack_times = []
-    for r in range(REPLICAS):
-        seqs = []
-        dense = []
-        for _ in range(BATCH):
-            k = torch.randn(TOKENS + RESIDUAL, KV_HEADS, HEAD_DIM, generator=gen, device=device)
-            k[:, :, outlier] *= 10.0
-            v = torch.randn(TOKENS + RESIDUAL, KV_HEADS, HEAD_DIM, generator=gen, device=device)
-            dense.append((k.to(torch.bfloat16), v.to(torch.bfloat16)))
-        torch.cuda.synchronize()
-        start = torch.cuda.Event(enable_timing=True)
-        stop = torch.cuda.Event(enable_timing=True)
-        start.record()
-        for k, v in dense:
-            seqs.append([PackedKIVICache.from_dense(k, v, logical_token_ids=torch.arange(TOKENS + RESIDUAL, device=device),
-                                                    token_type_id=3, k_bits=BITS, v_bits=BITS, group_size=GROUP,
-                                                    residual_length=RESIDUAL)])
-        stop.record()
-        torch.cuda.synchronize()
-        pack_times.append(start.elapsed_time(stop) / 1000.0)
-        if r == 0:
-            pack_inputs = dense
-        del dense
-        replicas.append(PhysicalDecodeBatch(seqs, num_kv_heads=KV_HEADS, head_dim=HEAD_DIM))
-    torch.cuda.empty_cache()
-    query = (torch.randn(BATCH, Q_HEADS, HEAD_DIM, generator=gen, device=device)).to(torch.bfloat16)
-    out = torch.empty_like(query)
-    lse = torch.empty(BATCH, Q_HEADS, device=device, dtype=torch.float32)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    # ---- device-resident timed loop: the K decode steps (one decode kernel and
-    # one state-merge kernel each, rotating over the replicas) are captured
-    # once in a CUDA graph; W eager steps and one untimed replay warm it up.
-    for i in range(args.warmup):
-        replicas[i % REPLICAS](query, out=out, lse=lse)
-    torch.cuda.synchronize()
-    capture_stream = torch.cuda.Stream(device=device)
-    capture_stream.wait_stream(torch.cuda.current_stream(device))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(capture_stream):
-        with torch.cuda.graph(graph, stream=capture_stream):
-            for i in range(args.steps):
-                replicas[i % REPLICAS](query, out=out, lse=lse)
-    torch.cuda.current_stream(device).wait_stream(capture_stream)
-    graph.replay()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        t0.record()
-        graph.replay()
-        t1.record()
-        torch.cuda.synchronize()
-    barrier()
-    elapsed = t0.elapsed_time(t1) / 1000.0
-    kernel_s = [elapsed / args.steps]
-    status = kernels.device_status()
-    del graph
-
-    # ---- end-to-end through the public API with host buffers.  Each step
-    # copies the query from pinned host memory, decodes and copies the output
-    # and LSE back to pinned host memory; DecodeStepGraph replays those five
-    # operations as one graph (the eager per-call path is timed as well).
-    from unicache_b200 import DecodeStepGraph
-
-    host_q = torch.empty_like(query, device="cpu").pin_memory()
-    host_q.copy_(query.cpu())
-    host_o = torch.empty_like(out, device="cpu").pin_memory()
-    host_l = torch.empty_like(lse, device="cpu").pin_memory()
-    steps = [DecodeStepGraph(rep, host_q, host_o, host_l) for rep in replicas]
-    for step in steps:  # first replays upload each graph
-        step()
-        step()
-    for i in range(args.warmup):
-        steps[i % REPLICAS]()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        steps[i % REPLICAS]()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_elapsed = e0.elapsed_time(e1) / 1000.0
-    del steps
-
-    dev_q = torch.empty_like(query)
-    for i in range(args.warmup):
-        dev_q.copy_(host_q, non_blocking=True)
-        o, l = replicas[i % REPLICAS](dev_q)
-        host_o.copy_(o, non_blocking=True)
-        host_l.copy_(l, non_blocking=True)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for i in range(args.steps):
-        dev_q.copy_(host_q, non_blocking=True)
-        o, l = replicas[i % REPLICAS](dev_q)
-        host_o.copy_(o, non_blocking=True)
-        host_l.copy_(l, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    eager_elapsed = e0.elapsed_time(e1) / 1000.0
-
-    if world > 1:
-        t = torch.tensor([elapsed, e2e_elapsed, eager_elapsed, float(status)], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, e2e_elapsed, eager_elapsed, status = float(t[0]), float(t[1]), float(t[2]), int(t[3])
-
-    if rank == 0:
-        tokens = BATCH * world * args.steps
-        value = tokens / elapsed
-        step_bytes = algorithmic_bytes_per_pair() * BATCH * KV_HEADS
-        mean_kernel = statistics.mean(kernel_s)
-        achieved = step_bytes / mean_kernel / 1e9
-        peak, peak_kind = measured_peaks()
-        cpu_s, cpu_tokens = cpu_oracle_sample(4242)
+    run = Run(args)
+    wl = WORKLOADS[args.workload]
+    head = decode_leg(run, wl, headline=True)
+    pack = pack_leg(run, wl, head.pop("first_dense")) if run.world == 1 else None
+    sub3 = None
+    if wl.name != "config3":
+        r3 = decode_leg(run, WORKLOADS["config3"], headline=False)
+        r3.pop("first_dense")
+        c3 = WORKLOADS["config3"]
+        sub3 = {"workload": c3.describe(), "n_gpus": run.world, "scaling": "weak", "global_batch": c3.batch * run.world,
+                "value": r3["value"], "unit": "tokens/s", "ms_per_step": r3["ms_per_step"],
+                "roofline": r3["roofline"], "device_status": r3["device_status"]}
+    split = split_leg(run)
+    extra = {}
+    if run.world == 1:
+        extra["long_query"] = long_query_leg(run)
+        extra["config1"] = config1_leg(run)
+    if run.rank == 0:
         line = {
             "metric": METRIC,
-            "value": value,
+            "value": head["value"],
             "unit": "tokens/s",
-            "n_gpus": world,
+            "n_gpus": run.world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": 1000.0 * elapsed / args.steps,
+            "ms_per_step": head["ms_per_step"],
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": workload_name(),
-                "global_batch": BATCH * world,
-                "seq_len": TOKENS + RESIDUAL,
-                "parallelism": f"batch-partitioned x{world}",
-                "l2": f"steps rotate over {REPLICAS} cache replicas ({REPLICAS * step_bytes / 1e6:.0f} MB > 126 MB L2)",
-            },
-            "hbm_gbs": achieved,
-            "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "peak_source": peak_kind,
-                "traffic": ncu_traffic() if WORKLOAD == "config2" else None,
-                "algorithmic_bytes_per_launch": step_bytes,
-                "kernel_ms": 1000.0 * mean_kernel,
-                "kernel": "decode step = decode_kernel + state_merge_kernel, timed over a graph replay",
-            },
-            "pack": dict(pack_leg(device, pack_inputs),
-                         from_dense_seconds_per_16_seqs=statistics.median(pack_times)),
-            "e2e": {"value": tokens / e2e_elapsed, "unit": "tokens/s",
-                    "h2d_bytes_per_step": query.numel() * query.element_size(),
-                    "d2h_bytes_per_step": out.numel() * out.element_size() + lse.numel() * lse.element_size(),
+            "config": headline_config(wl, run.world),
+            "hbm_gbs": head["roofline"]["achieved"],
+            "roofline": dict(head["roofline"], traffic=ncu_traffic() if wl.name == "config2" else None),
+            "e2e": {"value": head["e2e_value"], "unit": "tokens/s", "h2d_bytes_per_step": head["h2d"],
+                    "d2h_bytes_per_step": head["d2h"],
                     "api": "DecodeStepGraph (per step: H2D query, decode, merge, D2H out + LSE, one graph launch)"},
-            "e2e_eager": {"value": tokens / eager_elapsed, "unit": "tokens/s",
+            "e2e_eager": {"value": head["eager_value"], "unit": "tokens/s",
                           "api": "PhysicalDecodeBatch.__call__ with per-step copy_ calls"},
             "gpu_launches": 2 * args.steps,
-            "long_query": long_query_leg(device) if world == 1 else None,
-            "clocks": clocks.summary(),
-            "device_status": status,
-            "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
-                             "sample": f"one {WORKLOAD} sequence, one decode token (dequantize + float64 attention), "
-                                       f"timed on one of the {KV_HEADS} KV heads and scaled x{KV_HEADS}"},
+            "clocks": head["clocks"],
+            "device_status": head["device_status"],
+            "config3": sub3,
+            "config3split": split,
         }
+        if pack is not None:
+            line["pack"] = dict(pack, from_dense_seconds_per_batch=head["pack_seconds"])
+        line.update(extra)
+        if run.world == 1:
+            value, sample, cores = cpu_reference_steps(wl, 3, 1, 4)
+            line["cpu_baseline"] = {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                    "sample": sample}
         print(json.dumps(line))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    run.close()
 
 
-def shard_bytes(tokens: int, residual: int) -> int:
-    """Bytes one decode step moves for one sequence shard of ``tokens`` packed
-    + ``residual`` bf16 tokens, over all KV heads (query and output included)."""
+def run_split_headline(args) -> None:
+    """--workload config3split: the split leg as the headline line."""
 
-    codes = 2 * tokens * HEAD_DIM * BITS // 8
-    key_stats = (tokens // GROUP) * HEAD_DIM * 2 * 2
-    value_stats = tokens * (HEAD_DIM // GROUP) * 2 * 2
-    res = residual * HEAD_DIM * 2 * 2
-    q_and_o = (Q_HEADS // KV_HEADS) * HEAD_DIM * 2 * 2
-    return KV_HEADS * (codes + key_stats + value_stats + res + q_and_o)
-
-
-def run_split(args) -> None:
-    """BASELINE config 3, long-context half: ONE sequence of TOKENS packed
-    (4-bit, group 64) + RESIDUAL bf16 tokens split over the ranks in
-    contiguous group-aligned shards (the last rank also holds the residual).
-    A step = every rank decodes its shard (decode + state merge), one NCCL
-    all-gather of every rank's (out, LSE), and the LSE merge; the step time is
-    the max over ranks (strong scaling: the sequence is fixed).  Steps rotate
-    over enough shard replicas to exceed the 126 MB L2."""
-
-    import torch
-    import torch.distributed as dist
-
-    from unicache_b200 import PackedKIVICache, kernels
-    from unicache_b200.distributed import PeerExchange, SequenceSplitDecode, split_tokens
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    group = None
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
-    start, stop = split_tokens(TOKENS + RESIDUAL, world, GROUP, RESIDUAL)[rank]
-    n_local = stop - start
-    residual = RESIDUAL if rank == world - 1 else 0
-    local_bytes = shard_bytes(n_local - residual, residual)
-    replicas_n = max(2, math.ceil(256e6 / local_bytes))
-    gen = torch.Generator(device=device).manual_seed(4321 + 7919 * rank)
-    outlier = torch.randperm(HEAD_DIM, generator=torch.Generator().manual_seed(0))[:4].to(device)
-    decoders, nccl_decoders = [], []
-    peer = PeerExchange(Q_HEADS, device) if world > 1 else None
-    for _ in range(replicas_n):
-        k = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=device)
-        k[:, :, outlier] *= 10.0
-        v = torch.randn(n_local, KV_HEADS, HEAD_DIM, generator=gen, device=device)
-        cache = PackedKIVICache.from_dense(k.to(torch.bfloat16), v.to(torch.bfloat16),
-                                           logical_token_ids=torch.arange(start, stop, device=device),
-                                           token_type_id=3, k_bits=BITS, v_bits=BITS, group_size=GROUP,
-                                           residual_length=residual)
-        del k, v
-        decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group,
-                                            exchange="peer", peer_exchange=peer))
-        nccl_decoders.append(SequenceSplitDecode([[cache]], num_kv_heads=KV_HEADS, head_dim=HEAD_DIM, group=group))
-    torch.cuda.empty_cache()
-    qgen = torch.Generator(device=device).manual_seed(99)  # every rank decodes the same query
-    query = torch.randn(1, Q_HEADS, HEAD_DIM, generator=qgen, device=device).to(torch.bfloat16)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def timed(step_fn) -> float:
-        for i in range(args.warmup):
-            step_fn(i)
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(args.steps):
-            step_fn(i)
-        e1.record()
-        torch.cuda.synchronize()
-        barrier()
-        return e0.elapsed_time(e1) / 1000.0
-
-    # eager per-call steps (also warm the NCCL communicator before capture)
-    eager_elapsed = timed(lambda i: decoders[i % replicas_n](query))
-    timed(lambda i: nccl_decoders[i % replicas_n](query))
-    local_elapsed = timed(lambda i: decoders[i % replicas_n].plan.run(query))
-
-    def graph_timed(decs):
-        # the K steps captured once in a CUDA graph (the exchange included)
-        capture_stream = torch.cuda.Stream(device=device)
-        capture_stream.wait_stream(torch.cuda.current_stream(device))
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(capture_stream):
-            with torch.cuda.graph(graph, stream=capture_stream):
-                for i in range(args.steps):
-                    decs[i % replicas_n](query)
-        torch.cuda.current_stream(device).wait_stream(capture_stream)
-        graph.replay()
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local_rank) as sampler:
-            g0.record()
-            graph.replay()
-            g1.record()
-            torch.cuda.synchronize()
-        barrier()
-        del graph  # released before the process group is destroyed
-        return g0.elapsed_time(g1) / 1000.0, sampler
-
-    # device-timed region: decode, state merge and the peer-memory exchange +
-    # merge kernel per step; the NCCL exchange is timed the same way for
-    # comparison
-    elapsed, clocks = graph_timed(decoders)
-    nccl_elapsed, _ = graph_timed(nccl_decoders)
-    host_q = query.cpu().pin_memory()
-    host_o = torch.empty(query.shape, dtype=query.dtype).pin_memory()
-    host_l = torch.empty((1, Q_HEADS), dtype=torch.float32).pin_memory()
-    dev_q = torch.empty_like(query)
-
-    def e2e_step(i):
-        dev_q.copy_(host_q, non_blocking=True)
-        o, l = decoders[i % replicas_n](dev_q)
-        host_o.copy_(o, non_blocking=True)
-        host_l.copy_(l, non_blocking=True)
-
-    e2e_elapsed = timed(e2e_step)
-    status = kernels.device_status()
-    if world > 1:
-        t = torch.tensor([elapsed, local_elapsed, e2e_elapsed, eager_elapsed, nccl_elapsed, float(status)],
-                         device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, local_elapsed, e2e_elapsed, eager_elapsed, nccl_elapsed, status = (
-            float(t[0]), float(t[1]), float(t[2]), float(t[3]), float(t[4]), int(t[5]))
-    total_bytes = shard_bytes(TOKENS, RESIDUAL)
-    if rank == 0:
-        step_s = elapsed / args.steps
-        peak, peak_kind = measured_peaks()
-        achieved = total_bytes / world / step_s / 1e9  # per GPU
-        cpu_s, cpu_tokens = cpu_oracle_sample(4242)
+    run = Run(args)
+    split = split_leg(run)
+    if run.rank == 0:
+        wl = WORKLOADS["config3split"]
         line = {
-            "metric": METRIC,
-            "value": args.steps / elapsed,
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": 1000.0 * step_s,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
+            "metric": METRIC, "value": split["value"], "unit": "tokens/s", "n_gpus": run.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": split["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": (f"config3split: one sequence of {TOKENS} packed KIVI {BITS}-bit G{GROUP} + {RESIDUAL} bf16 "
-                             f"tokens split over {world} GPU(s), 28/4 heads, D=128"),
-                "global_batch": 1,
-                "seq_len": TOKENS + RESIDUAL,
-                "parallelism": (f"sequence-split x{world} + one kernel: epoch-tagged peer stores of (out, LSE) "
-                                f"over NVLink + LSE merge" if world > 1 else "one GPU"),
-                "l2": f"steps rotate over {replicas_n} shard replicas ({replicas_n * local_bytes / 1e6:.0f} MB per GPU > 126 MB L2)",
-            },
-            "hbm_gbs": achieved,
-            "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "peak_source": peak_kind,
-                "traffic": None,
-                "algorithmic_bytes_per_launch": total_bytes // world,
-                "kernel_ms": 1000.0 * step_s,
-                "kernel": "per GPU: shard decode + state merge + peer exchange/merge, one graph replay of K steps",
-            },
-            "local_decode_ms_per_step": 1000.0 * local_elapsed / args.steps,
-            "eager_ms_per_step": 1000.0 * eager_elapsed / args.steps,
-            "nccl_exchange_ms_per_step": 1000.0 * nccl_elapsed / args.steps,
-            "e2e": {"value": args.steps / e2e_elapsed, "unit": "tokens/s",
-                    "h2d_bytes_per_step": query.numel() * query.element_size(),
-                    "d2h_bytes_per_step": host_o.numel() * host_o.element_size() + host_l.numel() * 4,
-                    "api": "SequenceSplitDecode.__call__ with the query copied from and the result copied to pinned host memory"},
-            "gpu_launches": (3 if world > 1 else 2) * args.steps,
-            "clocks": clocks.summary(),
-            "device_status": status,
-            "cpu_baseline": {"value": cpu_tokens / cpu_s, "unit": "tokens/s", "cores": 1, "kind": "port",
-                             "sample": f"the whole {TOKENS}+{RESIDUAL}-token sequence, one decode token (dequantize + "
-                                       f"float64 attention), timed on one of the {KV_HEADS} KV heads and scaled x{KV_HEADS}"},
+            "config": {"workload": wl.describe(), "global_batch": 1, "seq_len": wl.tokens + wl.residual,
+                       "parallelism": f"sequence-split x{run.world}", "l2": split["l2"]},
+            "roofline": dict(split["roofline_per_gpu"], traffic=None),
+            "gpu_launches": (3 if run.world > 1 else 2) * args.steps,
+            "config3split": split,
         }
         print(json.dumps(line))
-    if peer is not None:
-        torch.cuda.synchronize()
-        peer.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-WORKLOADS = {
-    # BASELINE config 2: 16 sequences per GPU, 8192 + 128 tokens, 2-bit, group 32
-    "config2": dict(BATCH=16, TOKENS=8192, RESIDUAL=128, BITS=2, GROUP=32, REPLICAS=8),
-    # BASELINE config 3 per GPU (batch 64 over 8 GPUs): 8 sequences, 32768 + 128
-    # tokens, 4-bit, group 64
-    "config3": dict(BATCH=8, TOKENS=32768, RESIDUAL=128, BITS=4, GROUP=64, REPLICAS=2),
-    # BASELINE config 3, long-context half: one 131072 + 128 token sequence,
-    # 4-bit, group 64, split over the GPUs (strong scaling)
-    "config3split": dict(BATCH=1, TOKENS=131072, RESIDUAL=128, BITS=4, GROUP=64, REPLICAS=0),
-}
-
-
-def workload_name() -> str:
-    if WORKLOAD == "config3split":
-        return (f"{WORKLOAD}: one sequence of {TOKENS} packed KIVI {BITS}-bit G{GROUP} + {RESIDUAL} bf16 tokens "
-                f"split over the GPUs, 28/4 heads, D=128")
-    return (f"{WORKLOAD}: packed KIVI {BITS}-bit G{GROUP} decode, {BATCH} seqs/GPU, T={TOKENS}+{RESIDUAL} "
-            f"bf16 residual, 28/4 heads, D=128")
+    run.close()
 
 
 def main() -> None:
-    global WORKLOAD
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=256)
@@ -775,14 +744,12 @@ def main() -> None:
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
     args = parser.parse_args()
-    WORKLOAD = args.workload
-    globals().update(WORKLOADS[args.workload])
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
-    elif WORKLOAD == "config3split":
-        run_split(args)
+    elif args.workload == "config3split":
+        run_split_headline(args)
     else:
         run_b200(args)
 
