@@ -1,0 +1,132 @@
+"""Long-query attention reading the segments in place (ucb_long_query_attention):
+dense and H2O rows copied into the tensor-core operand tiles, packed KIVI
+tiles restored in shared memory.
+
+Checked against (a) the workspace path it replaces: the bit-exact dequant
+kernel restores every packed span into a bf16 workspace, then the TMA-fed
+kernel runs over it (same operand values, so the outputs agree to a few bf16
+ulps), and (b) the float64 oracle within the north-star bound (max-abs 2e-2,
+mean-abs 1e-3; LSE 2e-2).  Span layouts cover packed spans that start
+mid-tile and mid-word, spans straddling tile boundaries, 4-bit codes, group
+64/128, head-major H2O rows, and ragged last tiles."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention, kivi
+from unicache_b200 import GQAH2OCache, PackedKIVICache, kernels
+from unicache_b200.adapters.attention import batched_long_query_attention, long_query_attention_summary
+from unicache_b200.synthetic import make_kv, make_query
+
+from .gpu_util import assert_attention_close, host, need_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+def _segments(seed, layout, bits, group):
+    segs, keys, vals = [], [], []
+    for i, (kind, n) in enumerate(layout):
+        k, v = make_kv(n, 4, 128, seed=seed * 10 + i, device="cuda")
+        if kind == "packed":
+            seg = PackedKIVICache.from_dense(k, v, logical_token_ids=torch.arange(n, device="cuda"), token_type_id=3,
+                                             k_bits=bits, v_bits=bits, group_size=group, residual_length=group // 2)
+            ref = kivi.packed_from_dense(host(k), host(v), "bfloat16", k_bits=bits, v_bits=bits, group_size=group,
+                                         residual_length=group // 2)
+            rk, rv = kivi.packed_dequantize(ref)
+        elif kind == "h2o":
+            sc = torch.rand(4, n, generator=torch.Generator().manual_seed(seed + i)).to("cuda")
+            seg = GQAH2OCache.from_dense(k, v, logical_token_ids=torch.arange(n, device="cuda"), token_type_id=1,
+                                         per_kv_head_scores=sc, target_tokens=max(1, n // 3), recent_tokens=n // 12)
+            rk, rv = host(seg.key).transpose(1, 0, 2), host(seg.value).transpose(1, 0, 2)
+        else:
+            seg = (k, v)
+            rk, rv = host(k), host(v)
+        segs.append(seg)
+        keys.append(rk)
+        vals.append(rv)
+    return segs, keys, vals
+
+
+def _workspace_path(query, segs):
+    """The replaced path: every segment restored into [H, Np, D] / [H, D, Np] bf16 workspaces."""
+
+    hkv = 4
+    parts_k, parts_v = [], []
+    for seg in segs:
+        if isinstance(seg, PackedKIVICache):
+            k, v = seg.dequantize(dtype=torch.bfloat16)
+            parts_k.append(k.transpose(0, 1))
+            parts_v.append(v.transpose(0, 1))
+        elif isinstance(seg, GQAH2OCache):
+            parts_k.append(seg.key)
+            parts_v.append(seg.value)
+        else:
+            parts_k.append(seg[0].transpose(0, 1))
+            parts_v.append(seg[1].transpose(0, 1))
+    kw = torch.cat(parts_k, dim=1)
+    vw = torch.cat(parts_v, dim=1)
+    n = int(kw.shape[1])
+    pad = (n + 7) // 8 * 8
+    k = torch.zeros(hkv, pad, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.zeros_like(k)
+    k[:, :n] = kw
+    v[:, :n] = vw
+    lq, hq, d = map(int, query.shape)
+    grp = hq // hkv
+    q = query.reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, lq * grp, d).contiguous()
+    out, lse = kernels.prefill_attention(q, k, v.transpose(1, 2).contiguous(), n)
+    out = out.view(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
+    return out, lse.view(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
+
+
+LAYOUTS = [
+    # (bits, group, [(kind, tokens)], query length)
+    (2, 32, [("dense", 16), ("h2o", 150), ("packed", 1024), ("dense", 100)], 1024),
+    (2, 32, [("h2o", 7), ("packed", 333), ("packed", 200), ("dense", 1)], 96),
+    (4, 64, [("packed", 700), ("dense", 129)], 300),
+    (4, 128, [("dense", 40), ("packed", 1000)], 37),
+    (2, 64, [("packed", 64)], 512),
+]
+
+
+@pytest.mark.parametrize("case", range(len(LAYOUTS)))
+def test_long_query_spans_match_workspace_path_and_oracle(case):
+    need_gpu()
+    bits, group, layout, lq = LAYOUTS[case]
+    segs, keys, vals = _segments(50 + case, layout, bits, group)
+    query = make_query(lq, 28, 128, seed=60 + case, device="cuda")
+    out, lse = long_query_attention_summary(query, segs)
+    w_out, w_lse = _workspace_path(query, segs)
+    torch.cuda.synchronize()
+    diff = (out.float() - w_out.float()).abs()
+    assert float(diff.max()) <= 8e-3, f"span path vs workspace path: {float(diff.max()):.3e}"
+    assert float((lse - w_lse).abs().max()) <= 1e-3
+    e_out, e_lse = attention.mixed_attention(host(query), keys, vals)
+    assert_attention_close(out, e_out, what=f"long-query spans case {case}")
+    assert np.abs(host(lse) - e_lse).max() <= 2e-2
+    # a second call reuses the cached span tables and is bitwise identical
+    out2, lse2 = long_query_attention_summary(query, segs)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
+    assert kernels.device_status() == 0
+
+
+def test_batched_long_query_spans_three_samples():
+    need_gpu()
+    samples, queries, expects = [], [], []
+    for i, (layout, lq) in enumerate([([("h2o", 90), ("packed", 500)], 40),
+                                      ([("packed", 1088)], 300), ([("dense", 70), ("h2o", 150)], 7)]):
+        segs, keys, vals = _segments(80 + i, layout, 2, 32)
+        q = make_query(lq, 28, 128, seed=90 + i, device="cuda")
+        samples.append(segs)
+        queries.append(q)
+        expects.append(attention.mixed_attention(host(q), keys, vals))
+    results = batched_long_query_attention(queries, samples)
+    torch.cuda.synchronize()
+    for (out, lse), (e_out, e_lse) in zip(results, expects):
+        assert_attention_close(out, e_out, what="batched spans")
+        assert np.abs(host(lse) - e_lse).max() <= 2e-2
+    assert kernels.device_status() == 0

@@ -151,55 +151,6 @@ def fused_mixed_decode(query: torch.Tensor, dense_key: torch.Tensor | None, dens
                                    int(query.shape[-1]))
 
 
-def _span_tokens(segments, include_residual: bool) -> list:
-    spans = []
-    for seg in segments:
-        if isinstance(seg, PackedKIVICache):
-            spans.append((seg, seg.quantized_tokens + (int(seg.residual_key.shape[0]) if include_residual else 0)))
-        elif isinstance(seg, GQAH2OCache):
-            spans.append((seg, seg.retained_tokens))
-        else:
-            spans.append((seg, int(seg[0].shape[0])))
-    return spans
-
-
-def _fill_kv(spans, kw: torch.Tensor, vw: torch.Tensor, t0: int) -> None:
-    """Write the segments' key/value rows into head-major workspaces [H, N, D]
-    from row t0 on (packed spans restored by the bit-exact dequant kernel)."""
-
-    for seg, n in spans:
-        if isinstance(seg, PackedKIVICache):
-            q = seg.quantized_tokens
-            if q:
-                seg.dequantize_range(0, q, dtype=torch.bfloat16, output_key=kw[:, t0:t0 + q].transpose(0, 1),
-                                     output_value=vw[:, t0:t0 + q].transpose(0, 1))
-            if n > q:
-                kw[:, t0 + q:t0 + n] = seg.residual_key[:n - q].transpose(0, 1)
-                vw[:, t0 + q:t0 + n] = seg.residual_value[:n - q].transpose(0, 1)
-        elif isinstance(seg, GQAH2OCache):
-            kw[:, t0:t0 + n] = seg.key
-            vw[:, t0:t0 + n] = seg.value
-        else:
-            kw[:, t0:t0 + n] = seg[0].transpose(0, 1)
-            vw[:, t0:t0 + n] = seg[1].transpose(0, 1)
-        t0 += n
-
-
-def _kv_workspace(segments, num_kv_heads: int, head_dim: int, device, include_residual: bool = True):
-    """Head-major bf16 key rows [H, Np, D] and transposed values [H, D, Np]
-    of all segments; Np is the token count rounded up to 8 and the padding is
-    zero.  Mirrors the reference's mixed-attention workspace
-    (bagel.py:1410-1450)."""
-
-    spans = _span_tokens(segments, include_residual)
-    total = sum(n for _, n in spans)
-    padded = max(8, (total + 7) // 8 * 8)
-    kw = torch.zeros((num_kv_heads, padded, head_dim), device=device, dtype=torch.bfloat16)
-    vw = torch.zeros_like(kw)
-    _fill_kv(spans, kw, vw, 0)
-    return kw, vw.transpose(1, 2).contiguous(), total
-
-
 def _kv_heads_of(segs) -> int:
     first = segs[0]
     if isinstance(first, (PackedKIVICache, GQAH2OCache)):
@@ -207,11 +158,22 @@ def _kv_heads_of(segs) -> int:
     return int(first[0].shape[1])
 
 
+def _query_rows(query: torch.Tensor, hkv: int) -> torch.Tensor:
+    """[Lq, Hq, D] -> the per-KV-head query rows [Hkv, Lq * grp, D] (row =
+    position * grp + head-in-group), bf16."""
+
+    lq, hq, d = map(int, query.shape)
+    grp = hq // hkv
+    return query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, lq * grp, d)
+
+
 def batched_long_query_attention(queries: list, segments_by_sample: list, *, dense_by_sample: list | None = None,
                                  include_residual: bool = True) -> list:
     """Non-causal attention of several samples' query blocks over their own
     physical segments in one tcgen05 launch, the counterpart of the varlen
-    launch of apply_static_physical_attention_batch (bagel.py:773-980).
+    launch of apply_static_physical_attention_batch (bagel.py:773-980).  The
+    segments are read in place through a span table: dense and H2O rows by
+    cp.async, packed KIVI tiles restored in shared memory (no workspace).
 
     queries[i] [Lq_i, Hq, D]; segments_by_sample[i] the sample's segments;
     dense_by_sample[i] an optional (key, value) [N, Hkv, D] pair of the
@@ -231,41 +193,24 @@ def batched_long_query_attention(queries: list, segments_by_sample: list, *, den
     hkv = _kv_heads_of(samples[0][1])
     d = int(samples[0][0].shape[-1])
     device = samples[0][0].device
-    q_rows, k_rows, metas = 0, 0, []
+    q_rows, starts, counts = 0, [], []
     for query, segs in samples:
         if _kv_heads_of(segs) != hkv or int(query.shape[-1]) != d:
             raise ValueError("all samples must share KV heads and head_dim")
         lq, hq = int(query.shape[0]), int(query.shape[1])
         if hq % hkv:
             raise ValueError("Query heads must be divisible by KV heads")
-        spans = _span_tokens(segs, include_residual)
-        total = sum(n for _, n in spans)
-        if total == 0:
-            raise ValueError("every sample needs at least one key token")
         rows = lq * (hq // hkv)
-        metas.append((q_rows, rows, k_rows, total, spans))
+        starts.append(q_rows)
+        counts.append(rows)
         q_rows += (rows + 255) // 256 * 256
-        k_rows += (total + 63) // 64 * 64
-    qp = torch.zeros((hkv, q_rows, d), device=device, dtype=torch.bfloat16)
-    kw = torch.zeros((hkv, k_rows, d), device=device, dtype=torch.bfloat16)
-    vw = torch.zeros_like(kw)
-    items = []
-    for (query, _), (q0, rows, k0, total, spans) in zip(samples, metas):
-        lq, hq = int(query.shape[0]), int(query.shape[1])
-        grp = hq // hkv
-        qp[:, q0:q0 + rows] = query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, rows, d)
-        _fill_kv(spans, kw, vw, k0)
-        for h in range(hkv):
-            for r in range(0, rows, 256):
-                items.append([h, q0 + r, min(256, rows - r), k0, total, 0, 0, 0])
-    # fewer row blocks than SMs: split keys so the idle SMs take second parts
-    items, slots = kernels.split_prefill_items(items, torch.cuda.get_device_properties(device).multi_processor_count)
-    table = torch.tensor(items, dtype=torch.int32).to(device)
-    workspace = kernels.prefill_split_workspace(device, slots, kernels.stream_of(qp)) if slots else None
-    out, lse = kernels.prefill_attention_batched(qp, kw, vw.transpose(1, 2).contiguous(), table,
-                                                 split_workspace=workspace)
+    qp = torch.empty((hkv, q_rows, d), device=device, dtype=torch.bfloat16)
+    for (query, _), r0, rows in zip(samples, starts, counts):
+        qp[:, r0:r0 + rows] = _query_rows(query, hkv)
+    tables = kernels.long_query_tables([segs for _, segs in samples], hkv, starts, counts, device, include_residual)
+    out, lse = kernels.long_query_attention(qp, tables)
     results = []
-    for (query, _), (q0, rows, _, _, _) in zip(samples, metas):
+    for (query, _), q0, rows in zip(samples, starts, counts):
         lq, hq = int(query.shape[0]), int(query.shape[1])
         grp = hq // hkv
         o = out[:, q0:q0 + rows].reshape(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
@@ -280,7 +225,9 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
     tensor cores: (out [Lq, Hq, D], lse [Hq, Lq] natural log).
 
     The query rows of each KV head ((position, head-in-group) pairs) form one
-    M x N attention problem; keys and values come from a bf16 workspace."""
+    M x N attention problem; the kernel reads the segments in place through a
+    span table (dense and H2O rows copied, packed KIVI tiles restored in
+    shared memory), so no bf16 workspace is assembled."""
 
     kernels.require_cuda(query, "query")
     segs = _segments_for(dense_key, dense_value, segments)
@@ -291,9 +238,9 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
     if hq % hkv:
         raise ValueError("Query heads must be divisible by KV heads")
     grp = hq // hkv
-    kw, vt, total = _kv_workspace(segs, hkv, d, query.device, include_residual=include_residual)
-    q = query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, lq * grp, d).contiguous()
-    out, lse = kernels.prefill_attention(q, kw, vt, total)
+    q = _query_rows(query, hkv).contiguous()
+    tables = kernels.long_query_tables([segs], hkv, [0], [lq * grp], query.device, include_residual)
+    out, lse = kernels.long_query_attention(q, tables)
     out = out.view(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
     lse = lse.view(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
     return out.to(query.dtype), lse

@@ -236,11 +236,216 @@ __device__ __forceinline__ bool wait_flag(const unsigned int* flag, uint64_t bud
   }
 }
 
+// Item of a segment-table launch (ucb_lq_item): like WorkItem, plus the
+// range of spans (in ucb_span order) that hold the item's KV head's keys; the
+// item's keys are tokens [k_row0, k_row0 + n_tokens) of the concatenation of
+// those spans, and span s covers tokens [unit_begin, unit_begin + tokens).
+struct LqItem {
+  int head, q_row0, q_rows, k_row0, n_tokens, mode, slot, span_begin, span_count, pad0, pad1, pad2;
+};
+
+// ---------------------------------------------------------------- span producers
+// In a segment-table launch the keys and values are read in place: threads
+// of warps 8, 10 and 11 (96 producers) fill each K and V tile from the item's
+// spans.  Both tiles take the layout a 128-byte-swizzled TMA load of
+// 64-channel boxes produces: two 16 KB halves (channels 0-63, 64-127), token
+// row r at r * 128 bytes, 16-byte chunk c of the row at (c ^ (r & 7)) * 16.
+// K is the K-major B operand of S = Q K^T as before; V is read as an
+// MN-major B operand of O += P V (channels contiguous), so no transpose is
+// needed.  Dense rows are copied with 16-byte cp.async; packed KIVI codes are
+// restored as code * scale + minimum with one rounding to bf16 (the
+// reference, unicache/storage/physical.py:178-201, rounds the fp32 result
+// once more first, which can differ in the last bf16 bit in rare ties) and
+// stored with plain shared-memory stores.  Rows past the item's last key are
+// zero-filled (the softmax masks them; V must stay finite).
+constexpr int PRODUCERS = 96;
+
+__device__ __forceinline__ uint32_t tile_chunk(int row, int chunk) {
+  return (uint32_t)((chunk >> 3) * (BN * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void dense_rows(const __nv_bfloat16* base, int64_t stride, int off, int r0, int n,
+                                           uint32_t tile, int pid) {
+  for (int idx = pid; idx < n * 16; idx += PRODUCERS) {
+    const int rr = idx >> 4, c = idx & 15;
+    cp_async16(tile + tile_chunk(r0 + rr, c), base + (int64_t)(off + rr) * stride + 8 * c);
+  }
+}
+
+__device__ __forceinline__ void zero_rows(int r0, unsigned char* tile, int pid) {
+  for (int idx = pid; idx < (BN - r0) * 16; idx += PRODUCERS)
+    *reinterpret_cast<uint4*>(tile + tile_chunk(r0 + (idx >> 4), idx & 15)) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    f[2 * k] = bf16lo(w[k]);
+    f[2 * k + 1] = bf16hi(w[k]);
+  }
+}
+
+// Packed codes are restored on bf16 pairs: a code placed in the mantissa of
+// a bf16 magic number (M + code, exact) loses M in one exact FMA, and a
+// second FMA forms code * scale + minimum with one rounding to bf16 (the
+// decode kernel restores its keys the same way).  M = 128, 32 or 8 takes a
+// 2-bit code at bits 0-1, 2-3 or 4-5 of a half without a shift.
+__device__ __forceinline__ uint32_t restore2(uint32_t z, uint32_t mask_magic_and, uint32_t magic, uint32_t neg_m,
+                                             uint32_t s, uint32_t m) {
+  return bf16x2_dequant((z & mask_magic_and) | magic, neg_m, s, m);
+}
+
+// Keys packed along tokens ([T/f, D] words of this head, f = 32/KB tokens per
+// word; statistics [T/G, D]).  Unit = (word row, 8-channel chunk, half of the
+// word's tokens): 8 words and the chunk's 8 scales and minima in (channel
+// pairs already adjacent), f/2 rows of one 16-byte chunk out.
+template <int KB>
+__device__ void packed_keys(const ucb_span& S, int G, int off, int r0, int n, unsigned char* tile, int pid) {
+  constexpr int F = 32 / KB, HALF_TOK = F / 2;
+  const int w0 = off / F, w1 = (off + n - 1) / F;
+  const uint32_t* codes = static_cast<const uint32_t*>(S.key_code);
+  const uint16_t* sc = static_cast<const uint16_t*>(S.key_scale);
+  const uint16_t* mn = static_cast<const uint16_t*>(S.key_minimum);
+  for (int u = pid; u < (w1 - w0 + 1) * 32; u += PRODUCERS) {
+    const int w = w0 + (u >> 5), c = (u >> 1) & 15, hh = u & 1;
+    const int t_first = w * F + hh * HALF_TOK;  // first span token of this unit
+    if (t_first + HALF_TOK <= off || t_first >= off + n) continue;
+    const uint32_t* cw = codes + (int64_t)w * D + 8 * c;
+    const uint4 ca = __ldg(reinterpret_cast<const uint4*>(cw));
+    const uint4 cb = __ldg(reinterpret_cast<const uint4*>(cw + 4));
+    const int64_t g = (int64_t)(w * F) / G;
+    const uint4 s4 = __ldg(reinterpret_cast<const uint4*>(sc + g * D + 8 * c));
+    const uint4 m4 = __ldg(reinterpret_cast<const uint4*>(mn + g * D + 8 * c));
+    const uint32_t word[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    const uint32_t sp[4] = {s4.x, s4.y, s4.z, s4.w}, mp[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {  // the two bytes (KB = 2: 4 tokens each; KB = 4: 2 tokens each) of this half
+      const int byte = 2 * hh + b;
+      const uint32_t sel = byte | (byte << 4) | ((4 + byte) << 8) | ((4 + byte) << 12);
+      uint32_t z[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) z[k] = prmt(word[2 * k], word[2 * k + 1], sel);
+#pragma unroll
+      for (int p = 0; p < 8 / KB; ++p) {  // tokens of the byte
+        const int t = w * F + byte * (8 / KB) + p;
+        if (t < off || t >= off + n) continue;
+        uint32_t out[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if constexpr (KB == 2) {
+            if (p == 0) out[k] = restore2(z[k], 0x00030003u, 0x43004300u, 0xC300C300u, sp[k], mp[k]);
+            else if (p == 1) out[k] = restore2(z[k], 0x000C000Cu, 0x42004200u, 0xC200C200u, sp[k], mp[k]);
+            else if (p == 2) out[k] = restore2(z[k], 0x00300030u, 0x41004100u, 0xC100C100u, sp[k], mp[k]);
+            else out[k] = restore2(z[k] >> 6, 0x00030003u, 0x43004300u, 0xC300C300u, sp[k], mp[k]);
+          } else {
+            out[k] = restore2(p == 0 ? z[k] : z[k] >> 4, 0x000F000Fu, 0x43004300u, 0xC300C300u, sp[k], mp[k]);
+          }
+        }
+        *reinterpret_cast<uint4*>(tile + tile_chunk(r0 + (t - off), c)) = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+    }
+  }
+}
+
+// Values packed along channels ([T, D/f] words, f = 32/VB channels per word;
+// statistics [T, D/G]).  Unit = (token, 64-channel half row): the half row's
+// words and its groups' statistics in, 8 chunks out.
+template <int VB>
+__device__ void packed_values(const ucb_span& S, int G, int off, int r0, int n, unsigned char* tile, int pid) {
+  constexpr int F = 32 / VB, W = D / F, HW = W / 2;  // words per token, per half row
+  const uint32_t* codes = static_cast<const uint32_t*>(S.value_code);
+  const uint16_t* sc = static_cast<const uint16_t*>(S.value_scale);
+  const uint16_t* mn = static_cast<const uint16_t*>(S.value_minimum);
+  const int ng = D / G;
+  for (int u = pid; u < 2 * n; u += PRODUCERS) {
+    const int64_t t = off + (u >> 1);
+    const int hh = u & 1, r = r0 + (u >> 1);
+    uint32_t word[HW];
+#pragma unroll
+    for (int k = 0; k < HW; k += 4) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(codes + t * W + hh * HW + k));
+      word[k] = v.x;
+      word[k + 1] = v.y;
+      word[k + 2] = v.z;
+      word[k + 3] = v.w;
+    }
+    // groups covering channels [64 hh, 64 hh + 64): G = 32 -> 2, else 1
+    const int g0 = (64 * hh) / G;
+    const uint32_t s_a = sc[t * ng + g0], m_a = mn[t * ng + g0];
+    const uint32_t s_b = (G == 32) ? (uint32_t)sc[t * ng + g0 + 1] : s_a;
+    const uint32_t m_b = (G == 32) ? (uint32_t)mn[t * ng + g0 + 1] : m_a;
+    const uint32_t s2a = s_a | (s_a << 16), m2a = m_a | (m_a << 16);
+    const uint32_t s2b = s_b | (s_b << 16), m2b = m_b | (m_b << 16);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {  // 8-channel chunks of the half row
+      const bool second = (8 * c) >= 32;  // second 32-channel group of the half (G = 32)
+      const uint32_t s2 = second ? s2b : s2a, m2 = second ? m2b : m2a;
+      uint32_t out[4];
+      if constexpr (VB == 2) {
+        const uint32_t wv = word[c / 2];  // 16 channels per word, chunk = 2 bytes
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const int byte = 2 * (c & 1) + b;
+          const uint32_t y = prmt(wv, 0u, byte | (byte << 4) | (byte << 8) | (byte << 12));
+          // channels 4 byte + {0, 1} at bits 0-1 / 18-19, then + {2, 3} after a 4-bit shift
+          out[2 * b] = restore2(y, 0x000C0003u, 0x42004300u, 0xC200C300u, s2, m2);
+          out[2 * b + 1] = restore2(y >> 4, 0x000C0003u, 0x42004300u, 0xC200C300u, s2, m2);
+        }
+      } else {
+        const uint32_t wv = word[c], wh = wv >> 4;  // 8 channels per word, chunk = 1 word
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          out[k] = restore2(prmt(wv, wh, k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12)), 0x000F000Fu, 0x43004300u,
+                            0xC300C300u, s2, m2);
+      }
+      *reinterpret_cast<uint4*>(tile + tile_chunk(r, 8 * hh + c)) = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+  }
+}
+
+// Fill rows [0, valid) of a K (keys) or V tile with tokens [tok0, tok0 +
+// valid) of the item's spans, then zero rows [valid, BN).
+__device__ void fill_tile(bool keys, const ucb_span* spans, int span_count, int tok0, int valid, int kb, int vb,
+                          int G, unsigned char* tile, int pid) {
+  const uint32_t tile_addr = smem_u32(tile);
+  for (int si = 0; si < span_count; ++si) {
+    const ucb_span& S = spans[si];
+    const int s0 = S.unit_begin, s1 = S.unit_begin + S.tokens;
+    const int a = max(tok0, s0), b = min(tok0 + valid, s1);
+    if (a >= b) continue;
+    const int r0 = a - tok0, off = a - s0, n = b - a;
+    if (S.kind == 1) {
+      dense_rows(static_cast<const __nv_bfloat16*>(keys ? S.key_code : S.value_code),
+                 keys ? S.key_stride : S.value_stride, off, r0, n, tile_addr, pid);
+    } else if (keys) {
+      if (kb == 2) packed_keys<2>(S, G, off, r0, n, tile, pid);
+      else packed_keys<4>(S, G, off, r0, n, tile, pid);
+    } else {
+      if (vb == 2) packed_values<2>(S, G, off, r0, n, tile, pid);
+      else packed_values<4>(S, G, off, r0, n, tile, pid);
+    }
+  }
+  if (valid < BN) zero_rows(valid, tile, pid);
+}
+
+// Shared-memory descriptor of the MN-major V operand: 64-channel (128-byte)
+// swizzle atoms along N are LBO = 16 KB apart (the two channel halves) and
+// 8-token groups along K are SBO = 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((BN * 128) >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+constexpr uint32_t IDESC_O_MN = IDESC_O | (1u << 16);  // B (V) MN-major
+
 struct Params {
   int m_rows;        // query rows per head in q / out / lse (row stride of the head)
   int n_tokens;      // key tokens per head (single-problem launches)
   float scale_log2;  // softmax scale * log2(e)
   const WorkItem* items;  // per-CTA problems (batched launches), or null: CTA (x, y) = rows 2*BM*x.. of head y
+  const LqItem* lq_items; // segment-table launches: per-CTA problems reading spans in place
+  const ucb_span* spans;  // the spans lq_items refer to
+  int k_bits, v_bits, group;  // packed spans of a segment-table launch
   float* partials;        // PARTIAL_SLOT_FLOATS per slot (split row blocks), or null
   unsigned int* flags;    // one per slot, even between launches, or null
   __nv_bfloat16* out;  // [heads, m_rows, D]
@@ -248,13 +453,31 @@ struct Params {
   unsigned int* err;
 };
 
+// SPANS: keys and values come from the item's spans (producer warps 8, 10,
+// 11); otherwise from the K / V^T tensor maps (loader warp 8).
+template <bool SPANS>
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0;
-  if (P.items) {
+  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0, span_begin = 0, span_count = 0;
+  if constexpr (SPANS) {
+    const LqItem it = P.lq_items[blockIdx.x];
+    head = it.head;
+    m0 = it.q_row0;
+    m_end = it.q_row0 + it.q_rows;
+    k0 = it.k_row0;
+    n_tokens = it.n_tokens;
+    mode = it.mode;
+    slot = it.slot;
+    span_begin = it.span_begin;
+    span_count = it.span_count;
+    if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
+      if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+      mode = ITEM_FINAL;
+    }
+  } else if (P.items) {
     const WorkItem it = P.items[blockIdx.x];
     head = it.head;
     m0 = it.q_row0;
@@ -300,9 +523,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     failed = 0;
     mbar_init(q_full, 1);
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&k_full[i], 1);
+      mbar_init(&k_full[i], SPANS ? PRODUCERS : 1);
       mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
+      mbar_init(&v_full[i], SPANS ? PRODUCERS : 1);
       mbar_init(&v_empty[i], 1);
     }
     for (int x = 0; x < 2; ++x) {
@@ -325,7 +548,41 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   auto fail = [&]() { atomicOr(&failed, 1); };
 
-  if (warp == 8) {
+  if (SPANS && (warp == 8 || warp == 10 || warp == 11)) {
+    // ---------------- span producers
+    const int pid = (warp == 8 ? 0 : warp - 9) * 32 + lane;
+    if (pid == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * QTILE);
+      for (int x = 0; x < 2; ++x) {
+        tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
+        tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+      }
+    }
+    const ucb_span* spans = P.spans + span_begin;
+    for (int j = 0; j < n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++j) {
+      const int st = j % STAGES;
+      const uint32_t ph = ((j / STAGES) - 1) & 1;
+      const int tok0 = k0 + j * BN, valid = min(BN, n_tokens - j * BN);
+      if (j >= STAGES && !mbar_wait_for(&k_empty[st], ph, WAIT_NS)) {
+        fail();
+        break;
+      }
+      fill_tile(true, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group, smem + OFF_K + st * KTILE, pid);
+      cp_async_wait_all();
+      fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
+      mbar_arrive(&k_full[st]);
+      if (j >= STAGES && !mbar_wait_for(&v_empty[st], ph, WAIT_NS)) {
+        fail();
+        break;
+      }
+      fill_tile(false, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group, smem + OFF_V + st * VTILE, pid);
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      mbar_arrive(&v_full[st]);
+    }
+    cp_async_wait_all();
+    if (pid == 0) mbar_wait_for(q_full, 0, WAIT_NS);  // the Q copies land before shared memory is released
+  } else if (!SPANS && warp == 8) {
     // ---------------- loader
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * QTILE);
@@ -375,9 +632,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto issue_pv = [&](int j, int x) {
         const uint32_t v_addr = smem_u32(smem + OFF_V + (j % STAGES) * VTILE);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)  // P_x: 8 TMEM columns (16 tokens) per step
-          tc_mma_ts(tmem + O_COL + 128 * x, tmem + S_COL + 128 * x + 8 * kk,
-                    sw128_desc(v_addr + (kk >> 2) * VHALF + (kk & 3) * 32), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BN / 16; ++kk) {  // P_x: 8 TMEM columns (16 tokens) per step
+          if constexpr (SPANS)  // V rows = tokens: 16 tokens = two 8-row groups = 2048 bytes
+            tc_mma_ts(tmem + O_COL + 128 * x, tmem + S_COL + 128 * x + 8 * kk, sw128_mn_desc(v_addr + kk * 2048),
+                      IDESC_O_MN, (j > 0 || kk > 0) ? 1u : 0u);
+          else  // V^T rows = channels: 16 tokens = 32 bytes of a 64-token half
+            tc_mma_ts(tmem + O_COL + 128 * x, tmem + S_COL + 128 * x + 8 * kk,
+                      sw128_desc(v_addr + (kk >> 2) * VHALF + (kk & 3) * 32), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
         tc_commit(&o_done[x]);
       };
       bool ok = mbar_wait_for(q_full, 0, WAIT_NS) && mbar_wait_for(&k_full[0], 0, WAIT_NS);
@@ -579,29 +841,38 @@ int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_
 }  // namespace ucb
 
 namespace {
+// k == vt == nullptr: a segment-table launch (keys and values from P.spans).
 int launch_prefill(const void* q, const void* k, const void* vt, int heads, int m_rows, int n_padded,
                    ucb::prefill::Params P, dim3 grid, void* stream) {
   using namespace ucb::prefill;
+  const bool spans = (k == nullptr);
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(vt)) & 15)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: operands must be 16-byte aligned");
-  if (n_padded % 8) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: n_padded must be a multiple of 8");
+  if (!spans && n_padded % 8)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: n_padded must be a multiple of 8");
   unsigned int* err = ucb_host::device_error_word();
   if (!err) return ucb_host::set_error(UCB_ERR_CUDA, "ucb_prefill_attention: device error word unavailable");
   CUtensorMap tq, tk, tv;
   int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads, BM);
-  if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
-  if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
+  if (!rc && !spans) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
+  if (!rc && !spans) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
   if (rc) return rc;
-  static bool configured[64] = {false};
+  if (spans) tk = tv = tq;  // unused by the segment-table kernel
+  static bool configured[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+  if (dev < 0 || dev >= 64 || !configured[spans][dev]) {
+    const cudaError_t e = spans ? cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)
+                                : cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess)
       return ucb_host::set_error(UCB_ERR_CUDA, "prefill: cannot reserve %d bytes of shared memory", SMEM);
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[spans][dev] = true;
   }
   P.err = err;
-  prefill_kernel<<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
+  if (spans)
+    prefill_kernel<true><<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
+  else
+    prefill_kernel<false><<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
   return ucb_host::check_launch("prefill_kernel");
 }
 }  // namespace
@@ -620,6 +891,9 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   P.n_tokens = n_tokens;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
   P.items = nullptr;
+  P.lq_items = nullptr;
+  P.spans = nullptr;
+  P.k_bits = P.v_bits = P.group = 0;
   P.partials = nullptr;
   P.flags = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
@@ -643,6 +917,9 @@ extern "C" int ucb_prefill_attention_items(const void* q, const void* k, const v
   P.n_tokens = 0;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
   P.items = static_cast<const WorkItem*>(items);
+  P.lq_items = nullptr;
+  P.spans = nullptr;
+  P.k_bits = P.v_bits = P.group = 0;
   P.partials = partials;
   P.flags = flags;
   P.out = static_cast<__nv_bfloat16*>(out);
@@ -659,4 +936,35 @@ extern "C" int ucb_prefill_attention_batched(const void* q, const void* k, const
 
 extern "C" int64_t ucb_prefill_partial_bytes() {
   return (int64_t)ucb::prefill::PARTIAL_SLOT_FLOATS * (int64_t)sizeof(float);
+}
+
+extern "C" int ucb_long_query_attention(const void* q, int heads, int m_rows, const void* items, int num_items,
+                                        const ucb_span* spans, int num_spans, int k_bits, int v_bits, int group_size,
+                                        float softmax_scale, void* out, float* lse, float* partials,
+                                        unsigned int* flags, void* stream) {
+  using namespace ucb::prefill;
+  if (!q || !items || !spans || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: null pointer");
+  if (heads <= 0 || m_rows <= 0 || num_items <= 0 || num_spans <= 0)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: empty problem");
+  if ((k_bits != 2 && k_bits != 4) || (v_bits != 2 && v_bits != 4))
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_attention: packed spans must be 2- or 4-bit");
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_attention: group_size must be 32, 64 or 128");
+  if ((partials == nullptr) != (flags == nullptr))
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: partials and flags go together");
+  Params P;
+  P.m_rows = m_rows;
+  P.n_tokens = 0;
+  P.scale_log2 = softmax_scale * 1.4426950408889634f;
+  P.items = nullptr;
+  P.lq_items = static_cast<const LqItem*>(items);
+  P.spans = spans;
+  P.k_bits = k_bits;
+  P.v_bits = v_bits;
+  P.group = group_size;
+  P.partials = partials;
+  P.flags = flags;
+  P.out = static_cast<__nv_bfloat16*>(out);
+  P.lse = lse;
+  return launch_prefill(q, nullptr, nullptr, heads, m_rows, 0, P, dim3(num_items), stream);
 }

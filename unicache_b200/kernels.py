@@ -10,6 +10,7 @@ reference's fail-closed CUDA backend (unicache/storage/kivi_cuda.py:174-175,
 from __future__ import annotations
 
 import ctypes
+import functools
 import math
 from dataclasses import dataclass, field
 
@@ -755,6 +756,7 @@ _KEY_SPLITS: dict = {}
 PREFILL_CTA_FIXED_TILES = 4.0  # a CTA's set-up, pipeline fill and epilogue, in key-tile times (measured)
 
 
+@functools.lru_cache(maxsize=4096)
 def plan_key_split(row_blocks: int, key_tiles: int, sms: int) -> int | None:
     """Key tiles of the first part when splitting every row block's keys in
     two fills the GPU better than one CTA per row block, else None.
@@ -823,8 +825,9 @@ def _key_split_launch(device, heads: int, m_rows: int, n_tokens: int, n_padded: 
 
 
 def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
-    """Item rows (head, q_row0, q_rows, k_row0, n_tokens, 0, 0, 0) with each
-    row block's keys split in two where ``plan_key_split`` says it pays
+    """Item rows (head, q_row0, q_rows, k_row0, n_tokens, 0, 0, ...; any
+    further columns, such as a segment-table item's span range, are kept)
+    with each row block's keys split in two where ``plan_key_split`` says it pays
     (fewer row blocks than SMs): the first parts as merge items (mode 2)
     first, then the unsplit items, then the second parts as partial items
     (mode 1), slot i shared by the i-th pair.  Returns (rows, slots)."""
@@ -833,15 +836,16 @@ def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
         return [list(r) for r in items], 0
     merges, whole, partials = [], [], []
     for row in items:
-        h, q0, rows, k0, n = (int(x) for x in row[:5])
+        row = [int(x) for x in row]
+        k0, n = row[3], row[4]
         first = plan_key_split(len(items), -(-n // PREFILL_KEY_TILE), sms)
         if first is None:
-            whole.append([h, q0, rows, k0, n, 0, 0, 0])
+            whole.append(row[:5] + [0, 0] + row[7:])
             continue
         cut = first * PREFILL_KEY_TILE
         slot = len(merges)
-        merges.append([h, q0, rows, k0, cut, 2, slot, 0])
-        partials.append([h, q0, rows, k0 + cut, n - cut, 1, slot, 0])
+        merges.append(row[:3] + [k0, cut, 2, slot] + row[7:])
+        partials.append(row[:3] + [k0 + cut, n - cut, 1, slot] + row[7:])
     return merges + whole + partials, len(merges)
 
 
@@ -938,3 +942,184 @@ def selftest_mma_subnormal() -> float:
     err = ctypes.c_float(-1.0)
     call("ucb_selftest_mma_subnormal", ctypes.byref(err), torch.cuda.current_stream().cuda_stream)
     return float(err.value)
+
+
+# ---------------------------------------------------------------- long-query over spans
+LQ_ITEM_INTS = 12  # ucb_lq_item
+
+
+@dataclass
+class LongQueryTables:
+    """Device tables of a segment-table long-query launch: the spans every KV
+    head of every sample reads in place, and one item per CTA."""
+
+    spans: torch.Tensor         # ucb_span structs (raw bytes)
+    items: torch.Tensor         # int32 [num_items, 12]
+    num_spans: int
+    num_items: int
+    k_bits: int
+    v_bits: int
+    group_size: int
+    slots: int                  # key-split slots (partials/flags) the items use
+    keepalive: list = field(default_factory=list)
+
+
+def long_query_spans(segments: list, num_kv_heads: int, head: int, include_residual: bool = True):
+    """The spans of one KV head of one sample, in segment order: (list of
+    UcbSpan with ``unit_begin`` = first token, tokens, (k_bits, v_bits, group)
+    of its packed spans or None, objects to keep alive)."""
+
+    from .storage.physical import GQAH2OCache, PackedKIVICache
+
+    spans, keep, cfg, t0 = [], [], None, 0
+
+    def add(sp):
+        nonlocal t0
+        sp.unit_begin = t0
+        sp.pair = 0
+        spans.append(sp)
+        t0 += int(sp.tokens)
+
+    for seg in segments:
+        if isinstance(seg, PackedKIVICache):
+            if seg.backend != "b200":
+                raise ValueError("long-query spans need b200-layout packed segments")
+            if seg.quantized_tokens:
+                if seg.k_bits not in (2, 4) or seg.v_bits not in (2, 4):
+                    raise ValueError("the long-query kernel reads 2- or 4-bit packed segments")
+                if seg.key_scale.dtype != torch.bfloat16 or seg.head_dim != 128:
+                    raise ValueError("the long-query kernel reads bf16 statistics and head_dim 128")
+                this = (seg.k_bits, seg.v_bits, seg.group_size)
+                if cfg is not None and cfg != this:
+                    raise ValueError("all packed segments of a long-query launch must share bits and group")
+                cfg = this
+                add(_packed_span(seg, head))
+            if include_residual and int(seg.residual_key.shape[0]):
+                add(_dense_span(dense_rows_token_major(seg.residual_key, seg.residual_value, head)))
+            keep.append(seg)
+        elif isinstance(seg, GQAH2OCache):
+            if seg.retained_tokens:
+                add(_dense_span(dense_rows_head_major(seg.key, seg.value, head)))
+            keep.append(seg)
+        else:
+            key, value = seg
+            if int(key.shape[0]):
+                add(_dense_span(dense_rows_token_major(key, value, head)))
+            keep.append((key, value))
+    return spans, t0, cfg, keep
+
+
+@functools.lru_cache(maxsize=64)
+def _sm_count(index: int) -> int:
+    return torch.cuda.get_device_properties(index).multi_processor_count
+
+
+def _segment_signature(seg) -> tuple:
+    """Everything a span table records about a segment: its identity, the
+    addresses and strides of its tensors and its token counts."""
+
+    from .storage.physical import GQAH2OCache, PackedKIVICache
+
+    if isinstance(seg, PackedKIVICache):
+        packed = (seg.key_code.data_ptr(), seg.value_code.data_ptr()) if seg.quantized_tokens else (0, 0)
+        return (id(seg), *packed, seg.quantized_tokens,
+                seg.residual_key.data_ptr(), seg.residual_value.data_ptr(), int(seg.residual_key.shape[0]),
+                tuple(seg.residual_key.stride()), tuple(seg.residual_value.stride()), seg.k_bits, seg.v_bits,
+                seg.group_size)
+    if isinstance(seg, GQAH2OCache):
+        return (id(seg), seg.key.data_ptr(), seg.value.data_ptr(), tuple(seg.key.shape), tuple(seg.key.stride()),
+                tuple(seg.value.stride()))
+    key, value = seg
+    return (key.data_ptr(), value.data_ptr(), tuple(key.shape), tuple(key.stride()), tuple(value.stride()),
+            key.dtype, value.dtype)
+
+
+_LQ_BY_SIGNATURE: dict = {}
+
+
+def long_query_tables(samples: list, num_kv_heads: int, q_row0: list, q_rows: list, device,
+                      include_residual: bool = True) -> LongQueryTables:
+    """Segment-table launch tables for several samples: sample i's query rows
+    are [q_row0[i], q_row0[i] + q_rows[i]) of every KV head's rows in the q
+    workspace, its keys the concatenation of its segments.  Tables are cached
+    on the segments' signatures (identity, addresses, strides, lengths), so a
+    layer called again over the same frozen segments costs a dictionary
+    lookup on the host."""
+
+    index = torch.device(device).index
+    signature = (index, num_kv_heads, bool(include_residual), tuple(q_row0), tuple(q_rows),
+                 tuple(tuple(_segment_signature(seg) for seg in segs) for segs in samples))
+    hit = _LQ_BY_SIGNATURE.get(signature)
+    if hit is not None:
+        return hit
+    tables = _build_long_query_tables(samples, num_kv_heads, q_row0, q_rows, device, include_residual)
+    if len(_LQ_BY_SIGNATURE) >= _LQ_TABLES_MAX:
+        _LQ_BY_SIGNATURE.pop(next(iter(_LQ_BY_SIGNATURE)))
+    _LQ_BY_SIGNATURE[signature] = tables
+    return tables
+
+
+def _build_long_query_tables(samples: list, num_kv_heads: int, q_row0: list, q_rows: list, device,
+                             include_residual: bool) -> LongQueryTables:
+    all_spans, rows, cfg = [], [], None
+    for segs, r0, nrows in zip(samples, q_row0, q_rows):
+        for h in range(num_kv_heads):
+            spans, tokens, this, _ = long_query_spans(segs, num_kv_heads, h, include_residual)
+            if tokens == 0:
+                raise ValueError("every sample needs at least one key token")
+            if this is not None:
+                if cfg is not None and cfg != this:
+                    raise ValueError("all packed segments of a long-query launch must share bits and group")
+                cfg = this
+            begin = len(all_spans)
+            all_spans.extend(spans)
+            for r in range(0, nrows, PREFILL_ROWS_PER_CTA):
+                rows.append([h, r0 + r, min(PREFILL_ROWS_PER_CTA, nrows - r), 0, tokens, 0, 0, begin, len(spans),
+                             0, 0, 0])
+    rows, slots = split_prefill_items(rows, _sm_count(torch.device(device).index))
+    k_bits, v_bits, group = cfg if cfg is not None else (2, 2, 32)
+    raw = _capi.struct_array_bytes(all_spans)
+    # Device tables are reused while the spans (addresses, strides, lengths)
+    # and items are the same, so a layer called again over the same segments
+    # uploads nothing.
+    key = (torch.device(device).index, raw, tuple(tuple(r) for r in rows))
+    cached = _LQ_TABLES.get(key)
+    if cached is None:
+        spans_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
+        items_dev = torch.tensor(rows, dtype=torch.int32).to(device)
+        if len(_LQ_TABLES) >= _LQ_TABLES_MAX:
+            _LQ_TABLES.pop(next(iter(_LQ_TABLES)))
+        cached = _LQ_TABLES[key] = (spans_dev, items_dev)
+    # The tables hold addresses only: the caller keeps the segments alive for
+    # the launch, and a cached entry whose tensors were freed is never stale
+    # in content, because its signature records every address it holds.
+    return LongQueryTables(cached[0], cached[1], len(all_spans), len(rows), k_bits, v_bits, group, slots)
+
+
+_LQ_TABLES: dict = {}
+_LQ_TABLES_MAX = 64
+
+
+def long_query_attention(q: torch.Tensor, tables: LongQueryTables, *, softmax_scale: float | None = None,
+                         out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+    """Non-causal attention of the query rows q [H, M, 128] (bf16) over the
+    spans of ``tables``, read in place (packed KIVI tiles restored in shared
+    memory): (out [H, M, 128] bf16, lse [H, M] fp32 natural log); rows no
+    item covers are left unwritten."""
+
+    require_cuda(q, "q")
+    if q.dtype != torch.bfloat16 or not q.is_contiguous() or q.dim() != 3 or int(q.shape[2]) != 128:
+        raise ValueError("q must be a contiguous bfloat16 [heads, rows, 128] tensor")
+    heads, m_rows, d = map(int, q.shape)
+    scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
+    partials = flags = None
+    if tables.slots:
+        partials, flags = prefill_split_workspace(q.device, tables.slots, stream_of(q))
+    call("ucb_long_query_attention", q.data_ptr(), heads, m_rows, tables.items.data_ptr(), tables.num_items,
+         tables.spans.data_ptr(), tables.num_spans, tables.k_bits, tables.v_bits, tables.group_size, scale,
+         out.data_ptr(), lse.data_ptr(), ptr(partials), ptr(flags), stream_of(q))
+    return out, lse
