@@ -295,8 +295,11 @@ UCB_API int64_t ucb_prefill_partial_bytes(void);
 /* Long-query attention that reads the physical segments in place (replaces
  * the bf16 workspace that unicache/adapters/bagel.py:1410-1450 assembles and
  * the dequantize + flash_attn_func(causal=False) calls of bagel.py:1598-1858
- * and :773-980).  q_dev: bf16 [heads, m_rows, 128] query rows per KV head, as
- * for ucb_prefill_attention.  Each item (one CTA) covers query rows
+ * and :773-980).  q_dev and out_dev: bf16 [positions, num_q_heads, 128] in the
+ * caller's own layout; lse_dev: fp32 [num_q_heads, positions] (natural log).
+ * The query rows of KV head h are the (position, head-in-group) pairs: row m
+ * of an item is position pos0 + m / grp and query head h * grp + m % grp
+ * (grp = num_q_heads / num_kv_heads).  Each item (one CTA) covers rows
  * [q_row0, q_row0 + q_rows) (<= 256) of KV head `head` against tokens
  * [k_row0, k_row0 + n_tokens) of the concatenation of spans
  * spans_dev[span_begin .. span_begin + span_count): span s holds `tokens`
@@ -306,12 +309,11 @@ UCB_API int64_t ucb_prefill_partial_bytes(void);
  * 16-byte aligned.  A packed span (kind 0) is one KV head's b200-layout KIVI
  * tensors (key codes [T/f, 128], key statistics [T/G, 128], value codes
  * [T, 128/f], value statistics [T, 128/G], bf16 statistics), restored inside
- * the kernel exactly as the reference restores its cache (code * scale +
- * minimum in fp32, one rounding to bf16; unicache/storage/physical.py:178-201)
- * directly into the tensor-core operand tiles in shared memory.  All packed
- * spans of a call share (k_bits, v_bits, group_size).  mode / slot: as for
- * ucb_prefill_attention_items (key splits need partials_dev and flags_dev).
- * Outputs out_dev [heads, m_rows, 128] bf16 and lse_dev [heads, m_rows]. */
+ * the kernel as code * scale + minimum with one rounding to bf16 directly
+ * into the tensor-core operand tiles in shared memory.  All packed spans of a
+ * call share (k_bits in {2,4}, v_bits in {2,4}, group_size in {32,64,128}).
+ * mode / slot: as for ucb_prefill_attention_items (key splits need
+ * partials_dev and flags_dev). */
 typedef struct ucb_lq_item {
   int32_t head;
   int32_t q_row0;
@@ -322,13 +324,14 @@ typedef struct ucb_lq_item {
   int32_t slot;
   int32_t span_begin;
   int32_t span_count;
-  int32_t reserved[3];
+  int32_t pos0;              /* first query position of the item's sample     */
+  int32_t reserved[2];
 } ucb_lq_item;
 
-UCB_API int ucb_long_query_attention(const void* q_dev, int heads, int m_rows, const void* items_dev, int num_items,
-                                     const ucb_span* spans_dev, int num_spans, int k_bits, int v_bits, int group_size,
-                                     float softmax_scale, void* out_dev, float* lse_dev, float* partials_dev,
-                                     unsigned int* flags_dev, void* stream);
+UCB_API int ucb_long_query_attention(const void* q_dev, int positions, int num_q_heads, int num_kv_heads,
+                                     const void* items_dev, int num_items, const ucb_span* spans_dev, int num_spans,
+                                     int k_bits, int v_bits, int group_size, float softmax_scale, void* out_dev,
+                                     float* lse_dev, float* partials_dev, unsigned int* flags_dev, void* stream);
 
 /* ---- sequence-split merge over NVLink peer memory (no counterpart in the
  * reference, which decodes one sequence on one device).  Each rank allocates

@@ -158,15 +158,6 @@ def _kv_heads_of(segs) -> int:
     return int(first[0].shape[1])
 
 
-def _query_rows(query: torch.Tensor, hkv: int) -> torch.Tensor:
-    """[Lq, Hq, D] -> the per-KV-head query rows [Hkv, Lq * grp, D] (row =
-    position * grp + head-in-group), bf16."""
-
-    lq, hq, d = map(int, query.shape)
-    grp = hq // hkv
-    return query.to(torch.bfloat16).reshape(lq, hkv, grp, d).permute(1, 0, 2, 3).reshape(hkv, lq * grp, d)
-
-
 def batched_long_query_attention(queries: list, segments_by_sample: list, *, dense_by_sample: list | None = None,
                                  include_residual: bool = True) -> list:
     """Non-causal attention of several samples' query blocks over their own
@@ -191,31 +182,24 @@ def batched_long_query_attention(queries: list, segments_by_sample: list, *, den
             raise ValueError("every sample needs at least one segment")
         samples.append((query, all_segs))
     hkv = _kv_heads_of(samples[0][1])
-    d = int(samples[0][0].shape[-1])
-    device = samples[0][0].device
-    q_rows, starts, counts = 0, [], []
+    hq, d = int(samples[0][0].shape[1]), int(samples[0][0].shape[-1])
+    pos0, rows = [], []
+    start = 0
     for query, segs in samples:
-        if _kv_heads_of(segs) != hkv or int(query.shape[-1]) != d:
-            raise ValueError("all samples must share KV heads and head_dim")
-        lq, hq = int(query.shape[0]), int(query.shape[1])
+        if _kv_heads_of(segs) != hkv or int(query.shape[-1]) != d or int(query.shape[1]) != hq:
+            raise ValueError("all samples must share query heads, KV heads and head_dim")
         if hq % hkv:
             raise ValueError("Query heads must be divisible by KV heads")
-        rows = lq * (hq // hkv)
-        starts.append(q_rows)
-        counts.append(rows)
-        q_rows += (rows + 255) // 256 * 256
-    qp = torch.empty((hkv, q_rows, d), device=device, dtype=torch.bfloat16)
-    for (query, _), r0, rows in zip(samples, starts, counts):
-        qp[:, r0:r0 + rows] = _query_rows(query, hkv)
-    tables = kernels.long_query_tables([segs for _, segs in samples], hkv, starts, counts, device, include_residual)
-    out, lse = kernels.long_query_attention(qp, tables)
+        pos0.append(start)
+        rows.append(int(query.shape[0]) * (hq // hkv))
+        start += int(query.shape[0])
+    q = torch.cat([query.to(torch.bfloat16) for query, _ in samples]).contiguous()
+    tables = kernels.long_query_tables([segs for _, segs in samples], hkv, pos0, rows, q.device, include_residual)
+    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv)
     results = []
-    for (query, _), q0, rows in zip(samples, starts, counts):
-        lq, hq = int(query.shape[0]), int(query.shape[1])
-        grp = hq // hkv
-        o = out[:, q0:q0 + rows].reshape(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
-        l = lse[:, q0:q0 + rows].reshape(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
-        results.append((o.to(query.dtype), l))
+    for (query, _), p0 in zip(samples, pos0):
+        lq = int(query.shape[0])
+        results.append((out[p0:p0 + lq].to(query.dtype), lse[:, p0:p0 + lq]))
     return results
 
 
@@ -225,9 +209,9 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
     tensor cores: (out [Lq, Hq, D], lse [Hq, Lq] natural log).
 
     The query rows of each KV head ((position, head-in-group) pairs) form one
-    M x N attention problem; the kernel reads the segments in place through a
-    span table (dense and H2O rows copied, packed KIVI tiles restored in
-    shared memory), so no bf16 workspace is assembled."""
+    M x N attention problem; the kernel reads the query, the segments and
+    writes the outputs in place (dense and H2O rows copied, packed KIVI tiles
+    restored in shared memory), so no workspace is assembled."""
 
     kernels.require_cuda(query, "query")
     segs = _segments_for(dense_key, dense_value, segments)
@@ -237,10 +221,7 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
     lq, hq, d = map(int, query.shape)
     if hq % hkv:
         raise ValueError("Query heads must be divisible by KV heads")
-    grp = hq // hkv
-    q = _query_rows(query, hkv).contiguous()
-    tables = kernels.long_query_tables([segs], hkv, [0], [lq * grp], query.device, include_residual)
-    out, lse = kernels.long_query_attention(q, tables)
-    out = out.view(hkv, lq, grp, d).permute(1, 0, 2, 3).reshape(lq, hq, d)
-    lse = lse.view(hkv, lq, grp).permute(0, 2, 1).reshape(hq, lq)
+    q = query if (query.dtype == torch.bfloat16 and query.is_contiguous()) else query.to(torch.bfloat16).contiguous()
+    tables = kernels.long_query_tables([segs], hkv, [0], [lq * (hq // hkv)], query.device, include_residual)
+    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv)
     return out.to(query.dtype), lse

@@ -34,6 +34,8 @@
 //    issued after it, overwrites those columns.
 //  * Every wait has a time budget; on expiry the CTA sets the device error
 //    word, drains its tensor-core work (bounded) and frees TMEM.
+#include <cstring>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -240,8 +242,12 @@ __device__ __forceinline__ bool wait_flag(const unsigned int* flag, uint64_t bud
 // range of spans (in ucb_span order) that hold the item's KV head's keys; the
 // item's keys are tokens [k_row0, k_row0 + n_tokens) of the concatenation of
 // those spans, and span s covers tokens [unit_begin, unit_begin + tokens).
+// Query rows and outputs of a segment-table launch live in the caller's own
+// layout: query and out [positions, q_heads, 128], lse [q_heads, positions];
+// row m of an item's KV head is position pos0 + m / grp, query head
+// head * grp + m % grp.
 struct LqItem {
-  int head, q_row0, q_rows, k_row0, n_tokens, mode, slot, span_begin, span_count, pad0, pad1, pad2;
+  int head, q_row0, q_rows, k_row0, n_tokens, mode, slot, span_begin, span_count, pos0, pad1, pad2;
 };
 
 // ---------------------------------------------------------------- span producers
@@ -264,17 +270,27 @@ __device__ __forceinline__ uint32_t tile_chunk(int row, int chunk) {
   return (uint32_t)((chunk >> 3) * (BN * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
+// Each producer owns one 16-byte chunk column (pid % 16) and walks every
+// sixth row from row pid / 16, so a warp copies two whole rows per
+// instruction (coalesced) and the addresses advance by constants.
+constexpr int ROW_STEP = PRODUCERS / 16;
 __device__ __forceinline__ void dense_rows(const __nv_bfloat16* base, int64_t stride, int off, int r0, int n,
                                            uint32_t tile, int pid) {
-  for (int idx = pid; idx < n * 16; idx += PRODUCERS) {
-    const int rr = idx >> 4, c = idx & 15;
-    cp_async16(tile + tile_chunk(r0 + rr, c), base + (int64_t)(off + rr) * stride + 8 * c);
+  const int c = pid & 15, first = pid >> 4;
+  if (first >= n) return;
+  const char* src = reinterpret_cast<const char*>(base + (int64_t)(off + first) * stride + 8 * c);
+  const int64_t src_step = (int64_t)ROW_STEP * stride * 2;
+  const uint32_t half = tile + (uint32_t)((c >> 3) * (BN * 128)), cl = (uint32_t)(c & 7) << 4;
+  for (int rr = first; rr < n; rr += ROW_STEP, src += src_step) {
+    const int r = r0 + rr;
+    cp_async16(half + r * 128 + (cl ^ ((uint32_t)(r & 7) << 4)), src);
   }
 }
 
 __device__ __forceinline__ void zero_rows(int r0, unsigned char* tile, int pid) {
-  for (int idx = pid; idx < (BN - r0) * 16; idx += PRODUCERS)
-    *reinterpret_cast<uint4*>(tile + tile_chunk(r0 + (idx >> 4), idx & 15)) = make_uint4(0u, 0u, 0u, 0u);
+  const int c = pid & 15;
+  for (int r = r0 + (pid >> 4); r < BN; r += PRODUCERS / 16)
+    *reinterpret_cast<uint4*>(tile + tile_chunk(r, c)) = make_uint4(0u, 0u, 0u, 0u);
 }
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
@@ -299,26 +315,47 @@ __device__ __forceinline__ uint32_t restore2(uint32_t z, uint32_t mask_magic_and
 // Keys packed along tokens ([T/f, D] words of this head, f = 32/KB tokens per
 // word; statistics [T/G, D]).  Unit = (word row, 8-channel chunk, half of the
 // word's tokens): 8 words and the chunk's 8 scales and minima in (channel
-// pairs already adjacent), f/2 rows of one 16-byte chunk out.
+// pairs already adjacent), f/2 rows of one 16-byte chunk out.  The loads of
+// a thread's next unit are issued before the current unit is restored, so a
+// thread waits for memory about once per tile rather than once per unit.
+struct KeyUnit {
+  uint4 ca, cb, s4, m4;
+};
+
 template <int KB>
 __device__ void packed_keys(const ucb_span& S, int G, int off, int r0, int n, unsigned char* tile, int pid) {
   constexpr int F = 32 / KB, HALF_TOK = F / 2;
-  const int w0 = off / F, w1 = (off + n - 1) / F;
+  const int w0 = off / F, w1 = (off + n - 1) / F, nu = (w1 - w0 + 1) * 32;
   const uint32_t* codes = static_cast<const uint32_t*>(S.key_code);
   const uint16_t* sc = static_cast<const uint16_t*>(S.key_scale);
   const uint16_t* mn = static_cast<const uint16_t*>(S.key_minimum);
-  for (int u = pid; u < (w1 - w0 + 1) * 32; u += PRODUCERS) {
-    const int w = w0 + (u >> 5), c = (u >> 1) & 15, hh = u & 1;
-    const int t_first = w * F + hh * HALF_TOK;  // first span token of this unit
-    if (t_first + HALF_TOK <= off || t_first >= off + n) continue;
+  auto wanted = [&](int u) {
+    const int t_first = (w0 + (u >> 5)) * F + (u & 1) * HALF_TOK;
+    return t_first + HALF_TOK > off && t_first < off + n;
+  };
+  auto next = [&](int u) {
+    while (u < nu && !wanted(u)) u += PRODUCERS;
+    return u;
+  };
+  auto load = [&](int u, KeyUnit& d) {
+    const int w = w0 + (u >> 5), c = (u >> 1) & 15;
     const uint32_t* cw = codes + (int64_t)w * D + 8 * c;
-    const uint4 ca = __ldg(reinterpret_cast<const uint4*>(cw));
-    const uint4 cb = __ldg(reinterpret_cast<const uint4*>(cw + 4));
     const int64_t g = (int64_t)(w * F) / G;
-    const uint4 s4 = __ldg(reinterpret_cast<const uint4*>(sc + g * D + 8 * c));
-    const uint4 m4 = __ldg(reinterpret_cast<const uint4*>(mn + g * D + 8 * c));
-    const uint32_t word[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-    const uint32_t sp[4] = {s4.x, s4.y, s4.z, s4.w}, mp[4] = {m4.x, m4.y, m4.z, m4.w};
+    d.ca = __ldg(reinterpret_cast<const uint4*>(cw));
+    d.cb = __ldg(reinterpret_cast<const uint4*>(cw + 4));
+    d.s4 = __ldg(reinterpret_cast<const uint4*>(sc + g * D + 8 * c));
+    d.m4 = __ldg(reinterpret_cast<const uint4*>(mn + g * D + 8 * c));
+  };
+  int u = next(pid);
+  KeyUnit cur;
+  if (u < nu) load(u, cur);
+  while (u < nu) {
+    const int un = next(u + PRODUCERS);
+    KeyUnit nxt;
+    if (un < nu) load(un, nxt);
+    const int w = w0 + (u >> 5), c = (u >> 1) & 15, hh = u & 1;
+    const uint32_t word[8] = {cur.ca.x, cur.ca.y, cur.ca.z, cur.ca.w, cur.cb.x, cur.cb.y, cur.cb.z, cur.cb.w};
+    const uint32_t sp[4] = {cur.s4.x, cur.s4.y, cur.s4.z, cur.s4.w}, mp[4] = {cur.m4.x, cur.m4.y, cur.m4.z, cur.m4.w};
 #pragma unroll
     for (int b = 0; b < 2; ++b) {  // the two bytes (KB = 2: 4 tokens each; KB = 4: 2 tokens each) of this half
       const int byte = 2 * hh + b;
@@ -345,12 +382,21 @@ __device__ void packed_keys(const ucb_span& S, int G, int off, int r0, int n, un
         *reinterpret_cast<uint4*>(tile + tile_chunk(r0 + (t - off), c)) = make_uint4(out[0], out[1], out[2], out[3]);
       }
     }
+    cur = nxt;
+    u = un;
   }
 }
 
 // Values packed along channels ([T, D/f] words, f = 32/VB channels per word;
 // statistics [T, D/G]).  Unit = (token, 64-channel half row): the half row's
-// words and its groups' statistics in, 8 chunks out.
+// words and its groups' statistics in, 8 chunks out; loads of the next unit
+// are issued before the current one is restored.
+template <int VB>
+struct ValueUnit {
+  uint32_t word[D / (32 / VB) / 2];
+  uint32_t s_a, m_a, s_b, m_b;
+};
+
 template <int VB>
 __device__ void packed_values(const ucb_span& S, int G, int off, int r0, int n, unsigned char* tile, int pid) {
   constexpr int F = 32 / VB, W = D / F, HW = W / 2;  // words per token, per half row
@@ -358,32 +404,40 @@ __device__ void packed_values(const ucb_span& S, int G, int off, int r0, int n, 
   const uint16_t* sc = static_cast<const uint16_t*>(S.value_scale);
   const uint16_t* mn = static_cast<const uint16_t*>(S.value_minimum);
   const int ng = D / G;
-  for (int u = pid; u < 2 * n; u += PRODUCERS) {
+  auto load = [&](int u, ValueUnit<VB>& d) {
     const int64_t t = off + (u >> 1);
-    const int hh = u & 1, r = r0 + (u >> 1);
-    uint32_t word[HW];
+    const int hh = u & 1;
 #pragma unroll
     for (int k = 0; k < HW; k += 4) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(codes + t * W + hh * HW + k));
-      word[k] = v.x;
-      word[k + 1] = v.y;
-      word[k + 2] = v.z;
-      word[k + 3] = v.w;
+      d.word[k] = v.x;
+      d.word[k + 1] = v.y;
+      d.word[k + 2] = v.z;
+      d.word[k + 3] = v.w;
     }
-    // groups covering channels [64 hh, 64 hh + 64): G = 32 -> 2, else 1
-    const int g0 = (64 * hh) / G;
-    const uint32_t s_a = sc[t * ng + g0], m_a = mn[t * ng + g0];
-    const uint32_t s_b = (G == 32) ? (uint32_t)sc[t * ng + g0 + 1] : s_a;
-    const uint32_t m_b = (G == 32) ? (uint32_t)mn[t * ng + g0 + 1] : m_a;
-    const uint32_t s2a = s_a | (s_a << 16), m2a = m_a | (m_a << 16);
-    const uint32_t s2b = s_b | (s_b << 16), m2b = m_b | (m_b << 16);
+    const int g0 = (64 * hh) / G;  // groups covering channels [64 hh, 64 hh + 64): G = 32 -> 2, else 1
+    d.s_a = sc[t * ng + g0];
+    d.m_a = mn[t * ng + g0];
+    d.s_b = (G == 32) ? (uint32_t)sc[t * ng + g0 + 1] : d.s_a;
+    d.m_b = (G == 32) ? (uint32_t)mn[t * ng + g0 + 1] : d.m_a;
+  };
+  int u = pid;
+  ValueUnit<VB> cur;
+  if (u < 2 * n) load(u, cur);
+  while (u < 2 * n) {
+    const int un = u + PRODUCERS;
+    ValueUnit<VB> nxt;
+    if (un < 2 * n) load(un, nxt);
+    const int hh = u & 1, r = r0 + (u >> 1);
+    const uint32_t s2a = cur.s_a | (cur.s_a << 16), m2a = cur.m_a | (cur.m_a << 16);
+    const uint32_t s2b = cur.s_b | (cur.s_b << 16), m2b = cur.m_b | (cur.m_b << 16);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {  // 8-channel chunks of the half row
       const bool second = (8 * c) >= 32;  // second 32-channel group of the half (G = 32)
       const uint32_t s2 = second ? s2b : s2a, m2 = second ? m2b : m2a;
       uint32_t out[4];
       if constexpr (VB == 2) {
-        const uint32_t wv = word[c / 2];  // 16 channels per word, chunk = 2 bytes
+        const uint32_t wv = cur.word[c / 2];  // 16 channels per word, chunk = 2 bytes
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           const int byte = 2 * (c & 1) + b;
@@ -393,7 +447,7 @@ __device__ void packed_values(const ucb_span& S, int G, int off, int r0, int n, 
           out[2 * b + 1] = restore2(y >> 4, 0x000C0003u, 0x42004300u, 0xC200C300u, s2, m2);
         }
       } else {
-        const uint32_t wv = word[c], wh = wv >> 4;  // 8 channels per word, chunk = 1 word
+        const uint32_t wv = cur.word[c], wh = wv >> 4;  // 8 channels per word, chunk = 1 word
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           out[k] = restore2(prmt(wv, wh, k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12)), 0x000F000Fu, 0x43004300u,
@@ -401,6 +455,8 @@ __device__ void packed_values(const ucb_span& S, int G, int off, int r0, int n, 
       }
       *reinterpret_cast<uint4*>(tile + tile_chunk(r, 8 * hh + c)) = make_uint4(out[0], out[1], out[2], out[3]);
     }
+    cur = nxt;
+    u = un;
   }
 }
 
@@ -446,6 +502,8 @@ struct Params {
   const LqItem* lq_items; // segment-table launches: per-CTA problems reading spans in place
   const ucb_span* spans;  // the spans lq_items refer to
   int k_bits, v_bits, group;  // packed spans of a segment-table launch
+  const __nv_bfloat16* q;     // segment-table launches: query [positions, hq, 128]
+  int hq, grp, positions;     // query heads, query heads per KV head, positions (lse row length)
   float* partials;        // PARTIAL_SLOT_FLOATS per slot (split row blocks), or null
   unsigned int* flags;    // one per slot, even between launches, or null
   __nv_bfloat16* out;  // [heads, m_rows, D]
@@ -461,7 +519,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0, span_begin = 0, span_count = 0;
+  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0, span_begin = 0, span_count = 0, pos0 = 0;
   if constexpr (SPANS) {
     const LqItem it = P.lq_items[blockIdx.x];
     head = it.head;
@@ -473,6 +531,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     slot = it.slot;
     span_begin = it.span_begin;
     span_count = it.span_count;
+    pos0 = it.pos0;
     if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
       if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
       mode = ITEM_FINAL;
@@ -521,7 +580,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (tid == 0) {
     failed = 0;
-    mbar_init(q_full, 1);
+    mbar_init(q_full, SPANS ? PRODUCERS : 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&k_full[i], SPANS ? PRODUCERS : 1);
       mbar_init(&k_empty[i], 1);
@@ -551,37 +610,60 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (SPANS && (warp == 8 || warp == 10 || warp == 11)) {
     // ---------------- span producers
     const int pid = (warp == 8 ? 0 : warp - 9) * 32 + lane;
-    if (pid == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * QTILE);
-      for (int x = 0; x < 2; ++x) {
-        tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
-        tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+    // Q_A and Q_B straight from the caller's [positions, hq, 128] query
+    // (zero rows past the item's last row); their copies ride with the first
+    // K tile's and are published with it.
+    {
+      const uint32_t q_addr = smem_u32(smem + OFF_Q);
+      const int c = pid & 15;
+      const uint32_t cl = (uint32_t)(c & 7) << 4;
+      for (int rb = pid >> 4; rb < 2 * BM; rb += ROW_STEP) {
+        const int x = rb >> 7, rr = rb & (BM - 1), m = m0 + rb;
+        const uint32_t dst = x * QTILE + (c >> 3) * QHALF + rr * 128 + (cl ^ ((uint32_t)(rr & 7) << 4));
+        if (m < m_end)
+          cp_async16(q_addr + dst, P.q + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 8 * c);
+        else
+          *reinterpret_cast<uint4*>(smem + OFF_Q + dst) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
+    // Half-tiles h = 2j (K of tile j) and 2j + 1 (V of tile j) are filled in
+    // order, each as one cp.async group; half-tile h - 1 is published (its
+    // copies waited for, proxy fence, arrive) only once half-tile h is in
+    // flight, so K and V loads overlap like TMA loads do.  A half-tile's
+    // stage is released by the MMA thread; the producer runs at most one
+    // half-tile ahead of what it has published, which is what the MMA loop
+    // needs to release that stage, so the two cannot wait on each other.
     const ucb_span* spans = P.spans + span_begin;
-    for (int j = 0; j < n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++j) {
-      const int st = j % STAGES;
-      const uint32_t ph = ((j / STAGES) - 1) & 1;
-      const int tok0 = k0 + j * BN, valid = min(BN, n_tokens - j * BN);
-      if (j >= STAGES && !mbar_wait_for(&k_empty[st], ph, WAIT_NS)) {
-        fail();
-        break;
-      }
-      fill_tile(true, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group, smem + OFF_K + st * KTILE, pid);
-      cp_async_wait_all();
+    auto publish = [&](int h) {
       fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
-      mbar_arrive(&k_full[st]);
-      if (j >= STAGES && !mbar_wait_for(&v_empty[st], ph, WAIT_NS)) {
+      if (h == 0) mbar_arrive(q_full);
+      mbar_arrive((h & 1) ? &v_full[(h >> 1) % STAGES] : &k_full[(h >> 1) % STAGES]);
+    };
+    int filled = 0;
+    for (int h = 0; h < 2 * n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++h) {
+      const int j = h >> 1, st = j % STAGES;
+      const bool keys = (h & 1) == 0;
+      if (j >= STAGES && !mbar_wait_for(keys ? &k_empty[st] : &v_empty[st], ((j / STAGES) - 1) & 1, WAIT_NS)) {
         fail();
         break;
       }
-      fill_tile(false, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group, smem + OFF_V + st * VTILE, pid);
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&v_full[st]);
+      const int tok0 = k0 + j * BN, valid = min(BN, n_tokens - j * BN);
+      fill_tile(keys, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group,
+                smem + (keys ? OFF_K + st * KTILE : OFF_V + st * VTILE), pid);
+      cp_async_commit();
+      filled = h + 1;
+      if (h > 0) {
+        cp_async_wait_one();  // every group but the newest (half-tile h) has landed
+        publish(h - 1);
+      }
     }
     cp_async_wait_all();
-    if (pid == 0) mbar_wait_for(q_full, 0, WAIT_NS);  // the Q copies land before shared memory is released
+    if (filled > 0) {
+      publish(filled - 1);
+    } else {  // no key tile was filled (an empty item or an early failure): the Q copies still land
+      fence_proxy_async_smem();
+      mbar_arrive(q_full);
+    }
   } else if (!SPANS && warp == 8) {
     // ---------------- loader
     if (lane == 0) {
@@ -779,7 +861,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[i] = __uint_as_float(ov[i]) * inv;
             if (merged) v[i] = fmaf(w_p, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
           }
-          __nv_bfloat16* dst = P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
+          __nv_bfloat16* dst =
+              SPANS ? P.out + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 32 * c
+                    : P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 w4;
@@ -791,7 +875,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (m < m_end && P.lse) P.lse[(int64_t)head * P.m_rows + m] = lse2 * 0.6931471805599453f;
+      if (m < m_end && P.lse) {
+        const int64_t at = SPANS ? (int64_t)(head * P.grp + m % P.grp) * P.positions + pos0 + m / P.grp
+                                 : (int64_t)head * P.m_rows + m;
+        P.lse[at] = lse2 * 0.6931471805599453f;
+      }
     }
     // The softmax warps meet once: a partial is published after every row
     // is written; a consumed partial's flag advances after every row read.
@@ -845,7 +933,7 @@ namespace {
 int launch_prefill(const void* q, const void* k, const void* vt, int heads, int m_rows, int n_padded,
                    ucb::prefill::Params P, dim3 grid, void* stream) {
   using namespace ucb::prefill;
-  const bool spans = (k == nullptr);
+  const bool spans = (q == nullptr);
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(vt)) & 15)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: operands must be 16-byte aligned");
   if (!spans && n_padded % 8)
@@ -853,11 +941,15 @@ int launch_prefill(const void* q, const void* k, const void* vt, int heads, int 
   unsigned int* err = ucb_host::device_error_word();
   if (!err) return ucb_host::set_error(UCB_ERR_CUDA, "ucb_prefill_attention: device error word unavailable");
   CUtensorMap tq, tk, tv;
-  int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads, BM);
-  if (!rc && !spans) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
-  if (!rc && !spans) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
-  if (rc) return rc;
-  if (spans) tk = tv = tq;  // unused by the segment-table kernel
+  if (spans) {
+    memset(&tq, 0, sizeof(tq));  // unused by the segment-table kernel
+    tk = tv = tq;
+  } else {
+    int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads, BM);
+    if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
+    if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
+    if (rc) return rc;
+  }
   static bool configured[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -894,6 +986,8 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   P.lq_items = nullptr;
   P.spans = nullptr;
   P.k_bits = P.v_bits = P.group = 0;
+  P.q = nullptr;
+  P.hq = P.grp = P.positions = 0;
   P.partials = nullptr;
   P.flags = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
@@ -920,6 +1014,8 @@ extern "C" int ucb_prefill_attention_items(const void* q, const void* k, const v
   P.lq_items = nullptr;
   P.spans = nullptr;
   P.k_bits = P.v_bits = P.group = 0;
+  P.q = nullptr;
+  P.hq = P.grp = P.positions = 0;
   P.partials = partials;
   P.flags = flags;
   P.out = static_cast<__nv_bfloat16*>(out);
@@ -938,14 +1034,18 @@ extern "C" int64_t ucb_prefill_partial_bytes() {
   return (int64_t)ucb::prefill::PARTIAL_SLOT_FLOATS * (int64_t)sizeof(float);
 }
 
-extern "C" int ucb_long_query_attention(const void* q, int heads, int m_rows, const void* items, int num_items,
-                                        const ucb_span* spans, int num_spans, int k_bits, int v_bits, int group_size,
-                                        float softmax_scale, void* out, float* lse, float* partials,
-                                        unsigned int* flags, void* stream) {
+extern "C" int ucb_long_query_attention(const void* q, int positions, int num_q_heads, int num_kv_heads,
+                                        const void* items, int num_items, const ucb_span* spans, int num_spans,
+                                        int k_bits, int v_bits, int group_size, float softmax_scale, void* out,
+                                        float* lse, float* partials, unsigned int* flags, void* stream) {
   using namespace ucb::prefill;
   if (!q || !items || !spans || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: null pointer");
-  if (heads <= 0 || m_rows <= 0 || num_items <= 0 || num_spans <= 0)
+  if (positions <= 0 || num_items <= 0 || num_spans <= 0)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: empty problem");
+  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: query heads must be a multiple of KV heads");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: query/out must be 16-byte aligned");
   if ((k_bits != 2 && k_bits != 4) || (v_bits != 2 && v_bits != 4))
     return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_attention: packed spans must be 2- or 4-bit");
   if (group_size != 32 && group_size != 64 && group_size != 128)
@@ -953,10 +1053,14 @@ extern "C" int ucb_long_query_attention(const void* q, int heads, int m_rows, co
   if ((partials == nullptr) != (flags == nullptr))
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: partials and flags go together");
   Params P;
-  P.m_rows = m_rows;
+  P.m_rows = 0;
   P.n_tokens = 0;
   P.scale_log2 = softmax_scale * 1.4426950408889634f;
   P.items = nullptr;
+  P.q = static_cast<const __nv_bfloat16*>(q);
+  P.hq = num_q_heads;
+  P.grp = num_q_heads / num_kv_heads;
+  P.positions = positions;
   P.lq_items = static_cast<const LqItem*>(items);
   P.spans = spans;
   P.k_bits = k_bits;
@@ -966,5 +1070,5 @@ extern "C" int ucb_long_query_attention(const void* q, int heads, int m_rows, co
   P.flags = flags;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
-  return launch_prefill(q, nullptr, nullptr, heads, m_rows, 0, P, dim3(num_items), stream);
+  return launch_prefill(nullptr, nullptr, nullptr, 0, 0, 0, P, dim3(num_items), stream);
 }

@@ -965,20 +965,21 @@ class LongQueryTables:
 
 
 def long_query_spans(segments: list, num_kv_heads: int, head: int, include_residual: bool = True):
-    """The spans of one KV head of one sample, in segment order: (list of
-    UcbSpan with ``unit_begin`` = first token, tokens, (k_bits, v_bits, group)
-    of its packed spans or None, objects to keep alive)."""
+    """The spans of one KV head of one sample: (list of UcbSpan with
+    ``unit_begin`` = first token, tokens, (k_bits, v_bits, group) of its
+    packed spans or None, objects to keep alive).  Packed spans come first,
+    then the dense, H2O and residual rows in segment order: attention does not
+    depend on the order of its keys, and a key split hands the last key tiles
+    of a row block to the CTAs that run in several rounds, so those should be
+    the cheap dense tiles rather than the tiles restored from codes."""
 
     from .storage.physical import GQAH2OCache, PackedKIVICache
 
-    spans, keep, cfg, t0 = [], [], None, 0
+    packed, dense, keep, cfg = [], [], [], None
 
     def add(sp):
-        nonlocal t0
-        sp.unit_begin = t0
         sp.pair = 0
-        spans.append(sp)
-        t0 += int(sp.tokens)
+        (packed if sp.kind == 0 else dense).append(sp)
 
     for seg in segments:
         if isinstance(seg, PackedKIVICache):
@@ -1006,6 +1007,10 @@ def long_query_spans(segments: list, num_kv_heads: int, head: int, include_resid
             if int(key.shape[0]):
                 add(_dense_span(dense_rows_token_major(key, value, head)))
             keep.append((key, value))
+    spans, t0 = packed + dense, 0
+    for sp in spans:
+        sp.unit_begin = t0
+        t0 += int(sp.tokens)
     return spans, t0, cfg, keep
 
 
@@ -1037,32 +1042,33 @@ def _segment_signature(seg) -> tuple:
 _LQ_BY_SIGNATURE: dict = {}
 
 
-def long_query_tables(samples: list, num_kv_heads: int, q_row0: list, q_rows: list, device,
+def long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_rows: list, device,
                       include_residual: bool = True) -> LongQueryTables:
-    """Segment-table launch tables for several samples: sample i's query rows
-    are [q_row0[i], q_row0[i] + q_rows[i]) of every KV head's rows in the q
-    workspace, its keys the concatenation of its segments.  Tables are cached
+    """Segment-table launch tables for several samples: sample i's queries are
+    positions [pos0[i], pos0[i] + q_rows[i] / grp) of the launch's query
+    tensor (q_rows[i] = its positions x query heads per KV head), its keys the
+    concatenation of its segments.  Tables are cached
     on the segments' signatures (identity, addresses, strides, lengths), so a
     layer called again over the same frozen segments costs a dictionary
     lookup on the host."""
 
     index = torch.device(device).index
-    signature = (index, num_kv_heads, bool(include_residual), tuple(q_row0), tuple(q_rows),
+    signature = (index, num_kv_heads, bool(include_residual), tuple(pos0), tuple(q_rows),
                  tuple(tuple(_segment_signature(seg) for seg in segs) for segs in samples))
     hit = _LQ_BY_SIGNATURE.get(signature)
     if hit is not None:
         return hit
-    tables = _build_long_query_tables(samples, num_kv_heads, q_row0, q_rows, device, include_residual)
+    tables = _build_long_query_tables(samples, num_kv_heads, pos0, q_rows, device, include_residual)
     if len(_LQ_BY_SIGNATURE) >= _LQ_TABLES_MAX:
         _LQ_BY_SIGNATURE.pop(next(iter(_LQ_BY_SIGNATURE)))
     _LQ_BY_SIGNATURE[signature] = tables
     return tables
 
 
-def _build_long_query_tables(samples: list, num_kv_heads: int, q_row0: list, q_rows: list, device,
+def _build_long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_rows: list, device,
                              include_residual: bool) -> LongQueryTables:
     all_spans, rows, cfg = [], [], None
-    for segs, r0, nrows in zip(samples, q_row0, q_rows):
+    for segs, p0, nrows in zip(samples, pos0, q_rows):
         for h in range(num_kv_heads):
             spans, tokens, this, _ = long_query_spans(segs, num_kv_heads, h, include_residual)
             if tokens == 0:
@@ -1074,8 +1080,8 @@ def _build_long_query_tables(samples: list, num_kv_heads: int, q_row0: list, q_r
             begin = len(all_spans)
             all_spans.extend(spans)
             for r in range(0, nrows, PREFILL_ROWS_PER_CTA):
-                rows.append([h, r0 + r, min(PREFILL_ROWS_PER_CTA, nrows - r), 0, tokens, 0, 0, begin, len(spans),
-                             0, 0, 0])
+                rows.append([h, r, min(PREFILL_ROWS_PER_CTA, nrows - r), 0, tokens, 0, 0, begin, len(spans),
+                             p0, 0, 0])
     rows, slots = split_prefill_items(rows, _sm_count(torch.device(device).index))
     k_bits, v_bits, group = cfg if cfg is not None else (2, 2, 32)
     raw = _capi.struct_array_bytes(all_spans)
@@ -1100,26 +1106,30 @@ _LQ_TABLES: dict = {}
 _LQ_TABLES_MAX = 64
 
 
-def long_query_attention(q: torch.Tensor, tables: LongQueryTables, *, softmax_scale: float | None = None,
-                         out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
-    """Non-causal attention of the query rows q [H, M, 128] (bf16) over the
-    spans of ``tables``, read in place (packed KIVI tiles restored in shared
-    memory): (out [H, M, 128] bf16, lse [H, M] fp32 natural log); rows no
-    item covers are left unwritten."""
+def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv_heads: int,
+                         softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                         lse: torch.Tensor | None = None):
+    """Non-causal attention of query [positions, Hq, 128] (bf16, the caller's
+    layout) over the spans of ``tables``, read in place (packed KIVI tiles
+    restored in shared memory): (out [positions, Hq, 128] bf16, lse
+    [Hq, positions] fp32 natural log); positions no item covers are left
+    unwritten."""
 
-    require_cuda(q, "q")
-    if q.dtype != torch.bfloat16 or not q.is_contiguous() or q.dim() != 3 or int(q.shape[2]) != 128:
-        raise ValueError("q must be a contiguous bfloat16 [heads, rows, 128] tensor")
-    heads, m_rows, d = map(int, q.shape)
+    require_cuda(query, "query")
+    if query.dtype != torch.bfloat16 or not query.is_contiguous() or query.dim() != 3 or int(query.shape[2]) != 128:
+        raise ValueError("query must be a contiguous bfloat16 [positions, q_heads, 128] tensor")
+    positions, q_heads, d = map(int, query.shape)
+    if q_heads % num_kv_heads:
+        raise ValueError("Query heads must be divisible by KV heads")
     scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty_like(query)
     if lse is None:
-        lse = torch.empty((heads, m_rows), device=q.device, dtype=torch.float32)
+        lse = torch.empty((q_heads, positions), device=query.device, dtype=torch.float32)
     partials = flags = None
     if tables.slots:
-        partials, flags = prefill_split_workspace(q.device, tables.slots, stream_of(q))
-    call("ucb_long_query_attention", q.data_ptr(), heads, m_rows, tables.items.data_ptr(), tables.num_items,
-         tables.spans.data_ptr(), tables.num_spans, tables.k_bits, tables.v_bits, tables.group_size, scale,
-         out.data_ptr(), lse.data_ptr(), ptr(partials), ptr(flags), stream_of(q))
+        partials, flags = prefill_split_workspace(query.device, tables.slots, stream_of(query))
+    call("ucb_long_query_attention", query.data_ptr(), positions, q_heads, num_kv_heads, tables.items.data_ptr(),
+         tables.num_items, tables.spans.data_ptr(), tables.num_spans, tables.k_bits, tables.v_bits,
+         tables.group_size, scale, out.data_ptr(), lse.data_ptr(), ptr(partials), ptr(flags), stream_of(query))
     return out, lse
