@@ -1,5 +1,6 @@
 """Contracts shared with the reference's plugin API (unicache/core)."""
 
 from .decisions import PhysicalCacheRequest
+from .plugin import CapabilityDescriptor, ProcessingOperator
 
-__all__ = ["PhysicalCacheRequest"]
+__all__ = ["CapabilityDescriptor", "PhysicalCacheRequest", "ProcessingOperator"]

@@ -1,9 +1,11 @@
 """The two physical-cache operators of the plugin API, on the B200 path.
 
-Same names, parameters, validation and request contents as the reference's
-operators (Superone77/UniCache, unicache/operators/physical.py), so a plan
-that names ``h2o_physical_gqa`` or ``kivi_packed_quantization`` runs
-unchanged.  ``execute`` / ``update_after_attention`` take the reference's
+Same names, parameters, validation, capabilities and request contents as the
+reference's operators (Superone77/UniCache, unicache/operators/physical.py),
+derived from the plugin contract's ``ProcessingOperator``, so a plan that
+names ``h2o_physical_gqa`` or ``kivi_packed_quantization`` runs unchanged and
+the reference's ``KVRegistry`` accepts them.  Devices are ``cuda`` only: the
+B200 path has no CPU implementation.  ``execute`` / ``update_after_attention`` take the reference's
 ``OperatorExecutionContext`` (any object with its attributes: ``params``,
 ``k``, ``segment_mask``, ``step.segment_id``, ``runtime.kv_metadata``,
 ``storage_num_kv_heads``, ``record``, ``physical_request``).
@@ -15,9 +17,10 @@ import torch
 
 from .. import kernels
 from ..core.decisions import PhysicalCacheRequest
+from ..core.plugin import CapabilityDescriptor, ProcessingOperator
 
 
-class H2OPhysicalGQAOperator:
+class H2OPhysicalGQAOperator(ProcessingOperator):
     """H2O real-drop semantics on GQA storage (physical.py:14-101)."""
 
     name = "h2o_physical_gqa"
@@ -26,6 +29,16 @@ class H2OPhysicalGQAOperator:
     executable = True
     uses_final_attention = True
     preserves_attention_dispatch = False
+    capabilities = CapabilityDescriptor(
+        stages=frozenset(stages),
+        layouts=frozenset({"attention_view", "dense"}),
+        devices=frozenset({"cuda"}),
+        requires=frozenset({"query", "key", "value", "segment_mask", "cache_storage_view"}),
+        produces_selection=True,
+        stateful=True,
+        mutation_scope="persistent_cache",
+        physical_storage_mutation=True,
+    )
 
     def build_params(self, params: dict) -> dict:
         out = dict(params)
@@ -110,7 +123,7 @@ class H2OPhysicalGQAOperator:
         return ctx
 
 
-class KIVIPackedQuantizationOperator:
+class KIVIPackedQuantizationOperator(ProcessingOperator):
     """Move a typed dense segment into KIVI packed physical storage
     (physical.py:104-178)."""
 
@@ -120,6 +133,15 @@ class KIVIPackedQuantizationOperator:
     executable = True
     uses_final_attention = False
     preserves_attention_dispatch = False
+    capabilities = CapabilityDescriptor(
+        stages=frozenset(stages),
+        layouts=frozenset({"attention_view", "dense"}),
+        devices=frozenset({"cuda"}),
+        requires=frozenset({"key", "value", "segment_mask", "cache_storage_view"}),
+        mutation_scope="persistent_cache",
+        physical_storage_mutation=True,
+        accepts_quantized_input=False,
+    )
 
     def build_params(self, params: dict) -> dict:
         out = dict(params)

@@ -1,9 +1,11 @@
 """Dense cache compaction and physical materialisation on the GPU.
 
 Counterpart of the reference's ``TensorCacheStorageBackend``
-(Superone77/UniCache, unicache/storage/tensor_backend.py): the same request
-handling, budget arithmetic and error messages, with the boolean-mask gather
-and the H2O/KIVI layouts computed by the B200 kernels.
+(Superone77/UniCache, unicache/storage/tensor_backend.py): the same contract
+(arguments, budget arithmetic, error messages), with the boolean-mask gather
+and the H2O/KIVI layouts computed by the B200 kernels and the requests of a
+batch planned together so that host reads do not scale with the number of
+requests.
 """
 
 from __future__ import annotations
@@ -109,102 +111,29 @@ class TensorCacheStorageBackend:
         physical_requests: list[list[PhysicalCacheRequest]],
         sample_lengths: list[int] | None = None,
     ) -> CacheMutationResult:
-        """tensor_backend.py:103-239: build physical segments from requests and
-        remove their tokens from the dense cache."""
+        """Turn every sample's physical requests into H2O or packed KIVI
+        segments and drop the claimed tokens from the dense cache (the
+        contract of the reference's tensor_backend.py:103-239).
+
+        The requests of the whole batch are planned together: one device ->
+        host read checks every sample for overlapping claims, one reads the
+        token count of every mask-defined segment (their indices then come
+        from ``nonzero_static`` without further syncs), and one, only when a
+        request carries no type id, reads the type range of those segments.
+        The dense compaction is the single launch of ``compact``."""
 
         lengths = sample_lengths
         if lengths is None:
             lengths = [int(item) for item in sample_lens.to("cpu").tolist()]
         if len(physical_requests) != len(lengths):
             raise ValueError("Physical requests require one list per packed sample")
-        physical_by_sample: list[list[Any]] = []
-        offset = 0
-        for sample_idx, (length, requests) in enumerate(zip(lengths, physical_requests)):
-            sample_key = key[offset:offset + length]
-            sample_value = value[offset:offset + length]
-            occupied = torch.zeros(length, device=key.device, dtype=torch.bool)
-            segments: list[Any] = []
-            normalized = []
-            for request in requests:
-                if request.token_count < length:
-                    raise ValueError("PhysicalCacheRequest is shorter than the persistent cache sample")
-                normalized.append((request, request.segment_mask[:length].to(device=key.device, dtype=torch.bool)))
-            if len(normalized) > 1:
-                claims = torch.stack([mask for _, mask in normalized], dim=0).sum(dim=0)
-                if bool((claims > 1).any()):
-                    raise ValueError(f"Overlapping physical requests in sample {sample_idx} are not allowed")
-            for request, segment_mask in normalized:
-                occupied |= segment_mask
-                token_span = request.metadata.get("token_span")
-                segment_slice = None
-                if token_span is not None:
-                    if not isinstance(token_span, (tuple, list)) or len(token_span) != 2:
-                        raise ValueError("Physical token_span must be a (start, stop) pair")
-                    span_start, span_stop = map(int, token_span)
-                    if not 0 <= span_start < span_stop <= length:
-                        raise ValueError("Physical token_span is outside its packed sample")
-                    segment_slice = slice(span_start, span_stop)
-                    segment_idx = torch.arange(span_start, span_stop, device=key.device, dtype=torch.long)
-                else:
-                    segment_idx = torch.nonzero(segment_mask, as_tuple=False).flatten()
-                    if int(segment_idx.numel()) == 0:
-                        continue
-                metadata_type_id = request.metadata.get("token_type_id")
-                type_id = int(metadata_type_id) if metadata_type_id is not None else -1
-                if type_id < 0 and key_type_ids is not None:
-                    segment_types = torch.unique(key_type_ids[offset:offset + length][segment_idx.to(key_type_ids.device)])
-                    if int(segment_types.numel()) == 1:
-                        type_id = int(segment_types.item())
-                logical_ids = segment_idx.to(dtype=torch.int64)
-                if segment_slice is None:
-                    dense_key = sample_key[segment_idx].contiguous()
-                    dense_value = sample_value[segment_idx].contiguous()
-                else:
-                    dense_key = sample_key[segment_slice]
-                    dense_value = sample_value[segment_slice]
-                if request.operator == "kivi_packed_quantization":
-                    bits = int(request.params.get("bits", 4))
-                    segment = PackedKIVICache.from_dense(
-                        dense_key,
-                        dense_value,
-                        logical_token_ids=logical_ids,
-                        token_type_id=type_id,
-                        k_bits=int(request.params.get("k_bits", bits)),
-                        v_bits=int(request.params.get("v_bits", bits)),
-                        group_size=int(request.params.get("group_size", 64)),
-                        residual_length=int(request.params.get("residual_length", 32)),
-                        backend=str(request.params.get("backend", "b200")),
-                    )
-                elif request.operator == "h2o_physical_gqa":
-                    scores = request.per_kv_head_scores
-                    if scores is None:
-                        raise ValueError("Physical H2O request is missing per-KV-head scores")
-                    scores = scores[:, :length].to(device=key.device, dtype=torch.float32)
-                    segment_scores = scores[:, segment_idx]
-                    target = request.params.get("budget", request.params.get("keep_k"))
-                    if target is None:
-                        ratio = float(request.params.get("target_budget_ratio", 1.0))
-                        target = max(1, int(round(int(segment_idx.numel()) * ratio)))
-                    recent = request.params.get("recent_size")
-                    if recent is None:
-                        recent = int(round(int(target) * float(request.params.get("recent_budget_fraction", 0.25))))
-                    segment = GQAH2OCache.from_dense(
-                        dense_key,
-                        dense_value,
-                        logical_token_ids=logical_ids,
-                        token_type_id=type_id,
-                        per_kv_head_scores=segment_scores,
-                        target_tokens=int(target),
-                        recent_tokens=int(recent),
-                        selection_frozen=bool(request.params.get("selection_frozen", False)),
-                    )
-                else:
-                    raise ValueError(f"Unknown physical cache request: {request.operator}")
-                segments.append(segment)
-            keep_masks[sample_idx] &= ~occupied.to(keep_masks[sample_idx].device)
-            physical_by_sample.append(segments)
-            offset += length
-
+        plan = _ClaimPlan(key.device, lengths, physical_requests)
+        plan.check_overlaps()
+        plan.resolve_indices()
+        plan.resolve_types(key_type_ids)
+        physical_by_sample = plan.materialize(key, value)
+        for sample, occupied in enumerate(plan.occupied):
+            keep_masks[sample] &= ~occupied.to(keep_masks[sample].device)
         mutation = TensorCacheStorageBackend.compact(
             key=key,
             value=value,
@@ -215,3 +144,149 @@ class TensorCacheStorageBackend:
         )
         mutation.physical_segments_by_sample = physical_by_sample
         return mutation
+
+
+@dataclass
+class _Claim:
+    """One physical request resolved against its sample of the dense cache."""
+
+    sample: int
+    offset: int                      # first row of the sample in the packed cache
+    request: PhysicalCacheRequest
+    mask: torch.Tensor               # bool [sample length] on the cache's device
+    span: tuple[int, int] | None     # contiguous (start, stop) when the request names one
+    index: torch.Tensor | None = None  # int64 rows of the segment within its sample
+    type_id: int = -1
+
+
+def _h2o_budget(params: dict, tokens: int) -> tuple[int, int]:
+    """(target, recent) of an H2O request over ``tokens`` rows: an explicit
+    budget/keep_k and recent_size win, otherwise the ratio and the recent
+    fraction with Python's round (tensor_backend.py:199-210)."""
+
+    target = params.get("budget", params.get("keep_k"))
+    if target is None:
+        target = max(1, int(round(tokens * float(params.get("target_budget_ratio", 1.0)))))
+    recent = params.get("recent_size")
+    if recent is None:
+        recent = int(round(int(target) * float(params.get("recent_budget_fraction", 0.25))))
+    return int(target), int(recent)
+
+
+class _ClaimPlan:
+    """The batch's physical requests, validated and resolved with a fixed
+    number of host reads."""
+
+    def __init__(self, device, lengths: list[int], physical_requests: list[list[PhysicalCacheRequest]]):
+        self.claims: list[_Claim] = []
+        self.occupied: list[torch.Tensor] = []
+        self.lengths = lengths
+        offset = 0
+        for sample, (length, requests) in enumerate(zip(lengths, physical_requests)):
+            for request in requests:
+                if request.token_count < length:
+                    raise ValueError("PhysicalCacheRequest is shorter than the persistent cache sample")
+                span = request.metadata.get("token_span")
+                if span is not None:
+                    if not isinstance(span, (tuple, list)) or len(span) != 2:
+                        raise ValueError("Physical token_span must be a (start, stop) pair")
+                    start, stop = (int(x) for x in span)
+                    if not 0 <= start < stop <= length:
+                        raise ValueError("Physical token_span is outside its packed sample")
+                    span = (start, stop)
+                mask = request.segment_mask[:length].to(device=device, dtype=torch.bool)
+                type_id = request.metadata.get("token_type_id")
+                self.claims.append(_Claim(sample, offset, request, mask, span,
+                                          type_id=int(type_id) if type_id is not None else -1))
+            offset += length
+        self.device = device
+
+    def _by_sample(self, sample: int) -> list[_Claim]:
+        return [c for c in self.claims if c.sample == sample]
+
+    def check_overlaps(self) -> None:
+        """A token may belong to one request at most: claim counts of every
+        sample are formed on the device and read back once."""
+
+        counts, multi = [], []
+        for sample, length in enumerate(self.lengths):
+            claims = self._by_sample(sample)
+            total = torch.zeros(length, device=self.device, dtype=torch.int32)
+            for claim in claims:
+                total += claim.mask
+            self.occupied.append(total > 0)
+            if len(claims) > 1:
+                counts.append(total.max() if length else torch.zeros((), device=self.device, dtype=torch.int32))
+                multi.append(sample)
+        if counts:
+            peaks = torch.stack(counts).cpu().tolist()
+            for sample, peak in zip(multi, peaks):
+                if peak > 1:
+                    raise ValueError(f"Overlapping physical requests in sample {sample} are not allowed")
+
+    def resolve_indices(self) -> None:
+        """Rows of every segment: a named span is an arange; a mask-defined
+        segment is compacted with ``nonzero_static`` once all counts are known
+        (one read for the batch)."""
+
+        masked = [c for c in self.claims if c.span is None]
+        if masked:
+            sizes = torch.stack([c.mask.sum() for c in masked]).cpu().tolist()
+            for claim, size in zip(masked, sizes):
+                claim.index = torch.nonzero_static(claim.mask, size=int(size)).flatten()
+        for claim in self.claims:
+            if claim.span is not None:
+                claim.index = torch.arange(claim.span[0], claim.span[1], device=self.device, dtype=torch.long)
+
+    def resolve_types(self, key_type_ids: torch.Tensor | None) -> None:
+        """A request without a type id takes its segment's type when every row
+        shares one (min == max over the segment), read once for the batch."""
+
+        pending = [c for c in self.claims if c.type_id < 0 and key_type_ids is not None and c.index.numel()]
+        if not pending:
+            return
+        bounds = []
+        for claim in pending:
+            types = key_type_ids[claim.offset:claim.offset + self.lengths[claim.sample]]
+            picked = types[claim.index.to(types.device)]
+            bounds.append(torch.stack([picked.min(), picked.max()]).to(torch.int64))
+        for claim, (low, high) in zip(pending, torch.stack(bounds).cpu().tolist()):
+            if low == high:
+                claim.type_id = int(low)
+
+    def materialize(self, key: torch.Tensor, value: torch.Tensor) -> list[list[Any]]:
+        out: list[list[Any]] = [[] for _ in self.lengths]
+        for claim in self.claims:
+            rows = int(claim.index.numel())
+            if claim.span is None and rows == 0:
+                continue
+            base = claim.offset
+            if claim.span is not None:
+                dense_key = key[base + claim.span[0]:base + claim.span[1]]
+                dense_value = value[base + claim.span[0]:base + claim.span[1]]
+            else:
+                dense_key = key.index_select(0, claim.index + base)
+                dense_value = value.index_select(0, claim.index + base)
+            request, params = claim.request, claim.request.params
+            if request.operator == "kivi_packed_quantization":
+                bits = int(params.get("bits", 4))
+                segment = PackedKIVICache.from_dense(
+                    dense_key, dense_value, logical_token_ids=claim.index, token_type_id=claim.type_id,
+                    k_bits=int(params.get("k_bits", bits)), v_bits=int(params.get("v_bits", bits)),
+                    group_size=int(params.get("group_size", 64)),
+                    residual_length=int(params.get("residual_length", 32)),
+                    backend=str(params.get("backend", "b200")))
+            elif request.operator == "h2o_physical_gqa":
+                if request.per_kv_head_scores is None:
+                    raise ValueError("Physical H2O request is missing per-KV-head scores")
+                length = self.lengths[claim.sample]
+                scores = request.per_kv_head_scores[:, :length].to(device=key.device, dtype=torch.float32)
+                target, recent = _h2o_budget(params, rows)
+                segment = GQAH2OCache.from_dense(
+                    dense_key, dense_value, logical_token_ids=claim.index, token_type_id=claim.type_id,
+                    per_kv_head_scores=scores.index_select(1, claim.index), target_tokens=target,
+                    recent_tokens=recent, selection_frozen=bool(params.get("selection_frozen", False)))
+            else:
+                raise ValueError(f"Unknown physical cache request: {request.operator}")
+            out[claim.sample].append(segment)
+        return out
