@@ -24,6 +24,9 @@ The same JSON line carries, at every N:
   split over the ranks (strong scaling), each step ending with the exchange of
   every rank's (out, LSE) over NVLink peer memory and the LSE merge (the NCCL
   all-gather variant timed beside it);
+* ``config5``: the Qwen2-7B-shaped decoder (28 layers, random bf16 weights)
+  decoding 32 sequences per GPU over H2O 20% + 2-bit KIVI prompt caches with
+  a growing dense suffix, one CUDA-graph replay per step (weak scaling);
 and at N = 1: ``long_query`` (config 4: the tcgen05 kernel alone and the whole
 ``long_query_attention_summary`` call over the real segment mix), ``config1``
 (the GPU pipeline and its CPU port), ``pack`` and the CPU baseline.
@@ -570,6 +573,86 @@ def config1_leg(run: Run) -> dict:
             "cpu_kind": "port (numpy restatement of the reference algorithm, float64 attention)"}
 
 
+def config5_leg(run: Run) -> dict:
+    """the Qwen2-7B-shaped decoder (random bf16 weights, 28
+    layers) decoding 32 sequences per GPU over a 16384-token prompt cache per
+    layer compressed by H2O to 20% (3277 tokens per KV head) and packed in
+    2-bit KIVI (group 32, 32-token residual), new tokens in a dense bf16
+    suffix.  One step (every layer and the LM head, greedy) is one CUDA-graph
+    replay.  The suffix is pre-filled so that the timed steps sit around the
+    middle of the 512-token decode (its mean length).  Bytes per step: every
+    weight matrix once, every layer's packed prompt and the live suffix."""
+
+    import torch
+
+    from unicache_b200 import kernels
+    from unicache_b200.workloads import Qwen2PackedDecode
+
+    args = run.args
+    steps = min(args.steps, 256)
+    mean_len = 256
+    prefilled = max(0, mean_len - (args.warmup + 1 + steps) // 2)
+    build0 = time.perf_counter()
+    model = Qwen2PackedDecode(run.device, batch=32, prompt=16384, new_tokens=512, prefilled=prefilled,
+                              seed=5 + run.rank)
+    build_s = time.perf_counter() - build0
+    model.step()  # first-call set-up
+    torch.cuda.synchronize()
+    model.capture()
+    for _ in range(args.warmup):
+        model.replay()
+    torch.cuda.synchronize()
+    run.barrier()
+    torch.cuda.synchronize()
+    len0 = int(model.length)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        model.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    run.barrier()
+    elapsed = t0.elapsed_time(t1) / 1000.0
+    # end to end: each step's next-token ids read back to pinned host memory
+    host_ids = torch.empty(model.batch, dtype=torch.int64).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e_steps = min(steps, 512 - int(model.length))
+    e0.record()
+    for _ in range(e_steps):
+        model.replay()
+        host_ids.copy_(model.ids, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = e0.elapsed_time(e1) / 1000.0
+    status = kernels.device_status()
+    elapsed, e2e, status = run.max_over_ranks([elapsed, e2e, float(status)])
+    mean_suffix = len0 + (steps + 1) / 2
+    step_bytes = model.weight_bytes() + model.cache_bytes(int(round(mean_suffix)))
+    step_s = elapsed / steps
+    per_gpu = model.batch * steps / elapsed
+    result = {
+        "workload": "config5: Qwen2-7B-shaped decoder (hidden 3584, 28 layers, 28/4 heads, FFN 18944, vocab "
+                    "151936, random bf16 weights), 32 seqs/GPU, 16384-token prompt per layer -> H2O 20% "
+                    "(3277/KV head) -> KIVI 2-bit G32 (R=32), dense bf16 suffix, greedy decode",
+        "n_gpus": run.world, "scaling": "weak", "global_batch": model.batch * run.world,
+        "value": per_gpu * run.world, "unit": "tokens/s", "tokens_per_s_per_gpu": per_gpu,
+        "ms_per_step": 1000.0 * step_s, "steps": steps, "suffix_tokens_timed": [len0 + 1, len0 + steps],
+        "roofline": dict(hbm_roofline(step_bytes, step_s), algorithmic_bytes_per_step=step_bytes,
+                         weight_bytes=model.weight_bytes()),
+        "e2e": {"value": model.batch * e_steps * run.world / e2e, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": model.batch * 8,
+                "api": "Qwen2PackedDecode.replay + next-token ids copied to pinned host memory per step"},
+        "gpu_launches_ours_per_step": 2 * model.layers,
+        "build_seconds": build_s,
+        "device_status": int(status),
+    }
+    del model
+    torch.cuda.empty_cache()
+    return result
+
+
 # ------------------------------------------------------------------ CPU reference path
 _CPU_CACHES: dict = {}
 
@@ -671,6 +754,7 @@ def run_b200(args) -> None:
                 "value": r3["value"], "unit": "tokens/s", "ms_per_step": r3["ms_per_step"],
                 "roofline": r3["roofline"], "device_status": r3["device_status"]}
     split = split_leg(run)
+    cfg5 = config5_leg(run)
     extra = {}
     if run.world == 1:
         extra["long_query"] = long_query_leg(run)
@@ -702,6 +786,7 @@ def run_b200(args) -> None:
             "device_status": head["device_status"],
             "config3": sub3,
             "config3split": split,
+            "config5": cfg5,
         }
         if pack is not None:
             line["pack"] = dict(pack, from_dense_seconds_per_batch=head["pack_seconds"])

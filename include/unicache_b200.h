@@ -150,7 +150,11 @@ UCB_API int ucb_fake_quant(const void* x_dev, void* out_dev, int dtype, int64_t 
  * nothing needs zeroing.  Calls sharing a workspace must not overlap. */
 typedef struct ucb_span {
   const void* key_code;      /* packed: int32/uint8 codes; dense: key rows    */
-  const void* key_scale;     /* packed only                                   */
+  const void* key_scale;     /* packed: key scales; dense: NULL, or a device
+                                int32 live length (a growing decode suffix:
+                                the decode kernel reads min(tokens, *it)
+                                rows, so one plan sized for the capacity
+                                serves every step)                            */
   const void* key_minimum;   /* packed only                                   */
   const void* value_code;    /* packed: codes; dense: value rows              */
   const void* value_scale;   /* packed only                                   */

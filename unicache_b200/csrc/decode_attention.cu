@@ -145,6 +145,17 @@ __device__ __forceinline__ bool softmax_update(float (&lg)[NTILE][4], float scal
 __device__ __forceinline__ uint2 lds64(const unsigned char* p) { return *reinterpret_cast<const uint2*>(p); }
 __device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// Tokens of a span this launch reads: a dense span whose key_scale field
+// points at a device int32 (a growing decode suffix) holds min(tokens, that
+// value) live tokens; every other span holds `tokens`.  The planner sizes a
+// growing span for its capacity, so one plan (and one captured graph) serves
+// every step while the suffix grows.
+__device__ __forceinline__ int live_tokens(const ucb_span& sp) {
+  if (sp.kind == 1 && sp.key_scale != nullptr)
+    return max(0, min(sp.tokens, *static_cast<const volatile int32_t*>(sp.key_scale)));
+  return sp.tokens;
+}
+
 struct Params {
   const __nv_bfloat16* query;
   int64_t query_stride;
@@ -200,7 +211,7 @@ struct Kernel {
 
   __device__ static void issue_dense(const ucb_span& sp, int t0, int t1, unsigned char* slot, uint64_t* bar,
                                      int lane) {
-    const int n = t1 - t0;
+    const int n = max(0, t1 - t0);  // a growing span's unit past its live length copies nothing
     if (lane == 0) {
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(bar, 2u * n * D * 2u);
@@ -597,7 +608,7 @@ struct Kernel {
       const ucb_span& sp = spans[issue_span];
       const int stage = sp.kind == 0 ? NT : DT;
       const int t0 = (issue_u - sp.unit_begin) * stage;
-      const int t1 = min(sp.tokens, t0 + stage);
+      const int t1 = min(live_tokens(sp), t0 + stage);
       unsigned char* slot = ring + slot_idx * C::SLOT;
       if (sp.kind == 0)
         issue_packed(sp, t0, t1, slot, &bars[slot_idx], lane);
@@ -666,13 +677,13 @@ struct Kernel {
       unsigned char* slot = ring + slot_idx * C::SLOT;
       const int stage = kind == 0 ? NT : DT;
       const int t0 = (u - sp.unit_begin) * stage;
-      const int n = min(sp.tokens, t0 + stage) - t0;
+      const int n = min(live_tokens(sp), t0 + stage) - t0;
       if (kind == 0) {
         if (n == NT)
           packed_stage<true>(slot, n, lane, qbp, P.scale_log2, st, o, accm);
         else
           packed_stage<false>(slot, n, lane, qbp, P.scale_log2, st, o, accm);
-      } else {
+      } else if (n > 0) {
         dense_stage(slot, n, lane, qs + pl * 8 * D * 2, zero_row, P.scale_log2, st, o);
       }
       __syncwarp();

@@ -317,7 +317,9 @@ SEGMENT_SWITCH_STAGES = 0.4
 
 @dataclass
 class DenseRows:
-    """A dense bf16 K/V span for one KV head: row i at base + i*stride."""
+    """A dense bf16 K/V span for one KV head: row i at base + i*stride.  With
+    ``live`` (a device int32 scalar) the span is a growing suffix of capacity
+    ``tokens`` whose first ``live`` rows are read."""
 
     key: torch.Tensor
     value: torch.Tensor
@@ -326,6 +328,7 @@ class DenseRows:
     key_stride: int
     value_stride: int
     tokens: int
+    live: torch.Tensor | None = None
 
 
 @dataclass
@@ -430,6 +433,10 @@ def _dense_span(rows: DenseRows) -> UcbSpan:
     sp.value_stride = rows.value_stride
     sp.kind = 1
     sp.tokens = rows.tokens
+    if rows.live is not None:
+        if not rows.live.is_cuda or rows.live.dtype != torch.int32 or rows.live.numel() != 1:
+            raise ValueError("a growing span's live length must be a CUDA int32 scalar")
+        sp.key_scale = rows.live.data_ptr()
     for name, base, off, stride in (("key", rows.key, rows.key_offset, rows.key_stride),
                                     ("value", rows.value, rows.value_offset, rows.value_stride)):
         if base.dtype != torch.bfloat16:
@@ -441,11 +448,25 @@ def _dense_span(rows: DenseRows) -> UcbSpan:
     return sp
 
 
-def dense_rows_token_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
-    """[N, H, D] tensors (dense cache, KIVI residual)."""
+def dense_rows_token_major(key: torch.Tensor, value: torch.Tensor, head: int,
+                           live: torch.Tensor | None = None) -> DenseRows:
+    """[N, H, D] tensors (dense cache, KIVI residual, or a growing suffix of
+    capacity N whose live length is the device scalar ``live``)."""
 
     return DenseRows(key, value, head * key.stride(1), head * value.stride(1), key.stride(0), value.stride(0),
-                     int(key.shape[0]))
+                     int(key.shape[0]), live)
+
+
+@dataclass
+class GrowingSuffix:
+    """Dense bf16 rows appended one decode step at a time: key/value
+    [capacity, H, D] and the device int32 ``length``; a decode plan reads the
+    first ``length`` rows (the reference appends decode tokens to its dense
+    cache, unicache/adapters/bagel.py:1199-1297)."""
+
+    key: torch.Tensor
+    value: torch.Tensor
+    length: torch.Tensor
 
 
 def dense_rows_head_major(key: torch.Tensor, value: torch.Tensor, head: int) -> DenseRows:
@@ -581,6 +602,12 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
                 elif isinstance(seg, GQAH2OCache):
                     rows = dense_rows_head_major(seg.key, seg.value, h)
                     add(_dense_span(rows), pair, rows.tokens * head_dim * 4)
+                    keepalive.append(seg)
+                    device = seg.key.device
+                elif isinstance(seg, GrowingSuffix):
+                    rows = dense_rows_token_major(seg.key, seg.value, h, seg.length)
+                    # weighted at half its capacity: its average fill over a decode run
+                    add(_dense_span(rows), pair, rows.tokens * head_dim * 4 * 0.5)
                     keepalive.append(seg)
                     device = seg.key.device
                 else:
