@@ -83,3 +83,27 @@ def test_append_rejects_mismatched_tokens():
         cache.append(key[64:70, :2], value[64:70, :2], logical_token_ids=torch.arange(6, device="cuda"))
     with pytest.raises(ValueError):
         cache.append(key[64:70], value[64:70], logical_token_ids=torch.arange(5, device="cuda"))
+
+
+def test_flushes_write_in_place_and_dequantize_exactly():
+    """Flushed groups land in capacity stores: between two store growths the
+    packed tensors keep their addresses (no whole-cache copy per flush), and
+    the appended cache dequantizes bit-identically to the rebuilt one."""
+
+    need_gpu()
+    key, value = make_kv(3000, 4, 128, seed=8, device="cuda")
+    cache = _from_dense(key, value, 256, 2, 2, 32, 32)
+    cache.append(key[256:300], value[256:300], logical_token_ids=torch.arange(256, 300, device="cuda"))
+    addresses, moves = cache.key_code.data_ptr(), 0
+    for t in range(300, 3000, 9):
+        cache.append(key[t:t + 9], value[t:t + 9], logical_token_ids=torch.arange(t, t + 9, device="cuda"))
+        if cache.key_code.data_ptr() != addresses:
+            moves += 1
+            addresses = cache.key_code.data_ptr()
+    assert cache.quantized_tokens == 2944 and moves <= 4, moves
+    rebuilt = _from_dense(key, value, 3000, 2, 2, 32, 32)
+    _assert_same(cache, rebuilt)
+    ka, va = cache.dequantize(dtype=torch.bfloat16)
+    kb, vb = rebuilt.dequantize(dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(ka, kb) and torch.equal(va, vb)

@@ -182,8 +182,11 @@ class PackedKIVICache:
         leaves it is quantized and packed on the GPU and appended to the packed
         tensors, oldest first, so the cache stays equal, bit for bit, to
         ``from_dense`` over the whole sequence with the same residual length.
-        Returns the number of tokens packed.  Decode plans built on this cache
-        must be rebuilt (its tensors move)."""
+        Returns the number of tokens packed.  Flushed groups are written in
+        place into capacity stores that double when full (the packed tensors
+        are views of them), so a flush moves only the new groups.  Decode
+        plans built on this cache must be rebuilt after an append (token
+        counts change; the cache drops the plans it cached itself)."""
 
         if key.shape != value.shape or key.dim() != 3 or tuple(key.shape[1:]) != (self.num_kv_heads, self.head_dim):
             raise ValueError("appended key/value must be [tokens, kv_heads, head_dim] matching the cache")
@@ -197,25 +200,68 @@ class PackedKIVICache:
         total = self.token_count + n
         target = max(0, (total - self.residual_length) // self.group_size * self.group_size)
         flush = target - self.quantized_tokens
+        # the residual window holds fewer than residual_length + group_size rows: small copies
         res_key = torch.cat([self.residual_key, key], dim=0)
         res_value = torch.cat([self.residual_value, value], dim=0)
         if flush > 0:
             new = kernels.kivi_pack_kv(res_key[:flush].contiguous(), res_value[:flush].contiguous(),
                                        k_bits=self.k_bits, v_bits=self.v_bits, group_size=self.group_size)
-            names = ("key_code", "key_scale", "key_minimum", "value_code", "value_scale", "value_minimum")
-            for name, tensor in zip(names, new):
-                old = getattr(self, name)
-                # b200 layout: tokens (or token groups, or packed words) run along dim 1
-                setattr(self, name, tensor if old is None else torch.cat([old, tensor], dim=1))
+            self._write_packed(new, self.quantized_tokens, target)
             self.quantized_tokens = target
             res_key = res_key[flush:].clone()
             res_value = res_value[flush:].clone()
         self.residual_key, self.residual_value = res_key, res_value
-        self.logical_token_ids = torch.cat(
-            [self.logical_token_ids, logical_token_ids.to(self.logical_token_ids.device,
-                                                          self.logical_token_ids.dtype)])
+        self._append_ids(logical_token_ids.to(self.logical_token_ids.device, self.logical_token_ids.dtype))
         self.__dict__.pop("_decode_plans", None)
         return max(0, flush)
+
+    _PACKED = ("key_code", "key_scale", "key_minimum", "value_code", "value_scale", "value_minimum")
+
+    def _units(self, name: str, tokens: int) -> int:
+        """Length along dim 1 (b200 layout) of ``name`` holding ``tokens`` tokens."""
+
+        if name == "key_code":
+            return tokens if self.k_bits == 8 else tokens // (32 // self.k_bits)
+        if name in ("key_scale", "key_minimum"):
+            return tokens // self.group_size
+        return tokens  # value codes and statistics run per token
+
+    def _write_packed(self, new: tuple, start: int, stop: int) -> None:
+        """Store freshly packed tokens [start, stop) in place.  The packed
+        tensors are views of capacity stores that grow geometrically, so a
+        flush copies only the new groups (and, rarely, the store once when it
+        doubles) instead of concatenating the whole cache."""
+
+        store = self.__dict__.get("_store")
+        capacity = self.__dict__.get("_capacity", 0)
+        if store is None or stop > capacity:
+            grown = max(stop, 2 * capacity, 4 * self.group_size)
+            grown = -(-grown // self.group_size) * self.group_size
+            fresh = {}
+            for name, tensor in zip(self._PACKED, new):
+                shape = list(tensor.shape)
+                shape[1] = self._units(name, grown)
+                fresh[name] = torch.empty(shape, device=tensor.device, dtype=tensor.dtype)
+                old = getattr(self, name)
+                if old is not None and start:
+                    fresh[name][:, :self._units(name, start)].copy_(old)
+            self.__dict__["_store"], self.__dict__["_capacity"] = fresh, grown
+            store = fresh
+        for name, tensor in zip(self._PACKED, new):
+            a, b = self._units(name, start), self._units(name, stop)
+            store[name][:, a:b].copy_(tensor)
+            setattr(self, name, store[name][:, :b])
+
+    def _append_ids(self, ids: torch.Tensor) -> None:
+        store = self.__dict__.get("_id_store")
+        used = int(self.logical_token_ids.numel())
+        need = used + int(ids.numel())
+        if store is None or need > int(store.numel()):
+            grown = torch.empty(max(need, 2 * used, 64), device=ids.device, dtype=self.logical_token_ids.dtype)
+            grown[:used].copy_(self.logical_token_ids)
+            self.__dict__["_id_store"] = store = grown
+        store[used:need].copy_(ids)
+        self.logical_token_ids = store[:need]
 
     def to_host(self):
         """A contiguous host replica of this cache (``storage.hierarchy``)."""
@@ -268,7 +314,13 @@ class PackedKIVICache:
                          output_value: torch.Tensor) -> None:
         """Write quantized tokens [start, stop) into the given [N, H, D] views."""
 
-        common = dict(bits=0, group_size=self.group_size, quantized_tokens=self.quantized_tokens,
+        # appended caches keep their packed tensors in capacity stores: the
+        # per-head extent the kernels step over is the store's capacity
+        extent = self.__dict__.get("_capacity", self.quantized_tokens) if "_store" in self.__dict__ \
+            else self.quantized_tokens
+        if not 0 <= start <= stop <= self.quantized_tokens:
+            raise ValueError("dequantize range outside the quantized tokens")
+        common = dict(bits=0, group_size=self.group_size, quantized_tokens=extent,
                       heads=self.num_kv_heads, head_dim=self.head_dim, start=start, stop=stop)
         common["bits"] = self.k_bits
         kernels.kivi_dequant("key", self.key_code, self.key_scale, self.key_minimum, out=output_key, **common)
