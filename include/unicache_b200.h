@@ -401,6 +401,34 @@ UCB_API int ucb_h2o_accumulate_probs(const void* probs_dev, int dtype, int q_hea
                              int64_t tokens, int kv_heads, float* scores_dev, int accumulate,
                              void* stream);
 
+/* A packed segment's generic attention parts (kivi_cuda.py:238-329 /
+ * physical.py:452-475 of the reference): the caller materialises the softmax.
+ * Tokens are the segment's quantized prefix followed by its residual rows.
+ * Packed tensors of one KV head start at codes + kv*codes_head_stride
+ * (elements of the code dtype: int32 words, uint8 at 8 bits) and
+ * stats + kv*stats_head_stride (bf16 statistics); residual row t of head kv
+ * is at residual + t*res_token_stride + kv*res_head_stride (bf16, 16-byte
+ * aligned rows).  Codes are restored as the reference's dequantize() does
+ * (code * scale + minimum in fp32, one rounding to bf16).
+ *   logits: query bf16 [queries, q_heads, 128] -> logits fp32
+ *           [q_heads, queries, quantized + residual], scaled by softmax_scale.
+ *   apply:  probs [q_heads, queries, quantized + residual] (bf16, f16 or f32;
+ *           rounded to bf16 as the reference casts them to the value dtype)
+ *           -> out bf16 [q_heads, queries, 128]. */
+UCB_API int ucb_kivi_attention_logits(const void* query_dev, int64_t queries, int q_heads, int kv_heads,
+                                      const void* key_code_dev, const void* key_scale_dev,
+                                      const void* key_minimum_dev, int64_t codes_head_stride,
+                                      int64_t stats_head_stride, const void* residual_key_dev,
+                                      int64_t res_token_stride, int64_t res_head_stride, int64_t quantized_tokens,
+                                      int64_t residual_tokens, int bits, int group_size, float softmax_scale,
+                                      float* logits_dev, void* stream);
+UCB_API int ucb_kivi_attention_apply(const void* probs_dev, int probs_dtype, int64_t queries, int q_heads,
+                                     int kv_heads, const void* value_code_dev, const void* value_scale_dev,
+                                     const void* value_minimum_dev, int64_t codes_head_stride,
+                                     int64_t stats_head_stride, const void* residual_value_dev,
+                                     int64_t res_token_stride, int64_t res_head_stride, int64_t quantized_tokens,
+                                     int64_t residual_tokens, int bits, int group_size, void* out_dev, void* stream);
+
 /* Fused H2O scoring without materialised probabilities (adapters/bagel.py:1845-1856):
  * scores[kv, t] (+)= sum_{g, q} exp(scale * q_{kv*G+g, q} . k_t - lse[kv*G+g, q]).
  * query_dev bf16 [queries, q_heads, head_dim]; key rows bf16, row (t, kv) at

@@ -125,6 +125,12 @@ SIGNATURES = {
                                          c_void_p]),
     "ucb_h2o_scores_from_lse": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int,
                                         c_int, c_void_p, c_float, c_void_p, c_int, c_void_p]),
+    "ucb_kivi_attention_logits": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                                          c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                          c_float, c_void_p, c_void_p]),
+    "ucb_kivi_attention_apply": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                         c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                         c_void_p, c_void_p]),
     "ucb_h2o_scores": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p]),
     "ucb_compact_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,

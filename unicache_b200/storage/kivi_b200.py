@@ -15,7 +15,6 @@ from typing import TYPE_CHECKING, Callable
 import torch
 
 from .. import kernels
-from .physical import gqa_probability_value, gqa_query_key_logits
 
 if TYPE_CHECKING:
     from .physical import PackedKIVICache
@@ -129,17 +128,46 @@ def packed_kivi_attention_parts(
 ) -> tuple[torch.Tensor, Callable[[torch.Tensor], torch.Tensor]]:
     """kivi_cuda.py:238-329: logits [Hq, Lq, T+R] (fp32, scaled by 1/sqrt(D))
     and an AV closure.  This is the generic path used when probabilities must
-    be materialised; it restores the segment once with the bit-exact dequant
-    kernel and contracts with the library GEMM.  Fused paths never call it."""
+    be materialised.  Both halves run on this library's kernels, restoring
+    the codes tile by tile in shared memory (no dequantized copy of the
+    segment, no library GEMM).  Fused paths never call it."""
 
     kernels.require_cuda(query, "query")
+    if query.dim() != 3 or int(query.shape[-1]) != cache.head_dim or cache.head_dim != 128:
+        raise ValueError("query must be [queries, q_heads, 128]")
     repeat = int(query.shape[1]) // cache.num_kv_heads
     if repeat * cache.num_kv_heads != int(query.shape[1]):
         raise ValueError("Query heads must be divisible by KIVI KV heads")
-    key, value = cache.dequantize(dtype=query.dtype)
-    logits = gqa_query_key_logits(query, key) / math.sqrt(query.shape[-1])
+    if query.dtype != torch.bfloat16 or cache.residual_key.dtype != torch.bfloat16:
+        raise ValueError("the b200 attention parts take a bfloat16 query and cache")
+    if cache.quantized_tokens and cache.key_scale.dtype != torch.bfloat16:
+        raise ValueError("the b200 attention parts read bfloat16 statistics")
+    q = query.contiguous()
+    lq, hq = int(q.shape[0]), int(q.shape[1])
+    total = cache.quantized_tokens + int(cache.residual_key.shape[0])
+    packed = cache.quantized_tokens > 0
+    rk, rv = cache.residual_key, cache.residual_value
+    logits = torch.empty((hq, lq, total), device=q.device, dtype=torch.float32)
+    kernels.call("ucb_kivi_attention_logits", q.data_ptr(), lq, hq, cache.num_kv_heads,
+                 cache.key_code.data_ptr() if packed else None, cache.key_scale.data_ptr() if packed else None,
+                 cache.key_minimum.data_ptr() if packed else None, cache.key_code.stride(0) if packed else 0,
+                 cache.key_scale.stride(0) if packed else 0, rk.data_ptr() if rk.numel() else None,
+                 rk.stride(0), rk.stride(1), cache.quantized_tokens, int(rk.shape[0]), cache.k_bits,
+                 cache.group_size, 1.0 / math.sqrt(cache.head_dim), logits.data_ptr(), kernels.stream_of(q))
 
     def apply_value(probabilities: torch.Tensor) -> torch.Tensor:
-        return gqa_probability_value(probabilities, value)
+        kernels.require_cuda(probabilities, "probabilities")
+        if tuple(probabilities.shape) != (hq, lq, total):
+            raise ValueError("GQA AV probability key width must match value tokens")
+        p = probabilities.contiguous()
+        out = torch.empty((hq, lq, cache.head_dim), device=p.device, dtype=torch.bfloat16)
+        kernels.call("ucb_kivi_attention_apply", p.data_ptr(), kernels.dtype_code(p.dtype), lq, hq,
+                     cache.num_kv_heads, cache.value_code.data_ptr() if packed else None,
+                     cache.value_scale.data_ptr() if packed else None,
+                     cache.value_minimum.data_ptr() if packed else None,
+                     cache.value_code.stride(0) if packed else 0, cache.value_scale.stride(0) if packed else 0,
+                     rv.data_ptr() if rv.numel() else None, rv.stride(0), rv.stride(1), cache.quantized_tokens,
+                     int(rv.shape[0]), cache.v_bits, cache.group_size, out.data_ptr(), kernels.stream_of(p))
+        return out
 
     return logits, apply_value
