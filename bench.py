@@ -448,28 +448,25 @@ def split_leg(run: Run) -> dict:
 
 # ------------------------------------------------------------------ N = 1 legs
 def pack_leg(run: Run, wl: Workload, dense_kv) -> dict:
-    """Quantize + pack of the sequences' quantized tokens, one fused key+value
-    launch per sequence, captured in a CUDA graph.  Algorithmic bytes = bf16 K
-    and V read + codes and statistics written."""
+    """Quantize + pack of the batch's quantized tokens: every sequence's key
+    and value halves in ONE launch over a device job table
+    (``KiviPackBatch``, what ``PackedKIVICache.from_dense_batch`` runs),
+    captured in a CUDA graph.  Algorithmic bytes = bf16 K and V read + codes
+    and statistics written."""
 
     from unicache_b200 import kernels
 
-    keys = [k[:wl.tokens] for k, _ in dense_kv]
-    vals = [v[:wl.tokens] for _, v in dense_kv]
-
-    def step(_i):
-        for k, v in zip(keys, vals):
-            kernels.kivi_pack_kv(k, v, k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group)
-
-    step(0)
+    pairs = [(k[:wl.tokens], v[:wl.tokens]) for k, v in dense_kv]
+    batch = kernels.KiviPackBatch(pairs, k_bits=wl.bits, v_bits=wl.bits, group_size=wl.group)
+    batch.run()
     reps = 5
-    elapsed, _ = run.graph_seconds(step, reps)
-    seconds = elapsed / reps / len(keys)
+    elapsed, _ = run.graph_seconds(lambda _i: batch.run(), reps)
+    seconds = elapsed / reps / len(pairs)
     per_seq = (2 * wl.tokens * KV_HEADS * HEAD_DIM * 2
                + 2 * wl.tokens * KV_HEADS * HEAD_DIM * wl.bits // 8
                + 2 * 2 * wl.tokens * KV_HEADS * HEAD_DIM // wl.group * 2)
     return {"us_per_sequence": seconds * 1e6, "algorithmic_bytes_per_sequence": per_seq,
-            "roofline": hbm_roofline(per_seq, seconds)}
+            "sequences_per_launch": len(pairs) if batch.fused else 1, "roofline": hbm_roofline(per_seq, seconds)}
 
 
 def long_query_leg(run: Run) -> dict:

@@ -91,6 +91,22 @@ UCB_API int ucb_kivi_pack_kv(const void* key_dev, const void* value_dev, int dty
                              int group_size, void* key_codes_dev, void* key_scale_dev, void* key_minimum_dev,
                              void* value_codes_dev, void* value_scale_dev, void* value_minimum_dev, void* stream);
 
+/* Batched ucb_kivi_pack_kv: one launch packs every job of a device table of
+ * ucb_kivi_pack_job_bytes() bytes each (no counterpart in the reference,
+ * which packs one segment per call).  A job is, in order: the key side
+ * {input, token stride, head stride (int64, elements), codes, scale, minimum}
+ * and the value side in the same form, then int32 tokens, key_blocks =
+ * ceil(tokens/32 * heads / 4), blocks = key_blocks + ceil(tokens * heads *
+ * 128/32 / 256), and one int32 of padding.  Every job satisfies the
+ * conditions of ucb_kivi_pack_kv (bf16, head_dim 128, group 32, tokens a
+ * multiple of 32, 16-byte-aligned value rows) with the same bits and heads;
+ * max_blocks is the largest job's `blocks`.  Validation of the table's
+ * contents is the caller's (the Python wrapper builds it from checked
+ * tensors). */
+UCB_API int64_t ucb_kivi_pack_job_bytes(void);
+UCB_API int ucb_kivi_pack_kv_batched(const void* jobs_dev, int num_jobs, int max_blocks, int64_t heads, int k_bits,
+                                     int v_bits, int group_size, void* stream);
+
 /* ------------------------------------------------------------------ KIVI dequantize
  * Replaces PackedKIVICache.dequantize (physical.py:379-423 -> _dequantize_grouped
  * :178-201) and dequantize_kivi_chunk (unicache/storage/kivi_cuda.py:58-93 ->

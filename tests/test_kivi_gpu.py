@@ -262,3 +262,29 @@ def test_fused_pack_other_groups_use_the_separate_kernels():
                     *kernels.kivi_pack_value(value, bits=2, group_size=g))
         for a, b in zip(fused, separate):
             assert torch.equal(a, b)
+
+
+def test_from_dense_batch_equals_per_segment_packing():
+    """One pack launch for a batch of segments (ragged lengths, one with no
+    quantized tokens) gives the tensors from_dense gives segment by segment,
+    bit for bit; a group-64 batch takes the per-segment fallback."""
+
+    need_gpu()
+    from unicache_b200 import PackedKIVICache
+
+    lengths = [1000, 64, 2080, 20, 513]
+    kv = [make_kv(n, 4, 128, seed=200 + i, device="cuda") for i, n in enumerate(lengths)]
+    for kb, vb, group in ((2, 2, 32), (4, 2, 32), (2, 4, 64)):
+        batch = PackedKIVICache.from_dense_batch(
+            [k for k, _ in kv], [v for _, v in kv], logical_token_ids=[torch.arange(n, device="cuda") for n in lengths],
+            token_type_id=3, k_bits=kb, v_bits=vb, group_size=group, residual_length=32)
+        for (k, v), n, got in zip(kv, lengths, batch):
+            want = PackedKIVICache.from_dense(k, v, logical_token_ids=torch.arange(n, device="cuda"), token_type_id=3,
+                                              k_bits=kb, v_bits=vb, group_size=group, residual_length=32)
+            assert got.quantized_tokens == want.quantized_tokens
+            for name in ("key_code", "key_scale", "key_minimum", "value_code", "value_scale", "value_minimum",
+                         "residual_key", "residual_value"):
+                a, b = getattr(got, name), getattr(want, name)
+                assert (a is None) == (b is None), name
+                if a is not None:
+                    assert torch.equal(a, b), (kb, vb, group, n, name)

@@ -52,6 +52,16 @@ class UcbSpan(ctypes.Structure):
     ]
 
 
+class UcbPackSide(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("stride_t", c_int64), ("stride_h", c_int64), ("codes", c_void_p),
+                ("scale", c_void_p), ("minimum", c_void_p)]
+
+
+class UcbPackJob(ctypes.Structure):
+    _fields_ = [("k", UcbPackSide), ("v", UcbPackSide), ("tokens", ctypes.c_int32), ("key_blocks", ctypes.c_int32),
+                ("blocks", ctypes.c_int32), ("pad", ctypes.c_int32)]
+
+
 class UcbDecodeCta(ctypes.Structure):
     _fields_ = [
         ("unit_begin", ctypes.c_int32),
@@ -86,6 +96,8 @@ SIGNATURES = {
     "ucb_kivi_pack_kv": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                                  c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p]),
+    "ucb_kivi_pack_job_bytes": (c_int64, []),
+    "ucb_kivi_pack_kv_batched": (c_int, [c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int, c_void_p]),
     "ucb_kivi_dequant_key": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_int,
                                      c_int64, c_int64, c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "ucb_kivi_dequant_value": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int,

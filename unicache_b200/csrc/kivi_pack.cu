@@ -262,6 +262,38 @@ __global__ void __launch_bounds__(256, 2) pack_kv_kernel(PackSide k, PackSide v,
   }
 }
 
+// Many segments in one launch: blockIdx.y picks a job (one segment's key and
+// value sides and its token count), blockIdx.x runs the fused kernel's block
+// index inside that job; blocks past a shorter job's end exit.  One launch
+// (and one memory ramp) packs a whole batch of sequences.
+struct PackJob {
+  PackSide k, v;
+  int tokens, key_blocks, blocks, pad;
+};
+
+template <int KB, int VB, int G>
+__global__ void __launch_bounds__(256, 2) pack_kv_batched_kernel(const PackJob* __restrict__ jobs, int heads) {
+  using T = __nv_bfloat16;
+  constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
+  const PackJob& j = jobs[blockIdx.y];
+  const int b = static_cast<int>(blockIdx.x);
+  if (b >= j.blocks) return;
+  if (b < j.key_blocks) {
+    const int groups = j.tokens / G;
+    const int item = b * ITEMS + threadIdx.x / PAIRS;
+    if (item >= groups * heads) return;
+    pack_key_item<T, KB, G>(static_cast<const T*>(j.k.x), j.k.stride_t, j.k.stride_h, j.tokens, D,
+                            static_cast<uint32_t*>(j.k.codes), static_cast<uint8_t*>(j.k.codes),
+                            static_cast<T*>(j.k.scale), static_cast<T*>(j.k.minimum), item % groups, item / groups,
+                            threadIdx.x % PAIRS);
+  } else {
+    const int64_t item = static_cast<int64_t>(b - j.key_blocks) * 256 + threadIdx.x;
+    pack_value_item<T, VB, D, G, true>(static_cast<const T*>(j.v.x), j.v.stride_t, j.v.stride_h, j.tokens, heads,
+                                       static_cast<uint32_t*>(j.v.codes), static_cast<uint8_t*>(j.v.codes),
+                                       static_cast<T*>(j.v.scale), static_cast<T*>(j.v.minimum), item);
+  }
+}
+
 // ---------------------------------------------------------------- dequantize
 __device__ __forceinline__ float dequant(uint32_t code, float s, float m) {
   return __fadd_rn(__fmul_rn(static_cast<float>(code), s), m);
@@ -648,4 +680,27 @@ extern "C" int ucb_fake_quant(const void* x, void* out, int dtype, int64_t outer
       return set_error(UCB_ERR_INVALID, "ucb_fake_quant: dtype %d unsupported", dtype);
   }
   return check_launch("fake_quant_kernel");
+}
+
+extern "C" int64_t ucb_kivi_pack_job_bytes(void) { return (int64_t)sizeof(ucb::PackJob); }
+
+extern "C" int ucb_kivi_pack_kv_batched(const void* jobs, int num_jobs, int max_blocks, int64_t heads, int k_bits,
+                                        int v_bits, int group_size, void* stream) {
+  if (!jobs || num_jobs <= 0 || num_jobs > 65535 || max_blocks <= 0)
+    return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv_batched: bad job table");
+  if (group_size != 32 || heads <= 0)
+    return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_kv_batched: group 32 only");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(max_blocks), static_cast<unsigned>(num_jobs));
+  const auto* j = static_cast<const ucb::PackJob*>(jobs);
+#define UCB_PACK_KVB(KB_, VB_)                                                                       \
+  if (k_bits == KB_ && v_bits == VB_) {                                                              \
+    ucb::pack_kv_batched_kernel<KB_, VB_, 32><<<grid, 256, 0, s>>>(j, (int)heads);                   \
+    return check_launch("pack_kv_batched_kernel");                                                   \
+  }
+  UCB_PACK_KVB(2, 2) UCB_PACK_KVB(2, 4) UCB_PACK_KVB(2, 8)
+  UCB_PACK_KVB(4, 2) UCB_PACK_KVB(4, 4) UCB_PACK_KVB(4, 8)
+  UCB_PACK_KVB(8, 2) UCB_PACK_KVB(8, 4) UCB_PACK_KVB(8, 8)
+#undef UCB_PACK_KVB
+  return set_error(UCB_ERR_UNSUPPORTED, "ucb_kivi_pack_kv_batched: unsupported bits %d/%d", k_bits, v_bits);
 }

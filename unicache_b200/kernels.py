@@ -124,6 +124,77 @@ def kivi_pack_kv(key: torch.Tensor, value: torch.Tensor, *, k_bits: int, v_bits:
     return kc, ks, km, vc, vs, vm
 
 
+class KiviPackBatch:
+    """``kivi_pack_kv`` of several segments (key, value [T_i, H, 128] bf16
+    pairs, the same H) as one launch over a device job table.  The outputs
+    and the table are allocated when the batch is built, so ``run`` is a
+    single launch that a CUDA graph can capture; ``outputs`` holds one 6-tuple
+    of b200-layout tensors per pair.  Pairs the fused kernel does not take
+    (group other than 32, unaligned value rows) fall back to one
+    ``kivi_pack_kv`` call each inside ``run``."""
+
+    def __init__(self, pairs: list, *, k_bits: int, v_bits: int, group_size: int):
+        if not pairs:
+            raise ValueError("a pack batch needs at least one segment")
+        self.pairs, self.k_bits, self.v_bits, self.group_size = pairs, k_bits, v_bits, group_size
+        self.fused = group_size == 32 and all(
+            k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16 and k.shape == v.shape and k.dim() == 3
+            and int(k.shape[2]) == 128 and k.stride(2) == 1 and v.stride(2) == 1 and int(k.shape[0]) > 0
+            and int(k.shape[0]) % 32 == 0 and v.data_ptr() % 16 == 0 and v.stride(0) % 8 == 0
+            and v.stride(1) % 8 == 0 and k.is_cuda and k.device == pairs[0][0].device
+            and int(k.shape[1]) == int(pairs[0][0].shape[1]) for k, v in pairs)
+        self.outputs: list = []
+        if not self.fused:
+            return
+        heads = int(pairs[0][0].shape[1])
+        dev = pairs[0][0].device
+        jobs, max_blocks = [], 0
+        for key, value in pairs:
+            tokens = int(key.shape[0])
+            kc = (torch.empty((heads, tokens, 128), device=dev, dtype=torch.uint8) if k_bits == 8 else
+                  torch.empty((heads, tokens // codes_per_word(k_bits), 128), device=dev, dtype=torch.int32))
+            vc = (torch.empty((heads, tokens, 128), device=dev, dtype=torch.uint8) if v_bits == 8 else
+                  torch.empty((heads, tokens, 128 // codes_per_word(v_bits)), device=dev, dtype=torch.int32))
+            ks = torch.empty((heads, tokens // 32, 128), device=dev, dtype=torch.bfloat16)
+            km = torch.empty_like(ks)
+            vs = torch.empty((heads, tokens, 4), device=dev, dtype=torch.bfloat16)
+            vm = torch.empty_like(vs)
+            job = _capi.UcbPackJob()
+            job.k = _capi.UcbPackSide(key.data_ptr(), key.stride(0), key.stride(1), kc.data_ptr(), ks.data_ptr(),
+                                      km.data_ptr())
+            job.v = _capi.UcbPackSide(value.data_ptr(), value.stride(0), value.stride(1), vc.data_ptr(),
+                                      vs.data_ptr(), vm.data_ptr())
+            job.tokens = tokens
+            job.key_blocks = -(-(tokens // 32) * heads // 4)
+            job.blocks = job.key_blocks + -(-tokens * heads * 4 // 256)
+            max_blocks = max(max_blocks, job.blocks)
+            jobs.append(job)
+            self.outputs.append((kc, ks, km, vc, vs, vm))
+        if int(_capi.load().ucb_kivi_pack_job_bytes()) != ctypes.sizeof(_capi.UcbPackJob):
+            raise RuntimeError("pack job layout mismatch between the library and its binding")
+        self.table = torch.frombuffer(bytearray(_capi.struct_array_bytes(jobs)), dtype=torch.uint8).to(dev)
+        self.heads, self.max_blocks, self.jobs = heads, max_blocks, len(jobs)
+
+    def run(self) -> list:
+        if not self.fused:
+            self.outputs = [kivi_pack_kv(k, v, k_bits=self.k_bits, v_bits=self.v_bits, group_size=self.group_size)
+                            for k, v in self.pairs]
+            return self.outputs
+        call("ucb_kivi_pack_kv_batched", self.table.data_ptr(), self.jobs, self.max_blocks, self.heads, self.k_bits,
+             self.v_bits, self.group_size, stream_of(self.pairs[0][0]))
+        return self.outputs
+
+
+def kivi_pack_kv_batch(pairs: list, *, k_bits: int, v_bits: int, group_size: int) -> list:
+    """One-shot ``KiviPackBatch``: the packed 6-tuples of every (key, value) pair."""
+
+    batch = KiviPackBatch(pairs, k_bits=k_bits, v_bits=v_bits, group_size=group_size)
+    out = batch.run()
+    for t in out:  # the job table must outlive the launch on its stream
+        t[0].__dict__.setdefault("_ucb_pack_batch", batch)
+    return out
+
+
 def kivi_dequant(which: str, codes, scale, minimum, *, bits: int, group_size: int, quantized_tokens: int,
                  heads: int, head_dim: int, start: int, stop: int, out: torch.Tensor) -> torch.Tensor:
     """Dequantize tokens [start, stop) into ``out`` rows [0, stop-start) ([N, H, D] view)."""

@@ -118,6 +118,7 @@ class PackedKIVICache:
         group_size: int,
         residual_length: int,
         backend: str = "b200",
+        _packed=None,
     ) -> "PackedKIVICache":
         """physical.py:228-332: split ``((T - R) // G) * G`` quantized tokens
         from a full-precision suffix and pack them on the GPU."""
@@ -138,6 +139,7 @@ class PackedKIVICache:
             raise ValueError("The b200 KIVI kernels require head_dim 64/128 divisible by group_size")
         requested_residual = min(tokens, max(0, int(residual_length)))
         quantized = ((tokens - requested_residual) // group_size) * group_size
+        packed = None
         if quantized:
             q_key = key[:quantized]
             q_value = value[:quantized]
@@ -145,13 +147,50 @@ class PackedKIVICache:
                 q_key = q_key.contiguous()
             if q_value.stride(2) != 1:
                 q_value = q_value.contiguous()
-            (key_code, key_scale, key_minimum, value_code, value_scale,
-             value_minimum) = kernels.kivi_pack_kv(q_key, q_value, k_bits=k_bits, v_bits=v_bits,
-                                                   group_size=group_size)
-        else:
-            key_code = key_scale = key_minimum = None
-            value_code = value_scale = value_minimum = None
-        return cls(
+            if _packed is not None:
+                packed = _packed(q_key, q_value)
+            else:
+                packed = kernels.kivi_pack_kv(q_key, q_value, k_bits=k_bits, v_bits=v_bits, group_size=group_size)
+        return cls._assemble(key, value, packed, quantized, logical_token_ids, token_type_id, k_bits, v_bits,
+                             group_size, head_dim, heads, backend, residual_length)
+
+    @classmethod
+    def from_dense_batch(cls, keys: list, values: list, *, logical_token_ids: list, token_type_id: int, k_bits: int,
+                         v_bits: int, group_size: int, residual_length: int,
+                         backend: str = "b200") -> list["PackedKIVICache"]:
+        """``from_dense`` of several segments with one pack launch for all of
+        them (group 32 and aligned rows; other shapes pack segment by segment):
+        a batch prefill or all layers of one sequence at once."""
+
+        if not (len(keys) == len(values) == len(logical_token_ids)) or not keys:
+            raise ValueError("from_dense_batch needs matching, non-empty key/value/id lists")
+        pending: list = []
+
+        def defer(q_key, q_value):
+            pending.append((q_key, q_value))
+            return len(pending) - 1
+
+        caches = [cls.from_dense(k, v, logical_token_ids=ids, token_type_id=token_type_id, k_bits=k_bits,
+                                 v_bits=v_bits, group_size=group_size, residual_length=residual_length,
+                                 backend=backend, _packed=defer)
+                  for k, v, ids in zip(keys, values, logical_token_ids)]
+        if pending:
+            outputs = kernels.kivi_pack_kv_batch(pending, k_bits=k_bits, v_bits=v_bits, group_size=group_size)
+            for cache in caches:
+                if cache.quantized_tokens:
+                    slot = cache.__dict__.pop("_pending_pack")
+                    (cache.key_code, cache.key_scale, cache.key_minimum, cache.value_code, cache.value_scale,
+                     cache.value_minimum) = outputs[slot]
+        return caches
+
+    @classmethod
+    def _assemble(cls, key, value, packed, quantized, logical_token_ids, token_type_id, k_bits, v_bits, group_size,
+                  head_dim, heads, backend, residual_length) -> "PackedKIVICache":
+        if isinstance(packed, tuple):
+            key_code, key_scale, key_minimum, value_code, value_scale, value_minimum = packed
+        else:  # not packed yet (from_dense_batch fills these in) or nothing to pack
+            key_code = key_scale = key_minimum = value_code = value_scale = value_minimum = None
+        cache = cls(
             key_code=key_code,
             key_scale=key_scale,
             key_minimum=key_minimum,
@@ -172,6 +211,9 @@ class PackedKIVICache:
             kernel_native_layout=True,
             residual_length=max(0, int(residual_length)),
         )
+        if isinstance(packed, int):
+            cache.__dict__["_pending_pack"] = packed
+        return cache
 
     # ---------------------------------------------------------------- streaming append
     def append(self, key: torch.Tensor, value: torch.Tensor, *, logical_token_ids: torch.Tensor) -> int:
