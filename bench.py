@@ -471,11 +471,14 @@ def pack_leg(run: Run, wl: Workload, dense_kv) -> dict:
 
 def long_query_leg(run: Run) -> dict:
     """BASELINE config 4, one layer: the 1024-token latent block (28 query / 4
-    KV heads) over 3095 cached tokens per KV head, non-causal.  ``kernel``:
-    the tcgen05 kernel alone on resident dense operands; ``e2e``: the whole
-    ``long_query_attention_summary`` call over the real segment mix (H2O
-    instruction and ViT rows, packed VAE tokens, residual, boundary and latent
-    rows).  FLOPs = 4 * Lq * Hq * D * N."""
+    KV heads) over 3095 cached tokens per KV head (H2O instruction and ViT
+    rows, packed VAE tokens, residual, boundary and latent rows), non-causal.
+    ``us_per_layer``: the product path's launches on that segment mix with
+    its span tables built (the staged form: one staging kernel, then the
+    tcgen05 kernel by TMA); ``in_place_us``: the same call reading the spans
+    in place; ``dense_operand_us``: the tcgen05 kernel alone on resident
+    dense bf16 operands of the same size; ``e2e``: the whole
+    ``long_query_attention_summary`` call.  FLOPs = 4 * Lq * Hq * D * N."""
 
     import torch
 
@@ -495,9 +498,20 @@ def long_query_leg(run: Run) -> dict:
     out = torch.empty_like(q)
     lse = torch.empty(heads, lq * grp, device=dev, dtype=torch.float32)
     reps = 20
-    kernel_s = run.eager_seconds(lambda i: kernels.prefill_attention(q, k, vt, n, out=out, lse=lse), reps, 3) / reps
+    dense_s = run.eager_seconds(lambda i: kernels.prefill_attention(q, k, vt, n, out=out, lse=lse), reps, 3) / reps
     layer = config4_layer(dev, seed=1)
     assert layer.key_tokens == n
+    segs = [(layer.dense_key, layer.dense_value), *layer.segments]
+    tables = kernels.long_query_tables([segs], heads, [0], [lq * grp], dev)
+    lq_out = torch.empty_like(layer.query)
+    lq_lse = torch.empty(Q_HEADS, lq, device=dev, dtype=torch.float32)
+
+    def product(staged):
+        return lambda i: kernels.long_query_attention(layer.query, tables, num_kv_heads=heads, out=lq_out,
+                                                      lse=lq_lse, staged=staged)
+
+    kernel_s = run.eager_seconds(product(True), reps, 3) / reps
+    in_place_s = run.eager_seconds(product(False), reps, 3) / reps
     e2e_s = run.eager_seconds(lambda i: long_query_attention_summary(layer.query, layer.segments,
                                                                      dense_key=layer.dense_key,
                                                                      dense_value=layer.dense_value), reps, 3) / reps
@@ -512,6 +526,9 @@ def long_query_leg(run: Run) -> dict:
     return {"workload": "config4 layer: Lq=1024 x 28/4 heads over 3095 keys (51+980 H2O, 992 packed 2-bit G32 + "
                         "32 residual, 16 boundary, 1024 latent), D=128, bf16, non-causal",
             "us_per_layer": kernel_s * 1e6, "tflops": flops / kernel_s / 1e12, "roofline": roof(kernel_s),
+            "kernel": "staged long-query call: stage_kernel (key spaces gathered once) + prefill_kernel (TMA)",
+            "in_place_us_per_layer": in_place_s * 1e6, "in_place_roofline": roof(in_place_s),
+            "dense_operand_us_per_layer": dense_s * 1e6, "dense_operand_roofline": roof(dense_s),
             "e2e_us_per_layer": e2e_s * 1e6, "e2e_roofline": roof(e2e_s),
             "e2e_api": "long_query_attention_summary over the segment list"}
 

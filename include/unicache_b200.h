@@ -353,6 +353,46 @@ UCB_API int ucb_long_query_attention(const void* q_dev, int positions, int num_q
                                      int k_bits, int v_bits, int group_size, float softmax_scale, void* out_dev,
                                      float* lse_dev, float* partials_dev, unsigned int* flags_dev, void* stream);
 
+/* Staging job of a staged long-query launch: one key space (the keys of one
+ * KV head of one sample, i.e. the span list its items read) gathered into
+ * workspace rows [ws_row0, ws_row0 + rows) of KV head `head`; tokens
+ * [tokens, rows) are written as zeros.  ws_row0 and rows are multiples of
+ * 128, rows >= tokens. */
+typedef struct ucb_lq_stage_job {
+  int32_t head;
+  int32_t span_begin;
+  int32_t span_count;
+  int32_t tokens;
+  int32_t ws_row0;
+  int32_t rows;
+  int32_t reserved[2];
+} ucb_lq_stage_job;
+
+/* Gathers every job's key space into a bf16 workspace: k_ws [heads, ws_rows,
+ * 128] (token rows) and vt_ws [heads, 128, ws_rows] (values transposed).
+ * Dense spans are copied; packed spans are restored as code * scale +
+ * minimum with one rounding to bf16, the values ucb_long_query_attention
+ * restores in its operand tiles.  Grid: max_chunks x num_jobs blocks of 64
+ * tokens (max_chunks * 64 >= the largest `rows`; ws_rows a multiple of 128). */
+UCB_API int ucb_long_query_stage(const ucb_span* spans_dev, int num_spans, const void* jobs_dev, int num_jobs,
+                                 int max_chunks, int k_bits, int v_bits, int group_size, void* k_ws_dev,
+                                 void* vt_ws_dev, int64_t ws_rows, void* stream);
+
+/* ucb_long_query_attention with its keys and values staged first
+ * (ucb_long_query_stage, then the tensor-core kernel streaming both by TMA):
+ * same arguments and results, plus the staging jobs and workspace; each
+ * item's key space starts at workspace row reserved[0] of the item (the
+ * ws_row0 of its job), so items keep k_row0 relative to their key space.
+ * Preferable when several row blocks read the same keys: each packed tile is
+ * restored once per launch instead of once per row block. */
+UCB_API int ucb_long_query_attention_staged(const void* q_dev, int positions, int num_q_heads, int num_kv_heads,
+                                            const void* items_dev, int num_items, const ucb_span* spans_dev,
+                                            int num_spans, const void* jobs_dev, int num_jobs, int max_chunks,
+                                            int k_bits, int v_bits, int group_size, float softmax_scale,
+                                            void* k_ws_dev, void* vt_ws_dev, int64_t ws_rows, void* out_dev,
+                                            float* lse_dev, float* partials_dev, unsigned int* flags_dev,
+                                            void* stream);
+
 /* ---- sequence-split merge over NVLink peer memory (no counterpart in the
  * reference, which decodes one sequence on one device).  Each rank allocates
  * one exchange buffer of ucb_peer_buffer_bytes(rows) bytes

@@ -1,6 +1,11 @@
-"""Long-query attention reading the segments in place (ucb_long_query_attention):
-dense and H2O rows copied into the tensor-core operand tiles, packed KIVI
-tiles restored in shared memory.
+"""Long-query attention over span tables, both launch forms: reading the
+segments in place (ucb_long_query_attention: dense and H2O rows copied into
+the tensor-core operand tiles, packed KIVI tiles restored in shared memory)
+and staged (ucb_long_query_attention_staged: every key space gathered once
+into a bf16 workspace by ucb_long_query_stage, then streamed by TMA).  The
+staged workspace is checked bit for bit against a numpy restore of the same
+codes (code * scale + minimum, one rounding to bf16), and both launch forms
+against each other.
 
 Checked against (a) the workspace path it replaces: the bit-exact dequant
 kernel restores every packed span into a bf16 workspace, then the TMA-fed
@@ -92,13 +97,14 @@ LAYOUTS = [
 ]
 
 
+@pytest.mark.parametrize("staged", [False, True])
 @pytest.mark.parametrize("case", range(len(LAYOUTS)))
-def test_long_query_spans_match_workspace_path_and_oracle(case):
+def test_long_query_spans_match_workspace_path_and_oracle(case, staged):
     need_gpu()
     bits, group, layout, lq = LAYOUTS[case]
     segs, keys, vals = _segments(50 + case, layout, bits, group)
     query = make_query(lq, 28, 128, seed=60 + case, device="cuda")
-    out, lse = long_query_attention_summary(query, segs)
+    out, lse = long_query_attention_summary(query, segs, staged=staged)
     w_out, w_lse = _workspace_path(query, segs)
     torch.cuda.synchronize()
     diff = (out.float() - w_out.float()).abs()
@@ -109,13 +115,19 @@ def test_long_query_spans_match_workspace_path_and_oracle(case):
     assert_attention_close(out, e_out, what=f"long-query spans case {case}")
     assert np.abs(host(lse) - e_lse).max() <= 2e-2
     # a second call reuses the cached span tables and is bitwise identical
-    out2, lse2 = long_query_attention_summary(query, segs)
+    out2, lse2 = long_query_attention_summary(query, segs, staged=staged)
     torch.cuda.synchronize()
     assert torch.equal(out, out2) and torch.equal(lse, lse2)
+    # the other launch form: the same operand values in the same key order
+    o_out, o_lse = long_query_attention_summary(query, segs, staged=not staged)
+    torch.cuda.synchronize()
+    assert float((out.float() - o_out.float()).abs().max()) <= 1e-2
+    assert float((lse - o_lse).abs().max()) <= 1e-4
     assert kernels.device_status() == 0
 
 
-def test_batched_long_query_spans_three_samples():
+@pytest.mark.parametrize("staged", [False, True])
+def test_batched_long_query_spans_three_samples(staged):
     need_gpu()
     samples, queries, expects = [], [], []
     for i, (layout, lq) in enumerate([([("h2o", 90), ("packed", 500)], 40),
@@ -125,9 +137,84 @@ def test_batched_long_query_spans_three_samples():
         samples.append(segs)
         queries.append(q)
         expects.append(attention.mixed_attention(host(q), keys, vals))
-    results = batched_long_query_attention(queries, samples)
+    results = batched_long_query_attention(queries, samples, staged=staged)
     torch.cuda.synchronize()
     for (out, lse), (e_out, e_lse) in zip(results, expects):
         assert_attention_close(out, e_out, what="batched spans")
         assert np.abs(host(lse) - e_lse).max() <= 2e-2
+    assert kernels.device_status() == 0
+
+
+def _bf16_single_round(x: np.ndarray) -> np.ndarray:
+    """Round float64 values (exact here: code * scale + minimum of bf16
+    operands) to bf16 once, round-half-even."""
+
+    mant, exp = np.frexp(x)
+    return np.ldexp(np.rint(mant * 256.0), exp - 8)
+
+
+def _unpack(code: np.ndarray, bits: int, count: int, axis: int) -> np.ndarray:
+    f, mask = 32 // bits, (1 << bits) - 1
+    w = code.astype(np.int64) & 0xFFFFFFFF
+    idx = np.arange(count)
+    if axis == 0:  # packed along tokens: [T/f, D] -> [T, D]
+        return (w[idx // f] >> (bits * (idx % f))[:, None]) & mask
+    return (w[:, idx // f] >> (bits * (idx % f))[None, :]) & mask  # along channels: [T, D/f] -> [T, D]
+
+
+def _restored(seg: PackedKIVICache, h: int):
+    n, g = seg.quantized_tokens, seg.group_size
+    kc = _unpack(host(seg.key_code[h]), seg.k_bits, n, 0)
+    ks = np.repeat(host(seg.key_scale[h]).astype(np.float64), g, axis=0)[:n]
+    km = np.repeat(host(seg.key_minimum[h]).astype(np.float64), g, axis=0)[:n]
+    vc = _unpack(host(seg.value_code[h]), seg.v_bits, 128, 1)
+    vs = np.repeat(host(seg.value_scale[h]).astype(np.float64), g, axis=1)
+    vm = np.repeat(host(seg.value_minimum[h]).astype(np.float64), g, axis=1)
+    return _bf16_single_round(kc * ks + km), _bf16_single_round(vc * vs + vm)
+
+
+def _expected_key_space(segs, h):
+    """Keys and values of KV head h in span order: packed spans first, then
+    the dense, H2O and residual rows in segment order."""
+
+    pk, pv, dk, dv = [], [], [], []
+    for seg in segs:
+        if isinstance(seg, PackedKIVICache):
+            if seg.quantized_tokens:
+                k, v = _restored(seg, h)
+                pk.append(k)
+                pv.append(v)
+            dk.append(host(seg.residual_key[:, h]))
+            dv.append(host(seg.residual_value[:, h]))
+        elif isinstance(seg, GQAH2OCache):
+            dk.append(host(seg.key[h]))
+            dv.append(host(seg.value[h]))
+        else:
+            dk.append(host(seg[0][:, h]))
+            dv.append(host(seg[1][:, h]))
+    return np.concatenate(pk + dk), np.concatenate(pv + dv)
+
+
+@pytest.mark.parametrize("bits,group", [(2, 32), (4, 64), (2, 128)])
+def test_stage_workspace_is_the_single_rounding_restore(bits, group):
+    need_gpu()
+    samples = [_segments(120, [("dense", 40), ("packed", 333), ("h2o", 150)], bits, group)[0],
+               _segments(121, [("packed", 700), ("dense", 9)], bits, group)[0]]
+    tables = kernels.long_query_tables(samples, 4, [0, 5], [35, 21], "cuda")
+    k_ws, vt_ws = kernels.long_query_stage(tables, 4, "cuda")
+    torch.cuda.synchronize()
+    kh, vth = host(k_ws), host(vt_ws)
+    base = 0
+    for segs in samples:
+        extent = 0
+        for h in range(4):
+            ek, ev = _expected_key_space(segs, h)
+            n = int(ek.shape[0])
+            padded = -(-n // 128) * 128
+            extent = max(extent, padded)
+            assert np.array_equal(kh[h, base:base + n], ek.astype(np.float32)), (h, base)
+            assert np.array_equal(vth[h, :, base:base + n], ev.T.astype(np.float32)), (h, base)
+            assert not kh[h, base + n:base + padded].any() and not vth[h, :, base + n:base + padded].any()
+        base += extent
+    assert tables.ws_rows == base
     assert kernels.device_status() == 0

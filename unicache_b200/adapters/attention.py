@@ -159,12 +159,15 @@ def _kv_heads_of(segs) -> int:
 
 
 def batched_long_query_attention(queries: list, segments_by_sample: list, *, dense_by_sample: list | None = None,
-                                 include_residual: bool = True) -> list:
+                                 include_residual: bool = True, staged: bool | None = None) -> list:
     """Non-causal attention of several samples' query blocks over their own
     physical segments in one tcgen05 launch, the counterpart of the varlen
     launch of apply_static_physical_attention_batch (bagel.py:773-980).  The
-    segments are read in place through a span table: dense and H2O rows by
-    cp.async, packed KIVI tiles restored in shared memory (no workspace).
+    segments are described by a span table: either read in place (dense and
+    H2O rows by cp.async, packed KIVI tiles restored in shared memory by
+    every row block) or, when several row blocks read each key space
+    (``staged`` None picks; see ``kernels.long_query_attention``), gathered
+    once per launch into a bf16 workspace that the kernel streams by TMA.
 
     queries[i] [Lq_i, Hq, D]; segments_by_sample[i] the sample's segments;
     dense_by_sample[i] an optional (key, value) [N, Hkv, D] pair of the
@@ -195,7 +198,7 @@ def batched_long_query_attention(queries: list, segments_by_sample: list, *, den
         start += int(query.shape[0])
     q = torch.cat([query.to(torch.bfloat16) for query, _ in samples]).contiguous()
     tables = kernels.long_query_tables([segs for _, segs in samples], hkv, pos0, rows, q.device, include_residual)
-    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv)
+    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv, staged=staged)
     results = []
     for (query, _), p0 in zip(samples, pos0):
         lq = int(query.shape[0])
@@ -204,14 +207,18 @@ def batched_long_query_attention(queries: list, segments_by_sample: list, *, den
 
 
 def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_key=None, dense_value=None,
-                                 include_residual: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+                                 include_residual: bool = True,
+                                 staged: bool | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Multi-query (non-causal) attention over physical segments on the tcgen05
     tensor cores: (out [Lq, Hq, D], lse [Hq, Lq] natural log).
 
     The query rows of each KV head ((position, head-in-group) pairs) form one
-    M x N attention problem; the kernel reads the query, the segments and
-    writes the outputs in place (dense and H2O rows copied, packed KIVI tiles
-    restored in shared memory), so no workspace is assembled."""
+    M x N attention problem; the kernel reads the query and writes the
+    outputs in the caller's layout.  Keys and values are read in place (dense
+    and H2O rows copied, packed KIVI tiles restored in shared memory) or,
+    when several row blocks read them, staged once per call into a bf16
+    workspace streamed by TMA (``staged``: see
+    ``kernels.long_query_attention``)."""
 
     kernels.require_cuda(query, "query")
     segs = _segments_for(dense_key, dense_value, segments)
@@ -223,5 +230,5 @@ def long_query_attention_summary(query: torch.Tensor, segments: list, *, dense_k
         raise ValueError("Query heads must be divisible by KV heads")
     q = query if (query.dtype == torch.bfloat16 and query.is_contiguous()) else query.to(torch.bfloat16).contiguous()
     tables = kernels.long_query_tables([segs], hkv, [0], [lq * (hq // hkv)], query.device, include_residual)
-    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv)
+    out, lse = kernels.long_query_attention(q, tables, num_kv_heads=hkv, staged=staged)
     return out.to(query.dtype), lse

@@ -34,6 +34,15 @@
 //    issued after it, overwrites those columns.
 //  * Every wait has a time budget; on expiry the CTA sets the device error
 //    word, drains its tensor-core work (bounded) and frees TMEM.
+//
+// Three launch forms share the kernel: workspace launches (Q, K and V^T by
+// TMA from [heads, rows, 128] / [heads, 128, rows] bf16 tensors), segment-
+// table launches (SPANS: the query and outputs in the caller's layout, keys
+// and values read in place by producer warps 8, 10 and 11, packed KIVI tiles
+// restored in shared memory), and staged launches (the caller's layout for
+// the query and outputs, keys and values by TMA from a workspace that
+// stage_kernel gathered once per launch).  In the caller-layout forms the
+// softmax warps (and warps 10-11 of a staged launch) load Q with cp.async.
 #include <cstring>
 
 #include <cuda.h>
@@ -511,8 +520,191 @@ struct Params {
   unsigned int* err;
 };
 
+// Q_A and Q_B of a caller-layout item straight from the query [positions,
+// hq, 128] into the swizzled Q tiles (zero rows past the item's last row):
+// thread pid of `threads` (a multiple of 16) owns 16-byte chunk column
+// pid % 16 and every (threads / 16)-th row from pid / 16; the row's
+// (position, head-in-group) pair advances by an add and one wrap per step
+// rather than a division.  The caller waits for its cp.async group and
+// fences the async proxy before publishing.
+__device__ __forceinline__ void load_q_caller(const Params& P, unsigned char* smem, int m0, int m_end, int pos0,
+                                              int head, int pid, int threads) {
+  const uint32_t q_addr = smem_u32(smem + OFF_Q);
+  const int c = pid & 15, step = threads >> 4;
+  const uint32_t cl = (uint32_t)(c & 7) << 4;
+  const int step_pos = step / P.grp, step_g = step % P.grp;
+  int rb = pid >> 4, pos = (m0 + rb) / P.grp, g = (m0 + rb) % P.grp;
+  const int64_t row_stride = (int64_t)P.hq * D;
+  const __nv_bfloat16* qh = P.q + (int64_t)pos0 * row_stride + (int64_t)head * P.grp * D + 8 * c;
+  for (; rb < 2 * BM; rb += step) {
+    const int x = rb >> 7, rr = rb & (BM - 1);
+    const uint32_t dst = x * QTILE + (c >> 3) * QHALF + rr * 128 + (cl ^ ((uint32_t)(rr & 7) << 4));
+    if (m0 + rb < m_end)
+      cp_async16(q_addr + dst, qh + (int64_t)pos * row_stride + g * D);
+    else
+      *reinterpret_cast<uint4*>(smem + OFF_Q + dst) = make_uint4(0u, 0u, 0u, 0u);
+    pos += step_pos;
+    g += step_g;
+    if (g >= P.grp) {
+      g -= P.grp;
+      ++pos;
+    }
+  }
+}
+// Threads that load Q in a caller-layout launch: the softmax warps (idle
+// until the first S tile, which needs Q) and, in a staged launch, the spare
+// warps 10 and 11.
+constexpr int SPAN_Q_THREADS = 256;
+constexpr int STAGED_Q_THREADS = 320;
+
+// ---------------------------------------------------------------- staging
+// A staged launch first gathers each key space (the keys of one KV head of
+// one sample: the span list of its items) once into a bf16 workspace, K as
+// rows [heads, ws_rows, 128] and V transposed [heads, 128, ws_rows], rows
+// [ws_row0, ws_row0 + rows) of the job's head with tokens past `tokens`
+// zeroed; the attention kernel then streams both by TMA.  Dense spans are
+// copied; packed spans are restored with the arithmetic of the in-tile
+// restore (code * scale + minimum, one rounding to bf16), so a staged launch
+// and a segment-table launch see the same key and value values.  Restoring
+// once per launch rather than once per row block pays when several row
+// blocks read the same keys (the configuration-4 layer has 28 per KV head).
+struct StageJob {
+  int head, span_begin, span_count, tokens, ws_row0, rows, pad0, pad1;
+};
+constexpr int STAGE_T = 64;          // tokens per staging block
+constexpr int STAGE_THREADS = 256;
+constexpr int STAGE_PITCH = D + 8;   // bf16 per token row of a block's value rows
+
+// Block (x, job): tokens [64 x, 64 x + 64) of the job's key space.  The job's
+// span records are staged in shared memory (STAGE_SPANS at a time) and each
+// token is mapped to its span once; each thread then issues the loads of all
+// its (token, 8-channel chunk) items before restoring any, so a block waits
+// for memory about once per span batch.  K rows go straight to the workspace
+// (16-byte chunks, coalesced); value rows gather in shared memory and leave
+// as V^T rows of 64 tokens (128 bytes per channel).
+constexpr int STAGE_SPANS = 16;
+constexpr int STAGE_ITEMS = STAGE_T * 16 / STAGE_THREADS;  // items per thread per block
+
+struct StageLoad {
+  uint4 a, b, c, d;  // dense: key, value chunk; packed: key code words (a, b), key scales (c), key minima (d)
+  uint32_t vword, vs, vm;
+};
+
+template <int KB, int VB>
+__global__ void __launch_bounds__(STAGE_THREADS) stage_kernel(const StageJob* __restrict__ jobs,
+                                                              const ucb_span* __restrict__ spans, int G,
+                                                              __nv_bfloat16* __restrict__ k_ws,
+                                                              __nv_bfloat16* __restrict__ vt_ws, int64_t ws_rows) {
+  __shared__ __align__(16) __nv_bfloat16 vblk[STAGE_T * STAGE_PITCH];
+  __shared__ __align__(16) ucb_span sps[STAGE_SPANS];
+  __shared__ int span_of[STAGE_T];
+  const StageJob J = jobs[blockIdx.y];
+  const int c0 = blockIdx.x * STAGE_T;
+  if (c0 >= J.rows) return;
+  const int tid = threadIdx.x;
+  __nv_bfloat16* kdst = k_ws + ((int64_t)J.head * ws_rows + J.ws_row0 + c0) * D;
+  constexpr int KF = 32 / KB, VF = 32 / VB, VW = D / VF;
+  constexpr uint32_t KMASK = (1u << KB) - 1u, VMASK = (1u << VB) - 1u;
+  const int ng = D / G;
+  for (int sb = 0; sb < J.span_count; sb += STAGE_SPANS) {
+    const int nb = min(STAGE_SPANS, J.span_count - sb);
+    __syncthreads();  // the previous batch's records are no longer read
+    for (int i = tid; i < nb * (int)(sizeof(ucb_span) / 8); i += STAGE_THREADS)
+      reinterpret_cast<uint64_t*>(sps)[i] = reinterpret_cast<const uint64_t*>(spans + J.span_begin + sb)[i];
+    __syncthreads();
+    if (tid < STAGE_T) {
+      const int tok = c0 + tid;
+      int found = -1;
+      for (int k = 0; k < nb; ++k)
+        if (tok < J.tokens && tok >= sps[k].unit_begin && tok < sps[k].unit_begin + sps[k].tokens) found = k;
+      span_of[tid] = found;
+    }
+    __syncthreads();
+    StageLoad L[STAGE_ITEMS];
+#pragma unroll
+    for (int it = 0; it < STAGE_ITEMS; ++it) {
+      const int i = tid + it * STAGE_THREADS, t = i >> 4, cc = i & 15, k = span_of[t];
+      if (k < 0) continue;
+      const ucb_span& S = sps[k];
+      const int off = c0 + t - S.unit_begin;
+      if (S.kind == 1) {
+        L[it].a = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(S.key_code) +
+                                                       (int64_t)off * S.key_stride + 8 * cc));
+        L[it].b = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(S.value_code) +
+                                                       (int64_t)off * S.value_stride + 8 * cc));
+      } else {
+        const uint32_t* cw = static_cast<const uint32_t*>(S.key_code) + (int64_t)(off / KF) * D + 8 * cc;
+        const int64_t g = off / G;
+        L[it].a = __ldg(reinterpret_cast<const uint4*>(cw));
+        L[it].b = __ldg(reinterpret_cast<const uint4*>(cw + 4));
+        L[it].c = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(S.key_scale) + g * D + 8 * cc));
+        L[it].d = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(S.key_minimum) + g * D + 8 * cc));
+        L[it].vword = __ldg(static_cast<const uint32_t*>(S.value_code) + (int64_t)off * VW + (8 * cc) / VF);
+        L[it].vs = __ldg(static_cast<const uint16_t*>(S.value_scale) + (int64_t)off * ng + (8 * cc) / G);
+        L[it].vm = __ldg(static_cast<const uint16_t*>(S.value_minimum) + (int64_t)off * ng + (8 * cc) / G);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < STAGE_ITEMS; ++it) {
+      const int i = tid + it * STAGE_THREADS, t = i >> 4, cc = i & 15, k = span_of[t];
+      if (k < 0) continue;
+      uint4 kv, vv;
+      if (sps[k].kind == 1) {
+        kv = L[it].a;
+        vv = L[it].b;
+      } else {
+        // keys: code of token `off` in each of the 8 channel words (restore as in the operand tiles)
+        const int sh = KB * ((c0 + t - sps[k].unit_begin) % KF);
+        const uint32_t w[8] = {L[it].a.x, L[it].a.y, L[it].a.z, L[it].a.w, L[it].b.x, L[it].b.y, L[it].b.z, L[it].b.w};
+        const uint32_t sp[4] = {L[it].c.x, L[it].c.y, L[it].c.z, L[it].c.w};
+        const uint32_t mp[4] = {L[it].d.x, L[it].d.y, L[it].d.z, L[it].d.w};
+        uint32_t ko[4], vo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t code = ((w[2 * q] >> sh) & KMASK) | (((w[2 * q + 1] >> sh) & KMASK) << 16);
+          ko[q] = bf16x2_dequant(code | 0x43004300u, 0xC300C300u, sp[q], mp[q]);
+        }
+        // values: channels 8 cc .. 8 cc + 7 of the token, one word
+        const int base = VB * ((8 * cc) % VF);
+        const uint32_t s2 = L[it].vs | (L[it].vs << 16), m2 = L[it].vm | (L[it].vm << 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t a = (L[it].vword >> (base + VB * 2 * q)) & VMASK;
+          const uint32_t b = (L[it].vword >> (base + VB * (2 * q + 1))) & VMASK;
+          vo[q] = bf16x2_dequant((a | (b << 16)) | 0x43004300u, 0xC300C300u, s2, m2);
+        }
+        kv = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+        vv = make_uint4(vo[0], vo[1], vo[2], vo[3]);
+      }
+      *reinterpret_cast<uint4*>(kdst + (int64_t)t * D + 8 * cc) = kv;
+      *reinterpret_cast<uint4*>(&vblk[t * STAGE_PITCH + 8 * cc]) = vv;
+    }
+  }
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < STAGE_T * 16; i += STAGE_THREADS) {  // tokens past the key space
+    const int t = i >> 4, cc = i & 15;
+    if (c0 + t >= J.tokens) {
+      *reinterpret_cast<uint4*>(kdst + (int64_t)t * D + 8 * cc) = zero;
+      *reinterpret_cast<uint4*>(&vblk[t * STAGE_PITCH + 8 * cc]) = zero;
+    }
+  }
+  __syncthreads();
+  const uint16_t* vb = reinterpret_cast<const uint16_t*>(vblk);
+  for (int i = tid; i < D * (STAGE_T / 8); i += STAGE_THREADS) {
+    const int ch = i % D, q = i / D;
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = (uint32_t)vb[(8 * q + 2 * k) * STAGE_PITCH + ch] | ((uint32_t)vb[(8 * q + 2 * k + 1) * STAGE_PITCH + ch] << 16);
+    *reinterpret_cast<uint4*>(vt_ws + ((int64_t)J.head * D + ch) * ws_rows + J.ws_row0 + c0 + 8 * q) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // SPANS: keys and values come from the item's spans (producer warps 8, 10,
-// 11); otherwise from the K / V^T tensor maps (loader warp 8).
+// 11); otherwise from the K / V^T tensor maps (loader warp 8), with the query
+// from the Q tensor map (workspace launches) or the caller's layout (staged
+// launches: P.lq_items set).
 template <bool SPANS>
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -520,7 +712,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0, span_begin = 0, span_count = 0, pos0 = 0;
-  if constexpr (SPANS) {
+  // A staged launch: LqItem problems in the caller's layout, keys and values
+  // by TMA from the staging workspace (the item's key space starts at its
+  // workspace row, reserved[0] of the item).
+  const bool staged = !SPANS && P.lq_items != nullptr;
+  if (SPANS || staged) {
     const LqItem it = P.lq_items[blockIdx.x];
     head = it.head;
     m0 = it.q_row0;
@@ -532,6 +728,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     span_begin = it.span_begin;
     span_count = it.span_count;
     pos0 = it.pos0;
+    if (staged) k0 += it.pad1;
     if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
       if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
       mode = ITEM_FINAL;
@@ -580,7 +777,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (tid == 0) {
     failed = 0;
-    mbar_init(q_full, SPANS ? PRODUCERS : 1);
+    mbar_init(q_full, SPANS ? SPAN_Q_THREADS : (staged ? STAGED_Q_THREADS : 1));
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&k_full[i], SPANS ? PRODUCERS : 1);
       mbar_init(&k_empty[i], 1);
@@ -610,23 +807,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (SPANS && (warp == 8 || warp == 10 || warp == 11)) {
     // ---------------- span producers
     const int pid = (warp == 8 ? 0 : warp - 9) * 32 + lane;
-    // Q_A and Q_B straight from the caller's [positions, hq, 128] query
-    // (zero rows past the item's last row); their copies ride with the first
-    // K tile's and are published with it.
-    {
-      const uint32_t q_addr = smem_u32(smem + OFF_Q);
-      const int c = pid & 15;
-      const uint32_t cl = (uint32_t)(c & 7) << 4;
-      for (int rb = pid >> 4; rb < 2 * BM; rb += ROW_STEP) {
-        const int x = rb >> 7, rr = rb & (BM - 1), m = m0 + rb;
-        const uint32_t dst = x * QTILE + (c >> 3) * QHALF + rr * 128 + (cl ^ ((uint32_t)(rr & 7) << 4));
-        if (m < m_end)
-          cp_async16(q_addr + dst, P.q + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 8 * c);
-        else
-          *reinterpret_cast<uint4*>(smem + OFF_Q + dst) = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    // Half-tiles h = 2j (K of tile j) and 2j + 1 (V of tile j) are filled in
+    // (Q_A and Q_B are loaded by the softmax warps.)  Half-tiles h = 2j (K of tile j) and 2j + 1 (V of tile j) are filled in
     // order, each as one cp.async group; half-tile h - 1 is published (its
     // copies waited for, proxy fence, arrive) only once half-tile h is in
     // flight, so K and V loads overlap like TMA loads do.  A half-tile's
@@ -636,7 +817,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const ucb_span* spans = P.spans + span_begin;
     auto publish = [&](int h) {
       fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
-      if (h == 0) mbar_arrive(q_full);
       mbar_arrive((h & 1) ? &v_full[(h >> 1) % STAGES] : &k_full[(h >> 1) % STAGES]);
     };
     int filled = 0;
@@ -658,19 +838,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     cp_async_wait_all();
-    if (filled > 0) {
-      publish(filled - 1);
-    } else {  // no key tile was filled (an empty item or an early failure): the Q copies still land
-      fence_proxy_async_smem();
-      mbar_arrive(q_full);
-    }
+    if (filled > 0) publish(filled - 1);
+  } else if (staged && (warp == 10 || warp == 11)) {
+    // ---------------- caller-layout Q of a staged launch (with the softmax warps)
+    load_q_caller(P, smem, m0, m_end, pos0, head, SPAN_Q_THREADS + (warp - 10) * 32 + lane, STAGED_Q_THREADS);
+    cp_async_wait_all();
+    fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
+    mbar_arrive(q_full);
   } else if (!SPANS && warp == 8) {
     // ---------------- loader
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * QTILE);
-      for (int x = 0; x < 2; ++x) {
-        tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
-        tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+      if (!staged) {
+        mbar_arrive_expect_tx(q_full, 2 * QTILE);
+        for (int x = 0; x < 2; ++x) {
+          tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
+          tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+        }
       }
       int issued = 0;
       for (int j = 0; j < n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++j) {
@@ -761,6 +944,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp < 8) {
     // ---------------- softmax warpgroups
+    if (SPANS || staged) {
+      // caller-layout Q_A and Q_B (the first S tile waits for them anyway)
+      load_q_caller(P, smem, m0, m_end, pos0, head, tid, SPANS ? SPAN_Q_THREADS : STAGED_Q_THREADS);
+      cp_async_wait_all();
+      fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
+      mbar_arrive(q_full);
+    }
     const int x = warp >> 2;             // tile
     const int row = tid & (BM - 1);      // query row in the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
@@ -862,7 +1052,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (merged) v[i] = fmaf(w_p, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
           }
           __nv_bfloat16* dst =
-              SPANS ? P.out + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 32 * c
+              (SPANS || staged) ? P.out + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 32 * c
                     : P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -876,7 +1066,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (m < m_end && P.lse) {
-        const int64_t at = SPANS ? (int64_t)(head * P.grp + m % P.grp) * P.positions + pos0 + m / P.grp
+        const int64_t at = (SPANS || staged) ? (int64_t)(head * P.grp + m % P.grp) * P.positions + pos0 + m / P.grp
                                  : (int64_t)head * P.m_rows + m;
         P.lse[at] = lse2 * 0.6931471805599453f;
       }
@@ -929,11 +1119,15 @@ int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_
 }  // namespace ucb
 
 namespace {
-// k == vt == nullptr: a segment-table launch (keys and values from P.spans).
+// q == k == vt == nullptr: a segment-table launch (keys and values from
+// P.spans).  q == nullptr with k and vt: a staged launch (caller-layout query
+// in P.q, keys and values from the staging workspace k [heads, n_padded, 128]
+// and vt [heads, 128, n_padded]).
 int launch_prefill(const void* q, const void* k, const void* vt, int heads, int m_rows, int n_padded,
                    ucb::prefill::Params P, dim3 grid, void* stream) {
   using namespace ucb::prefill;
-  const bool spans = (q == nullptr);
+  const bool spans = (q == nullptr && k == nullptr);
+  const bool staged = (q == nullptr && k != nullptr);
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(vt)) & 15)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_prefill_attention: operands must be 16-byte aligned");
   if (!spans && n_padded % 8)
@@ -944,6 +1138,11 @@ int launch_prefill(const void* q, const void* k, const void* vt, int heads, int 
   if (spans) {
     memset(&tq, 0, sizeof(tq));  // unused by the segment-table kernel
     tk = tv = tq;
+  } else if (staged) {
+    memset(&tq, 0, sizeof(tq));  // the query is loaded in the caller's layout
+    int rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
+    if (!rc) rc = make_map(&tv, vt, (uint64_t)n_padded, D, (uint64_t)heads, D);
+    if (rc) return rc;
   } else {
     int rc = make_map(&tq, q, D, (uint64_t)m_rows, (uint64_t)heads, BM);
     if (!rc) rc = make_map(&tk, k, D, (uint64_t)n_padded, (uint64_t)heads, BN);
@@ -1034,24 +1233,35 @@ extern "C" int64_t ucb_prefill_partial_bytes() {
   return (int64_t)ucb::prefill::PARTIAL_SLOT_FLOATS * (int64_t)sizeof(float);
 }
 
+namespace {
+int check_lq_common(const char* fn, const void* q, int positions, int num_q_heads, int num_kv_heads,
+                    const void* items, int num_items, const ucb_span* spans, int num_spans, int k_bits, int v_bits,
+                    int group_size, const void* out, const float* partials, const unsigned int* flags) {
+  if (!q || !items || !spans || !out) return ucb_host::set_error(UCB_ERR_INVALID, "%s: null pointer", fn);
+  if (positions <= 0 || num_items <= 0 || num_spans <= 0)
+    return ucb_host::set_error(UCB_ERR_INVALID, "%s: empty problem", fn);
+  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+    return ucb_host::set_error(UCB_ERR_INVALID, "%s: query heads must be a multiple of KV heads", fn);
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return ucb_host::set_error(UCB_ERR_INVALID, "%s: query/out must be 16-byte aligned", fn);
+  if ((k_bits != 2 && k_bits != 4) || (v_bits != 2 && v_bits != 4))
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "%s: packed spans must be 2- or 4-bit", fn);
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "%s: group_size must be 32, 64 or 128", fn);
+  if ((partials == nullptr) != (flags == nullptr))
+    return ucb_host::set_error(UCB_ERR_INVALID, "%s: partials and flags go together", fn);
+  return UCB_OK;
+}
+}  // namespace
+
 extern "C" int ucb_long_query_attention(const void* q, int positions, int num_q_heads, int num_kv_heads,
                                         const void* items, int num_items, const ucb_span* spans, int num_spans,
                                         int k_bits, int v_bits, int group_size, float softmax_scale, void* out,
                                         float* lse, float* partials, unsigned int* flags, void* stream) {
   using namespace ucb::prefill;
-  if (!q || !items || !spans || !out) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: null pointer");
-  if (positions <= 0 || num_items <= 0 || num_spans <= 0)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: empty problem");
-  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: query heads must be a multiple of KV heads");
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: query/out must be 16-byte aligned");
-  if ((k_bits != 2 && k_bits != 4) || (v_bits != 2 && v_bits != 4))
-    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_attention: packed spans must be 2- or 4-bit");
-  if (group_size != 32 && group_size != 64 && group_size != 128)
-    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_attention: group_size must be 32, 64 or 128");
-  if ((partials == nullptr) != (flags == nullptr))
-    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention: partials and flags go together");
+  const int rc = check_lq_common("ucb_long_query_attention", q, positions, num_q_heads, num_kv_heads, items,
+                                 num_items, spans, num_spans, k_bits, v_bits, group_size, out, partials, flags);
+  if (rc) return rc;
   Params P;
   P.m_rows = 0;
   P.n_tokens = 0;
@@ -1071,4 +1281,69 @@ extern "C" int ucb_long_query_attention(const void* q, int positions, int num_q_
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(nullptr, nullptr, nullptr, 0, 0, 0, P, dim3(num_items), stream);
+}
+
+
+extern "C" int ucb_long_query_stage(const ucb_span* spans, int num_spans, const void* jobs, int num_jobs,
+                                    int max_chunks, int k_bits, int v_bits, int group_size, void* k_ws,
+                                    void* vt_ws, int64_t ws_rows, void* stream) {
+  using namespace ucb::prefill;
+  if (!spans || !jobs || !k_ws || !vt_ws) return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_stage: null pointer");
+  if (num_spans <= 0 || num_jobs <= 0 || max_chunks <= 0 || num_jobs > 65535)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_stage: bad job grid");
+  if (ws_rows <= 0 || ws_rows % BN || (int64_t)max_chunks * STAGE_T > ws_rows)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_stage: ws_rows must be a positive multiple of 128 "
+                                                "covering max_chunks * 64 rows");
+  if ((reinterpret_cast<uintptr_t>(k_ws) | reinterpret_cast<uintptr_t>(vt_ws)) & 15)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_stage: workspaces must be 16-byte aligned");
+  if ((k_bits != 2 && k_bits != 4) || (v_bits != 2 && v_bits != 4))
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_stage: packed spans must be 2- or 4-bit");
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return ucb_host::set_error(UCB_ERR_UNSUPPORTED, "ucb_long_query_stage: group_size must be 32, 64 or 128");
+  const dim3 grid(max_chunks, num_jobs);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const StageJob* J = static_cast<const StageJob*>(jobs);
+  __nv_bfloat16* K = static_cast<__nv_bfloat16*>(k_ws);
+  __nv_bfloat16* VT = static_cast<__nv_bfloat16*>(vt_ws);
+  if (k_bits == 2 && v_bits == 2) stage_kernel<2, 2><<<grid, STAGE_THREADS, 0, st>>>(J, spans, group_size, K, VT, ws_rows);
+  else if (k_bits == 2) stage_kernel<2, 4><<<grid, STAGE_THREADS, 0, st>>>(J, spans, group_size, K, VT, ws_rows);
+  else if (v_bits == 2) stage_kernel<4, 2><<<grid, STAGE_THREADS, 0, st>>>(J, spans, group_size, K, VT, ws_rows);
+  else stage_kernel<4, 4><<<grid, STAGE_THREADS, 0, st>>>(J, spans, group_size, K, VT, ws_rows);
+  return ucb_host::check_launch("stage_kernel");
+}
+
+extern "C" int ucb_long_query_attention_staged(const void* q, int positions, int num_q_heads, int num_kv_heads,
+                                               const void* items, int num_items, const ucb_span* spans,
+                                               int num_spans, const void* jobs, int num_jobs, int max_chunks,
+                                               int k_bits, int v_bits, int group_size, float softmax_scale,
+                                               void* k_ws, void* vt_ws, int64_t ws_rows, void* out, float* lse,
+                                               float* partials, unsigned int* flags, void* stream) {
+  using namespace ucb::prefill;
+  int rc = check_lq_common("ucb_long_query_attention_staged", q, positions, num_q_heads, num_kv_heads, items,
+                           num_items, spans, num_spans, k_bits, v_bits, group_size, out, partials, flags);
+  if (rc) return rc;
+  if (ws_rows > (int64_t)1 << 30)
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention_staged: workspace too large");
+  rc = ucb_long_query_stage(spans, num_spans, jobs, num_jobs, max_chunks, k_bits, v_bits, group_size, k_ws, vt_ws,
+                            ws_rows, stream);
+  if (rc) return rc;
+  Params P;
+  P.m_rows = 0;
+  P.n_tokens = 0;
+  P.scale_log2 = softmax_scale * 1.4426950408889634f;
+  P.items = nullptr;
+  P.q = static_cast<const __nv_bfloat16*>(q);
+  P.hq = num_q_heads;
+  P.grp = num_q_heads / num_kv_heads;
+  P.positions = positions;
+  P.lq_items = static_cast<const LqItem*>(items);
+  P.spans = spans;
+  P.k_bits = k_bits;
+  P.v_bits = v_bits;
+  P.group = group_size;
+  P.partials = partials;
+  P.flags = flags;
+  P.out = static_cast<__nv_bfloat16*>(out);
+  P.lse = lse;
+  return launch_prefill(nullptr, k_ws, vt_ws, num_kv_heads, 0, (int)ws_rows, P, dim3(num_items), stream);
 }

@@ -1059,6 +1059,11 @@ class LongQueryTables:
     v_bits: int
     group_size: int
     slots: int                  # key-split slots (partials/flags) the items use
+    jobs: torch.Tensor | None = None  # int32 [num_jobs, 8] ucb_lq_stage_job: one per (sample, KV head) key space
+    num_jobs: int = 0
+    max_chunks: int = 0         # 64-token staging blocks of the largest key space
+    ws_rows: int = 0            # staging workspace rows per KV head (samples at 128-aligned bases)
+    row_blocks: int = 0         # row blocks (items before key splits) per key space, at most
     keepalive: list = field(default_factory=list)
 
 
@@ -1165,8 +1170,9 @@ def long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_rows: list
 
 def _build_long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_rows: list, device,
                              include_residual: bool) -> LongQueryTables:
-    all_spans, rows, cfg = [], [], None
+    all_spans, rows, jobs, cfg, base, row_blocks = [], [], [], None, 0, 0
     for segs, p0, nrows in zip(samples, pos0, q_rows):
+        extent = 0
         for h in range(num_kv_heads):
             spans, tokens, this, _ = long_query_spans(segs, num_kv_heads, h, include_residual)
             if tokens == 0:
@@ -1177,41 +1183,76 @@ def _build_long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_row
                 cfg = this
             begin = len(all_spans)
             all_spans.extend(spans)
+            padded = -(-tokens // PREFILL_KEY_TILE) * PREFILL_KEY_TILE
+            extent = max(extent, padded)
+            # staging job: this key space at workspace rows [base, base + padded) of head h
+            jobs.append([h, begin, len(spans), tokens, base, padded, 0, 0])
+            blocks = 0
             for r in range(0, nrows, PREFILL_ROWS_PER_CTA):
                 rows.append([h, r, min(PREFILL_ROWS_PER_CTA, nrows - r), 0, tokens, 0, 0, begin, len(spans),
-                             p0, 0, 0])
+                             p0, base, 0])
+                blocks += 1
+            row_blocks = max(row_blocks, blocks)
+        base += extent
     rows, slots = split_prefill_items(rows, _sm_count(torch.device(device).index))
     k_bits, v_bits, group = cfg if cfg is not None else (2, 2, 32)
     raw = _capi.struct_array_bytes(all_spans)
     # Device tables are reused while the spans (addresses, strides, lengths)
     # and items are the same, so a layer called again over the same segments
     # uploads nothing.
-    key = (torch.device(device).index, raw, tuple(tuple(r) for r in rows))
+    key = (torch.device(device).index, raw, tuple(tuple(r) for r in rows), tuple(tuple(j) for j in jobs))
     cached = _LQ_TABLES.get(key)
     if cached is None:
         spans_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
         items_dev = torch.tensor(rows, dtype=torch.int32).to(device)
+        jobs_dev = torch.tensor(jobs, dtype=torch.int32).to(device)
         if len(_LQ_TABLES) >= _LQ_TABLES_MAX:
             _LQ_TABLES.pop(next(iter(_LQ_TABLES)))
-        cached = _LQ_TABLES[key] = (spans_dev, items_dev)
+        cached = _LQ_TABLES[key] = (spans_dev, items_dev, jobs_dev)
     # The tables hold addresses only: the caller keeps the segments alive for
     # the launch, and a cached entry whose tensors were freed is never stale
     # in content, because its signature records every address it holds.
-    return LongQueryTables(cached[0], cached[1], len(all_spans), len(rows), k_bits, v_bits, group, slots)
+    max_rows = max(j[5] for j in jobs)
+    return LongQueryTables(cached[0], cached[1], len(all_spans), len(rows), k_bits, v_bits, group, slots,
+                           jobs=cached[2], num_jobs=len(jobs), max_chunks=max_rows // LQ_STAGE_TOKENS,
+                           ws_rows=base, row_blocks=row_blocks)
 
 
 _LQ_TABLES: dict = {}
 _LQ_TABLES_MAX = 64
 
 
+LQ_STAGE_TOKENS = 64          # tokens per staging block (ucb_long_query_stage)
+LQ_STAGE_MIN_ROW_BLOCKS = 2   # stage the keys when at least this many row blocks read each key space
+
+
+def long_query_stage(tables: LongQueryTables, num_kv_heads: int, device, stream=None):
+    """Gather every key space of ``tables`` into a bf16 workspace (K rows
+    [num_kv_heads, ws_rows, 128], V transposed [num_kv_heads, 128, ws_rows]):
+    dense spans copied, packed spans restored as in the kernel's tiles."""
+
+    k_ws = torch.empty((num_kv_heads, tables.ws_rows, 128), device=device, dtype=torch.bfloat16)
+    vt_ws = torch.empty((num_kv_heads, 128, tables.ws_rows), device=device, dtype=torch.bfloat16)
+    call("ucb_long_query_stage", tables.spans.data_ptr(), tables.num_spans, tables.jobs.data_ptr(), tables.num_jobs,
+         tables.max_chunks, tables.k_bits, tables.v_bits, tables.group_size, k_ws.data_ptr(), vt_ws.data_ptr(),
+         tables.ws_rows, stream if stream is not None else stream_of(k_ws))
+    return k_ws, vt_ws
+
+
 def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv_heads: int,
                          softmax_scale: float | None = None, out: torch.Tensor | None = None,
-                         lse: torch.Tensor | None = None):
+                         lse: torch.Tensor | None = None, staged: bool | None = None):
     """Non-causal attention of query [positions, Hq, 128] (bf16, the caller's
-    layout) over the spans of ``tables``, read in place (packed KIVI tiles
-    restored in shared memory): (out [positions, Hq, 128] bf16, lse
+    layout) over the spans of ``tables``: (out [positions, Hq, 128] bf16, lse
     [Hq, positions] fp32 natural log); positions no item covers are left
-    unwritten."""
+    unwritten.
+
+    ``staged=False`` reads the spans in place (packed KIVI tiles restored in
+    shared memory by every row block); ``staged=True`` first gathers each key
+    space once into a bf16 workspace (``ucb_long_query_stage``) and streams it
+    by TMA, which is faster once several row blocks read the same keys;
+    ``None`` stages when every key space has at least
+    ``LQ_STAGE_MIN_ROW_BLOCKS`` row blocks."""
 
     require_cuda(query, "query")
     if query.dtype != torch.bfloat16 or not query.is_contiguous() or query.dim() != 3 or int(query.shape[2]) != 128:
@@ -1227,6 +1268,19 @@ def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv
     partials = flags = None
     if tables.slots:
         partials, flags = prefill_split_workspace(query.device, tables.slots, stream_of(query))
+    if staged is None:
+        staged = tables.jobs is not None and tables.row_blocks >= LQ_STAGE_MIN_ROW_BLOCKS
+    if staged:
+        if tables.jobs is None:
+            raise ValueError("these tables carry no staging jobs")
+        k_ws = torch.empty((num_kv_heads, tables.ws_rows, 128), device=query.device, dtype=torch.bfloat16)
+        vt_ws = torch.empty((num_kv_heads, 128, tables.ws_rows), device=query.device, dtype=torch.bfloat16)
+        call("ucb_long_query_attention_staged", query.data_ptr(), positions, q_heads, num_kv_heads,
+             tables.items.data_ptr(), tables.num_items, tables.spans.data_ptr(), tables.num_spans,
+             tables.jobs.data_ptr(), tables.num_jobs, tables.max_chunks, tables.k_bits, tables.v_bits,
+             tables.group_size, scale, k_ws.data_ptr(), vt_ws.data_ptr(), tables.ws_rows, out.data_ptr(),
+             lse.data_ptr(), ptr(partials), ptr(flags), stream_of(query))
+        return out, lse
     call("ucb_long_query_attention", query.data_ptr(), positions, q_heads, num_kv_heads, tables.items.data_ptr(),
          tables.num_items, tables.spans.data_ptr(), tables.num_spans, tables.k_bits, tables.v_bits,
          tables.group_size, scale, out.data_ptr(), lse.data_ptr(), ptr(partials), ptr(flags), stream_of(query))
