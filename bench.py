@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--workload config2|config3|config3split]
+    python bench.py --leg long_query|config1|config5    (one secondary leg alone, for profiling)
 
 Headline (default, config 2) per GPU: 16 sequences, 28 query / 4 KV heads,
 head_dim 128, 8192 KIVI 2-bit (group 32) packed tokens + 128 bf16 residual
@@ -475,10 +476,12 @@ def long_query_leg(run: Run) -> dict:
     rows, packed VAE tokens, residual, boundary and latent rows), non-causal.
     ``us_per_layer``: the product path's launches on that segment mix with
     its span tables built (the staged form: one staging kernel, then the
-    tcgen05 kernel by TMA); ``in_place_us``: the same call reading the spans
-    in place; ``dense_operand_us``: the tcgen05 kernel alone on resident
-    dense bf16 operands of the same size; ``e2e``: the whole
-    ``long_query_attention_summary`` call.  FLOPs = 4 * Lq * Hq * D * N."""
+    tcgen05 kernel by TMA), device time of a CUDA-graph replay;
+    ``in_place_us``: the same call reading the spans in place;
+    ``dense_operand_us``: the tcgen05 kernel alone on resident dense bf16
+    operands of the same size (eager); ``e2e``: the whole
+    ``long_query_attention_summary`` call, eager (host work included).
+    FLOPs = 4 * Lq * Hq * D * N."""
 
     import torch
 
@@ -510,8 +513,12 @@ def long_query_leg(run: Run) -> dict:
         return lambda i: kernels.long_query_attention(layer.query, tables, num_kv_heads=heads, out=lq_out,
                                                       lse=lq_lse, staged=staged)
 
-    kernel_s = run.eager_seconds(product(True), reps, 3) / reps
-    in_place_s = run.eager_seconds(product(False), reps, 3) / reps
+    def graphed(fn):  # device time of `reps` calls in one CUDA graph, after eager warm-up calls
+        run.eager_seconds(fn, 1, 3)
+        return run.graph_seconds(fn, reps)[0] / reps
+
+    kernel_s = graphed(product(True))
+    in_place_s = graphed(product(False))
     e2e_s = run.eager_seconds(lambda i: long_query_attention_summary(layer.query, layer.segments,
                                                                      dense_key=layer.dense_key,
                                                                      dense_value=layer.dense_value), reps, 3) / reps
@@ -835,6 +842,10 @@ def run_split_headline(args) -> None:
     run.close()
 
 
+LEGS = {"long_query": lambda run: long_query_leg(run), "config1": lambda run: config1_leg(run),
+        "config5": lambda run: config5_leg(run)}
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -842,10 +853,16 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=16)
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    parser.add_argument("--leg", default=None, choices=sorted(LEGS),
+                        help="run one secondary leg alone on one GPU and print its JSON object (for profiling)")
     args = parser.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.leg:
+        run = Run(args)
+        print(json.dumps({args.leg: LEGS[args.leg](run)}))
+        run.close()
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "config3split":
         run_split_headline(args)

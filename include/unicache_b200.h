@@ -374,6 +374,14 @@ typedef struct ucb_lq_stage_job {
  * minimum with one rounding to bf16, the values ucb_long_query_attention
  * restores in its operand tiles.  Grid: max_chunks x num_jobs blocks of 64
  * tokens (max_chunks * 64 >= the largest `rows`; ws_rows a multiple of 128). */
+/* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
+ * NULL, later long-query and prefill launches record per CTA (global timer,
+ * ns): word 0 = kernel entry, 1 = set-up done, 2 = SM id, 3 = exit, 4 = items
+ * run, and for its first 12 items i: word 6 + 2i = the softmax warps start
+ * the item (its query rows loaded), 7 + 2i = the item's results written.
+ * NULL switches it off. */
+UCB_API int ucb_prefill_set_trace(void* trace_dev);
+
 UCB_API int ucb_long_query_stage(const ucb_span* spans_dev, int num_spans, const void* jobs_dev, int num_jobs,
                                  int max_chunks, int k_bits, int v_bits, int group_size, void* k_ws_dev,
                                  void* vt_ws_dev, int64_t ws_rows, void* stream);
@@ -383,15 +391,26 @@ UCB_API int ucb_long_query_stage(const ucb_span* spans_dev, int num_spans, const
  * same arguments and results, plus the staging jobs and workspace; each
  * item's key space starts at workspace row reserved[0] of the item (the
  * ws_row0 of its job), so items keep k_row0 relative to their key space.
- * Preferable when several row blocks read the same keys: each packed tile is
- * restored once per launch instead of once per row block. */
+ * Each packed tile is restored once per launch instead of once per row block.
+ *
+ * cta_items_dev NULL: one CTA per item, as ucb_long_query_attention.
+ * Otherwise a persistent launch of num_ctas CTAs: CTA b runs items
+ * [cta_items_dev[b], cta_items_dev[b + 1]) one after the other (int32,
+ * num_ctas + 1 entries, non-decreasing, ending at num_items), so work can be
+ * split evenly over the SMs in (row block, key tile) units.  A row block cut
+ * into pieces runs its first piece as a merge item (mode 2, listed last in
+ * its CTA) and the others as partial items (mode 1, each the first item of
+ * its CTA) in consecutive slots [slot, slot + reserved[1]) of the merge item
+ * (reserved[1] >= 1); every item settles its flags once per launch as for
+ * ucb_prefill_attention_items.  num_ctas must not exceed the number of SMs
+ * that can hold one CTA each (merge items wait for partials). */
 UCB_API int ucb_long_query_attention_staged(const void* q_dev, int positions, int num_q_heads, int num_kv_heads,
-                                            const void* items_dev, int num_items, const ucb_span* spans_dev,
-                                            int num_spans, const void* jobs_dev, int num_jobs, int max_chunks,
-                                            int k_bits, int v_bits, int group_size, float softmax_scale,
-                                            void* k_ws_dev, void* vt_ws_dev, int64_t ws_rows, void* out_dev,
-                                            float* lse_dev, float* partials_dev, unsigned int* flags_dev,
-                                            void* stream);
+                                            const void* items_dev, int num_items, const int32_t* cta_items_dev,
+                                            int num_ctas, const ucb_span* spans_dev, int num_spans,
+                                            const void* jobs_dev, int num_jobs, int max_chunks, int k_bits,
+                                            int v_bits, int group_size, float softmax_scale, void* k_ws_dev,
+                                            void* vt_ws_dev, int64_t ws_rows, void* out_dev, float* lse_dev,
+                                            float* partials_dev, unsigned int* flags_dev, void* stream);
 
 /* ---- sequence-split merge over NVLink peer memory (no counterpart in the
  * reference, which decodes one sequence on one device).  Each rank allocates

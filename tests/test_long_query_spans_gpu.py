@@ -118,11 +118,13 @@ def test_long_query_spans_match_workspace_path_and_oracle(case, staged):
     out2, lse2 = long_query_attention_summary(query, segs, staged=staged)
     torch.cuda.synchronize()
     assert torch.equal(out, out2) and torch.equal(lse, lse2)
-    # the other launch form: the same operand values in the same key order
+    # the other launch form: the same operand values in the same key order,
+    # key ranges split differently (merges round differently: bf16 ulps)
     o_out, o_lse = long_query_attention_summary(query, segs, staged=not staged)
     torch.cuda.synchronize()
-    assert float((out.float() - o_out.float()).abs().max()) <= 1e-2
-    assert float((lse - o_lse).abs().max()) <= 1e-4
+    cross = (out.float() - o_out.float()).abs()
+    assert float(cross.max()) <= 2e-2 and float(cross.mean()) <= 5e-4, (float(cross.max()), float(cross.mean()))
+    assert float((lse - o_lse).abs().max()) <= 1e-3
     assert kernels.device_status() == 0
 
 
@@ -217,4 +219,51 @@ def test_stage_workspace_is_the_single_rounding_restore(bits, group):
             assert not kh[h, base + n:base + padded].any() and not vth[h, :, base + n:base + padded].any()
         base += extent
     assert tables.ws_rows == base
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("case", range(len(LAYOUTS)))
+def test_persistent_staged_launch_matches_one_cta_per_item(case):
+    """The persistent staged launch (at most one CTA per SM, each running an
+    equal share of (row block, key tile) units, cut row blocks merged from
+    several partials) against the one-CTA-per-item staged launch and the
+    oracle; a repeated call is bitwise identical."""
+
+    need_gpu()
+    bits, group, layout, lq = LAYOUTS[case]
+    segs, keys, vals = _segments(50 + case, layout, bits, group)
+    query = make_query(lq, 28, 128, seed=60 + case, device="cuda")
+    tables = kernels.long_query_tables([segs], 4, [0], [lq * 7], "cuda")
+    assert tables.num_ctas <= torch.cuda.get_device_properties(0).multi_processor_count
+    out, lse = kernels.long_query_attention(query, tables, num_kv_heads=4, staged=True, persistent=True)
+    ref_out, ref_lse = kernels.long_query_attention(query, tables, num_kv_heads=4, staged=True, persistent=False)
+    out2, lse2 = kernels.long_query_attention(query, tables, num_kv_heads=4, staged=True, persistent=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
+    diff = (out.float() - ref_out.float()).abs()
+    assert float(diff.max()) <= 2e-2 and float(diff.mean()) <= 5e-4, (float(diff.max()), float(diff.mean()))
+    assert float((lse - ref_lse).abs().max()) <= 1e-3
+    e_out, e_lse = attention.mixed_attention(host(query), keys, vals)
+    assert_attention_close(out, e_out, what=f"persistent staged case {case}")
+    assert np.abs(host(lse) - e_lse).max() <= 2e-2
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("min_tiles", [2, 6])
+def test_persistent_staged_short_query_many_pieces(min_tiles, monkeypatch):
+    """8 query positions over a 3095-key segment mix: every row block is cut
+    into pieces of ``min_tiles`` tiles (about a dozen at 2), so each merge
+    item folds in several partials."""
+
+    need_gpu()
+    monkeypatch.setattr(kernels, "PERSIST_MIN_TILES", min_tiles)
+    segs, keys, vals = _segments(140 + min_tiles, [("h2o", 150), ("packed", 1024), ("dense", 1921)], 2, 32)
+    query = make_query(8, 28, 128, seed=141, device="cuda")
+    tables = kernels.long_query_tables([segs], 4, [0], [8 * 7], "cuda")
+    assert tables.p_slots >= 4 * (24 // min_tiles - 1)
+    out, lse = kernels.long_query_attention(query, tables, num_kv_heads=4, staged=True, persistent=True)
+    torch.cuda.synchronize()
+    e_out, e_lse = attention.mixed_attention(host(query), keys, vals)
+    assert_attention_close(out, e_out, what="persistent staged, 8 positions")
+    assert np.abs(host(lse) - e_lse).max() <= 2e-2
     assert kernels.device_status() == 0

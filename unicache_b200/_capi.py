@@ -121,11 +121,13 @@ SIGNATURES = {
     "ucb_prefill_partial_bytes": (ctypes.c_int64, []),
     "ucb_long_query_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
                                          c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ucb_prefill_set_trace": (c_int, [c_void_p]),
     "ucb_long_query_stage": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                      c_void_p, c_int64, c_void_p]),
     "ucb_long_query_attention_staged": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int,
-                                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
-                                                c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+                                                c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                                c_float, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                                c_void_p, c_void_p]),
     "ucb_peer_buffer_bytes": (ctypes.c_int64, [c_int64]),
     "ucb_peer_buffer_alloc": (c_int, [c_int64, ctypes.POINTER(c_void_p), c_void_p]),
     "ucb_peer_buffer_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),

@@ -515,6 +515,8 @@ struct Params {
   int hq, grp, positions;     // query heads, query heads per KV head, positions (lse row length)
   float* partials;        // PARTIAL_SLOT_FLOATS per slot (split row blocks), or null
   unsigned int* flags;    // one per slot, even between launches, or null
+  const int32_t* cta_items;  // caller-layout launches: CTA b runs items [cta_items[b], cta_items[b + 1]), or null
+  uint64_t* trace;           // optional: per CTA 32 words, see ucb_prefill_set_trace
   __nv_bfloat16* out;  // [heads, m_rows, D]
   float* lse;          // [heads, m_rows], may be null
   unsigned int* err;
@@ -551,11 +553,9 @@ __device__ __forceinline__ void load_q_caller(const Params& P, unsigned char* sm
     }
   }
 }
-// Threads that load Q in a caller-layout launch: the softmax warps (idle
-// until the first S tile, which needs Q) and, in a staged launch, the spare
-// warps 10 and 11.
-constexpr int SPAN_Q_THREADS = 256;
-constexpr int STAGED_Q_THREADS = 320;
+// Threads that load Q in a caller-layout launch: the softmax warps, idle
+// until the first S tile of an item, which needs Q.
+constexpr int Q_THREADS = 256;
 
 // ---------------------------------------------------------------- staging
 // A staged launch first gathers each key space (the keys of one KV head of
@@ -701,64 +701,109 @@ __global__ void __launch_bounds__(STAGE_THREADS) stage_kernel(const StageJob* __
   }
 }
 
+// One problem of a CTA, decoded from whichever table the launch uses.
+struct Item {
+  int head, m0, m_end, k0, n_tokens, mode, slot, nparts, span_begin, span_count, pos0;
+};
+
+// Item `idx` of the launch.  Segment-table and staged launches read LqItem
+// records (a staged item's key space starts at workspace row reserved[0]; a
+// merge item folds in reserved[1] partials, at least one, from slots
+// [slot, slot + reserved[1])); batched workspace launches read WorkItem
+// records; single-problem launches derive the item from the grid.
+template <bool SPANS>
+__device__ __forceinline__ Item load_item(const Params& P, bool staged, int idx, int tid) {
+  Item I;
+  I.nparts = 1;
+  I.span_begin = I.span_count = I.pos0 = 0;
+  I.mode = ITEM_FINAL;
+  I.slot = 0;
+  if (SPANS || staged) {
+    const LqItem it = P.lq_items[idx];
+    I.head = it.head;
+    I.m0 = it.q_row0;
+    I.m_end = it.q_row0 + it.q_rows;
+    I.k0 = it.k_row0 + (staged ? it.pad1 : 0);
+    I.n_tokens = it.n_tokens;
+    I.mode = it.mode;
+    I.slot = it.slot;
+    I.nparts = max(1, it.pad2);
+    I.span_begin = it.span_begin;
+    I.span_count = it.span_count;
+    I.pos0 = it.pos0;
+  } else if (P.items) {
+    const WorkItem it = P.items[idx];
+    I.head = it.head;
+    I.m0 = it.q_row0;
+    I.m_end = it.q_row0 + it.q_rows;
+    I.k0 = it.k_row0;
+    I.n_tokens = it.n_tokens;
+    I.mode = it.mode;
+    I.slot = it.slot;
+  } else {
+    I.head = blockIdx.y;
+    I.m0 = blockIdx.x * 2 * BM;
+    I.m_end = P.m_rows;
+    I.k0 = 0;
+    I.n_tokens = P.n_tokens;
+  }
+  if (I.mode != ITEM_FINAL && (!P.partials || !P.flags || I.slot < 0)) {
+    if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
+    I.mode = ITEM_FINAL;
+  }
+  return I;
+}
+
+// The flag additions an item owes each launch (a partial's own slot; a
+// merge item's partner slots), made even when the item could not run.
+__device__ __forceinline__ void settle_flags(const Params& P, const Item& I) {
+  if (I.mode == ITEM_PARTIAL) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.flags + I.slot), "r"(1u) : "memory");
+  } else if (I.mode == ITEM_MERGE) {
+    for (int k = 0; k < I.nparts; ++k)
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.flags + I.slot + k), "r"(1u) : "memory");
+  }
+}
+
 // SPANS: keys and values come from the item's spans (producer warps 8, 10,
 // 11); otherwise from the K / V^T tensor maps (loader warp 8), with the query
 // from the Q tensor map (workspace launches) or the caller's layout (staged
 // launches: P.lq_items set).
+//
+// A CTA runs the items [cta_items[b], cta_items[b + 1]) of P.cta_items one
+// after the other when that table is given (segment-table and staged
+// launches), else item blockIdx.x.  Across items the K/V ring, the S/P/O
+// hand-offs and their mbarrier phases simply continue (tile counters run
+// over the CTA's whole item list); at an item boundary the softmax warps
+// write the item's result, then load the next item's query rows, which the
+// MMA thread waits for before the next S tile.
 template <bool SPANS>
 __global__ void __launch_bounds__(THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, Params P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int head, m0, m_end, k0, n_tokens, mode = ITEM_FINAL, slot = 0, span_begin = 0, span_count = 0, pos0 = 0;
-  // A staged launch: LqItem problems in the caller's layout, keys and values
-  // by TMA from the staging workspace (the item's key space starts at its
-  // workspace row, reserved[0] of the item).
-  const bool staged = !SPANS && P.lq_items != nullptr;
-  if (SPANS || staged) {
-    const LqItem it = P.lq_items[blockIdx.x];
-    head = it.head;
-    m0 = it.q_row0;
-    m_end = it.q_row0 + it.q_rows;
-    k0 = it.k_row0;
-    n_tokens = it.n_tokens;
-    mode = it.mode;
-    slot = it.slot;
-    span_begin = it.span_begin;
-    span_count = it.span_count;
-    pos0 = it.pos0;
-    if (staged) k0 += it.pad1;
-    if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
-      if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-      mode = ITEM_FINAL;
-    }
-  } else if (P.items) {
-    const WorkItem it = P.items[blockIdx.x];
-    head = it.head;
-    m0 = it.q_row0;
-    m_end = it.q_row0 + it.q_rows;
-    k0 = it.k_row0;
-    n_tokens = it.n_tokens;
-    mode = it.mode;
-    slot = it.slot;
-    if (mode != ITEM_FINAL && (!P.partials || !P.flags || slot < 0)) {
-      if (tid == 0) atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-      mode = ITEM_FINAL;
-    }
-  } else {
-    head = blockIdx.y;
-    m0 = blockIdx.x * 2 * BM;
-    m_end = P.m_rows;
-    k0 = 0;
-    n_tokens = P.n_tokens;
+  uint64_t* trace = P.trace ? P.trace + 32 * (size_t)blockIdx.x : nullptr;
+  if (trace && tid == 0) {
+    trace[0] = global_timer_ns();
+    trace[2] = sm_id();
   }
-  const int n_tiles = (n_tokens + BN - 1) / BN;
+  // A staged launch: LqItem problems in the caller's layout, keys and values
+  // by TMA from the staging workspace.
+  const bool staged = !SPANS && P.lq_items != nullptr;
+  const bool caller_layout = SPANS || staged;
+  int ib = blockIdx.x, ie = blockIdx.x + 1;
+  if (caller_layout && P.cta_items) {
+    ib = P.cta_items[blockIdx.x];
+    ie = P.cta_items[blockIdx.x + 1];
+  }
+  const int n_items = max(0, ie - ib);
+  auto tiles_of = [](const Item& I) { return (I.n_tokens + BN - 1) / BN; };
   // The swizzled operand layout needs a 1024-byte aligned base.
   if (smem_u32(smem) & 1023) {
     if (tid == 0) {
       atomicOr(P.err, DEVERR_BAD_DESCRIPTOR);
-      if (mode != ITEM_FINAL) atomicAdd(P.flags + slot, 1u);  // keep the flag's parity rule
+      for (int it = ib; it < ie; ++it) settle_flags(P, load_item<SPANS>(P, staged, it, 1));  // keep the parity rule
     }
     return;
   }
@@ -774,10 +819,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
   __shared__ int failed;
+  __shared__ int stop_items;
 
   if (tid == 0) {
     failed = 0;
-    mbar_init(q_full, SPANS ? SPAN_Q_THREADS : (staged ? STAGED_Q_THREADS : 1));
+    stop_items = 0;
+    mbar_init(q_full, caller_layout ? Q_THREADS : 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&k_full[i], SPANS ? PRODUCERS : 1);
       mbar_init(&k_empty[i], 1);
@@ -802,90 +849,106 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (trace && tid == 0) trace[1] = global_timer_ns();
   auto fail = [&]() { atomicOr(&failed, 1); };
+  auto is_failed = [&]() { return *reinterpret_cast<volatile int*>(&failed) != 0; };
 
   if (SPANS && (warp == 8 || warp == 10 || warp == 11)) {
-    // ---------------- span producers
+    // ---------------- span producers.  Half-tiles h = 2g (K of the CTA's
+    // g-th tile) and 2g + 1 (V of it) are filled in order, each as one
+    // cp.async group; half-tile h - 1 is published (its copies waited for,
+    // proxy fence, arrive) only once half-tile h is in flight, so K and V
+    // loads overlap like TMA loads do.  A half-tile's stage is released by
+    // the MMA thread; the producer runs at most one half-tile ahead of what
+    // it has published, which is what the MMA loop needs to release that
+    // stage, so the two cannot wait on each other.
     const int pid = (warp == 8 ? 0 : warp - 9) * 32 + lane;
-    // (Q_A and Q_B are loaded by the softmax warps.)  Half-tiles h = 2j (K of tile j) and 2j + 1 (V of tile j) are filled in
-    // order, each as one cp.async group; half-tile h - 1 is published (its
-    // copies waited for, proxy fence, arrive) only once half-tile h is in
-    // flight, so K and V loads overlap like TMA loads do.  A half-tile's
-    // stage is released by the MMA thread; the producer runs at most one
-    // half-tile ahead of what it has published, which is what the MMA loop
-    // needs to release that stage, so the two cannot wait on each other.
-    const ucb_span* spans = P.spans + span_begin;
     auto publish = [&](int h) {
       fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
       mbar_arrive((h & 1) ? &v_full[(h >> 1) % STAGES] : &k_full[(h >> 1) % STAGES]);
     };
-    int filled = 0;
-    for (int h = 0; h < 2 * n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++h) {
-      const int j = h >> 1, st = j % STAGES;
-      const bool keys = (h & 1) == 0;
-      if (j >= STAGES && !mbar_wait_for(keys ? &k_empty[st] : &v_empty[st], ((j / STAGES) - 1) & 1, WAIT_NS)) {
-        fail();
-        break;
+    int filled = 0, g0 = 0;
+    bool ok = true;
+    for (int it = ib; it < ie && ok; ++it) {
+      const Item I = load_item<SPANS>(P, staged, it, tid);
+      const ucb_span* spans = P.spans + I.span_begin;
+      const int nt = tiles_of(I);
+      for (int h = 2 * g0; h < 2 * (g0 + nt); ++h) {
+        if (is_failed()) {
+          ok = false;
+          break;
+        }
+        const int g = h >> 1, j = g - g0, st = g % STAGES;
+        const bool keys = (h & 1) == 0;
+        if (g >= STAGES && !mbar_wait_for(keys ? &k_empty[st] : &v_empty[st], ((g / STAGES) - 1) & 1, WAIT_NS)) {
+          fail();
+          ok = false;
+          break;
+        }
+        const int tok0 = I.k0 + j * BN, valid = min(BN, I.n_tokens - j * BN);
+        fill_tile(keys, spans, I.span_count, tok0, valid, P.k_bits, P.v_bits, P.group,
+                  smem + (keys ? OFF_K + st * KTILE : OFF_V + st * VTILE), pid);
+        cp_async_commit();
+        filled = h + 1;
+        if (h > 0) {
+          cp_async_wait_one();  // every group but the newest (half-tile h) has landed
+          publish(h - 1);
+        }
       }
-      const int tok0 = k0 + j * BN, valid = min(BN, n_tokens - j * BN);
-      fill_tile(keys, spans, span_count, tok0, valid, P.k_bits, P.v_bits, P.group,
-                smem + (keys ? OFF_K + st * KTILE : OFF_V + st * VTILE), pid);
-      cp_async_commit();
-      filled = h + 1;
-      if (h > 0) {
-        cp_async_wait_one();  // every group but the newest (half-tile h) has landed
-        publish(h - 1);
-      }
+      g0 += nt;
     }
     cp_async_wait_all();
     if (filled > 0) publish(filled - 1);
-  } else if (staged && (warp == 10 || warp == 11)) {
-    // ---------------- caller-layout Q of a staged launch (with the softmax warps)
-    load_q_caller(P, smem, m0, m_end, pos0, head, SPAN_Q_THREADS + (warp - 10) * 32 + lane, STAGED_Q_THREADS);
-    cp_async_wait_all();
-    fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
-    mbar_arrive(q_full);
   } else if (!SPANS && warp == 8) {
     // ---------------- loader
     if (lane == 0) {
-      if (!staged) {
-        mbar_arrive_expect_tx(q_full, 2 * QTILE);
-        for (int x = 0; x < 2; ++x) {
-          tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, m0 + x * BM, head, q_full);
-          tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, m0 + x * BM, head, q_full);
+      int issued = 0, g = 0;
+      bool ok = true;
+      for (int it = ib; it < ie && ok; ++it) {
+        const Item I = load_item<SPANS>(P, staged, it, tid);
+        if (!staged) {  // workspace launches run one item
+          mbar_arrive_expect_tx(q_full, 2 * QTILE);
+          for (int x = 0; x < 2; ++x) {
+            tma_load_3d(smem + OFF_Q + x * QTILE, &tm_q, 0, I.m0 + x * BM, I.head, q_full);
+            tma_load_3d(smem + OFF_Q + x * QTILE + QHALF, &tm_q, 64, I.m0 + x * BM, I.head, q_full);
+          }
         }
-      }
-      int issued = 0;
-      for (int j = 0; j < n_tiles && !*reinterpret_cast<volatile int*>(&failed); ++j) {
-        const int st = j % STAGES;
-        const uint32_t ph = ((j / STAGES) - 1) & 1;
-        if (j >= STAGES && (!mbar_wait_for(&k_empty[st], ph, WAIT_NS) || !mbar_wait_for(&v_empty[st], ph, WAIT_NS))) {
-          fail();
-          break;
+        const int nt = tiles_of(I);
+        for (int j = 0; j < nt; ++j, ++g) {
+          const int st = g % STAGES;
+          const uint32_t ph = ((g / STAGES) - 1) & 1;
+          if (is_failed() ||
+              (g >= STAGES && (!mbar_wait_for(&k_empty[st], ph, WAIT_NS) || !mbar_wait_for(&v_empty[st], ph, WAIT_NS)))) {
+            fail();
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[st], KTILE);
+          tma_load_3d(smem + OFF_K + st * KTILE, &tm_k, 0, I.k0 + j * BN, I.head, &k_full[st]);
+          tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, I.k0 + j * BN, I.head, &k_full[st]);
+          mbar_arrive_expect_tx(&v_full[st], VTILE);
+          tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, I.k0 + j * BN, 0, I.head, &v_full[st]);
+          tma_load_3d(smem + OFF_V + st * VTILE + VHALF, &tm_v, I.k0 + j * BN + 64, 0, I.head, &v_full[st]);
+          issued = g + 1;
         }
-        mbar_arrive_expect_tx(&k_full[st], KTILE);
-        tma_load_3d(smem + OFF_K + st * KTILE, &tm_k, 0, k0 + j * BN, head, &k_full[st]);
-        tma_load_3d(smem + OFF_K + st * KTILE + KHALF, &tm_k, 64, k0 + j * BN, head, &k_full[st]);
-        mbar_arrive_expect_tx(&v_full[st], VTILE);
-        tma_load_3d(smem + OFF_V + st * VTILE, &tm_v, k0 + j * BN, 0, head, &v_full[st]);
-        tma_load_3d(smem + OFF_V + st * VTILE + VHALF, &tm_v, k0 + j * BN + 64, 0, head, &v_full[st]);
-        issued = j + 1;
+        if (!staged) break;
       }
       // Copies still in flight must land before the shared memory is released.
-      mbar_wait_for(q_full, 0, WAIT_NS);
+      if (!staged) mbar_wait_for(q_full, 0, WAIT_NS);
       for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j) {
         mbar_wait_for(&k_full[j % STAGES], (j / STAGES) & 1, WAIT_NS);
         mbar_wait_for(&v_full[j % STAGES], (j / STAGES) & 1, WAIT_NS);
       }
     }
   } else if (warp == 9) {
-    // ---------------- MMA issuer.  Order on the tensor core: S_A(0) S_B(0) |
-    // PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ..., so that while one tile's
-    // softmax runs the other tile's products are in flight.
+    // ---------------- MMA issuer.  Order on the tensor core per item: S_A(0)
+    // S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ..., so that while one
+    // tile's softmax runs the other tile's products are in flight.  g counts
+    // the CTA's tiles over all its items (ring stages and phases).
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(smem + OFF_Q);
-      auto issue_s = [&](int j, int x) {
-        const uint32_t k_addr = smem_u32(smem + OFF_K + (j % STAGES) * KTILE);
+      auto issue_s = [&](int g, int x) {
+        const uint32_t k_addr = smem_u32(smem + OFF_K + (g % STAGES) * KTILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t col = (kk & 3) * 32;
@@ -894,8 +957,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&s_full[x]);
       };
-      auto issue_pv = [&](int j, int x) {
-        const uint32_t v_addr = smem_u32(smem + OFF_V + (j % STAGES) * VTILE);
+      auto issue_pv = [&](int g, int j, int x) {
+        const uint32_t v_addr = smem_u32(smem + OFF_V + (g % STAGES) * VTILE);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {  // P_x: 8 TMEM columns (16 tokens) per step
           if constexpr (SPANS)  // V rows = tokens: 16 tokens = two 8-row groups = 2048 bytes
@@ -907,35 +970,42 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&o_done[x]);
       };
-      bool ok = mbar_wait_for(q_full, 0, WAIT_NS) && mbar_wait_for(&k_full[0], 0, WAIT_NS);
-      if (ok) {
+      bool ok = true;
+      int g = 0;
+      for (int it = ib, n = 0; it < ie && ok; ++it, ++n) {
+        const Item I = load_item<SPANS>(P, staged, it, tid);
+        const int nt = tiles_of(I);
+        ok = mbar_wait_for(q_full, n & 1, WAIT_NS) &&
+             (nt == 0 || mbar_wait_for(&k_full[g % STAGES], (g / STAGES) & 1, WAIT_NS));
+        if (!ok || nt == 0) continue;
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(0, 1);
-        tc_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % STAGES, st1 = (j + 1) % STAGES;
-        const bool more = j + 1 < n_tiles;
-        ok = mbar_wait_for(&v_full[st], (j / STAGES) & 1, WAIT_NS) && mbar_wait_for(&p_full[0], j & 1, WAIT_NS);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(j, 0);
-        if (more) {
-          ok = mbar_wait_for(&k_full[st1], ((j + 1) / STAGES) & 1, WAIT_NS);
+        issue_s(g, 0);
+        issue_s(g, 1);
+        tc_commit(&k_empty[g % STAGES]);
+        for (int j = 0; j < nt && ok; ++j) {
+          const int gj = g + j, st = gj % STAGES, st1 = (gj + 1) % STAGES;
+          const bool more = j + 1 < nt;
+          ok = mbar_wait_for(&v_full[st], (gj / STAGES) & 1, WAIT_NS) && mbar_wait_for(&p_full[0], gj & 1, WAIT_NS);
           if (!ok) break;
           tc_fence_after();
-          issue_s(j + 1, 0);
+          issue_pv(gj, j, 0);
+          if (more) {
+            ok = mbar_wait_for(&k_full[st1], ((gj + 1) / STAGES) & 1, WAIT_NS);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(gj + 1, 0);
+          }
+          ok = mbar_wait_for(&p_full[1], gj & 1, WAIT_NS);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(gj, j, 1);
+          tc_commit(&v_empty[st]);
+          if (more) {
+            issue_s(gj + 1, 1);
+            tc_commit(&k_empty[st1]);
+          }
         }
-        ok = mbar_wait_for(&p_full[1], j & 1, WAIT_NS);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(j, 1);
-        tc_commit(&v_empty[st]);
-        if (more) {
-          issue_s(j + 1, 1);
-          tc_commit(&k_empty[st1]);
-        }
+        g += nt;
       }
       if (!ok) fail();
       // Everything issued has finished before TMEM can be released.
@@ -944,144 +1014,187 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp < 8) {
     // ---------------- softmax warpgroups
-    if (SPANS || staged) {
-      // caller-layout Q_A and Q_B (the first S tile waits for them anyway)
-      load_q_caller(P, smem, m0, m_end, pos0, head, tid, SPANS ? SPAN_Q_THREADS : STAGED_Q_THREADS);
-      cp_async_wait_all();
-      fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
-      mbar_arrive(q_full);
-    }
     const int x = warp >> 2;             // tile
     const int row = tid & (BM - 1);      // query row in the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t t_s = tmem + S_COL + 128 * x + lane_off, t_o = tmem + O_COL + 128 * x + lane_off;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      ok = mbar_wait_for(&s_full[x], j & 1, WAIT_NS);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      const int valid = min(BN, n_tokens - j * BN);
-      const float mx = (valid < BN ? row_max<true>(t_s, valid) : row_max<false>(t_s, valid)) * P.scale_log2;
-      // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
-      if (j > 0) {
-        ok = mbar_wait_for(&o_done[x], (j - 1) & 1, WAIT_NS);
+    const int r_blk = x * BM + row;  // row within the item's 2*BM-row block
+    int g = 0, it = ib;
+    for (; it < ie; ++it) {
+      const Item I = load_item<SPANS>(P, staged, it, tid);
+      const int nt = tiles_of(I);
+      if (caller_layout) {
+        // caller-layout Q_A and Q_B of this item: every tensor-core operation
+        // of the previous item has completed (its last O hand-off was
+        // waited for), so the Q tiles are free
+        load_q_caller(P, smem, I.m0, I.m_end, I.pos0, I.head, tid, Q_THREADS);
+        cp_async_wait_all();
+        fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
+        mbar_arrive(q_full);
+      }
+      if (trace && tid == 0 && it - ib < 12) trace[6 + 2 * (it - ib)] = global_timer_ns();
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nt; ++j) {
+        const int gj = g + j;
+        ok = mbar_wait_for(&s_full[x], gj & 1, WAIT_NS);
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
-      }
-      const bool move = mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
-      if (__any_sync(0xffffffffu, move)) {
-        const float m_new = move ? fmaxf(mx, m_run) : m_run;
-        const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+        const int valid = min(BN, I.n_tokens - j * BN);
+        const float mx = (valid < BN ? row_max<true>(t_s, valid) : row_max<false>(t_s, valid)) * P.scale_log2;
+        // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
         if (j > 0) {
+          ok = mbar_wait_for(&o_done[x], (gj - 1) & 1, WAIT_NS);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          tc_fence_after();
+        }
+        const bool move = mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY;
+        if (__any_sync(0xffffffffu, move)) {
+          const float m_new = move ? fmaxf(mx, m_run) : m_run;
+          const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+          if (j > 0) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ov[32];
-            tc_ld32(t_o + 32 * c, ov);
-            tc_wait_ld();
+            for (int c = 0; c < 4; ++c) {
+              uint32_t ov[32];
+              tc_ld32(t_o + 32 * c, ov);
+              tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float2 v = __fmul2_rn(make_float2(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])),
-                                          make_float2(alpha, alpha));
-              ov[i] = __float_as_uint(v.x);
-              ov[i + 1] = __float_as_uint(v.y);
+              for (int i = 0; i < 32; i += 2) {
+                const float2 v = __fmul2_rn(make_float2(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])),
+                                            make_float2(alpha, alpha));
+                ov[i] = __float_as_uint(v.x);
+                ov[i + 1] = __float_as_uint(v.y);
+              }
+              tc_st32(t_o + 32 * c, ov);
             }
-            tc_st32(t_o + 32 * c, ov);
+            tc_wait_st();
           }
-          tc_wait_st();
+          l_run *= alpha;
+          m_run = m_new;
         }
-        l_run *= alpha;
-        m_run = m_new;
+        l_run += valid < BN ? write_p<true>(t_s, valid, P.scale_log2, -m_run)
+                            : write_p<false>(t_s, valid, P.scale_log2, -m_run);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
       }
-      l_run += valid < BN ? write_p<true>(t_s, valid, P.scale_log2, -m_run)
-                          : write_p<false>(t_s, valid, P.scale_log2, -m_run);
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[x]);
+      if (ok && nt > 0) ok = mbar_wait_for(&o_done[x], (g + nt - 1) & 1, WAIT_NS);
+      tc_fence_after();
+      const bool good = __all_sync(0xffffffffu, ok);
+      const int m = I.m0 + r_blk;
+      const bool live = m < I.m_end;
+      bool merged = false;
+      if (!good) {
+        if (lane == 0) fail();
+      } else if (nt == 0) {
+        // an item without keys writes nothing (the host never builds one)
+      } else if (I.mode == ITEM_PARTIAL) {
+        float* part = P.partials + (int64_t)I.slot * PARTIAL_SLOT_FLOATS;
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tc_ld32(t_o + 32 * c, ov);
+          tc_wait_ld();
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) part[(32 * c + i) * (2 * BM) + r_blk] = __uint_as_float(ov[i]) * inv;
+          }
+        }
+        if (live) part[D * 2 * BM + r_blk] = m_run + __log2f(l_run);
+        __threadfence();
+      } else {
+        // ITEM_FINAL, or ITEM_MERGE: fold in the partners' rows once published.
+        float w_own = 1.f, lse2 = m_run + __log2f(l_run), mx = lse2, inv_sum = 1.f;
+        if (I.mode == ITEM_MERGE) {
+          bool all_in = true;
+          for (int k = 0; k < I.nparts; ++k) all_in = all_in && wait_flag(P.flags + I.slot + k, WAIT_NS);
+          merged = __all_sync(0xffffffffu, all_in);
+          if (!merged) {
+            if (lane == 0) fail();
+          } else if (live) {
+            for (int k = 0; k < I.nparts; ++k)
+              mx = fmaxf(mx, __ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk));
+            float sum = fast_exp2(lse2 - mx);
+            for (int k = 0; k < I.nparts; ++k)
+              sum += fast_exp2(__ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk) - mx);
+            inv_sum = 1.f / sum;
+            w_own = fast_exp2(lse2 - mx) * inv_sum;
+            lse2 = mx + __log2f(sum);
+          }
+        }
+        const float inv = w_own / l_run;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tc_ld32(t_o + 32 * c, ov);
+          tc_wait_ld();
+          if (live) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[i]) * inv;
+            if (merged) {
+#pragma unroll 2
+              for (int k = 0; k < I.nparts; ++k) {
+                const float* part = P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS;
+                const float wp = fast_exp2(__ldcg(part + D * 2 * BM + r_blk) - mx) * inv_sum;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = fmaf(wp, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
+              }
+            }
+            __nv_bfloat16* dst =
+                caller_layout
+                    ? P.out + ((int64_t)(I.pos0 + m / P.grp) * P.hq + I.head * P.grp + m % P.grp) * D + 32 * c
+                    : P.out + ((int64_t)I.head * P.m_rows + m) * D + 32 * c;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w4;
+              w4.x = pack_bf16x2(v[i], v[i + 1]);
+              w4.y = pack_bf16x2(v[i + 2], v[i + 3]);
+              w4.z = pack_bf16x2(v[i + 4], v[i + 5]);
+              w4.w = pack_bf16x2(v[i + 6], v[i + 7]);
+              *reinterpret_cast<uint4*>(dst + i) = w4;
+            }
+          }
+        }
+        if (live && P.lse) {
+          const int64_t at = caller_layout
+                                 ? (int64_t)(I.head * P.grp + m % P.grp) * P.positions + I.pos0 + m / P.grp
+                                 : (int64_t)I.head * P.m_rows + m;
+          P.lse[at] = lse2 * 0.6931471805599453f;
+        }
+      }
+      // The softmax warps meet once per item: a partial is published after
+      // every row is written; consumed partials' flags advance after every
+      // row is read.  A failed item still settles its flags (its CTA has set
+      // the error word), so the parity stays in step.
+      // After a failure anywhere in the CTA every softmax warp stops at the
+      // same item (thread 0's reading of the failure word, shared between
+      // two barriers), so no warp waits at a barrier the others have left.
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (tid == 0) {
+        settle_flags(P, I);
+        stop_items = is_failed() ? 1 : 0;
+        if (trace && it - ib < 12) trace[6 + 2 * (it - ib) + 1] = global_timer_ns();
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      g += nt;
+      if (stop_items) {
+        ++it;
+        break;
+      }
     }
-    if (ok && n_tiles > 0) ok = mbar_wait_for(&o_done[x], (n_tiles - 1) & 1, WAIT_NS);
-    tc_fence_after();
-    const bool good = __all_sync(0xffffffffu, ok);
-    const int r_blk = x * BM + row;  // row within the item's 2*BM-row block
-    const int m = m0 + r_blk;
-    float* part = P.partials + (int64_t)slot * PARTIAL_SLOT_FLOATS;
-    bool merged = false;
-    if (!good) {
-      if (lane == 0) fail();
-    } else if (mode == ITEM_PARTIAL) {
-      const float inv = 1.f / l_run;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tc_ld32(t_o + 32 * c, ov);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) part[(32 * c + i) * (2 * BM) + r_blk] = __uint_as_float(ov[i]) * inv;
-      }
-      part[D * 2 * BM + r_blk] = m_run + __log2f(l_run);
-      __threadfence();
-    } else {
-      // ITEM_FINAL, or ITEM_MERGE: fold in the partner's rows once published.
-      float w_own = 1.f, w_p = 0.f, lse2 = m_run + __log2f(l_run);
-      if (mode == ITEM_MERGE) {
-        merged = __all_sync(0xffffffffu, wait_flag(P.flags + slot, WAIT_NS));
-        if (!merged) {
-          if (lane == 0) fail();
-        } else {
-          const float lp = __ldcg(part + D * 2 * BM + r_blk);
-          const float mx = fmaxf(lse2, lp);
-          w_own = fast_exp2(lse2 - mx);
-          w_p = fast_exp2(lp - mx);
-          const float sum = w_own + w_p;
-          lse2 = mx + __log2f(sum);
-          w_own /= sum;
-          w_p /= sum;
-        }
-      }
-      const float inv = w_own / l_run;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tc_ld32(t_o + 32 * c, ov);
-        tc_wait_ld();
-        if (m < m_end) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = __uint_as_float(ov[i]) * inv;
-            if (merged) v[i] = fmaf(w_p, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
-          }
-          __nv_bfloat16* dst =
-              (SPANS || staged) ? P.out + ((int64_t)(pos0 + m / P.grp) * P.hq + head * P.grp + m % P.grp) * D + 32 * c
-                    : P.out + ((int64_t)head * P.m_rows + m) * D + 32 * c;
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w4;
-            w4.x = pack_bf16x2(v[i], v[i + 1]);
-            w4.y = pack_bf16x2(v[i + 2], v[i + 3]);
-            w4.z = pack_bf16x2(v[i + 4], v[i + 5]);
-            w4.w = pack_bf16x2(v[i + 6], v[i + 7]);
-            *reinterpret_cast<uint4*>(dst + i) = w4;
-          }
-        }
-      }
-      if (m < m_end && P.lse) {
-        const int64_t at = (SPANS || staged) ? (int64_t)(head * P.grp + m % P.grp) * P.positions + pos0 + m / P.grp
-                                 : (int64_t)head * P.m_rows + m;
-        P.lse[at] = lse2 * 0.6931471805599453f;
-      }
-    }
-    // The softmax warps meet once: a partial is published after every row
-    // is written; a consumed partial's flag advances after every row read.
-    // A failed partial still publishes (its CTA has set the error word), so
-    // the parity stays in step.
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (tid == 0 && mode != ITEM_FINAL)
-      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.flags + slot), "r"(1u) : "memory");
+    // items this CTA could not reach after a failure still settle their flags
+    if (tid == 0)
+      for (; it < ie; ++it) settle_flags(P, load_item<SPANS>(P, staged, it, 1));
   }
   tc_fence_before();
   __syncthreads();
   if (failed && tid == 0) atomicOr(P.err, DEVERR_MBAR_TIMEOUT);
+  if (trace && tid == 0) {
+    trace[3] = global_timer_ns();
+    trace[4] = (uint64_t)n_items;
+  }
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
@@ -1117,6 +1230,15 @@ int make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_
 
 }  // namespace prefill
 }  // namespace ucb
+
+namespace {
+uint64_t* g_prefill_trace = nullptr;  // diagnostics only; see ucb_prefill_set_trace
+}  // namespace
+
+extern "C" int ucb_prefill_set_trace(void* trace_dev) {
+  g_prefill_trace = static_cast<uint64_t*>(trace_dev);
+  return UCB_OK;
+}
 
 namespace {
 // q == k == vt == nullptr: a segment-table launch (keys and values from
@@ -1160,6 +1282,7 @@ int launch_prefill(const void* q, const void* k, const void* vt, int heads, int 
     if (dev >= 0 && dev < 64) configured[spans][dev] = true;
   }
   P.err = err;
+  P.trace = g_prefill_trace;
   if (spans)
     prefill_kernel<true><<<grid, THREADS, SMEM, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, P);
   else
@@ -1189,6 +1312,7 @@ extern "C" int ucb_prefill_attention(const void* q, const void* k, const void* v
   P.hq = P.grp = P.positions = 0;
   P.partials = nullptr;
   P.flags = nullptr;
+  P.cta_items = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3((m_rows + 2 * BM - 1) / (2 * BM), heads), stream);
@@ -1217,6 +1341,7 @@ extern "C" int ucb_prefill_attention_items(const void* q, const void* k, const v
   P.hq = P.grp = P.positions = 0;
   P.partials = partials;
   P.flags = flags;
+  P.cta_items = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(q, k, vt, heads, m_rows, n_padded, P, dim3(num_items), stream);
@@ -1278,6 +1403,7 @@ extern "C" int ucb_long_query_attention(const void* q, int positions, int num_q_
   P.group = group_size;
   P.partials = partials;
   P.flags = flags;
+  P.cta_items = nullptr;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
   return launch_prefill(nullptr, nullptr, nullptr, 0, 0, 0, P, dim3(num_items), stream);
@@ -1313,17 +1439,20 @@ extern "C" int ucb_long_query_stage(const ucb_span* spans, int num_spans, const 
 }
 
 extern "C" int ucb_long_query_attention_staged(const void* q, int positions, int num_q_heads, int num_kv_heads,
-                                               const void* items, int num_items, const ucb_span* spans,
-                                               int num_spans, const void* jobs, int num_jobs, int max_chunks,
-                                               int k_bits, int v_bits, int group_size, float softmax_scale,
-                                               void* k_ws, void* vt_ws, int64_t ws_rows, void* out, float* lse,
-                                               float* partials, unsigned int* flags, void* stream) {
+                                               const void* items, int num_items, const int32_t* cta_items,
+                                               int num_ctas, const ucb_span* spans, int num_spans, const void* jobs,
+                                               int num_jobs, int max_chunks, int k_bits, int v_bits,
+                                               int group_size, float softmax_scale, void* k_ws, void* vt_ws,
+                                               int64_t ws_rows, void* out, float* lse, float* partials,
+                                               unsigned int* flags, void* stream) {
   using namespace ucb::prefill;
   int rc = check_lq_common("ucb_long_query_attention_staged", q, positions, num_q_heads, num_kv_heads, items,
                            num_items, spans, num_spans, k_bits, v_bits, group_size, out, partials, flags);
   if (rc) return rc;
   if (ws_rows > (int64_t)1 << 30)
     return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention_staged: workspace too large");
+  if (cta_items && (num_ctas <= 0 || num_ctas > num_items))
+    return ucb_host::set_error(UCB_ERR_INVALID, "ucb_long_query_attention_staged: num_ctas must be in [1, num_items]");
   rc = ucb_long_query_stage(spans, num_spans, jobs, num_jobs, max_chunks, k_bits, v_bits, group_size, k_ws, vt_ws,
                             ws_rows, stream);
   if (rc) return rc;
@@ -1343,7 +1472,8 @@ extern "C" int ucb_long_query_attention_staged(const void* q, int positions, int
   P.group = group_size;
   P.partials = partials;
   P.flags = flags;
+  P.cta_items = cta_items;
   P.out = static_cast<__nv_bfloat16*>(out);
   P.lse = lse;
-  return launch_prefill(nullptr, k_ws, vt_ws, num_kv_heads, 0, (int)ws_rows, P, dim3(num_items), stream);
+  return launch_prefill(nullptr, k_ws, vt_ws, num_kv_heads, 0, (int)ws_rows, P, dim3(cta_items ? num_ctas : num_items), stream);
 }

@@ -947,6 +947,66 @@ def split_prefill_items(items: list, sms: int) -> tuple[list, int]:
     return merges + whole + partials, len(merges)
 
 
+PERSIST_MIN_TILES = 6  # smallest share of key tiles a persistent CTA is given (fewer, larger pieces:
+#                        a merge item folds its partials in with chains of L2 loads)
+
+
+def plan_stream_k(blocks: list, sms: int, min_tiles: int = PERSIST_MIN_TILES) -> tuple[list, list, int]:
+    """Split the (row block, key tile) units of ``blocks`` (segment-table
+    item rows, one per row block: head, q_row0, q_rows, k_row0 = 0, n_tokens,
+    0, 0, span_begin, span_count, pos0, ws_row0, 0) into at most ``sms``
+    contiguous ranges of equal size, one per persistent CTA.  A row block
+    that a range boundary cuts becomes pieces: its first piece a merge item
+    (mode 2; the last item of its CTA) folding in the others, partial items
+    (mode 1; each the first item of its CTA) in consecutive slots [slot, slot
+    + reserved[1]).  Returns (item rows, cta_items offsets, slots)."""
+
+    tiles = [-(-int(b[4]) // PREFILL_KEY_TILE) for b in blocks]
+    total = sum(tiles)
+    if total == 0:
+        raise ValueError("every row block needs at least one key")
+    ctas = max(1, min(sms, total // max(1, min_tiles)))
+    cuts = [(c * total) // ctas for c in range(ctas + 1)]
+    starts, acc = [], 0
+    for t in tiles:
+        starts.append(acc)
+        acc += t
+    pieces = [[] for _ in blocks]      # per block: [item index, tile_begin, tile_end]
+    order = []                         # item index -> (block, piece number)
+    offsets = [0]
+    b = 0
+    for c in range(ctas):
+        lo, hi = cuts[c], cuts[c + 1]
+        while b < len(blocks) and starts[b] + tiles[b] <= lo:
+            b += 1
+        bb = b
+        while bb < len(blocks) and starts[bb] < hi:
+            t0, t1 = max(lo, starts[bb]) - starts[bb], min(hi, starts[bb] + tiles[bb]) - starts[bb]
+            if t1 > t0:
+                pieces[bb].append([len(order), t0, t1])
+                order.append((bb, len(pieces[bb]) - 1))
+            bb += 1
+        offsets.append(len(order))
+    rows, slots = [None] * len(order), 0
+    for bi, plist in enumerate(pieces):
+        blk = [int(x) for x in blocks[bi]]
+        tokens = blk[4]
+        first_slot = slots
+        if len(plist) > 1:
+            slots += len(plist) - 1
+        for pi, (idx, t0, t1) in enumerate(plist):
+            k0 = t0 * PREFILL_KEY_TILE
+            n = min(tokens, t1 * PREFILL_KEY_TILE) - k0
+            if len(plist) == 1:
+                mode, slot, nparts = 0, 0, 0
+            elif pi == 0:
+                mode, slot, nparts = 2, first_slot, len(plist) - 1
+            else:
+                mode, slot, nparts = 1, first_slot + pi - 1, 0
+            rows[idx] = blk[:3] + [k0, n, mode, slot] + blk[7:11] + [nparts]
+    return rows, offsets, slots
+
+
 _SPLIT_WORKSPACES: dict = {}
 _RETIRED_WORKSPACES: list = []  # outgrown workspaces stay alive: a captured CUDA graph may still use them
 
@@ -1060,6 +1120,11 @@ class LongQueryTables:
     group_size: int
     slots: int                  # key-split slots (partials/flags) the items use
     jobs: torch.Tensor | None = None  # int32 [num_jobs, 8] ucb_lq_stage_job: one per (sample, KV head) key space
+    p_items: torch.Tensor | None = None  # persistent staged launch: item rows (plan_stream_k)
+    p_ctas: torch.Tensor | None = None   # int32 [num_ctas + 1] item offsets per CTA
+    num_p_items: int = 0
+    num_ctas: int = 0
+    p_slots: int = 0
     num_jobs: int = 0
     max_chunks: int = 0         # 64-token staging blocks of the largest key space
     ws_rows: int = 0            # staging workspace rows per KV head (samples at 128-aligned bases)
@@ -1194,28 +1259,34 @@ def _build_long_query_tables(samples: list, num_kv_heads: int, pos0: list, q_row
                 blocks += 1
             row_blocks = max(row_blocks, blocks)
         base += extent
-    rows, slots = split_prefill_items(rows, _sm_count(torch.device(device).index))
+    sms = _sm_count(torch.device(device).index)
+    p_rows, p_offsets, p_slots = plan_stream_k(rows, sms, PERSIST_MIN_TILES)
+    rows, slots = split_prefill_items(rows, sms)
     k_bits, v_bits, group = cfg if cfg is not None else (2, 2, 32)
     raw = _capi.struct_array_bytes(all_spans)
     # Device tables are reused while the spans (addresses, strides, lengths)
     # and items are the same, so a layer called again over the same segments
     # uploads nothing.
-    key = (torch.device(device).index, raw, tuple(tuple(r) for r in rows), tuple(tuple(j) for j in jobs))
+    key = (torch.device(device).index, raw, tuple(tuple(r) for r in rows), tuple(tuple(j) for j in jobs),
+           tuple(tuple(r) for r in p_rows), tuple(p_offsets))
     cached = _LQ_TABLES.get(key)
     if cached is None:
         spans_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
         items_dev = torch.tensor(rows, dtype=torch.int32).to(device)
         jobs_dev = torch.tensor(jobs, dtype=torch.int32).to(device)
+        p_items_dev = torch.tensor(p_rows, dtype=torch.int32).to(device)
+        p_ctas_dev = torch.tensor(p_offsets, dtype=torch.int32).to(device)
         if len(_LQ_TABLES) >= _LQ_TABLES_MAX:
             _LQ_TABLES.pop(next(iter(_LQ_TABLES)))
-        cached = _LQ_TABLES[key] = (spans_dev, items_dev, jobs_dev)
+        cached = _LQ_TABLES[key] = (spans_dev, items_dev, jobs_dev, p_items_dev, p_ctas_dev)
     # The tables hold addresses only: the caller keeps the segments alive for
     # the launch, and a cached entry whose tensors were freed is never stale
     # in content, because its signature records every address it holds.
     max_rows = max(j[5] for j in jobs)
     return LongQueryTables(cached[0], cached[1], len(all_spans), len(rows), k_bits, v_bits, group, slots,
                            jobs=cached[2], num_jobs=len(jobs), max_chunks=max_rows // LQ_STAGE_TOKENS,
-                           ws_rows=base, row_blocks=row_blocks)
+                           ws_rows=base, row_blocks=row_blocks, p_items=cached[3], p_ctas=cached[4],
+                           num_p_items=len(p_rows), num_ctas=len(p_offsets) - 1, p_slots=p_slots)
 
 
 _LQ_TABLES: dict = {}
@@ -1223,7 +1294,9 @@ _LQ_TABLES_MAX = 64
 
 
 LQ_STAGE_TOKENS = 64          # tokens per staging block (ucb_long_query_stage)
-LQ_STAGE_MIN_ROW_BLOCKS = 2   # stage the keys when at least this many row blocks read each key space
+LQ_STAGE_MIN_ROW_BLOCKS = 1   # stage the keys when at least this many row blocks read each key space
+# (measured on the configuration-4 segment mix, CUDA graphs: staged 45-70 us
+# against 64-100 us in place from 8 to 1024 query positions, so always)
 
 
 def long_query_stage(tables: LongQueryTables, num_kv_heads: int, device, stream=None):
@@ -1241,7 +1314,8 @@ def long_query_stage(tables: LongQueryTables, num_kv_heads: int, device, stream=
 
 def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv_heads: int,
                          softmax_scale: float | None = None, out: torch.Tensor | None = None,
-                         lse: torch.Tensor | None = None, staged: bool | None = None):
+                         lse: torch.Tensor | None = None, staged: bool | None = None,
+                         persistent: bool = True):
     """Non-causal attention of query [positions, Hq, 128] (bf16, the caller's
     layout) over the spans of ``tables``: (out [positions, Hq, 128] bf16, lse
     [Hq, positions] fp32 natural log); positions no item covers are left
@@ -1252,7 +1326,10 @@ def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv
     space once into a bf16 workspace (``ucb_long_query_stage``) and streams it
     by TMA, which is faster once several row blocks read the same keys;
     ``None`` stages when every key space has at least
-    ``LQ_STAGE_MIN_ROW_BLOCKS`` row blocks."""
+    ``LQ_STAGE_MIN_ROW_BLOCKS`` row blocks.  A staged launch is persistent
+    by default: at most one CTA per SM, each running an equal contiguous
+    share of the (row block, key tile) units (``plan_stream_k``);
+    ``persistent=False`` runs one CTA per row block (or per key-split part)."""
 
     require_cuda(query, "query")
     if query.dtype != torch.bfloat16 or not query.is_contiguous() or query.dim() != 3 or int(query.shape[2]) != 128:
@@ -1265,18 +1342,22 @@ def long_query_attention(query: torch.Tensor, tables: LongQueryTables, *, num_kv
         out = torch.empty_like(query)
     if lse is None:
         lse = torch.empty((q_heads, positions), device=query.device, dtype=torch.float32)
-    partials = flags = None
-    if tables.slots:
-        partials, flags = prefill_split_workspace(query.device, tables.slots, stream_of(query))
     if staged is None:
         staged = tables.jobs is not None and tables.row_blocks >= LQ_STAGE_MIN_ROW_BLOCKS
+    persistent = bool(staged and persistent and tables.p_items is not None)
+    slots = tables.p_slots if persistent else tables.slots
+    partials = flags = None
+    if slots:
+        partials, flags = prefill_split_workspace(query.device, slots, stream_of(query))
     if staged:
         if tables.jobs is None:
             raise ValueError("these tables carry no staging jobs")
         k_ws = torch.empty((num_kv_heads, tables.ws_rows, 128), device=query.device, dtype=torch.bfloat16)
         vt_ws = torch.empty((num_kv_heads, 128, tables.ws_rows), device=query.device, dtype=torch.bfloat16)
+        items, n_items = (tables.p_items, tables.num_p_items) if persistent else (tables.items, tables.num_items)
         call("ucb_long_query_attention_staged", query.data_ptr(), positions, q_heads, num_kv_heads,
-             tables.items.data_ptr(), tables.num_items, tables.spans.data_ptr(), tables.num_spans,
+             items.data_ptr(), n_items, tables.p_ctas.data_ptr() if persistent else None,
+             tables.num_ctas if persistent else 0, tables.spans.data_ptr(), tables.num_spans,
              tables.jobs.data_ptr(), tables.num_jobs, tables.max_chunks, tables.k_bits, tables.v_bits,
              tables.group_size, scale, k_ws.data_ptr(), vt_ws.data_ptr(), tables.ws_rows, out.data_ptr(),
              lse.data_ptr(), ptr(partials), ptr(flags), stream_of(query))
