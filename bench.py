@@ -665,7 +665,8 @@ def config5_leg(run: Run) -> dict:
         "e2e": {"value": model.batch * e_steps * run.world / e2e, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": model.batch * 8,
                 "api": "Qwen2PackedDecode.replay + next-token ids copied to pinned host memory per step"},
-        "gpu_launches_ours_per_step": 2 * model.layers,
+        # per layer: decode + state merge, two RMSNorms, rope + suffix append, SwiGLU gate; the final RMSNorm
+        "gpu_launches_ours_per_step": 6 * model.layers + 1,
         "build_seconds": build_s,
         "device_status": int(status),
     }

@@ -412,6 +412,26 @@ UCB_API int ucb_long_query_attention_staged(const void* q_dev, int positions, in
                                             void* vt_ws_dev, int64_t ws_rows, void* out_dev, float* lse_dev,
                                             float* partials_dev, unsigned int* flags_dev, void* stream);
 
+/* ---- element-wise steps of the configuration-5 decoder (the workload that
+ * drives the decode path at Qwen2-7B shape; no counterpart in the path's
+ * reference code).  All bf16, contiguous rows.
+ * ucb_rms_norm: out[r] = bf16(bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) * w).
+ * ucb_qkv_rope_append: qkv [batch, (hq + 2*hkv) * head_dim] (query, key, value
+ * heads); slot = *length - 1 (device int32), position = prompt + slot; the
+ * query heads, rotated (half-split rotary embedding with angles position *
+ * inv_freq[i], fp32 inv_freq [head_dim/2]), go to q_out [batch, hq,
+ * head_dim]; the rotated key heads and the value heads are written to row
+ * `slot` of suffix_k / suffix_v [batch, capacity, hkv, head_dim].  A slot
+ * outside [0, capacity) appends nothing and sets device error flag 2.
+ * ucb_silu_mul: gate_up [rows, 2*ffn] -> out [rows, ffn] =
+ * bf16(bf16(silu(gate)) * up). */
+UCB_API int ucb_rms_norm(const void* x_dev, const void* weight_dev, int rows, int hidden, float eps, void* out_dev,
+                         void* stream);
+UCB_API int ucb_qkv_rope_append(const void* qkv_dev, int batch, int hq, int hkv, int head_dim,
+                                const int32_t* length_dev, int prompt, const float* inv_freq_dev, void* q_out_dev,
+                                void* suffix_k_dev, void* suffix_v_dev, int capacity, void* stream);
+UCB_API int ucb_silu_mul(const void* gate_up_dev, int rows, int ffn, void* out_dev, void* stream);
+
 /* ---- sequence-split merge over NVLink peer memory (no counterpart in the
  * reference, which decodes one sequence on one device).  Each rank allocates
  * one exchange buffer of ucb_peer_buffer_bytes(rows) bytes

@@ -82,13 +82,11 @@ def test_qwen2_shaped_decode_steps_and_replays():
     model.replay()
     torch.cuda.synchronize()
     w = model.w[0]
-    from unicache_b200.workloads import _rms_norm
-
-    h = _rms_norm(x, w["in_norm"], model.eps)
+    h = _rms_norm_ref(x, w["in_norm"], model.eps)
     qkv = torch.addmm(w["qkv_bias"], h, w["qkv"])
     pos = torch.tensor([length - 1 + model.prompt], device="cuda", dtype=torch.float32)
     angle = pos * model.inv_freq
-    q = model._rope(qkv[:, :28 * 128].view(4, 28, 128), torch.cos(angle), torch.sin(angle))
+    q = _rope_ref(qkv[:, :28 * 128].view(4, 28, 128), torch.cos(angle), torch.sin(angle))
     for b in range(4):
         packed = model.packed[b]  # layer 0's caches are the first `batch` entries
         ref = packed.reference_layout()
@@ -101,3 +99,63 @@ def test_qwen2_shaped_decode_steps_and_replays():
         torch.cuda.synchronize()
         assert_attention_close(plan_out[b:b + 1], e_out, what=f"config-5 layer 0, sequence {b}")
     assert kernels.device_status() == 0
+
+
+# torch fp32 references of the decoder's element-wise steps (Qwen2's RMSNorm,
+# half-split rotary embedding and SwiGLU gate, rounding where torch rounds)
+def _rms_norm_ref(x, weight, eps):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * weight
+
+
+def _rope_ref(x, cos, sin):
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
+
+
+def _ulps_bf16(a, b):
+    """Largest difference between two bf16 tensors in units of the larger value's last place."""
+
+    a, b = a.float(), b.float()
+    scale = torch.maximum(a.abs(), b.abs()).clamp_min(1e-30)
+    ulp = torch.exp2(torch.floor(torch.log2(scale)) - 7)
+    return float(((a - b).abs() / ulp).max())
+
+
+def test_decoder_glue_kernels_match_torch_reference():
+    need_gpu()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    x = (torch.randn(32, 3584, generator=gen, device="cuda") * 3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(3584, generator=gen, device="cuda")).to(torch.bfloat16)
+    assert _ulps_bf16(kernels.rms_norm(x, w, 1e-6), _rms_norm_ref(x, w, 1e-6)) <= 1.0
+
+    gu = torch.randn(32, 2 * 512, generator=gen, device="cuda").to(torch.bfloat16)
+    ref = (torch.nn.functional.silu(gu[:, :512]) * gu[:, 512:])
+    assert _ulps_bf16(kernels.silu_mul(gu), ref) <= 1.0
+
+    hq, hkv, d, cap, prompt = 28, 4, 128, 16, 1000
+    qkv = torch.randn(32, (hq + 2 * hkv) * d, generator=gen, device="cuda").to(torch.bfloat16)
+    inv_freq = 1.0 / (1000000.0 ** (torch.arange(d // 2, device="cuda", dtype=torch.float32) / (d // 2)))
+    sk = torch.zeros(32, cap, hkv, d, device="cuda", dtype=torch.bfloat16)
+    sv = torch.zeros_like(sk)
+    q_out = torch.empty(32, hq, d, device="cuda", dtype=torch.bfloat16)
+    length = torch.tensor([6], device="cuda", dtype=torch.int32)
+    kernels.qkv_rope_append(qkv, hq=hq, hkv=hkv, length=length, prompt=prompt, inv_freq=inv_freq, q_out=q_out,
+                            suffix_k=sk, suffix_v=sv)
+    angle = torch.tensor([prompt + 5.0], device="cuda") * inv_freq
+    cos, sin = torch.cos(angle), torch.sin(angle)
+    assert _ulps_bf16(q_out, _rope_ref(qkv[:, :hq * d].view(32, hq, d), cos, sin)) <= 1.0
+    k_ref = _rope_ref(qkv[:, hq * d:(hq + hkv) * d].view(32, hkv, d), cos, sin)
+    assert _ulps_bf16(sk[:, 5], k_ref) <= 1.0
+    assert torch.equal(sv[:, 5], qkv[:, (hq + hkv) * d:].view(32, hkv, d))
+    others = torch.ones(cap, dtype=torch.bool)
+    others[5] = False
+    assert not sk[:, others].any() and not sv[:, others].any()
+    assert kernels.device_status() == 0
+    # a full suffix: the kernel's own bound check appends nothing and sets flag 2
+    length.fill_(cap + 1)
+    kernels.qkv_rope_append(qkv, hq=hq, hkv=hkv, length=length, prompt=prompt, inv_freq=inv_freq, q_out=q_out,
+                            suffix_k=sk, suffix_v=sv)
+    assert kernels.device_status() == 2
+    assert not sk[:, others].any()

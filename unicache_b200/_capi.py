@@ -128,6 +128,10 @@ SIGNATURES = {
                                                 c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                                 c_float, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                                 c_void_p, c_void_p]),
+    "ucb_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
+    "ucb_qkv_rope_append": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_int, c_void_p]),
+    "ucb_silu_mul": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "ucb_peer_buffer_bytes": (ctypes.c_int64, [c_int64]),
     "ucb_peer_buffer_alloc": (c_int, [c_int64, ctypes.POINTER(c_void_p), c_void_p]),
     "ucb_peer_buffer_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),

@@ -149,12 +149,11 @@ __device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinte
 // points at a device int32 (a growing decode suffix) holds min(tokens, that
 // value) live tokens; every other span holds `tokens`.  The planner sizes a
 // growing span for its capacity, so one plan (and one captured graph) serves
-// every step while the suffix grows.
-__device__ __forceinline__ int live_tokens(const ucb_span& sp) {
-  if (sp.kind == 1 && sp.key_scale != nullptr)
-    return max(0, min(sp.tokens, *static_cast<const volatile int32_t*>(sp.key_scale)));
-  return sp.tokens;
-}
+// every step while the suffix grows.  The CTA reads each growing span's
+// length once, after copying its span records into shared memory, and stores
+// the live count in the shared copy's `tokens` (the length does not change
+// during a launch).
+__device__ __forceinline__ int live_tokens(const ucb_span& sp) { return sp.tokens; }
 
 struct Params {
   const __nv_bfloat16* query;
@@ -598,6 +597,13 @@ struct Kernel {
       mbar_init(&bars[0], 1);
       mbar_init(&bars[1], 1);
       fence_mbarrier_init();
+    }
+    __syncthreads();
+    // growing suffixes: the live length, read once per launch
+    if (tid < n_spans) {
+      const ucb_span& g = P.spans[cta.span_begin + tid];
+      if (g.kind == 1 && g.key_scale != nullptr)
+        spans[tid].tokens = max(0, min(g.tokens, *static_cast<const volatile int32_t*>(g.key_scale)));
     }
     __syncthreads();
 

@@ -846,6 +846,54 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, n_toke
     return out, lse
 
 
+
+# ------------------------------------------------------------------ decoder glue (configuration 5)
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of bf16 rows [rows, hidden]: bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight)."""
+
+    require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("rms_norm takes contiguous bfloat16 [rows, hidden] rows and a bfloat16 weight")
+    out = torch.empty_like(x) if out is None else out
+    call("ucb_rms_norm", x.data_ptr(), weight.data_ptr(), int(x.shape[0]), int(x.shape[1]), float(eps),
+         out.data_ptr(), stream_of(x))
+    return out
+
+
+def qkv_rope_append(qkv: torch.Tensor, *, hq: int, hkv: int, length: torch.Tensor, prompt: int,
+                    inv_freq: torch.Tensor, q_out: torch.Tensor, suffix_k: torch.Tensor,
+                    suffix_v: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding of the new token's query and key heads at position
+    prompt + length - 1 (``length`` a device int32 [1]); the query goes to
+    ``q_out`` [batch, hq, d], the key and value heads to row length - 1 of
+    the dense suffixes [batch, capacity, hkv, d]."""
+
+    for name, t in (("qkv", qkv), ("q_out", q_out), ("suffix_k", suffix_k), ("suffix_v", suffix_v)):
+        require_cuda(t, name)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bfloat16 tensor")
+    batch, capacity, _, d = map(int, suffix_k.shape)
+    if tuple(qkv.shape) != (batch, (hq + 2 * hkv) * d) or tuple(q_out.shape) != (batch, hq, d) or \
+            tuple(suffix_v.shape) != tuple(suffix_k.shape) or int(suffix_k.shape[2]) != hkv:
+        raise ValueError("qkv, q_out and the suffixes disagree in shape")
+    if length.dtype != torch.int32 or inv_freq.dtype != torch.float32 or int(inv_freq.numel()) != d // 2:
+        raise ValueError("length must be int32 and inv_freq float32 [head_dim / 2]")
+    call("ucb_qkv_rope_append", qkv.data_ptr(), batch, hq, hkv, d, length.data_ptr(), int(prompt),
+         inv_freq.data_ptr(), q_out.data_ptr(), suffix_k.data_ptr(), suffix_v.data_ptr(), capacity, stream_of(qkv))
+    return q_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU gate of [rows, 2 * ffn] bf16: bf16(bf16(silu(gate)) * up) [rows, ffn]."""
+
+    require_cuda(gate_up, "gate_up")
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or not gate_up.is_contiguous() or gate_up.shape[1] % 2:
+        raise ValueError("silu_mul takes contiguous bfloat16 [rows, 2 * ffn]")
+    rows, ffn = int(gate_up.shape[0]), int(gate_up.shape[1]) // 2
+    out = torch.empty(rows, ffn, device=gate_up.device, dtype=gate_up.dtype) if out is None else out
+    call("ucb_silu_mul", gate_up.data_ptr(), rows, ffn, out.data_ptr(), stream_of(gate_up))
+    return out
+
 PREFILL_ROWS_PER_CTA = 256
 PREFILL_KEY_TILE = 128
 _KEY_SPLITS: dict = {}

@@ -92,11 +92,6 @@ QWEN2_7B = {"hidden": 3584, "layers": 28, "q_heads": 28, "kv_heads": 4, "head_di
             "vocab": 151936, "rope_theta": 1.0e6, "eps": 1.0e-6}
 
 
-def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * weight
-
-
 class Qwen2PackedDecode:
     """a Qwen2-7B-shaped decoder (hidden 3584, 28 layers, 28
     query / 4 KV heads, head_dim 128, FFN 18944, untied 151936-token head:
@@ -112,9 +107,13 @@ class Qwen2PackedDecode:
     137-144) applied as two steps.  New tokens go to a dense bf16 suffix of
     capacity ``new_tokens`` (the reference appends decode tokens to its dense
     cache).  Attention is the packed decode kernel over [packed prompt +
-    residual + live suffix]; projections, norms, RoPE and the MLP are torch
-    (cuBLAS GEMMs).  One decode step is captured once as a CUDA graph: the
-    suffix length, the RoPE position and the append index live on the device.
+    residual + live suffix]; the projections are cuBLAS GEMMs through torch
+    (residual adds in their epilogues), and RMSNorm, the rotary embedding
+    fused with the suffix append, and the SwiGLU gate are one library kernel
+    each (``kernels.rms_norm``, ``qkv_rope_append``, ``silu_mul``): ten
+    launches per layer.  One decode step is captured once as a CUDA graph:
+    the suffix length, the RoPE position and the append index live on the
+    device.
     """
 
     def __init__(self, device, *, batch: int = 32, prompt: int = 16384, new_tokens: int = 512,
@@ -186,6 +185,7 @@ class Qwen2PackedDecode:
         torch.cuda.empty_cache()
         self.ids = torch.zeros(batch, device=self.device, dtype=torch.int64)
         self.x = self.embed[self.ids].clone()
+        self.q_buf = torch.empty(batch, hq, d, device=self.device, dtype=torch.bfloat16)
         self.attn_out = torch.empty(batch, hq, d, device=self.device, dtype=torch.bfloat16)
         self.attn_lse = torch.empty(batch, hq, device=self.device, dtype=torch.float32)
         self.graph = None
@@ -203,38 +203,29 @@ class Qwen2PackedDecode:
         capacity = self.layers * self.batch * self.hkv * self.d * 4 * self.capacity
         return prompt - capacity // 2 + grown  # the plans weight the suffix at half its capacity
 
-    def _rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-        half = self.d // 2
-        x1, x2 = x[..., :half].float(), x[..., half:].float()
-        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
-
     def step(self) -> torch.Tensor:
         """One greedy decode step of every sequence (device-only, capturable):
         returns the next token ids [batch]."""
 
-        b, hq, hkv, d, f = self.batch, self.hq, self.hkv, self.d, self.ffn
+        from . import kernels
+
+        b, hq, hkv, d = self.batch, self.hq, self.hkv, self.d
         self.length += 1  # this step's token is row length - 1 of every suffix
-        slot = (self.length - 1).long()
-        pos = (self.length - 1 + self.prompt).float()
-        angle = pos * self.inv_freq
-        cos, sin = torch.cos(angle), torch.sin(angle)
         x = self.x
         for layer in range(self.layers):
             w = self.w[layer]
-            h = _rms_norm(x, w["in_norm"], self.eps)
+            h = kernels.rms_norm(x, w["in_norm"], self.eps)
             qkv = torch.addmm(w["qkv_bias"], h, w["qkv"])
-            q = self._rope(qkv[:, :hq * d].view(b, hq, d), cos, sin)
-            k = self._rope(qkv[:, hq * d:(hq + hkv) * d].view(b, hkv, d), cos, sin)
-            v = qkv[:, (hq + hkv) * d:].view(b, hkv, d)
             sk, sv = self.suffixes[layer]
-            sk.index_copy_(1, slot, k.unsqueeze(1))
-            sv.index_copy_(1, slot, v.unsqueeze(1))
-            self.plans[layer].run(q.contiguous(), out=self.attn_out, lse=self.attn_lse)
-            x = x + self.attn_out.view(b, hq * d) @ w["o"]
-            h = _rms_norm(x, w["post_norm"], self.eps)
-            gu = h @ w["gate_up"]
-            x = x + (torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]) @ w["down"]
-        logits = _rms_norm(x, self.final_norm, self.eps) @ self.lm_head
+            # rotary embedding, the query for the decode kernel, the key and
+            # value appended to the suffix row the device-side length names
+            kernels.qkv_rope_append(qkv, hq=hq, hkv=hkv, length=self.length, prompt=self.prompt,
+                                    inv_freq=self.inv_freq, q_out=self.q_buf, suffix_k=sk, suffix_v=sv)
+            self.plans[layer].run(self.q_buf, out=self.attn_out, lse=self.attn_lse)
+            x = torch.addmm(x, self.attn_out.view(b, hq * d), w["o"])
+            h = kernels.rms_norm(x, w["post_norm"], self.eps)
+            x = torch.addmm(x, kernels.silu_mul(h @ w["gate_up"]), w["down"])
+        logits = kernels.rms_norm(x, self.final_norm, self.eps) @ self.lm_head
         self.ids.copy_(torch.argmax(logits, dim=-1))
         self.x.copy_(self.embed[self.ids])
         return self.ids
