@@ -538,8 +538,11 @@ UCB_API int ucb_h2o_scores_from_lse(const void* query_dev, int64_t queries, int 
  * storage/physical.py:598-610, without the [Hq, Lq, T] probabilities) for
  * bf16 (tensor cores, mma.sync) or fp32 (CUDA cores) query and keys of one
  * dtype.  lse_dev NULL: the attention covers exactly these keys and the LSE of
- * every row is computed first into lse_workspace_dev (fp32 [q_heads, queries]).
- * bf16 needs a 16-byte aligned query and 4-byte aligned key rows. */
+ * every row is computed first into lse_workspace_dev (8-byte aligned,
+ * ucb_h2o_scores_workspace_floats(queries, q_heads, tokens) floats: the
+ * LSE [q_heads, queries] first, then per-64-token-block partial maxima and
+ * sums).  bf16 needs a 16-byte aligned query and 4-byte aligned key rows. */
+UCB_API int64_t ucb_h2o_scores_workspace_floats(int64_t queries, int q_heads, int64_t tokens);
 UCB_API int ucb_h2o_scores(const void* query_dev, int dtype, int64_t queries, int q_heads, const void* key_dev,
                            int64_t key_stride_token, int64_t key_stride_head, int64_t tokens, int kv_heads,
                            int head_dim, const float* lse_dev, float* lse_workspace_dev, float softmax_scale,

@@ -146,6 +146,7 @@ SIGNATURES = {
                                 c_void_p]),
     "ucb_h2o_accumulate_probs": (c_int, [c_void_p, c_int, c_int, c_int64, c_int64, c_int, c_void_p, c_int,
                                          c_void_p]),
+    "ucb_h2o_scores_workspace_floats": (c_int64, [c_int64, c_int, c_int64]),
     "ucb_h2o_scores_from_lse": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int,
                                         c_int, c_void_p, c_float, c_void_p, c_int, c_void_p]),
     "ucb_kivi_attention_logits": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64,

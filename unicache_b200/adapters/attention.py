@@ -111,9 +111,21 @@ class DecodeStepGraph:
         self.graph.replay()
 
 
+_PLANS_PER_OWNER = 8
+
+
 def _single_sequence_decode(query, segments, num_kv_heads, head_dim, owner=None, key=None):
+    """Decode of one query token over ``segments``.  The decode plan (device
+    tables) is cached on the first physical segment, keyed by every segment's
+    signature (identity, addresses, strides and lengths), so a decode loop
+    over the same segments plans once; a segment that changes (an append, a
+    trim, a repack) has a new signature and gets a new plan."""
+
     if int(query.shape[0]) != 1:
         raise ValueError("decode attention takes a single query token")
+    if owner is None:
+        owner = next((s for s in segments if isinstance(s, (PackedKIVICache, GQAH2OCache))), None)
+        key = (num_kv_heads, head_dim, tuple(kernels._segment_signature(s) for s in segments))
     plan = None
     if owner is not None:
         plans = owner.__dict__.setdefault("_decode_plans", {})
@@ -121,7 +133,12 @@ def _single_sequence_decode(query, segments, num_kv_heads, head_dim, owner=None,
     if plan is None:
         plan = kernels.build_decode_plan([segments], num_kv_heads=num_kv_heads, head_dim=head_dim)
         if owner is not None:
-            owner.__dict__["_decode_plans"][key] = plan
+            # the owner keeps itself alive; the plan keeps the other segments
+            plan.keepalive = [k for k in plan.keepalive if k is not owner]
+            plans = owner.__dict__["_decode_plans"]
+            if len(plans) >= _PLANS_PER_OWNER:
+                plans.pop(next(iter(plans)))
+            plans[key] = plan
     out, lse = plan.run(query.to(torch.bfloat16))
     return out.to(query.dtype), lse
 

@@ -296,20 +296,45 @@ __global__ void __launch_bounds__(128) scores_mma_kernel(const __nv_bfloat16* __
   }
 }
 
-// fp32 (or any dtype) on the CUDA cores, for fp32 caches: one thread per
-// token holds its key row; query rows are staged in shared memory.
-constexpr int kScoreQ = 32;  // query rows staged per round
+// fp32 (or any dtype) on the CUDA cores, for fp32 caches.  Block (x, kv):
+// 64 tokens of KV head kv x 4 row groups (256 threads); a thread holds its
+// token's key row and takes every fourth query row of each 32-row chunk
+// staged in shared memory, four rows per pass (four independent FMA chains);
+// the four groups' sums of a token are added in group order, so the result
+// does not depend on scheduling.  Row offsets of a chunk are formed once per
+// row (one division), not per staged element.
+constexpr int kScoreQ = 32;  // query rows staged per round (a multiple of 16)
+constexpr int kScoreTok = 64, kScoreGroups = 4;
+static_assert(kScoreQ % (4 * kScoreGroups) == 0, "each group takes four rows per pass");
+
 template <typename T>
-__global__ void __launch_bounds__(128) scores_cuda_core_kernel(const T* __restrict__ query, int64_t queries,
-                                                               int q_heads, const T* __restrict__ key, int64_t ks_t,
-                                                               int64_t ks_h, int64_t tokens, int grp,
-                                                               const float* __restrict__ lse, float scale,
-                                                               float* __restrict__ scores, int accumulate) {
+__device__ __forceinline__ void stage_rows(const T* __restrict__ query, int64_t queries, int q_heads, int kv,
+                                           int grp, int64_t rows, int64_t base, int nthreads, float (*qs)[128],
+                                           int64_t* qoff) {
   constexpr int D = 128;
-  const int kv = blockIdx.y;
-  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (threadIdx.x < kScoreQ) {
+    const int64_t rr = base + threadIdx.x;
+    qoff[threadIdx.x] = rr < rows ? ((rr % queries) * q_heads + kv * grp + rr / queries) * D : -1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kScoreQ * D; i += nthreads) {
+    const int64_t off = qoff[i >> 7];
+    qs[i >> 7][i & (D - 1)] = off >= 0 ? Dtype<T>::to_f(query[off + (i & (D - 1))]) : 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kScoreTok * kScoreGroups) scores_cuda_core_kernel(
+    const T* __restrict__ query, int64_t queries, int q_heads, const T* __restrict__ key, int64_t ks_t, int64_t ks_h,
+    int64_t tokens, int grp, const float* __restrict__ lse, float scale, float* __restrict__ scores,
+    int accumulate) {
+  constexpr int D = 128, THREADS = kScoreTok * kScoreGroups;
+  const int kv = blockIdx.y, tl = threadIdx.x % kScoreTok, rg = threadIdx.x / kScoreTok;
+  const int64_t t = blockIdx.x * (int64_t)kScoreTok + tl;
   __shared__ float qs[kScoreQ][D];
   __shared__ float ls[kScoreQ];
+  __shared__ int64_t qoff[kScoreQ];
+  __shared__ float part[kScoreGroups][kScoreTok];
   float k[D];
   if (t < tokens) {
     const T* kr = key + t * ks_t + kv * ks_h;
@@ -320,66 +345,119 @@ __global__ void __launch_bounds__(128) scores_cuda_core_kernel(const T* __restri
   const int64_t rows = (int64_t)grp * queries;
   for (int64_t base = 0; base < rows; base += kScoreQ) {
     __syncthreads();
-    for (int i = threadIdx.x; i < kScoreQ * D; i += blockDim.x) {
-      const int64_t rr = base + i / D;
-      float v = 0.f;
-      if (rr < rows) {
-        const int g = (int)(rr / queries);
-        const int64_t q = rr % queries;
-        v = Dtype<T>::to_f(query[(q * q_heads + kv * grp + g) * D + i % D]);
-      }
-      qs[i / D][i % D] = v;
-    }
-    for (int i = threadIdx.x; i < kScoreQ; i += blockDim.x) {
-      const int64_t rr = base + i;
-      ls[i] = (rr < rows) ? lse[(int64_t)(kv * grp + rr / queries) * queries + rr % queries] : INFINITY;
+    stage_rows(query, queries, q_heads, kv, grp, rows, base, THREADS, qs, qoff);
+    if (threadIdx.x < kScoreQ) {
+      const int64_t rr = base + threadIdx.x;
+      ls[threadIdx.x] = rr < rows ? lse[(int64_t)(kv * grp + rr / queries) * queries + rr % queries] : INFINITY;
     }
     __syncthreads();
     if (t < tokens) {
-      for (int j = 0; j < kScoreQ; ++j) {
-        float dot = 0.f;
+      for (int j = 4 * rg; j < kScoreQ; j += 4 * kScoreGroups) {
+        float dot[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int d = 0; d < D; ++d) dot = fmaf(qs[j][d], k[d], dot);
-        total += expf(dot * scale - ls[j]);
+        for (int d = 0; d < D; ++d) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) dot[r] = fmaf(qs[j + r][d], k[d], dot[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) total += expf(dot[r] * scale - ls[j + r]);
       }
     }
   }
-  if (t < tokens) {
+  part[rg][tl] = total;
+  __syncthreads();
+  if (rg == 0 && t < tokens) {
+    float sum = 0.f;
+#pragma unroll
+    for (int g = 0; g < kScoreGroups; ++g) sum += part[g][tl];
     float* o = scores + (int64_t)kv * tokens + t;
-    *o = accumulate ? *o + total : total;
+    *o = accumulate ? *o + sum : sum;
   }
 }
 
 // Natural-log normaliser of every (query head, query) row over the given keys
-// (for callers whose attention covers exactly these keys): one warp per row,
-// the lanes split the 128 channels, online max/sum over the tokens in fp32.
+// (for callers whose attention covers exactly these keys), in two launches.
+// lse_partial_kernel: block (x, kv, z) takes 64 tokens of KV head kv and the
+// z-th 32-row chunk of the head's query group (rows are independent, so the
+// chunks spread over the grid), one thread per token holding its key row;
+// each thread forms its logits (four rows per pass, as the scoring kernel
+// does) and each row's (max, sum of exp) over the block's tokens is reduced
+// by shuffles and across the warps, then stored as the block's partial.  lse_combine_kernel folds the partials
+// of every row over the token blocks: M = max m, L = sum l * exp(m - M),
+// lse = M + log(L).
+constexpr int kLseTok = 64;
 template <typename T>
-__global__ void __launch_bounds__(128) row_lse_kernel(const T* __restrict__ query, int64_t queries, int q_heads,
-                                                      const T* __restrict__ key, int64_t ks_t, int64_t ks_h,
-                                                      int64_t tokens, int grp, float scale, float* __restrict__ lse) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 4 + warp;  // row = h * queries + i
-  if (row >= (int64_t)q_heads * queries) return;
-  const int h = (int)(row / queries);
-  const int64_t qi = row % queries;
-  const int kv = h / grp;
-  float q[4];
+__global__ void __launch_bounds__(kLseTok) lse_partial_kernel(const T* __restrict__ query, int64_t queries,
+                                                              int q_heads, const T* __restrict__ key, int64_t ks_t,
+                                                              int64_t ks_h, int64_t tokens, int grp, float scale,
+                                                              float2* __restrict__ partial, int token_blocks) {
+  constexpr int D = 128, WARPS = kLseTok / 32;
+  const int kv = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x * (int64_t)kLseTok + threadIdx.x;
+  const int64_t base = (int64_t)blockIdx.z * kScoreQ;  // this block's 32-row chunk
+  const bool live = t < tokens;
+  __shared__ float qs[kScoreQ][D];
+  __shared__ int64_t qoff[kScoreQ];
+  __shared__ float2 red[kScoreQ][WARPS];
+  float k[D];
+  if (live) {
+    const T* kr = key + t * ks_t + kv * ks_h;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) q[j] = Dtype<T>::to_f(query[(qi * q_heads + h) * 128 + 4 * lane + j]);
-  float m = -INFINITY, l = 0.f;
-  for (int64_t t = 0; t < tokens; ++t) {
-    const T* kr = key + t * ks_t + (int64_t)kv * ks_h + 4 * lane;
-    float dot = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dot = fmaf(q[j], Dtype<T>::to_f(kr[j]), dot);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-    const float s = dot * scale;
-    const float mn = fmaxf(m, s);
-    l = l * expf(m - mn) + expf(s - mn);
-    m = mn;
+    for (int d = 0; d < D; ++d) k[d] = Dtype<T>::to_f(kr[d]);
   }
-  if (lane == 0) lse[row] = m + logf(l);
+  const int64_t rows = (int64_t)grp * queries;  // rr = g * queries + q of this KV head's group
+  stage_rows(query, queries, q_heads, kv, grp, rows, base, kLseTok, qs, qoff);
+  __syncthreads();
+  for (int j = 0; j < kScoreQ; j += 4) {
+    float dot[4] = {0.f, 0.f, 0.f, 0.f};
+    if (live) {
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) dot[r] = fmaf(qs[j + r][d], k[d], dot[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float sv = live ? dot[r] * scale : -INFINITY;
+      float m = sv;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      float l = (m == -INFINITY) ? 0.f : expf(sv - m);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+      if (lane == 0) red[j + r][warp] = make_float2(m, l);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kScoreQ && base + threadIdx.x < rows) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) m = fmaxf(m, red[threadIdx.x][w].x);
+    float l = 0.f;
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) {
+        const float2 p = red[threadIdx.x][w];
+        if (p.x != -INFINITY) l += p.y * expf(p.x - m);
+      }
+    }
+    const int64_t row = (int64_t)kv * rows + base + threadIdx.x;  // = h * queries + q
+    partial[row * token_blocks + blockIdx.x] = make_float2(m, l);
+  }
+}
+
+__global__ void lse_combine_kernel(const float2* __restrict__ partial, int64_t rows, int token_blocks,
+                                   float* __restrict__ lse) {
+  const int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float2* p = partial + row * token_blocks;
+  float m = -INFINITY;
+  for (int b = 0; b < token_blocks; ++b) m = fmaxf(m, p[b].x);
+  float l = 0.f;
+  for (int b = 0; b < token_blocks; ++b)
+    if (p[b].x != -INFINITY) l += p[b].y * expf(p[b].x - m);
+  lse[row] = m + logf(l);
 }
 
 // ---------------------------------------------------------------- compaction
@@ -532,16 +610,29 @@ extern "C" int ucb_h2o_scores(const void* query, int dtype, int64_t queries, int
   const int grp = q_heads / kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (lse == nullptr) {
-    const unsigned blocks = static_cast<unsigned>(((int64_t)q_heads * queries + 3) / 4);
+    // workspace: lse [q_heads * queries] floats, then the partials (8-byte aligned)
+    const int64_t rows = (int64_t)q_heads * queries;
+    const int token_blocks = static_cast<int>((tokens + ucb::kLseTok - 1) / ucb::kLseTok);
+    float2* partial = reinterpret_cast<float2*>(lse_workspace + ((rows + 1) & ~int64_t(1)));
+    if (reinterpret_cast<uintptr_t>(lse_workspace) & 7)
+      return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: lse_workspace must be 8-byte aligned");
+    const int64_t chunks = ((int64_t)grp * queries + ucb::kScoreQ - 1) / ucb::kScoreQ;
+    if (chunks > 65535) return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: too many query rows per KV head");
+    const dim3 pgrid(static_cast<unsigned>(token_blocks), static_cast<unsigned>(kv_heads),
+                     static_cast<unsigned>(chunks));
     if (dtype == UCB_BF16)
-      ucb::row_lse_kernel<__nv_bfloat16><<<blocks, 128, 0, s>>>(
+      ucb::lse_partial_kernel<__nv_bfloat16><<<pgrid, ucb::kLseTok, 0, s>>>(
           static_cast<const __nv_bfloat16*>(query), queries, q_heads, static_cast<const __nv_bfloat16*>(key),
-          key_stride_token, key_stride_head, tokens, grp, softmax_scale, lse_workspace);
+          key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial, token_blocks);
     else
-      ucb::row_lse_kernel<float><<<blocks, 128, 0, s>>>(static_cast<const float*>(query), queries, q_heads,
-                                                        static_cast<const float*>(key), key_stride_token,
-                                                        key_stride_head, tokens, grp, softmax_scale, lse_workspace);
-    const int rc = check_launch("row_lse_kernel");
+      ucb::lse_partial_kernel<float><<<pgrid, ucb::kLseTok, 0, s>>>(
+          static_cast<const float*>(query), queries, q_heads, static_cast<const float*>(key), key_stride_token,
+          key_stride_head, tokens, grp, softmax_scale, partial, token_blocks);
+    int rc = check_launch("lse_partial_kernel");
+    if (rc) return rc;
+    ucb::lse_combine_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, s>>>(partial, rows, token_blocks,
+                                                                                      lse_workspace);
+    rc = check_launch("lse_combine_kernel");
     if (rc) return rc;
     lse = lse_workspace;
   }
@@ -556,7 +647,10 @@ extern "C" int ucb_h2o_scores(const void* query, int dtype, int64_t queries, int
                                                 softmax_scale * 1.4426950408889634f, scores, accumulate);
     return check_launch("scores_mma_kernel");
   }
-  ucb::scores_cuda_core_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(query), queries, q_heads,
+  const dim3 grid64(static_cast<unsigned>((tokens + ucb::kScoreTok - 1) / ucb::kScoreTok),
+                    static_cast<unsigned>(kv_heads));
+  ucb::scores_cuda_core_kernel<float><<<grid64, ucb::kScoreTok * ucb::kScoreGroups, 0, s>>>(
+      static_cast<const float*>(query), queries, q_heads,
                                                            static_cast<const float*>(key), key_stride_token,
                                                            key_stride_head, tokens, grp, lse, softmax_scale, scores,
                                                            accumulate);
@@ -601,4 +695,10 @@ extern "C" int ucb_compact_rows(const void* src, int64_t row_bytes, const uint8_
       return set_error(UCB_ERR_CUDA, "ucb_compact_rows: reading the kept count failed");
   }
   return UCB_OK;
+}
+
+extern "C" int64_t ucb_h2o_scores_workspace_floats(int64_t queries, int q_heads, int64_t tokens) {
+  const int64_t rows = (int64_t)q_heads * queries;
+  const int64_t token_blocks = (tokens + ucb::kLseTok - 1) / ucb::kLseTok;
+  return ((rows + 1) & ~int64_t(1)) + 2 * rows * token_blocks;
 }

@@ -14,6 +14,7 @@ import functools
 import math
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from . import _capi
@@ -336,7 +337,8 @@ def h2o_scores(query: torch.Tensor, key: torch.Tensor, lse: torch.Tensor | None,
         raise ValueError("scores must be contiguous float32 [kv_heads, tokens]")
     workspace = None
     if lse is None:
-        workspace = torch.empty((q_heads, queries), device=q.device, dtype=torch.float32)
+        floats = int(_capi.load().ucb_h2o_scores_workspace_floats(queries, q_heads, tokens))
+        workspace = torch.empty(floats, device=q.device, dtype=torch.float32)
     else:
         lse = lse.float().contiguous()
     call("ucb_h2o_scores", q.data_ptr(), dtype_code(q.dtype), queries, q_heads, key.data_ptr(), stride_t, stride_h,
@@ -731,7 +733,9 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
     with torch.cuda.device(device):
         slots, warps = decode_config(k_bits, v_bits, group)
     if target_ctas is None:
-        target_ctas = slots
+        # every SM for a full-size batch; a small problem gets about one unit
+        # per warp (fewer CTAs plan faster and leave fewer states to merge)
+        target_ctas = min(slots, max(1, -(-len(unit_weights) // warps)))
     cta_bounds = _assign_ctas(unit_weights, unit_pair, unit_seg, target_ctas, warps, unit_span)
 
     span_starts = [sp.unit_begin for sp in spans]
@@ -782,10 +786,19 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
             raise AssertionError("every pair needs at least one warp state")
         pairs.append(pr)
 
-    def upload(structs) -> torch.Tensor:
-        raw = _capi.struct_array_bytes(structs)
-        host = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
-        return host.to(device)
+    # the five tables in one host -> device copy, each at a 256-byte offset
+    parts = [_capi.struct_array_bytes(spans), _capi.struct_array_bytes(ctas),
+             np.asarray(flat_bounds, dtype=np.int32).tobytes(), _capi.struct_array_bytes(pairs),
+             np.asarray(warp_slots, dtype=np.int32).tobytes()]
+    offsets, total = [], 0
+    for raw in parts:
+        offsets.append(total)
+        total += -(-len(raw) // 256) * 256
+    blob = bytearray(total)
+    for off, raw in zip(offsets, parts):
+        blob[off:off + len(raw)] = raw
+    dev_blob = torch.frombuffer(blob, dtype=torch.uint8).to(device)
+    table = [dev_blob[off:off + len(raw)] for off, raw in zip(offsets, parts)]
 
     partial_bytes = int(_capi.load().ucb_decode_partial_bytes(head_dim))
     return DecodePlan(
@@ -796,15 +809,15 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         k_bits=k_bits,
         v_bits=v_bits,
         group_size=group,
-        spans=upload(spans),
-        ctas=upload(ctas),
-        warp_bounds=torch.tensor(flat_bounds, dtype=torch.int32).to(device),
-        pairs=upload(pairs),
+        spans=table[0],
+        ctas=table[1],
+        warp_bounds=table[2].view(torch.int32),
+        pairs=table[3],
         num_spans=len(spans),
         num_ctas=len(ctas),
         num_pairs=len(pairs),
         partials=torch.empty(partial_total * partial_bytes, device=device, dtype=torch.uint8),
-        warp_slots=torch.tensor(warp_slots, dtype=torch.int32).to(device),
+        warp_slots=table[4].view(torch.int32),
         num_partials=partial_total,
         keepalive=keepalive,
         bytes_per_step=int(sum(span_bytes)),
