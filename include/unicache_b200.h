@@ -378,8 +378,9 @@ typedef struct ucb_lq_stage_job {
  * NULL, later long-query and prefill launches record per CTA (global timer,
  * ns): word 0 = kernel entry, 1 = set-up done, 2 = SM id, 3 = exit, 4 = items
  * run, and for its first 12 items i: word 6 + 2i = the softmax warps start
- * the item (its query rows loaded), 7 + 2i = the item's results written.
- * NULL switches it off. */
+ * the item (its query rows loaded), 7 + 2i = the item's results written;
+ * word 30 = the MMA thread's total wait for K/V tiles, 31 = its total wait
+ * for the softmax warps' P tiles (ns).  NULL switches it off. */
 UCB_API int ucb_prefill_set_trace(void* trace_dev);
 
 UCB_API int ucb_long_query_stage(const ucb_span* spans_dev, int num_spans, const void* jobs_dev, int num_jobs,

@@ -147,66 +147,71 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32])
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Row maximum of a 128-column S tile (this thread's TMEM lane), 64 columns
-// per load batch; RAGGED masks columns >= valid.
+// Row maximum over all 128 S columns (four loads, one wait); the first 64
+// columns stay in registers (s0) for the P pass, which reloads only the
+// second 64.
 template <bool RAGGED>
-__device__ __forceinline__ float row_max(uint32_t t_s, int valid) {
-  float mx = -INFINITY;
+__device__ __forceinline__ float row_max_keep(uint32_t t_s, int valid, uint32_t (&s0)[2][32]) {
+  uint32_t s1[2][32];
+  tc_ld32(t_s, s0[0]);
+  tc_ld32(t_s + 32, s0[1]);
+  tc_ld32(t_s + 64, s1[0]);
+  tc_ld32(t_s + 96, s1[1]);
+  tc_wait_ld();
+  float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t sv[2][32];
-    tc_ld32(t_s + 64 * h, sv[0]);
-    tc_ld32(t_s + 64 * h + 32, sv[1]);
-    tc_wait_ld();
-    float m0 = -INFINITY, m1 = -INFINITY;
+  for (int c = 0; c < 4; ++c)
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int col = 64 * h + 32 * c + i;
-        m0 = fmaxf(m0, (!RAGGED || col < valid) ? __uint_as_float(sv[c][i]) : -INFINITY);
-        m1 = fmaxf(m1, (!RAGGED || col + 1 < valid) ? __uint_as_float(sv[c][i + 1]) : -INFINITY);
-      }
-    mx = fmaxf(mx, fmaxf(m0, m1));
-  }
-  return mx;
+    for (int i = 0; i < 32; i += 2) {
+      const int col = 32 * c + i;
+      const uint32_t a = c < 2 ? s0[c][i] : s1[c - 2][i], b = c < 2 ? s0[c][i + 1] : s1[c - 2][i + 1];
+      m0 = fmaxf(m0, (!RAGGED || col < valid) ? __uint_as_float(a) : -INFINITY);
+      m1 = fmaxf(m1, (!RAGGED || col + 1 < valid) ? __uint_as_float(b) : -INFINITY);
+    }
+  return fmaxf(m0, m1);
 }
 
-// P = 2^(S * scale_log2 - m) in bf16 pairs over the first 64 columns of the
-// S tile (column c holds tokens 2c, 2c+1); each 64-column half of S is read
-// before the P columns it feeds overwrite any S column.  Returns the fp32
-// row sum of the weights.  The scaling and the sums run as packed fp32 pairs
-// (one FFMA2 and one FADD2 per two columns), the exponentials on the MUFU.
+// One 64-column half of P from S values in registers, stored over TMEM
+// columns [32 h, 32 h + 32) of the S tile; returns the two partial sums.
 template <bool RAGGED>
-__device__ __forceinline__ float write_p(uint32_t t_s, int valid, float scale_log2, float neg_m) {
-  const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
-  float2 sum = make_float2(0.f, 0.f);
+__device__ __forceinline__ float2 p_half(const uint32_t (&sv)[2][32], uint32_t t_s, int h, int valid, float2 sc,
+                                         float2 nm, float2 sum) {
+  uint32_t pw[32];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t sv[2][32];
-    tc_ld32(t_s + 64 * h, sv[0]);
-    tc_ld32(t_s + 64 * h + 32, sv[1]);
-    tc_wait_ld();
-    uint32_t pw[32];
+  for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int col = 64 * h + 32 * c + i;
-        const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1])), sc, nm);
-        float2 p;
-        if constexpr (RAGGED) {
-          p.x = col < valid ? fast_exp2(x.x) : 0.f;
-          p.y = col + 1 < valid ? fast_exp2(x.y) : 0.f;
-        } else {
-          p.x = fast_exp2(x.x);
-          p.y = fast_exp2(x.y);
-        }
-        sum = __fadd2_rn(sum, p);
-        pw[16 * c + i / 2] = pack_bf16x2(p.x, p.y);
+    for (int i = 0; i < 32; i += 2) {
+      const int col = 64 * h + 32 * c + i;
+      const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1])), sc, nm);
+      float2 p;
+      if constexpr (RAGGED) {
+        p.x = col < valid ? fast_exp2(x.x) : 0.f;
+        p.y = col + 1 < valid ? fast_exp2(x.y) : 0.f;
+      } else {
+        p.x = fast_exp2(x.x);
+        p.y = fast_exp2(x.y);
       }
-    tc_st32(t_s + 32 * h, pw);
-  }
+      sum = __fadd2_rn(sum, p);
+      pw[16 * c + i / 2] = pack_bf16x2(p.x, p.y);
+    }
+  tc_st32(t_s + 32 * h, pw);
+  return sum;
+}
+
+// P = 2^(S * scale_log2 - m): the first half from the registers row_max_keep
+// left, the second half reloaded (its S columns are untouched until then:
+// the first half's P overwrites S columns 0-31 only).  Returns the fp32 row
+// sum of the weights.
+template <bool RAGGED>
+__device__ __forceinline__ float write_p_keep(const uint32_t (&s0)[2][32], uint32_t t_s, int valid,
+                                              float scale_log2, float neg_m) {
+  const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(neg_m, neg_m);
+  float2 sum = p_half<RAGGED>(s0, t_s, 0, valid, sc, nm, make_float2(0.f, 0.f));
+  uint32_t s1[2][32];
+  tc_ld32(t_s + 64, s1[0]);
+  tc_ld32(t_s + 96, s1[1]);
+  tc_wait_ld();
+  sum = p_half<RAGGED>(s1, t_s, 1, valid, sc, nm, sum);
   return sum.x + sum.y;
 }
 
@@ -972,6 +977,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       bool ok = true;
       int g = 0;
+      uint64_t wait_kv = 0, wait_p = 0;  // diagnostics (trace): time spent waiting for K/V tiles and for P
+      auto timed_wait = [&](uint64_t* bar, uint32_t ph, uint64_t& acc) {
+        if (!trace) return mbar_wait_for(bar, ph, WAIT_NS);
+        const uint64_t t0 = global_timer_ns();
+        const bool r = mbar_wait_for(bar, ph, WAIT_NS);
+        acc += global_timer_ns() - t0;
+        return r;
+      };
       for (int it = ib, n = 0; it < ie && ok; ++it, ++n) {
         const Item I = load_item<SPANS>(P, staged, it, tid);
         const int nt = tiles_of(I);
@@ -985,17 +998,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < nt && ok; ++j) {
           const int gj = g + j, st = gj % STAGES, st1 = (gj + 1) % STAGES;
           const bool more = j + 1 < nt;
-          ok = mbar_wait_for(&v_full[st], (gj / STAGES) & 1, WAIT_NS) && mbar_wait_for(&p_full[0], gj & 1, WAIT_NS);
+          ok = timed_wait(&v_full[st], (gj / STAGES) & 1, wait_kv) && timed_wait(&p_full[0], gj & 1, wait_p);
           if (!ok) break;
           tc_fence_after();
           issue_pv(gj, j, 0);
           if (more) {
-            ok = mbar_wait_for(&k_full[st1], ((gj + 1) / STAGES) & 1, WAIT_NS);
+            ok = timed_wait(&k_full[st1], ((gj + 1) / STAGES) & 1, wait_kv);
             if (!ok) break;
             tc_fence_after();
             issue_s(gj + 1, 0);
           }
-          ok = mbar_wait_for(&p_full[1], gj & 1, WAIT_NS);
+          ok = timed_wait(&p_full[1], gj & 1, wait_p);
           if (!ok) break;
           tc_fence_after();
           issue_pv(gj, j, 1);
@@ -1008,6 +1021,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         g += nt;
       }
       if (!ok) fail();
+      if (trace) {
+        trace[30] = wait_kv;
+        trace[31] = wait_p;
+      }
       // Everything issued has finished before TMEM can be released.
       tc_commit(drain);
       mbar_wait_for(drain, 0, WAIT_NS);
@@ -1041,7 +1058,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
         const int valid = min(BN, I.n_tokens - j * BN);
-        const float mx = (valid < BN ? row_max<true>(t_s, valid) : row_max<false>(t_s, valid)) * P.scale_log2;
+        uint32_t s0[2][32];
+        const float mx =
+            (valid < BN ? row_max_keep<true>(t_s, valid, s0) : row_max_keep<false>(t_s, valid, s0)) * P.scale_log2;
         // P_x(j-1) consumed and O_x(j-1) complete before this tile writes either.
         if (j > 0) {
           ok = mbar_wait_for(&o_done[x], (gj - 1) & 1, WAIT_NS);
@@ -1072,8 +1091,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           l_run *= alpha;
           m_run = m_new;
         }
-        l_run += valid < BN ? write_p<true>(t_s, valid, P.scale_log2, -m_run)
-                            : write_p<false>(t_s, valid, P.scale_log2, -m_run);
+        l_run += valid < BN ? write_p_keep<true>(s0, t_s, valid, P.scale_log2, -m_run)
+                            : write_p_keep<false>(s0, t_s, valid, P.scale_log2, -m_run);
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[x]);
