@@ -386,6 +386,9 @@ MAX_SPANS_PER_CTA = 16
 # 2-bit packed stage) and entering a new segment costs 0.4 packed stages.
 DENSE_UNIT_COST = 0.83
 SEGMENT_SWITCH_STAGES = 0.4
+# A unit past a growing suffix's live length copies and computes nothing but
+# still passes through its warp's loop: about this fraction of a dense unit.
+EMPTY_UNIT_COST = 0.1
 
 
 @dataclass
@@ -635,6 +638,7 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
 
     spans: list[UcbSpan] = []
     span_bytes: list[float] = []
+    growing: set[int] = set()  # spans that are growing suffixes
     keepalive: list = []
     pairs_info: list[tuple[int, int]] = []
     cfg = None
@@ -679,8 +683,10 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
                     device = seg.key.device
                 elif isinstance(seg, GrowingSuffix):
                     rows = dense_rows_token_major(seg.key, seg.value, h, seg.length)
-                    # weighted at half its capacity: its average fill over a decode run
+                    # counted at half its capacity (its average fill over a decode run);
+                    # its units are weighted by how often each is live (below)
                     add(_dense_span(rows), pair, rows.tokens * head_dim * 4 * 0.5)
+                    growing.add(len(spans) - 1)
                     keepalive.append(seg)
                     device = seg.key.device
                 else:
@@ -724,6 +730,14 @@ def build_decode_plan(sequences: list[list], *, num_kv_heads: int, head_dim: int
         for k in range(units):
             n = min(stage, sp.tokens - k * stage)
             w = per_token * n * cost
+            if s in growing:
+                # unit k is live over the last (capacity - first row) / capacity
+                # of the decode steps: weight it by that share (live units sit at
+                # the suffix's front, so a uniform weight would overload the warps
+                # that hold them), plus the pass of an empty unit
+                live = (sp.tokens - k * stage) / sp.tokens
+                full = (head_dim * 4) * n * cost
+                w = full * (live + (1.0 - live) * EMPTY_UNIT_COST)
             if k == 0 and new_segment:
                 w += SEGMENT_SWITCH_STAGES * packed_stage_bytes
             unit_weights.append(w)
