@@ -212,3 +212,22 @@ def test_materialize_kivi_and_h2o_requests():
             key=key, value=value, key_type_ids=types, sample_lens=torch.tensor([96]),
             keep_masks=[torch.ones(96, dtype=torch.bool, device="cuda")],
             physical_requests=[[kivi_req, overlap]])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("tokens,queries", [(97, 5), (64, 1), (1000, 37)])
+def test_scores_without_lse_ragged(dtype, tokens, queries):
+    """The LSE pass (64-token blocks x 32-row chunks, partials folded over
+    the blocks) at sizes that fill neither, then the scores, against the
+    float64 column sums of the materialised probabilities."""
+
+    need_gpu()
+    key, _ = make_kv(tokens, 4, 128, seed=tokens, dtype=dtype, device="cuda")
+    query = (torch.randn(queries, 28, 128, generator=torch.Generator().manual_seed(queries)) * 0.5).to(dtype).cuda()
+    scores = kernels.h2o_scores(query, key, None, kv_heads=4, softmax_scale=1 / np.sqrt(128))
+    logits = attention.gqa_query_key_logits(host(query).astype(np.float64), host(key).astype(np.float64)) / np.sqrt(128)
+    probs = np.exp(logits - logits.max(-1, keepdims=True))
+    probs /= probs.sum(-1, keepdims=True)
+    expect = h2o.reduce_probabilities(probs, 4)
+    np.testing.assert_allclose(host(scores), expect, rtol=1e-4 if dtype == torch.float32 else 2e-3, atol=1e-6)
+    assert kernels.device_status() == 0
