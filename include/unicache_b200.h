@@ -372,8 +372,8 @@ typedef struct ucb_lq_stage_job {
  * 128] (token rows) and vt_ws [heads, 128, ws_rows] (values transposed).
  * Dense spans are copied; packed spans are restored as code * scale +
  * minimum with one rounding to bf16, the values ucb_long_query_attention
- * restores in its operand tiles.  Grid: max_chunks x num_jobs blocks of 64
- * tokens (max_chunks * 64 >= the largest `rows`; ws_rows a multiple of 128). */
+ * restores in its operand tiles.  Grid: max_chunks x num_jobs blocks of 32
+ * tokens (max_chunks * 32 >= the largest `rows`; ws_rows a multiple of 128). */
 /* Diagnostics: when trace_dev (device memory, 32 uint64 per CTA) is not
  * NULL, later long-query and prefill launches record per CTA (global timer,
  * ns): word 0 = kernel entry, 1 = set-up done, 2 = SM id, 3 = exit, 4 = items

@@ -576,17 +576,17 @@ constexpr int Q_THREADS = 256;
 struct StageJob {
   int head, span_begin, span_count, tokens, ws_row0, rows, pad0, pad1;
 };
-constexpr int STAGE_T = 64;          // tokens per staging block
-constexpr int STAGE_THREADS = 256;
+constexpr int STAGE_T = 32;          // tokens per staging block
+constexpr int STAGE_THREADS = 128;
 constexpr int STAGE_PITCH = D + 8;   // bf16 per token row of a block's value rows
 
-// Block (x, job): tokens [64 x, 64 x + 64) of the job's key space.  The job's
+// Block (x, job): tokens [32 x, 32 x + 32) of the job's key space.  The job's
 // span records are staged in shared memory (STAGE_SPANS at a time) and each
 // token is mapped to its span once; each thread then issues the loads of all
 // its (token, 8-channel chunk) items before restoring any, so a block waits
 // for memory about once per span batch.  K rows go straight to the workspace
 // (16-byte chunks, coalesced); value rows gather in shared memory and leave
-// as V^T rows of 64 tokens (128 bytes per channel).
+// as V^T rows of 32 tokens (64 bytes per channel).
 constexpr int STAGE_SPANS = 16;
 constexpr int STAGE_ITEMS = STAGE_T * 16 / STAGE_THREADS;  // items per thread per block
 

@@ -1368,7 +1368,7 @@ _LQ_TABLES: dict = {}
 _LQ_TABLES_MAX = 64
 
 
-LQ_STAGE_TOKENS = 64          # tokens per staging block (ucb_long_query_stage)
+LQ_STAGE_TOKENS = 32          # tokens per staging block (ucb_long_query_stage)
 LQ_STAGE_MIN_ROW_BLOCKS = 1   # stage the keys when at least this many row blocks read each key space
 # (measured on the configuration-4 segment mix, CUDA graphs: staged 45-70 us
 # against 64-100 us in place from 8 to 1024 query positions, so always)
