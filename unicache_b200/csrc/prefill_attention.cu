@@ -11,9 +11,11 @@
 // q rows are the (query position, head-in-group) pairs of one KV head, so the
 // grouped-query structure becomes a plain M x N attention per KV head.
 //
-// Design: one CTA per 256 query rows (two 128-row tiles A and B) of one KV
-// head, warp-specialised so that the tensor core works on one tile while the
-// other tile's softmax runs:
+// Design: a CTA works on 256 query rows (two 128-row tiles A and B) of one KV
+// head at a time -- one such item per CTA, or, in a persistent launch, a list
+// of items (pieces of row blocks over key-tile ranges) run back to back --
+// warp-specialised so that the tensor core works on one tile while the other
+// tile's softmax runs:
 //  * warp 8 (one lane) loads Q_A, Q_B once and streams K tiles (128 tokens x
 //    128 channels) and V^T tiles (128 channels x 128 tokens) by TMA with
 //    128-byte swizzle (the canonical K-major tcgen05 operand layout) through a
