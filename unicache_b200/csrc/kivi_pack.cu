@@ -243,7 +243,7 @@ struct PackSide {
 };
 
 template <int KB, int VB, int G>
-__global__ void __launch_bounds__(256, 2) pack_kv_kernel(PackSide k, PackSide v, int tokens, int heads, int key_blocks) {
+__global__ void __launch_bounds__(256, 4) pack_kv_kernel(PackSide k, PackSide v, int tokens, int heads, int key_blocks) {
   using T = __nv_bfloat16;
   constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
   if (static_cast<int>(blockIdx.x) < key_blocks) {
@@ -272,7 +272,7 @@ struct PackJob {
 };
 
 template <int KB, int VB, int G>
-__global__ void __launch_bounds__(256, 2) pack_kv_batched_kernel(const PackJob* __restrict__ jobs, int heads) {
+__global__ void __launch_bounds__(256, 4) pack_kv_batched_kernel(const PackJob* __restrict__ jobs, int heads) {
   using T = __nv_bfloat16;
   constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
   const PackJob& j = jobs[blockIdx.y];
