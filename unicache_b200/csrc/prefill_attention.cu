@@ -772,6 +772,99 @@ __device__ __forceinline__ void settle_flags(const Params& P, const Item& I) {
   }
 }
 
+// The item's result from its O accumulators (this thread's TMEM lane t_o)
+// and running max / sum: a partial item writes its normalised fp32 rows and
+// log2 LSE to its slot; a final or merge item (the latter after folding in
+// its partners' partials, which it waits for) writes bf16 rows and the
+// natural-log LSE in the launch's layout.  Called by every softmax thread.
+__device__ __forceinline__ void write_item_result(const Params& P, const Item& I, bool caller_layout, bool good,
+                                                  int nt, int r_blk, int lane, uint32_t t_o, float m_run,
+                                                  float l_run, int* failed) {
+  const int m = I.m0 + r_blk;
+  const bool live = m < I.m_end;
+  bool merged = false;
+  if (!good) {
+    if (lane == 0) atomicOr(failed, 1);
+  } else if (nt == 0) {
+    // an item without keys writes nothing (the host never builds one)
+  } else if (I.mode == ITEM_PARTIAL) {
+    float* part = P.partials + (int64_t)I.slot * PARTIAL_SLOT_FLOATS;
+    const float inv = 1.f / l_run;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tc_ld32(t_o + 32 * c, ov);
+      tc_wait_ld();
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) part[(32 * c + i) * (2 * BM) + r_blk] = __uint_as_float(ov[i]) * inv;
+      }
+    }
+    if (live) part[D * 2 * BM + r_blk] = m_run + __log2f(l_run);
+    __threadfence();
+  } else {
+    // ITEM_FINAL, or ITEM_MERGE: fold in the partners' rows once published.
+    float w_own = 1.f, lse2 = m_run + __log2f(l_run), mx = lse2, inv_sum = 1.f;
+    if (I.mode == ITEM_MERGE) {
+      bool all_in = true;
+      for (int k = 0; k < I.nparts; ++k) all_in = all_in && wait_flag(P.flags + I.slot + k, WAIT_NS);
+      merged = __all_sync(0xffffffffu, all_in);
+      if (!merged) {
+        if (lane == 0) atomicOr(failed, 1);
+      } else if (live) {
+        for (int k = 0; k < I.nparts; ++k)
+          mx = fmaxf(mx, __ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk));
+        float sum = fast_exp2(lse2 - mx);
+        for (int k = 0; k < I.nparts; ++k)
+          sum += fast_exp2(__ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk) - mx);
+        inv_sum = 1.f / sum;
+        w_own = fast_exp2(lse2 - mx) * inv_sum;
+        lse2 = mx + __log2f(sum);
+      }
+    }
+    const float inv = w_own / l_run;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tc_ld32(t_o + 32 * c, ov);
+      tc_wait_ld();
+      if (live) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[i]) * inv;
+        if (merged) {
+#pragma unroll 2
+          for (int k = 0; k < I.nparts; ++k) {
+            const float* part = P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS;
+            const float wp = fast_exp2(__ldcg(part + D * 2 * BM + r_blk) - mx) * inv_sum;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = fmaf(wp, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
+          }
+        }
+        __nv_bfloat16* dst =
+            caller_layout
+                ? P.out + ((int64_t)(I.pos0 + m / P.grp) * P.hq + I.head * P.grp + m % P.grp) * D + 32 * c
+                : P.out + ((int64_t)I.head * P.m_rows + m) * D + 32 * c;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w4;
+          w4.x = pack_bf16x2(v[i], v[i + 1]);
+          w4.y = pack_bf16x2(v[i + 2], v[i + 3]);
+          w4.z = pack_bf16x2(v[i + 4], v[i + 5]);
+          w4.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          *reinterpret_cast<uint4*>(dst + i) = w4;
+        }
+      }
+    }
+    if (live && P.lse) {
+      const int64_t at = caller_layout
+                             ? (int64_t)(I.head * P.grp + m % P.grp) * P.positions + I.pos0 + m / P.grp
+                             : (int64_t)I.head * P.m_rows + m;
+      P.lse[at] = lse2 * 0.6931471805599453f;
+    }
+  }
+}
+
 // SPANS: keys and values come from the item's spans (producer warps 8, 10,
 // 11); otherwise from the K / V^T tensor maps (loader warp 8), with the query
 // from the Q tensor map (workspace launches) or the caller's layout (staged
@@ -1102,89 +1195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok && nt > 0) ok = mbar_wait_for(&o_done[x], (g + nt - 1) & 1, WAIT_NS);
       tc_fence_after();
       const bool good = __all_sync(0xffffffffu, ok);
-      const int m = I.m0 + r_blk;
-      const bool live = m < I.m_end;
-      bool merged = false;
-      if (!good) {
-        if (lane == 0) fail();
-      } else if (nt == 0) {
-        // an item without keys writes nothing (the host never builds one)
-      } else if (I.mode == ITEM_PARTIAL) {
-        float* part = P.partials + (int64_t)I.slot * PARTIAL_SLOT_FLOATS;
-        const float inv = 1.f / l_run;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc_ld32(t_o + 32 * c, ov);
-          tc_wait_ld();
-          if (live) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) part[(32 * c + i) * (2 * BM) + r_blk] = __uint_as_float(ov[i]) * inv;
-          }
-        }
-        if (live) part[D * 2 * BM + r_blk] = m_run + __log2f(l_run);
-        __threadfence();
-      } else {
-        // ITEM_FINAL, or ITEM_MERGE: fold in the partners' rows once published.
-        float w_own = 1.f, lse2 = m_run + __log2f(l_run), mx = lse2, inv_sum = 1.f;
-        if (I.mode == ITEM_MERGE) {
-          bool all_in = true;
-          for (int k = 0; k < I.nparts; ++k) all_in = all_in && wait_flag(P.flags + I.slot + k, WAIT_NS);
-          merged = __all_sync(0xffffffffu, all_in);
-          if (!merged) {
-            if (lane == 0) fail();
-          } else if (live) {
-            for (int k = 0; k < I.nparts; ++k)
-              mx = fmaxf(mx, __ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk));
-            float sum = fast_exp2(lse2 - mx);
-            for (int k = 0; k < I.nparts; ++k)
-              sum += fast_exp2(__ldcg(P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS + D * 2 * BM + r_blk) - mx);
-            inv_sum = 1.f / sum;
-            w_own = fast_exp2(lse2 - mx) * inv_sum;
-            lse2 = mx + __log2f(sum);
-          }
-        }
-        const float inv = w_own / l_run;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc_ld32(t_o + 32 * c, ov);
-          tc_wait_ld();
-          if (live) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ov[i]) * inv;
-            if (merged) {
-#pragma unroll 2
-              for (int k = 0; k < I.nparts; ++k) {
-                const float* part = P.partials + (int64_t)(I.slot + k) * PARTIAL_SLOT_FLOATS;
-                const float wp = fast_exp2(__ldcg(part + D * 2 * BM + r_blk) - mx) * inv_sum;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = fmaf(wp, __ldcg(part + (32 * c + i) * (2 * BM) + r_blk), v[i]);
-              }
-            }
-            __nv_bfloat16* dst =
-                caller_layout
-                    ? P.out + ((int64_t)(I.pos0 + m / P.grp) * P.hq + I.head * P.grp + m % P.grp) * D + 32 * c
-                    : P.out + ((int64_t)I.head * P.m_rows + m) * D + 32 * c;
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 w4;
-              w4.x = pack_bf16x2(v[i], v[i + 1]);
-              w4.y = pack_bf16x2(v[i + 2], v[i + 3]);
-              w4.z = pack_bf16x2(v[i + 4], v[i + 5]);
-              w4.w = pack_bf16x2(v[i + 6], v[i + 7]);
-              *reinterpret_cast<uint4*>(dst + i) = w4;
-            }
-          }
-        }
-        if (live && P.lse) {
-          const int64_t at = caller_layout
-                                 ? (int64_t)(I.head * P.grp + m % P.grp) * P.positions + I.pos0 + m / P.grp
-                                 : (int64_t)I.head * P.m_rows + m;
-          P.lse[at] = lse2 * 0.6931471805599453f;
-        }
-      }
+      write_item_result(P, I, caller_layout, good, nt, r_blk, lane, t_o, m_run, l_run, &failed);
       // The softmax warps meet once per item: a partial is published after
       // every row is written; consumed partials' flags advance after every
       // row is read.  A failed item still settles its flags (its CTA has set
