@@ -188,6 +188,36 @@ def test_constant_groups_use_epsilon_scale():
     assert torch.equal(rk, key) and torch.equal(rv, value)
 
 
+@pytest.mark.parametrize("bits,pattern", [
+    (2, [0.0, 3.0, 0.5, 1.5, 2.5, 1.0, 2.0, 0.5]),
+    (4, [0.0, 15.0, 0.5, 7.5, 14.5, 3.0, 11.5, 6.5]),
+])
+@pytest.mark.parametrize("gain", [1.0, 0.3, -1.7])
+def test_half_integer_ties_bit_exact_vs_oracle(bits, pattern, gain):
+    """Every 32-token key group and every 32-channel value group holds its
+    minimum, its maximum and values whose code lies exactly on (gain 1) or
+    next to (other gains, after bf16 rounding) a half-integer: those take
+    the quantizer's exact-division fallback, whose round-half-even must match
+    the oracle bit for bit."""
+
+    need_gpu()
+    t, c = np.meshgrid(np.arange(256), np.arange(128), indexing="ij")
+    base = np.asarray(pattern, np.float32)[(t + c) % len(pattern)] * np.float32(gain)
+    key = torch.from_numpy(np.stack([base, base[::-1]], axis=1)).to(torch.bfloat16).cuda()
+    value = torch.from_numpy(np.stack([base[:, ::-1], base], axis=1)).to(torch.bfloat16).cuda()
+    cache = PackedKIVICache.from_dense(key, value, logical_token_ids=torch.arange(256, device="cuda"),
+                                       token_type_id=3, k_bits=bits, v_bits=bits, group_size=32,
+                                       residual_length=0)
+    expect = kivi.packed_from_dense(host(key), host(value), "bfloat16", k_bits=bits, v_bits=bits, group_size=32,
+                                    residual_length=0)
+    ref = cache.reference_layout()
+    for field in ("key_code", "value_code", "key_scale", "key_minimum", "value_scale", "value_minimum"):
+        np.testing.assert_array_equal(host(ref[field].contiguous()), expect[field], err_msg=field)
+    if gain == 1.0:  # scale exactly 1: the codes are the round-half-even of the values themselves
+        rk, _ = cache.dequantize(dtype=torch.float32)
+        np.testing.assert_array_equal(host(rk)[:, 0], np.rint(base))
+
+
 def test_full_size_config2_pack_is_bit_exact():
     """Config 2 shape (16 sequences x 8192+128 tokens, 2-bit, G32): codes and
     statistics of every sequence equal the oracle's; dequantize is idempotent

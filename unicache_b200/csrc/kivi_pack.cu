@@ -7,6 +7,7 @@
 // round-half-even (rintf), and stores into bf16/fp16 round to nearest even.
 // This translation unit must not be compiled with fast-math.
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -28,22 +29,69 @@ __device__ __forceinline__ uint32_t quant_code(float v, float mn, float scale, f
   return static_cast<uint32_t>(q);
 }
 
-// Two codes with the same results as quant_code, without a division per
-// element: |d * RN(1/scale) - RN(d/scale)| < 2^-22 * q, below 2^-14 for
-// q < 2^8, so a product more than 2^-12 away from a half-integer rounds to the
-// same integer; the rare products closer than that (or q >= 2^8) take the
-// exact division.  The subtraction and the product run as packed fp32 pairs
-// (each lane rounds like the scalar operation).
-__device__ __forceinline__ uint2 quant_code_fast2(float va, float vb, float mna, float mnb, float sca, float scb,
-                                                  float inva, float invb, float max_code) {
-  const float2 d = __fadd2_rn(make_float2(va, vb), make_float2(-mna, -mnb));
-  const float2 q = __fmul2_rn(d, make_float2(inva, invb));
-  float ca = rintf(q.x), cb = rintf(q.y);
-  if (!(0.5f - fabsf(q.x - ca) > 0x1p-12f) || q.x >= 256.0f) ca = rintf(__fdiv_rn(d.x, sca));
-  if (!(0.5f - fabsf(q.y - cb) > 0x1p-12f) || q.y >= 256.0f) cb = rintf(__fdiv_rn(d.y, scb));
-  ca = fminf(fmaxf(ca, 0.0f), max_code);
-  cb = fminf(fmaxf(cb, 0.0f), max_code);
-  return make_uint2(static_cast<uint32_t>(ca), static_cast<uint32_t>(cb));
+// Codes of two values with the results of quant_code, without a division or
+// a float-to-integer conversion per element.  q = RN(d * RN(1/scale)) differs
+// from RN(d / scale) by less than 2^-22 q, below 2^-14 because 0 <= q <=
+// max_code (1 + 2^-22) < 2^8 for finite inputs (d = RN(v - mn) lies in
+// [0, RN(mx - mn)]), so unless q is within 2^-12 of a half-integer both round
+// to the same integer.  Adding 1.5 * 2^23 rounds q to an integer, ties to
+// even like rintf, in the low mantissa bits: the sum's bit pattern is
+// kRoundBits + code, and the clamps of quant_code cannot act.  A product
+// within 2^-12 of a half-integer (or not finite) takes quant_code itself.
+// Returned as bit patterns kRoundBits + code, which pack_bits folds into a
+// word with one shift-add each.
+constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t kRoundBits = 0x4B400000u;
+
+// The exact fallback, out of line: inlined at every pair of the unrolled
+// loops its divisions would crowd the instruction cache for a path that is
+// almost never taken.
+__device__ __noinline__ uint2 quant_exact2(float2 v, float2 mn, float2 sc, float max_code) {
+  return make_uint2(kRoundBits + quant_code(v.x, mn.x, sc.x, max_code),
+                    kRoundBits + quant_code(v.y, mn.y, sc.y, max_code));
+}
+
+__device__ __forceinline__ uint2 quant_bits2(float2 v, float2 mn, float2 sc, float2 inv, float max_code) {
+  const float2 d = __fadd2_rn(v, make_float2(-mn.x, -mn.y));
+  const float2 q = __fmul2_rn(d, inv);
+  const float2 t = __fadd2_rn(q, make_float2(kRound, kRound));
+  const float2 c = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 e = __fadd2_rn(q, make_float2(-c.x, -c.y));
+  constexpr float kEdge = 0.5f - 0x1p-12f;
+  uint2 r = make_uint2(__float_as_uint(t.x), __float_as_uint(t.y));
+  if (!(fabsf(e.x) < kEdge && fabsf(e.y) < kEdge)) r = quant_exact2(v, mn, sc, max_code);
+  return r;
+}
+
+// What N codes of BITS bits, each carried as kRoundBits + code and added
+// in at shifts 0, BITS, 2 BITS, ..., leave in a 32-bit word beyond the codes
+// (arithmetic modulo 2^32).
+template <int BITS, int N>
+__host__ __device__ constexpr uint32_t round_bias() {
+  uint32_t s = 0;
+  for (int j = 0; j < N; ++j) s += kRoundBits << (j * BITS);
+  return s;
+}
+
+// Element-wise minimum and maximum of two packed pairs of 16-bit values
+// (NaN loses to a number, as with fminf / fmaxf; exact, no rounding).
+template <typename T>
+__device__ __forceinline__ uint32_t min_pair(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t max_pair(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
 // ---------------------------------------------------------------- key pack
@@ -51,40 +99,53 @@ __device__ __forceinline__ uint2 quant_code_fast2(float va, float vb, float mna,
 // so a warp reads 64 channels (a full 128-byte line for 16-bit inputs) per
 // token row.  Groups run along tokens: a thread reduces two columns of G
 // values and emits G*bits/32 words per channel.  Loads are issued 32 rows at
-// a time before any reduction; for G = 32 the values stay in registers for
-// the code pass, larger groups re-read them from L1.
+// a time before any reduction, and 16-bit inputs are reduced as packed pairs
+// (one min and one max instruction per row for both channels); for G = 32
+// the raw words stay in registers for the code pass, larger groups re-read
+// them from L1.
 template <typename T, int BITS, int G>
 __device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t stride_t, int64_t stride_h, int tokens,
                                               int head_dim, uint32_t* __restrict__ codes32,
                                               uint8_t* __restrict__ codes8, T* __restrict__ scale,
                                               T* __restrict__ minimum, int g, int h, int pair) {
   constexpr int CH = 32;
+  constexpr bool kPair16 = sizeof(T) == 2;
   using V2 = typename Dtype<T>::vec2;
   const int d = 2 * pair;
   if (d >= head_dim) return;
   const int groups = tokens / G;
   const T* col = x + static_cast<int64_t>(g) * G * stride_t + h * stride_h + d;
-  float a[CH], b[CH];
+  V2 w[CH];
   float mna = INFINITY, mxa = -INFINITY, mnb = INFINITY, mxb = -INFINITY;
 #pragma unroll
   for (int c0 = 0; c0 < G; c0 += CH) {
 #pragma unroll
-    for (int i = 0; i < CH; ++i) {
-      const V2 pr = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
-      a[i] = Dtype<T>::lo(pr);
-      b[i] = Dtype<T>::hi(pr);
-    }
+    for (int i = 0; i < CH; ++i) w[i] = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
+    if constexpr (kPair16) {
+      uint32_t lo = w[0], hi = w[0];
 #pragma unroll
-    for (int i = 0; i < CH; ++i) {
-      mna = fminf(mna, a[i]);
-      mxa = fmaxf(mxa, a[i]);
-      mnb = fminf(mnb, b[i]);
-      mxb = fmaxf(mxb, b[i]);
+      for (int i = 1; i < CH; ++i) {
+        lo = min_pair<T>(lo, w[i]);
+        hi = max_pair<T>(hi, w[i]);
+      }
+      mna = fminf(mna, Dtype<T>::lo(lo));
+      mnb = fminf(mnb, Dtype<T>::hi(lo));
+      mxa = fmaxf(mxa, Dtype<T>::lo(hi));
+      mxb = fmaxf(mxb, Dtype<T>::hi(hi));
+    } else {
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        mna = fminf(mna, Dtype<T>::lo(w[i]));
+        mxa = fmaxf(mxa, Dtype<T>::lo(w[i]));
+        mnb = fminf(mnb, Dtype<T>::hi(w[i]));
+        mxb = fmaxf(mxb, Dtype<T>::hi(w[i]));
+      }
     }
   }
   constexpr float kMax = static_cast<float>((1 << BITS) - 1);
   const float sca = quant_scale(mna, mxa, kMax), scb = quant_scale(mnb, mxb, kMax);
-  const float inva = __frcp_rn(sca), invb = __frcp_rn(scb);
+  const float2 mn = make_float2(mna, mnb), sc = make_float2(sca, scb);
+  const float2 inv = make_float2(__frcp_rn(sca), __frcp_rn(scb));
   const int64_t stat = (static_cast<int64_t>(h) * groups + g) * head_dim + d;
   scale[stat] = Dtype<T>::from_f(sca);
   scale[stat + 1] = Dtype<T>::from_f(scb);
@@ -94,34 +155,32 @@ __device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t s
   for (int c0 = 0; c0 < G; c0 += CH) {
     if (G > CH) {
 #pragma unroll
-      for (int i = 0; i < CH; ++i) {
-        const V2 pr = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
-        a[i] = Dtype<T>::lo(pr);
-        b[i] = Dtype<T>::hi(pr);
-      }
+      for (int i = 0; i < CH; ++i) w[i] = *reinterpret_cast<const V2*>(col + static_cast<int64_t>(c0 + i) * stride_t);
     }
     if constexpr (BITS == 8) {
       uint8_t* out = codes8 + (static_cast<int64_t>(h) * tokens + static_cast<int64_t>(g) * G + c0) * head_dim + d;
 #pragma unroll
-      for (int i = 0; i < CH; ++i)
-      {
-        const uint2 c = quant_code_fast2(a[i], b[i], mna, mnb, sca, scb, inva, invb, kMax);
-        *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) = static_cast<uint16_t>(c.x | (c.y << 8));
+      for (int i = 0; i < CH; ++i) {
+        const uint2 c = quant_bits2(make_float2(Dtype<T>::lo(w[i]), Dtype<T>::hi(w[i])), mn, sc, inv, kMax);
+        *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) =
+            static_cast<uint16_t>(c.x + (c.y << 8) - round_bias<8, 2>());
       }
     } else {
       constexpr int F = 32 / BITS;
       uint32_t* out = codes32 + (static_cast<int64_t>(h) * (tokens / F) + (static_cast<int64_t>(g) * G + c0) / F) *
                                     head_dim + d;
 #pragma unroll
-      for (int w = 0; w < CH / F; ++w) {
+      for (int k = 0; k < CH / F; ++k) {
         uint32_t wa = 0, wb = 0;
 #pragma unroll
         for (int j = 0; j < F; ++j) {
-          const uint2 c = quant_code_fast2(a[w * F + j], b[w * F + j], mna, mnb, sca, scb, inva, invb, kMax);
-          wa |= c.x << (j * BITS);
-          wb |= c.y << (j * BITS);
+          const V2 e = w[k * F + j];
+          const uint2 c = quant_bits2(make_float2(Dtype<T>::lo(e), Dtype<T>::hi(e)), mn, sc, inv, kMax);
+          wa += c.x << (j * BITS);
+          wb += c.y << (j * BITS);
         }
-        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(w) * head_dim) = make_uint2(wa, wb);
+        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(k) * head_dim) =
+            make_uint2(wa - round_bias<BITS, F>(), wb - round_bias<BITS, F>());
       }
     }
   }
@@ -139,9 +198,10 @@ __global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, i
 
 // ---------------------------------------------------------------- value pack
 // One thread per (token row, channel group): it reads the group's G channels
-// with 16-byte loads, reduces them locally and writes G*bits/32 words and its
-// two statistics.  Consecutive threads take consecutive groups of consecutive
-// rows, so a warp reads one contiguous span of the input.
+// with 16-byte loads, reduces them locally (16-bit inputs as packed pairs)
+// and writes G*bits/32 words and its two statistics.  Consecutive threads
+// take consecutive groups of consecutive rows, so a warp reads one
+// contiguous span of the input.
 template <typename T, int BITS, int D, int G, bool VEC>
 __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t stride_t, int64_t stride_h,
                                                 int tokens, int heads, uint32_t* __restrict__ codes32,
@@ -149,34 +209,66 @@ __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t
                                                 T* __restrict__ minimum, int64_t item) {
   constexpr int NG = D / G;                     // groups per row
   constexpr int EPV = 16 / (int)sizeof(T);      // elements per 16-byte load
+  constexpr bool kPair16 = VEC && sizeof(T) == 2;
   const int64_t n_items = static_cast<int64_t>(tokens) * heads * NG;
   if (item >= n_items) return;
   const int gi = static_cast<int>(item % NG);
   const int64_t row = item / NG;
   const int t = static_cast<int>(row / heads), h = static_cast<int>(row % heads);
   const T* src = x + t * stride_t + h * stride_h + gi * G;
-  float v[G];
-  if constexpr (VEC) {  // 16-byte aligned rows
+  // the group as G/2 pairs: raw 16-bit pairs, or fp32 pairs
+  uint32_t r[kPair16 ? G / 2 : 1];
+  float v[kPair16 ? 1 : G];
+  float mn, mx;
+  if constexpr (kPair16) {
 #pragma unroll
-    for (int c = 0; c < G; c += EPV) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(src + c);
-      const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int j = 0; j < EPV; ++j) v[c + j] = Dtype<T>::to_f(e[j]);
+    for (int c = 0; c < G / 2; c += 4) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + 2 * c);
+      r[c] = raw.x;
+      r[c + 1] = raw.y;
+      r[c + 2] = raw.z;
+      r[c + 3] = raw.w;
     }
+    uint32_t lo = r[0], hi = r[0];
+#pragma unroll
+    for (int j = 1; j < G / 2; ++j) {
+      lo = min_pair<T>(lo, r[j]);
+      hi = max_pair<T>(hi, r[j]);
+    }
+    mn = fminf(Dtype<T>::lo(lo), Dtype<T>::hi(lo));
+    mx = fmaxf(Dtype<T>::lo(hi), Dtype<T>::hi(hi));
   } else {
+    if constexpr (VEC) {  // 16-byte aligned rows
 #pragma unroll
-    for (int c = 0; c < G; ++c) v[c] = ld(src + c);
-  }
-  float mn = v[0], mx = v[0];
+      for (int c = 0; c < G; c += EPV) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src + c);
+        const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-  for (int j = 1; j < G; ++j) {
-    mn = fminf(mn, v[j]);
-    mx = fmaxf(mx, v[j]);
+        for (int j = 0; j < EPV; ++j) v[c + j] = Dtype<T>::to_f(e[j]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < G; ++c) v[c] = ld(src + c);
+    }
+    mn = v[0];
+    mx = v[0];
+#pragma unroll
+    for (int j = 1; j < G; ++j) {
+      mn = fminf(mn, v[j]);
+      mx = fmaxf(mx, v[j]);
+    }
   }
+  // values 2p and 2p + 1 of the group as fp32
+  auto pair_at = [&](int p) {
+    if constexpr (kPair16)
+      return make_float2(Dtype<T>::lo(r[p]), Dtype<T>::hi(r[p]));
+    else
+      return make_float2(v[2 * p], v[2 * p + 1]);
+  };
   constexpr float kMax = static_cast<float>((1 << BITS) - 1);
   const float sc = quant_scale(mn, mx, kMax);
   const float inv = __frcp_rn(sc);
+  const float2 mn2 = make_float2(mn, mn), sc2 = make_float2(sc, sc), inv2 = make_float2(inv, inv);
   const int64_t out_row = static_cast<int64_t>(h) * tokens + t;
   scale[out_row * NG + gi] = Dtype<T>::from_f(sc);
   minimum[out_row * NG + gi] = Dtype<T>::from_f(mn);
@@ -190,9 +282,10 @@ __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t
         w[q] = 0;
 #pragma unroll
         for (int j = 0; j < 4; j += 2) {
-          const uint2 cc = quant_code_fast2(v[c + 4 * q + j], v[c + 4 * q + j + 1], mn, mn, sc, sc, inv, inv, kMax);
-          w[q] |= (cc.x << (8 * j)) | (cc.y << (8 * (j + 1)));
+          const uint2 cc = quant_bits2(pair_at((c + 4 * q + j) / 2), mn2, sc2, inv2, kMax);
+          w[q] += (cc.x << (8 * j)) + (cc.y << (8 * (j + 1)));
         }
+        w[q] -= round_bias<8, 4>();
       }
       *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -205,9 +298,10 @@ __device__ __forceinline__ void pack_value_item(const T* __restrict__ x, int64_t
       w[k] = 0;
 #pragma unroll
       for (int j = 0; j < F; j += 2) {
-        const uint2 cc = quant_code_fast2(v[k * F + j], v[k * F + j + 1], mn, mn, sc, sc, inv, inv, kMax);
-        w[k] |= (cc.x << (j * BITS)) | (cc.y << ((j + 1) * BITS));
+        const uint2 cc = quant_bits2(pair_at((k * F + j) / 2), mn2, sc2, inv2, kMax);
+        w[k] += (cc.x << (j * BITS)) + (cc.y << ((j + 1) * BITS));
       }
+      w[k] -= round_bias<BITS, F>();
     }
     uint32_t* out = codes32 + out_row * (D / F) + gi * W;
 #pragma unroll
