@@ -329,7 +329,8 @@ def decode_leg(run: Run, wl: Workload, *, headline: bool) -> dict:
     e2e_elapsed = eager_elapsed = 0.0
     if headline:
         # end to end through the public API with host buffers: DecodeStepGraph
-        # (H2D query, decode, merge, D2H out + LSE as one graph per step), and
+        # (query read from pinned host memory, decode, merge storing out + LSE
+        # to pinned host memory, as one graph per step), and
         # the eager per-call path with copy_ calls
         host_q = torch.empty_like(query, device="cpu").pin_memory()
         host_q.copy_(query.cpu())
@@ -800,7 +801,7 @@ def run_b200(args) -> None:
             "roofline": dict(head["roofline"], traffic=ncu_traffic() if wl.name == "config2" else None),
             "e2e": {"value": head["e2e_value"], "unit": "tokens/s", "h2d_bytes_per_step": head["h2d"],
                     "d2h_bytes_per_step": head["d2h"],
-                    "api": "DecodeStepGraph (per step: H2D query, decode, merge, D2H out + LSE, one graph launch)"},
+                    "api": "DecodeStepGraph (per step, one graph launch: copy kernel reads the query from pinned host memory, decode, merge stores out + LSE to pinned host memory)"},
             "e2e_eager": {"value": head["eager_value"], "unit": "tokens/s",
                           "api": "PhysicalDecodeBatch.__call__ with per-step copy_ calls"},
             "gpu_launches": 2 * args.steps,

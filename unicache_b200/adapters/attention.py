@@ -69,13 +69,16 @@ class DecodeStepGraph:
     """One decode step of a ``PhysicalDecodeBatch`` with its host transfers,
     captured as a CUDA graph: every replay reads the query from
     ``host_query``, decodes, and writes the output and LSE to ``host_out`` /
-    ``host_lse`` (all three pinned host tensors).  The transfers ride inside
-    the two kernels over the mapped pinned buffers.  The decode kernel loads
-    the query rows across PCIe, and the state merge stores the results
-    across PCIe.  So one step is one graph of two kernels instead of five
-    operations.  Capture once, then call it every step after writing the
-    next query into ``host_query``.  The call is asynchronous on the current
-    stream: synchronize before reading the host outputs."""
+    ``host_lse`` (all three pinned host tensors).  The transfers run in
+    kernels over the mapped pinned buffers, not as DMA copies: a copy kernel
+    reads the query across PCIe once into a device buffer (the decode
+    kernel's CTAs then read it from there; several CTAs share a sequence's
+    query rows under split-KV, so reading the host rows from the decode
+    kernel itself moved several times the query's bytes across PCIe), and
+    the state merge stores the results across PCIe.  So one step is one
+    graph of three kernels.  Capture once, then call it every step after
+    writing the next query into ``host_query``.  The call is asynchronous on
+    the current stream: synchronize before reading the host outputs."""
 
     def __init__(self, batch: PhysicalDecodeBatch, host_query: torch.Tensor, host_out: torch.Tensor,
                  host_lse: torch.Tensor):
@@ -96,7 +99,13 @@ class DecodeStepGraph:
         device = plan.device
         stream = torch.cuda.Stream(device=device)
         stream.wait_stream(torch.cuda.current_stream(device))
-        launch = lambda: plan.launch(q_ptr, hq * d, hq, o_ptr, hq * d, l_ptr, stream.cuda_stream)
+        self._query = torch.empty(b, hq, d, dtype=torch.bfloat16, device=device)
+        dq_ptr, q_bytes = self._query.data_ptr(), host_query.numel() * host_query.element_size()
+
+        def launch():
+            kernels.copy_ranges([(dq_ptr, q_ptr, q_bytes)], stream.cuda_stream)
+            plan.launch(dq_ptr, hq * d, hq, o_ptr, hq * d, l_ptr, stream.cuda_stream)
+
         launch()  # first-call set-up outside the capture
         stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
