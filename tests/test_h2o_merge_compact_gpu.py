@@ -215,14 +215,24 @@ def test_materialize_kivi_and_h2o_requests():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("tokens,queries", [(97, 5), (64, 1), (1000, 37)])
-def test_scores_without_lse_ragged(dtype, tokens, queries):
-    """The LSE pass (64-token blocks x 32-row chunks, partials folded over
-    the blocks) at sizes that fill neither, then the scores, against the
-    float64 column sums of the materialised probabilities."""
+@pytest.mark.parametrize("tokens,queries,misaligned", [(97, 5, False), (64, 1, False), (1000, 37, False),
+                                                       (1000, 80, False), (203, 11, True)])
+def test_scores_without_lse_ragged(dtype, tokens, queries, misaligned):
+    """The LSE pass (64-row x 64-token logit tiles, partials folded over the
+    token blocks) at sizes that fill no tile, then the scores, against the
+    float64 column sums of the materialised probabilities.  80 queries give
+    560 rows per KV head: more 64-row tiles than the scoring cluster has
+    blocks.  ``misaligned`` starts the keys 4 bytes past an aligned address
+    (the bf16 scoring kernel's minimum), so the LSE tiles are staged element
+    by element."""
 
     need_gpu()
     key, _ = make_kv(tokens, 4, 128, seed=tokens, dtype=dtype, device="cuda")
+    if misaligned:
+        shift = 4 // key.element_size()
+        base = torch.empty(key.numel() + shift, dtype=dtype, device="cuda")
+        base[shift:].copy_(key.reshape(-1))
+        key = base[shift:].view(tokens, 4, 128)
     query = (torch.randn(queries, 28, 128, generator=torch.Generator().manual_seed(queries)) * 0.5).to(dtype).cuda()
     scores = kernels.h2o_scores(query, key, None, kv_heads=4, softmax_scale=1 / np.sqrt(128))
     logits = attention.gqa_query_key_logits(host(query).astype(np.float64), host(key).astype(np.float64)) / np.sqrt(128)

@@ -2,6 +2,8 @@
 // dense-cache row compaction.
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 using ucb_host::check_launch;
@@ -297,154 +299,226 @@ __global__ void __launch_bounds__(128) scores_mma_kernel(const __nv_bfloat16* __
 }
 
 // fp32 (or any dtype) on the CUDA cores, for fp32 caches.  Block (x, kv):
-// 64 tokens of KV head kv x 4 row groups (256 threads); a thread holds its
-// token's key row and takes every fourth query row of each 32-row chunk
-// staged in shared memory, four rows per pass (four independent FMA chains);
-// the four groups' sums of a token are added in group order, so the result
-// does not depend on scheduling.  Row offsets of a chunk are formed once per
-// row (one division), not per staged element.
-constexpr int kScoreQ = 32;  // query rows staged per round (a multiple of 16)
-constexpr int kScoreTok = 64, kScoreGroups = 4;
-static_assert(kScoreQ % (4 * kScoreGroups) == 0, "each group takes four rows per pass");
+// Logits of one KV head's query rows against its keys, as register-blocked
+// tiles on the CUDA cores (fp32 arithmetic, for fp32 callers whose scores
+// must keep fp32 accuracy; bf16 inputs are widened exactly).  A 256-thread
+// block holds a 64-row query tile and a 64-token key tile, all 128 channels,
+// in shared memory ([row][channel], 132-float pitch: the 16-byte loads of 8
+// consecutive rows fall in distinct banks).  Thread (ty, tx) = (tid / 16,
+// tid % 16) owns rows ty + 16i and tokens tx + 16j (i, j < 4): 16
+// accumulators, 64 independent FMAs per four channels.  Every logit is one
+// fmaf chain over channels 0..127 in order, the arithmetic of a plain dot
+// product loop.  Query row rr of the head's group (rr = g * queries + q) is
+// query[q, kv * grp + g, :].  Tiles are staged with 16-byte (fp32) or 8-byte
+// (bf16) loads, a warp per row, when every row start is aligned (VEC), else
+// element by element.
+constexpr int kTile = 64, kTileThreads = 256, kTilePitch = 132;
+constexpr int kLseTok = kTile;  // token block of the LSE partials
+constexpr int kTileSmemBytes = 2 * kTile * kTilePitch * 4;
 
-template <typename T>
-__device__ __forceinline__ void stage_rows(const T* __restrict__ query, int64_t queries, int q_heads, int kv,
-                                           int grp, int64_t rows, int64_t base, int nthreads, float (*qs)[128],
-                                           int64_t* qoff) {
-  constexpr int D = 128;
-  if (threadIdx.x < kScoreQ) {
-    const int64_t rr = base + threadIdx.x;
-    qoff[threadIdx.x] = rr < rows ? ((rr % queries) * q_heads + kv * grp + rr / queries) * D : -1;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < kScoreQ * D; i += nthreads) {
-    const int64_t off = qoff[i >> 7];
-    qs[i >> 7][i & (D - 1)] = off >= 0 ? Dtype<T>::to_f(query[off + (i & (D - 1))]) : 0.f;
+// The four channels [4c, 4c + 4) of one row, widened to fp32 (zeros for a
+// missing row: src == nullptr).
+template <typename T, bool VEC>
+__device__ __forceinline__ float4 load_quad(const T* src, int c) {
+  if (src == nullptr) return make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (VEC && sizeof(T) == 4) {
+    return *reinterpret_cast<const float4*>(src + 4 * c);
+  } else if constexpr (VEC) {
+    const uint2 w = *reinterpret_cast<const uint2*>(src + 4 * c);
+    return make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
+  } else {
+    return make_float4(Dtype<T>::to_f(src[4 * c]), Dtype<T>::to_f(src[4 * c + 1]), Dtype<T>::to_f(src[4 * c + 2]),
+                       Dtype<T>::to_f(src[4 * c + 3]));
   }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kScoreTok * kScoreGroups) scores_cuda_core_kernel(
+__device__ __forceinline__ const T* query_row(const T* query, int64_t queries, int q_heads, int kv, int grp,
+                                              int64_t rows, int64_t rr) {
+  if (rr >= rows) return nullptr;
+  return query + ((rr % queries) * q_heads + kv * grp + rr / queries) * 128;
+}
+
+// One thread's eight quads of a 64 x 128 tile (thread tid takes rows tid / 32
+// + 8n, channel quad tid % 32: a warp reads one row), to registers and then
+// to shared memory.
+template <typename T, bool VEC, typename RowFn>
+__device__ __forceinline__ void load_tile_regs(RowFn row_ptr, float4 (&v)[8]) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) v[n] = load_quad<T, VEC>(row_ptr(tid / 32 + 8 * n), tid % 32);
+}
+__device__ __forceinline__ void store_tile_regs(float* tile, const float4 (&v)[8]) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+    *reinterpret_cast<float4*>(tile + (tid / 32 + 8 * n) * kTilePitch + 4 * (tid % 32)) = v[n];
+}
+
+// acc[i][j] = logit of tile row ty + 16i and tile token tx + 16j.
+__device__ __forceinline__ void tile_logits(const float* qs, const float* ks, float (&acc)[4][4]) {
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < 32; ++c) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * kTilePitch + 4 * c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(ks + (tx + 16 * j) * kTilePitch + 4 * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
+        acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
+        acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
+        acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+      }
+  }
+}
+
+// H2O scores from the LSE: a cluster of kScoreCluster blocks owns tokens
+// [64y, 64y + 64) of KV head z; block x of the cluster keeps that key tile in
+// shared memory and walks row tiles x, x + 8, x + 16, ... of the head's query
+// rows (the next tile's rows loading into registers while the current
+// tile's logits run), adding exp(logit * scale - lse[row]) per token.  The 16
+// row groups of a block are added in group order, then rank 0 adds the
+// cluster's eight block sums in rank order through distributed shared
+// memory, so the result does not depend on scheduling.
+constexpr int kScoreCluster = 8;
+template <typename T, bool VEC>
+__global__ void __cluster_dims__(kScoreCluster, 1, 1) __launch_bounds__(kTileThreads) scores_tile_kernel(
     const T* __restrict__ query, int64_t queries, int q_heads, const T* __restrict__ key, int64_t ks_t, int64_t ks_h,
     int64_t tokens, int grp, const float* __restrict__ lse, float scale, float* __restrict__ scores,
     int accumulate) {
-  constexpr int D = 128, THREADS = kScoreTok * kScoreGroups;
-  const int kv = blockIdx.y, tl = threadIdx.x % kScoreTok, rg = threadIdx.x / kScoreTok;
-  const int64_t t = blockIdx.x * (int64_t)kScoreTok + tl;
-  __shared__ float qs[kScoreQ][D];
-  __shared__ float ls[kScoreQ];
-  __shared__ int64_t qoff[kScoreQ];
-  __shared__ float part[kScoreGroups][kScoreTok];
-  float k[D];
-  if (t < tokens) {
-    const T* kr = key + t * ks_t + kv * ks_h;
-#pragma unroll
-    for (int d = 0; d < D; ++d) k[d] = Dtype<T>::to_f(kr[d]);
-  }
-  float total = 0.f;
+  extern __shared__ __align__(16) float tile_smem[];
+  float* qs = tile_smem;
+  float* ks = tile_smem + kTile * kTilePitch;
+  __shared__ float part[16][kTile];
+  __shared__ float block_sum[kTile];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int kv = blockIdx.z, tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int64_t t0 = blockIdx.y * (int64_t)kTile;
   const int64_t rows = (int64_t)grp * queries;
-  for (int64_t base = 0; base < rows; base += kScoreQ) {
-    __syncthreads();
-    stage_rows(query, queries, q_heads, kv, grp, rows, base, THREADS, qs, qoff);
-    if (threadIdx.x < kScoreQ) {
-      const int64_t rr = base + threadIdx.x;
-      ls[threadIdx.x] = rr < rows ? lse[(int64_t)(kv * grp + rr / queries) * queries + rr % queries] : INFINITY;
-    }
-    __syncthreads();
-    if (t < tokens) {
-      for (int j = 4 * rg; j < kScoreQ; j += 4 * kScoreGroups) {
-        float dot[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int64_t kStride = (int64_t)kScoreCluster * kTile;
+  auto lse_of = [&](int64_t rr) {
+    return rr < rows ? lse[(int64_t)(kv * grp + rr / queries) * queries + rr % queries] : INFINITY;
+  };
+  float tot[4] = {0.f, 0.f, 0.f, 0.f};
+  int64_t r0 = (int64_t)rank * kTile;
+  if (r0 < rows) {
+    float4 v[8];
+    load_tile_regs<T, VEC>(
+        [&](int r) -> const T* { return t0 + r < tokens ? key + (t0 + r) * ks_t + kv * ks_h : nullptr; }, v);
+    store_tile_regs(ks, v);
+    load_tile_regs<T, VEC>([&](int r) { return query_row(query, queries, q_heads, kv, grp, rows, r0 + r); }, v);
+    store_tile_regs(qs, v);
+    for (; r0 < rows; r0 += kStride) {
+      float l[4];
 #pragma unroll
-        for (int d = 0; d < D; ++d) {
+      for (int i = 0; i < 4; ++i) l[i] = lse_of(r0 + ty + 16 * i);
+      const int64_t r1 = r0 + kStride;
+      if (r1 < rows)
+        load_tile_regs<T, VEC>([&](int r) { return query_row(query, queries, q_heads, kv, grp, rows, r1 + r); }, v);
+      __syncthreads();  // this tile's rows are in shared memory
+      float acc[4][4];
+      tile_logits(qs, ks, acc);
 #pragma unroll
-          for (int r = 0; r < 4; ++r) dot[r] = fmaf(qs[j + r][d], k[d], dot[r]);
-        }
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) total += expf(dot[r] * scale - ls[j + r]);
-      }
+        for (int j = 0; j < 4; ++j) tot[j] += expf(acc[i][j] * scale - l[i]);
+      __syncthreads();  // every thread is done with this tile's rows
+      if (r1 < rows) store_tile_regs(qs, v);
     }
   }
-  part[rg][tl] = total;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) part[ty][tx + 16 * j] = tot[j];
   __syncthreads();
-  if (rg == 0 && t < tokens) {
+  if (tid < kTile) {
     float sum = 0.f;
 #pragma unroll
-    for (int g = 0; g < kScoreGroups; ++g) sum += part[g][tl];
-    float* o = scores + (int64_t)kv * tokens + t;
+    for (int g = 0; g < 16; ++g) sum += part[g][tid];
+    block_sum[tid] = sum;
+  }
+  cluster.sync();  // every block's sums are visible to the cluster
+  if (rank == 0 && tid < kTile && t0 + tid < tokens) {
+    float sum = 0.f;
+#pragma unroll
+    for (int b = 0; b < kScoreCluster; ++b) sum += *cluster.map_shared_rank(&block_sum[tid], b);
+    float* o = scores + (int64_t)kv * tokens + t0 + tid;
     *o = accumulate ? *o + sum : sum;
   }
+  cluster.sync();  // the peers' shared memory stays alive until rank 0 has read it
 }
 
 // Natural-log normaliser of every (query head, query) row over the given keys
 // (for callers whose attention covers exactly these keys), in two launches.
-// lse_partial_kernel: block (x, kv, z) takes 64 tokens of KV head kv and the
-// z-th 32-row chunk of the head's query group (rows are independent, so the
-// chunks spread over the grid), one thread per token holding its key row;
-// each thread forms its logits (four rows per pass, as the scoring kernel
-// does) and each row's (max, sum of exp) over the block's tokens is reduced
-// by shuffles and across the warps, then stored as the block's partial.  lse_combine_kernel folds the partials
-// of every row over the token blocks: M = max m, L = sum l * exp(m - M),
+// lse_tile_kernel: block (x, y, kv) computes the 64-row x 64-token logit tile
+// (rows 64y.., tokens 64x..) and stores each row's (max, sum of exp) over
+// its tokens as the block's partial (four values per thread, then shuffles
+// across the 16 threads of a row).  lse_combine_kernel folds the partials of
+// every row over the token blocks: M = max m, L = sum l * exp(m - M),
 // lse = M + log(L).
-constexpr int kLseTok = 64;
-template <typename T>
-__global__ void __launch_bounds__(kLseTok) lse_partial_kernel(const T* __restrict__ query, int64_t queries,
-                                                              int q_heads, const T* __restrict__ key, int64_t ks_t,
-                                                              int64_t ks_h, int64_t tokens, int grp, float scale,
-                                                              float2* __restrict__ partial, int token_blocks) {
-  constexpr int D = 128, WARPS = kLseTok / 32;
-  const int kv = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = blockIdx.x * (int64_t)kLseTok + threadIdx.x;
-  const int64_t base = (int64_t)blockIdx.z * kScoreQ;  // this block's 32-row chunk
-  const bool live = t < tokens;
-  __shared__ float qs[kScoreQ][D];
-  __shared__ int64_t qoff[kScoreQ];
-  __shared__ float2 red[kScoreQ][WARPS];
-  float k[D];
-  if (live) {
-    const T* kr = key + t * ks_t + kv * ks_h;
-#pragma unroll
-    for (int d = 0; d < D; ++d) k[d] = Dtype<T>::to_f(kr[d]);
-  }
-  const int64_t rows = (int64_t)grp * queries;  // rr = g * queries + q of this KV head's group
-  stage_rows(query, queries, q_heads, kv, grp, rows, base, kLseTok, qs, qoff);
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kTileThreads) lse_tile_kernel(const T* __restrict__ query, int64_t queries,
+                                                                int q_heads, const T* __restrict__ key, int64_t ks_t,
+                                                                int64_t ks_h, int64_t tokens, int grp, float scale,
+                                                                float2* __restrict__ partial, int token_blocks) {
+  extern __shared__ __align__(16) float tile_smem[];
+  float* qs = tile_smem;
+  float* ks = tile_smem + kTile * kTilePitch;
+  const int kv = blockIdx.z, tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int64_t t0 = blockIdx.x * (int64_t)kTile, r0 = blockIdx.y * (int64_t)kTile;
+  const int64_t rows = (int64_t)grp * queries;
+  float4 v[8];
+  load_tile_regs<T, VEC>(
+      [&](int r) -> const T* { return t0 + r < tokens ? key + (t0 + r) * ks_t + kv * ks_h : nullptr; }, v);
+  store_tile_regs(ks, v);
+  load_tile_regs<T, VEC>([&](int r) { return query_row(query, queries, q_heads, kv, grp, rows, r0 + r); }, v);
+  store_tile_regs(qs, v);
   __syncthreads();
-  for (int j = 0; j < kScoreQ; j += 4) {
-    float dot[4] = {0.f, 0.f, 0.f, 0.f};
-    if (live) {
+  float acc[4][4];
+  tile_logits(qs, ks, acc);
 #pragma unroll
-      for (int d = 0; d < D; ++d) {
+  for (int i = 0; i < 4; ++i) {
+    float sv[4], m = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) dot[r] = fmaf(qs[j + r][d], k[d], dot[r]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      sv[j] = t0 + tx + 16 * j < tokens ? acc[i][j] * scale : -INFINITY;
+      m = fmaxf(m, sv[j]);
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float sv = live ? dot[r] * scale : -INFINITY;
-      float m = sv;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      float l = (m == -INFINITY) ? 0.f : expf(sv - m);
-#pragma unroll
-      for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      if (lane == 0) red[j + r][warp] = make_float2(m, l);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x < kScoreQ && base + threadIdx.x < rows) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) m = fmaxf(m, red[threadIdx.x][w].x);
+    for (int off = 8; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     float l = 0.f;
     if (m != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < WARPS; ++w) {
-        const float2 p = red[threadIdx.x][w];
-        if (p.x != -INFINITY) l += p.y * expf(p.x - m);
-      }
+      for (int j = 0; j < 4; ++j) l += expf(sv[j] - m);
     }
-    const int64_t row = (int64_t)kv * rows + base + threadIdx.x;  // = h * queries + q
-    partial[row * token_blocks + blockIdx.x] = make_float2(m, l);
+#pragma unroll
+    for (int off = 8; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    const int64_t rr = r0 + ty + 16 * i;
+    if (tx == 0 && rr < rows) partial[((int64_t)kv * rows + rr) * token_blocks + blockIdx.x] = make_float2(m, l);
   }
+}
+
+// Shared-memory reservation of the tile kernels, once per device.
+template <typename KernelT>
+int reserve_tile_smem(KernelT kernel, int slot) {
+  static bool done[4][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[slot][dev]) return UCB_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTileSmemBytes) != cudaSuccess)
+    return ucb_host::set_error(UCB_ERR_CUDA, "ucb_h2o_scores: cannot reserve %d bytes of shared memory",
+                               kTileSmemBytes);
+  if (dev >= 0 && dev < 64) done[slot][dev] = true;
+  return UCB_OK;
 }
 
 __global__ void lse_combine_kernel(const float2* __restrict__ partial, int64_t rows, int token_blocks,
@@ -616,19 +690,52 @@ extern "C" int ucb_h2o_scores(const void* query, int dtype, int64_t queries, int
     float2* partial = reinterpret_cast<float2*>(lse_workspace + ((rows + 1) & ~int64_t(1)));
     if (reinterpret_cast<uintptr_t>(lse_workspace) & 7)
       return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: lse_workspace must be 8-byte aligned");
-    const int64_t chunks = ((int64_t)grp * queries + ucb::kScoreQ - 1) / ucb::kScoreQ;
-    if (chunks > 65535) return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: too many query rows per KV head");
-    const dim3 pgrid(static_cast<unsigned>(token_blocks), static_cast<unsigned>(kv_heads),
-                     static_cast<unsigned>(chunks));
-    if (dtype == UCB_BF16)
-      ucb::lse_partial_kernel<__nv_bfloat16><<<pgrid, ucb::kLseTok, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(query), queries, q_heads, static_cast<const __nv_bfloat16*>(key),
-          key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial, token_blocks);
-    else
-      ucb::lse_partial_kernel<float><<<pgrid, ucb::kLseTok, 0, s>>>(
-          static_cast<const float*>(query), queries, q_heads, static_cast<const float*>(key), key_stride_token,
-          key_stride_head, tokens, grp, softmax_scale, partial, token_blocks);
-    int rc = check_launch("lse_partial_kernel");
+    const int64_t row_blocks = ((int64_t)grp * queries + ucb::kTile - 1) / ucb::kTile;
+    if (row_blocks > 65535 || kv_heads > 65535)
+      return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: too many query rows per KV head");
+    const dim3 pgrid(static_cast<unsigned>(token_blocks), static_cast<unsigned>(row_blocks),
+                     static_cast<unsigned>(kv_heads));
+    // quads of four elements load as one 8-byte (bf16) or 16-byte (fp32)
+    // access when every row start is aligned to that size
+    const uintptr_t align_mask = dtype == UCB_BF16 ? 7 : 15;
+    const bool vec = ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key)) & align_mask) == 0 &&
+                     key_stride_token % 4 == 0 && key_stride_head % 4 == 0;
+    int rc = UCB_OK;
+    if (dtype == UCB_BF16) {
+      const auto* qb = static_cast<const __nv_bfloat16*>(query);
+      const auto* kb = static_cast<const __nv_bfloat16*>(key);
+      if (vec) {
+        rc = ucb::reserve_tile_smem(ucb::lse_tile_kernel<__nv_bfloat16, true>, 0);
+        if (!rc)
+          ucb::lse_tile_kernel<__nv_bfloat16, true><<<pgrid, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+              qb, queries, q_heads, kb, key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial,
+              token_blocks);
+      } else {
+        rc = ucb::reserve_tile_smem(ucb::lse_tile_kernel<__nv_bfloat16, false>, 1);
+        if (!rc)
+          ucb::lse_tile_kernel<__nv_bfloat16, false><<<pgrid, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+              qb, queries, q_heads, kb, key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial,
+              token_blocks);
+      }
+    } else {
+      const auto* qf = static_cast<const float*>(query);
+      const auto* kf = static_cast<const float*>(key);
+      if (vec) {
+        rc = ucb::reserve_tile_smem(ucb::lse_tile_kernel<float, true>, 2);
+        if (!rc)
+          ucb::lse_tile_kernel<float, true><<<pgrid, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+              qf, queries, q_heads, kf, key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial,
+              token_blocks);
+      } else {
+        rc = ucb::reserve_tile_smem(ucb::lse_tile_kernel<float, false>, 3);
+        if (!rc)
+          ucb::lse_tile_kernel<float, false><<<pgrid, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+              qf, queries, q_heads, kf, key_stride_token, key_stride_head, tokens, grp, softmax_scale, partial,
+              token_blocks);
+      }
+    }
+    if (rc) return rc;
+    rc = check_launch("lse_tile_kernel");
     if (rc) return rc;
     ucb::lse_combine_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, s>>>(partial, rows, token_blocks,
                                                                                       lse_workspace);
@@ -647,14 +754,26 @@ extern "C" int ucb_h2o_scores(const void* query, int dtype, int64_t queries, int
                                                 softmax_scale * 1.4426950408889634f, scores, accumulate);
     return check_launch("scores_mma_kernel");
   }
-  const dim3 grid64(static_cast<unsigned>((tokens + ucb::kScoreTok - 1) / ucb::kScoreTok),
-                    static_cast<unsigned>(kv_heads));
-  ucb::scores_cuda_core_kernel<float><<<grid64, ucb::kScoreTok * ucb::kScoreGroups, 0, s>>>(
-      static_cast<const float*>(query), queries, q_heads,
-                                                           static_cast<const float*>(key), key_stride_token,
-                                                           key_stride_head, tokens, grp, lse, softmax_scale, scores,
-                                                           accumulate);
-  return check_launch("scores_cuda_core_kernel");
+  const int64_t score_blocks = (tokens + ucb::kTile - 1) / ucb::kTile;
+  if (score_blocks > 65535 || kv_heads > 65535)
+    return set_error(UCB_ERR_INVALID, "ucb_h2o_scores: too many keys for the fp32 scoring grid");
+  const dim3 grid64(ucb::kScoreCluster, static_cast<unsigned>(score_blocks), static_cast<unsigned>(kv_heads));
+  const bool vec = (((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key)) & 15) == 0) &&
+                   key_stride_token % 4 == 0 && key_stride_head % 4 == 0;
+  const auto* qf = static_cast<const float*>(query);
+  const auto* kf = static_cast<const float*>(key);
+  int rc2 = vec ? ucb::reserve_tile_smem(ucb::scores_tile_kernel<float, true>, 0)
+                : ucb::reserve_tile_smem(ucb::scores_tile_kernel<float, false>, 1);
+  if (rc2) return rc2;
+  if (vec)
+    ucb::scores_tile_kernel<float, true><<<grid64, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+        qf, queries, q_heads, kf, key_stride_token, key_stride_head, tokens, grp, lse, softmax_scale, scores,
+        accumulate);
+  else
+    ucb::scores_tile_kernel<float, false><<<grid64, ucb::kTileThreads, ucb::kTileSmemBytes, s>>>(
+        qf, queries, q_heads, kf, key_stride_token, key_stride_head, tokens, grp, lse, softmax_scale, scores,
+        accumulate);
+  return check_launch("scores_tile_kernel");
 }
 
 extern "C" int ucb_h2o_scores_from_lse(const void* query, int64_t queries, int q_heads, const void* key,
