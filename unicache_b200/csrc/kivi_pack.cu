@@ -466,18 +466,86 @@ __global__ void fake_quant_kernel(const T* __restrict__ x, T* __restrict__ out, 
   const int64_t start = gidx * group;
   const int64_t stop = min(length, start + group);
   const int64_t base = o * length * inner + i;
+  // The group's elements are read CH at a time (all CH loads in flight
+  // before the first is used) and folded in element order, as a plain loop
+  // over the group would fold them.
+  constexpr int CH = 16;
   float mn = INFINITY, mx = -INFINITY;
-  for (int64_t l = start; l < stop; ++l) {
-    const float v = ld(x + base + l * inner);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
+  for (int64_t l0 = start; l0 < stop; l0 += CH) {
+    float v[CH];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) v[j] = l0 + j < stop ? ld(x + base + (l0 + j) * inner) : 0.f;
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (l0 + j < stop) {
+        mn = fminf(mn, v[j]);
+        mx = fmaxf(mx, v[j]);
+      }
   }
   // builtin.py:50 clamps the range before dividing (unlike the packed quantizer).
   const float sc = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), FLT_EPSILON), max_code);
-  for (int64_t l = start; l < stop; ++l) {
-    const float v = ld(x + base + l * inner);
-    const float q = static_cast<float>(quant_code(v, mn, sc, max_code));
-    out[base + l * inner] = Dtype<T>::from_f(__fadd_rn(__fmul_rn(q, sc), mn));
+  for (int64_t l0 = start; l0 < stop; l0 += CH) {
+    float v[CH];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) v[j] = l0 + j < stop ? ld(x + base + (l0 + j) * inner) : 0.f;
+#pragma unroll
+    for (int j = 0; j < CH; ++j)
+      if (l0 + j < stop) {
+        const float q = static_cast<float>(quant_code(v[j], mn, sc, max_code));
+        out[base + (l0 + j) * inner] = Dtype<T>::from_f(__fadd_rn(__fmul_rn(q, sc), mn));
+      }
+  }
+}
+
+// Groups of `group` contiguous elements (the quantized dimension is the
+// innermost one and every group is full): one thread per group reads it with
+// 16-byte loads, four in flight at a time, folds min and max in element
+// order and writes the fake-quantized group with 16-byte stores.  Same
+// arithmetic as fake_quant_kernel.  group % (16 / sizeof(T)) == 0 and 16-byte
+// aligned tensors.
+template <typename T>
+__global__ void fake_quant_rows_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t groups, int group,
+                                       float max_code) {
+  constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  constexpr int UNROLL = 4;
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + g * group);
+  uint4* dst = reinterpret_cast<uint4*>(out + g * group);
+  const int vecs = group / EPV;
+  float mn = INFINITY, mx = -INFINITY;
+  for (int c0 = 0; c0 < vecs; c0 += UNROLL) {
+    uint4 w[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) w[u] = c0 + u < vecs ? src[c0 + u] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+      if (c0 + u < vecs) {
+        const T* e = reinterpret_cast<const T*>(&w[u]);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) {
+          const float v = Dtype<T>::to_f(e[j]);
+          mn = fminf(mn, v);
+          mx = fmaxf(mx, v);
+        }
+      }
+  }
+  const float sc = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), FLT_EPSILON), max_code);
+  for (int c0 = 0; c0 < vecs; c0 += UNROLL) {
+    uint4 w[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) w[u] = c0 + u < vecs ? src[c0 + u] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+      if (c0 + u < vecs) {
+        T* e = reinterpret_cast<T*>(&w[u]);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) {
+          const float q = static_cast<float>(quant_code(Dtype<T>::to_f(e[j]), mn, sc, max_code));
+          e[j] = Dtype<T>::from_f(__fadd_rn(__fmul_rn(q, sc), mn));
+        }
+        dst[c0 + u] = w[u];
+      }
   }
 }
 
@@ -759,6 +827,22 @@ extern "C" int ucb_fake_quant(const void* x, void* out, int dtype, int64_t outer
   const int64_t work = outer * n_groups * inner;
   const float max_code = static_cast<float>((1 << bits) - 1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int esize = dtype == UCB_F32 ? 4 : 2;
+  if (inner == 1 && length % group == 0 && group % (16 / esize) == 0 && aligned(x, 16) && aligned(out, 16) &&
+      (dtype == UCB_BF16 || dtype == UCB_F16 || dtype == UCB_F32)) {
+    // contiguous full groups: one thread per group, 16-byte accesses
+    const unsigned blocks = static_cast<unsigned>((work + 127) / 128);
+    if (dtype == UCB_BF16)
+      ucb::fake_quant_rows_kernel<__nv_bfloat16><<<blocks, 128, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), work, group, max_code);
+    else if (dtype == UCB_F16)
+      ucb::fake_quant_rows_kernel<__half><<<blocks, 128, 0, s>>>(static_cast<const __half*>(x),
+                                                                   static_cast<__half*>(out), work, group, max_code);
+    else
+      ucb::fake_quant_rows_kernel<float><<<blocks, 128, 0, s>>>(static_cast<const float*>(x),
+                                                                  static_cast<float*>(out), work, group, max_code);
+    return check_launch("fake_quant_rows_kernel");
+  }
   dim3 grid(static_cast<unsigned>((work + 255) / 256));
   switch (dtype) {
     case UCB_BF16:
