@@ -114,23 +114,54 @@ __global__ void __launch_bounds__(kSelThreads) h2o_select_kernel(const float* __
       const int shift = 24 - 8 * pass;
       for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
       __syncthreads();
-      for (int64_t i = tid; i < history_end; i += kSelThreads) {
-        const uint32_t key = score_key(row[i]);
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      // histogram of the candidates' next byte; the lanes of a warp that share
+      // a bin add once (scores of one row share their high bytes, so plain
+      // per-element atomics would queue on a few bins)
+      for (int64_t base = 0; base < history_end; base += kSelThreads) {
+        const int64_t i = base + tid;
+        const uint32_t key = i < history_end ? score_key(row[i]) : 0u;
+        const bool cand = i < history_end && (key & mask) == prefix;
+        const unsigned active = __ballot_sync(0xffffffffu, cand);
+        if (cand) {
+          const unsigned bin = (key >> shift) & 255u;
+          const unsigned peers = __match_any_sync(active, bin);
+          if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<unsigned>(__popc(peers)));
+        }
       }
       __syncthreads();
-      if (tid == 0) {
-        int64_t cum = 0;
-        int sel = 0;
-        for (int b = 255; b >= 0; --b) {
-          if (cum + hist[b] >= krem) {
-            sel = b;
-            break;
-          }
-          cum += hist[b];
+      if (tid < 32) {
+        // the bin holding the krem-th largest candidate: lane l sums bins
+        // 255 - 8l down to 248 - 8l, a scan over the lanes finds the lane,
+        // then that lane walks its eight bins (as a scan from bin 255 would)
+        const int lane = tid;
+        int64_t own = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) own += hist[255 - 8 * lane - q];
+        int64_t incl = own;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int64_t v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
         }
-        s_prefix = prefix | (static_cast<uint32_t>(sel) << shift);
-        s_krem = krem - cum;
+        const unsigned hit = __ballot_sync(0xffffffffu, incl >= krem);
+        const int first = hit ? __ffs(hit) - 1 : -1;
+        if (first < 0 && lane == 31) {  // not reached for a consistent budget
+          s_prefix = prefix;
+          s_krem = krem - incl;
+        } else if (lane == first) {
+          int64_t cum = incl - own;
+          int sel = 0;
+          for (int q = 0; q < 8; ++q) {
+            const int b = 255 - 8 * lane - q;
+            if (cum + hist[b] >= krem) {
+              sel = b;
+              break;
+            }
+            cum += hist[b];
+          }
+          s_prefix = prefix | (static_cast<uint32_t>(sel) << shift);
+          s_krem = krem - cum;
+        }
       }
       __syncthreads();
       prefix = s_prefix;
