@@ -96,6 +96,12 @@ constexpr int kSelThreads = 1024;
 // One CTA per KV head: radix-select the heavy_k-th largest key of the history
 // (4 passes of 8 bits), then emit, in ascending index order, every index whose
 // key is larger plus the lowest-index entries equal to it.
+// STAGED: the history's keys are read from global memory once into shared
+// memory (history_end * 4 bytes of dynamic shared memory, at most
+// kSelStagedMax keys) and every pass reads them there; otherwise each pass
+// reads the scores again.
+constexpr int64_t kSelStagedMax = 51200;
+template <bool STAGED>
 __global__ void __launch_bounds__(kSelThreads) h2o_select_kernel(const float* __restrict__ scores,
                                                                  int64_t stride, int64_t tokens,
                                                                  int64_t history_end, int64_t heavy_k,
@@ -103,11 +109,17 @@ __global__ void __launch_bounds__(kSelThreads) h2o_select_kernel(const float* __
   const int h = blockIdx.x, tid = threadIdx.x;
   const float* row = scores + h * stride;
   int64_t* orow = out + h * (heavy_k + recent);
+  extern __shared__ uint32_t staged_keys[];
   __shared__ unsigned int hist[256];
   __shared__ uint32_t s_prefix;
   __shared__ int64_t s_krem;
   __shared__ int scan_smem[32];
+  auto key_at = [&](int64_t i) { return STAGED ? staged_keys[i] : score_key(row[i]); };
   if (heavy_k > 0) {
+    if constexpr (STAGED) {
+      for (int64_t i = tid; i < history_end; i += kSelThreads) staged_keys[i] = score_key(row[i]);
+      __syncthreads();
+    }
     uint32_t prefix = 0, mask = 0;
     int64_t krem = heavy_k;
     for (int pass = 0; pass < 4; ++pass) {
@@ -119,7 +131,7 @@ __global__ void __launch_bounds__(kSelThreads) h2o_select_kernel(const float* __
       // per-element atomics would queue on a few bins)
       for (int64_t base = 0; base < history_end; base += kSelThreads) {
         const int64_t i = base + tid;
-        const uint32_t key = i < history_end ? score_key(row[i]) : 0u;
+        const uint32_t key = i < history_end ? key_at(i) : 0u;
         const bool cand = i < history_end && (key & mask) == prefix;
         const unsigned active = __ballot_sync(0xffffffffu, cand);
         if (cand) {
@@ -171,21 +183,32 @@ __global__ void __launch_bounds__(kSelThreads) h2o_select_kernel(const float* __
     }
     const uint32_t thr = prefix;
     const int64_t need_eq = krem;  // entries equal to thr to keep (lowest indices)
-    int64_t eq_carry = 0, out_carry = 0;
-    for (int64_t base = 0; base < history_end; base += kSelThreads) {
-      const int64_t i = base + tid;
-      uint32_t key = 0;
-      const bool in = i < history_end;
-      if (in) key = score_key(row[i]);
-      const int is_eq = (in && key == thr) ? 1 : 0;
-      int eq_total;
-      const int eq_rank = block_exclusive_scan<kSelThreads>(is_eq, scan_smem, eq_total);
-      const int take = (in && (key > thr || (is_eq && eq_carry + eq_rank < need_eq))) ? 1 : 0;
-      int take_total;
-      const int pos = block_exclusive_scan<kSelThreads>(take, scan_smem, take_total);
-      if (take) orow[out_carry + pos] = i;
-      eq_carry += eq_total;
-      out_carry += take_total;
+    // Thread t owns the contiguous slice [t * chunk, (t + 1) * chunk) of the
+    // history: it counts the keys above thr and equal to it, one scan over
+    // the equal counts tells it how many of its equal keys are among the
+    // need_eq lowest-index ones, a second scan over the kept counts gives its
+    // output offset, and it writes its kept indices in ascending order.
+    const int64_t chunk = (history_end + kSelThreads - 1) / kSelThreads;
+    const int64_t lo = min(history_end, tid * chunk), hi = min(history_end, lo + chunk);
+    int n_gt = 0, n_eq = 0;
+    for (int64_t i = lo; i < hi; ++i) {
+      const uint32_t key = key_at(i);
+      n_gt += key > thr;
+      n_eq += key == thr;
+    }
+    int eq_total;
+    const int eq_before = block_exclusive_scan<kSelThreads>(n_eq, scan_smem, eq_total);
+    const int64_t eq_room = need_eq - eq_before;  // equal keys still wanted before this slice
+    const int eq_take = eq_room <= 0 ? 0 : (eq_room < n_eq ? static_cast<int>(eq_room) : n_eq);
+    int take_total;
+    int64_t pos = block_exclusive_scan<kSelThreads>(n_gt + eq_take, scan_smem, take_total);
+    int eq_left = eq_take;
+    for (int64_t i = lo; i < hi; ++i) {
+      const uint32_t key = key_at(i);
+      if (key > thr || (key == thr && eq_left > 0)) {
+        eq_left -= key == thr;
+        orow[pos++] = i;
+      }
     }
   }
   for (int64_t i = tid; i < recent; i += kSelThreads) orow[heavy_k + i] = tokens - recent + i;
@@ -644,8 +667,24 @@ extern "C" int ucb_h2o_select(const float* scores, int64_t score_stride, int hea
     return set_error(UCB_ERR_INVALID, "ucb_h2o_select: inconsistent budget (history_end=%lld heavy=%lld recent=%lld)",
                      (long long)history_end, (long long)heavy_k, (long long)recent);
   if (heavy_k + recent == 0) return UCB_OK;
-  ucb::h2o_select_kernel<<<heads, ucb::kSelThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      scores, score_stride, tokens, history_end, heavy_k, recent, index_out);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (history_end <= ucb::kSelStagedMax) {
+    const int bytes = static_cast<int>(history_end * 4);
+    static bool reserved[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !reserved[dev]) {
+      if (cudaFuncSetAttribute(ucb::h2o_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(ucb::kSelStagedMax * 4)) != cudaSuccess)
+        return set_error(UCB_ERR_CUDA, "ucb_h2o_select: cannot reserve shared memory");
+      if (dev >= 0 && dev < 64) reserved[dev] = true;
+    }
+    ucb::h2o_select_kernel<true><<<heads, ucb::kSelThreads, bytes, s>>>(scores, score_stride, tokens, history_end,
+                                                                       heavy_k, recent, index_out);
+  } else {
+    ucb::h2o_select_kernel<false><<<heads, ucb::kSelThreads, 0, s>>>(scores, score_stride, tokens, history_end,
+                                                                     heavy_k, recent, index_out);
+  }
   return check_launch("h2o_select_kernel");
 }
 
