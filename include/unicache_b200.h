@@ -96,7 +96,7 @@ UCB_API int ucb_kivi_pack_kv(const void* key_dev, const void* value_dev, int dty
  * which packs one segment per call).  A job is, in order: the key side
  * {input, token stride, head stride (int64, elements), codes, scale, minimum}
  * and the value side in the same form, then int32 tokens, key_blocks =
- * ceil(tokens/32 * heads / 4), blocks = key_blocks + ceil(tokens * heads *
+ * ceil(tokens/32 * heads / 2), blocks = key_blocks + ceil(tokens * heads *
  * 128/32 / 256), and one int32 of padding.  Every job satisfies the
  * conditions of ucb_kivi_pack_kv (bf16, head_dim 128, group 32, tokens a
  * multiple of 32, 16-byte-aligned value rows) with the same bits and heads;

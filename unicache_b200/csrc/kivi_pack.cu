@@ -186,6 +186,77 @@ __device__ __forceinline__ void pack_key_item(const T* __restrict__ x, int64_t s
   }
 }
 
+// Group 32 with the two halves of a group on a lane pair: lanes 2p and 2p + 1
+// take rows 0-15 and 16-31 of channel pair p, so a thread holds 16 raw pairs;
+// the halves' packed minimum and maximum are exchanged with one shuffle, both
+// lanes compute the group's statistics (lane 2p stores them) and each writes
+// the codes of its own 16 rows (one word per channel for 2-bit codes).  The
+// codes and statistics are those of pack_key_item<T, BITS, 32>.  Both lanes of
+// a pair must reach this function.
+template <int BITS>
+__device__ __forceinline__ void pack_key_half_item(const __nv_bfloat16* __restrict__ x, int64_t stride_t,
+                                                   int64_t stride_h, int tokens, int head_dim,
+                                                   uint32_t* __restrict__ codes32, uint8_t* __restrict__ codes8,
+                                                   __nv_bfloat16* __restrict__ scale,
+                                                   __nv_bfloat16* __restrict__ minimum, int g, int h, int pair,
+                                                   int half) {
+  using T = __nv_bfloat16;
+  constexpr int G = 32, R = 16;
+  const int d = 2 * pair;
+  const int groups = tokens / G;
+  const T* col = x + (static_cast<int64_t>(g) * G + half * R) * stride_t + h * stride_h + d;
+  uint32_t w[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) w[i] = *reinterpret_cast<const uint32_t*>(col + static_cast<int64_t>(i) * stride_t);
+  uint32_t lo = w[0], hi = w[0];
+#pragma unroll
+  for (int i = 1; i < R; ++i) {
+    lo = min_pair<T>(lo, w[i]);
+    hi = max_pair<T>(hi, w[i]);
+  }
+  const unsigned pair_mask = 3u << ((threadIdx.x & 31) & ~1);
+  lo = min_pair<T>(lo, __shfl_xor_sync(pair_mask, lo, 1));
+  hi = max_pair<T>(hi, __shfl_xor_sync(pair_mask, hi, 1));
+  constexpr float kMax = static_cast<float>((1 << BITS) - 1);
+  const float mna = Dtype<T>::lo(lo), mnb = Dtype<T>::hi(lo);
+  const float sca = quant_scale(mna, Dtype<T>::lo(hi), kMax), scb = quant_scale(mnb, Dtype<T>::hi(hi), kMax);
+  const float2 mn = make_float2(mna, mnb), sc = make_float2(sca, scb);
+  const float2 inv = make_float2(__frcp_rn(sca), __frcp_rn(scb));
+  if (half == 0) {
+    const int64_t stat = (static_cast<int64_t>(h) * groups + g) * head_dim + d;
+    scale[stat] = Dtype<T>::from_f(sca);
+    scale[stat + 1] = Dtype<T>::from_f(scb);
+    minimum[stat] = Dtype<T>::from_f(mna);
+    minimum[stat + 1] = Dtype<T>::from_f(mnb);
+  }
+  const int64_t row0 = static_cast<int64_t>(g) * G + half * R;
+  if constexpr (BITS == 8) {
+    uint8_t* out = codes8 + (static_cast<int64_t>(h) * tokens + row0) * head_dim + d;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const uint2 c = quant_bits2(make_float2(Dtype<T>::lo(w[i]), Dtype<T>::hi(w[i])), mn, sc, inv, kMax);
+      *reinterpret_cast<uint16_t*>(out + static_cast<int64_t>(i) * head_dim) =
+          static_cast<uint16_t>(c.x + (c.y << 8) - round_bias<8, 2>());
+    }
+  } else {
+    constexpr int F = 32 / BITS;
+    uint32_t* out = codes32 + (static_cast<int64_t>(h) * (tokens / F) + row0 / F) * head_dim + d;
+#pragma unroll
+    for (int k = 0; k < R / F; ++k) {
+      uint32_t wa = 0, wb = 0;
+#pragma unroll
+      for (int j = 0; j < F; ++j) {
+        const uint32_t e = w[k * F + j];
+        const uint2 c = quant_bits2(make_float2(Dtype<T>::lo(e), Dtype<T>::hi(e)), mn, sc, inv, kMax);
+        wa += c.x << (j * BITS);
+        wb += c.y << (j * BITS);
+      }
+      *reinterpret_cast<uint2*>(out + static_cast<int64_t>(k) * head_dim) =
+          make_uint2(wa - round_bias<BITS, F>(), wb - round_bias<BITS, F>());
+    }
+  }
+}
+
 template <typename T, int BITS, int G>
 __global__ void __launch_bounds__(64) pack_key_kernel(const T* __restrict__ x, int64_t stride_t,
                                                       int64_t stride_h, int tokens, int head_dim,
@@ -321,13 +392,14 @@ __global__ void __launch_bounds__(256) pack_value_kernel(const T* __restrict__ x
 
 // ---------------------------------------------------------------- fused key + value pack
 // One launch for both halves of PackedKIVICache.from_dense's pack step: blocks
-// [0, key_blocks) quantize keys, four (token group, head) items of 64 channel
-// pairs per 256-thread block; the remaining blocks quantize values, one
-// (token row, channel group) per thread.  Each item runs the same code as the
-// separate kernels, so the results are identical; one launch instead of two
-// saves one launch and one memory ramp per sequence.  Built for group 32
-// only: two 256-thread blocks per SM hold both paths without spilling there
-// (groups 64 and 128 would spill, so they keep the separate kernels).
+// [0, key_blocks) quantize keys, two (token group, head) items per 256-thread
+// block with a lane pair per channel pair (pack_key_half_item); the remaining
+// blocks quantize values, one (token row, channel group) per thread.  The
+// codes and statistics equal the separate kernels'; one launch instead of
+// two saves one launch and one memory ramp per sequence.  Built for group 32
+// only.  Six blocks per SM (40 registers, a 12-byte spill) beat four or five
+// without a spill and eight (32 registers, an 84-byte spill): each thread's
+// load -> reduce -> store pass is latency-bound, so resident warps count most.
 struct PackSide {
   const void* x;
   int64_t stride_t, stride_h;
@@ -337,17 +409,18 @@ struct PackSide {
 };
 
 template <int KB, int VB, int G>
-__global__ void __launch_bounds__(256, 4) pack_kv_kernel(PackSide k, PackSide v, int tokens, int heads, int key_blocks) {
+__global__ void __launch_bounds__(256, 6) pack_kv_kernel(PackSide k, PackSide v, int tokens, int heads, int key_blocks) {
   using T = __nv_bfloat16;
-  constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
+  constexpr int D = 128, LANES = D, ITEMS = 256 / LANES;  // a lane pair per channel pair
+  static_assert(G == 32, "the fused kernels run group 32");
   if (static_cast<int>(blockIdx.x) < key_blocks) {
     const int groups = tokens / G;
-    const int item = blockIdx.x * ITEMS + threadIdx.x / PAIRS;
+    const int item = blockIdx.x * ITEMS + threadIdx.x / LANES;
     if (item >= groups * heads) return;
-    pack_key_item<T, KB, G>(static_cast<const T*>(k.x), k.stride_t, k.stride_h, tokens, D,
-                            static_cast<uint32_t*>(k.codes), static_cast<uint8_t*>(k.codes),
-                            static_cast<T*>(k.scale), static_cast<T*>(k.minimum), item % groups, item / groups,
-                            threadIdx.x % PAIRS);
+    pack_key_half_item<KB>(static_cast<const T*>(k.x), k.stride_t, k.stride_h, tokens, D,
+                           static_cast<uint32_t*>(k.codes), static_cast<uint8_t*>(k.codes),
+                           static_cast<T*>(k.scale), static_cast<T*>(k.minimum), item % groups, item / groups,
+                           (threadIdx.x % LANES) >> 1, threadIdx.x & 1);
   } else {
     const int64_t item = static_cast<int64_t>(blockIdx.x - key_blocks) * 256 + threadIdx.x;
     pack_value_item<T, VB, D, G, true>(static_cast<const T*>(v.x), v.stride_t, v.stride_h, tokens, heads,
@@ -366,20 +439,21 @@ struct PackJob {
 };
 
 template <int KB, int VB, int G>
-__global__ void __launch_bounds__(256, 4) pack_kv_batched_kernel(const PackJob* __restrict__ jobs, int heads) {
+__global__ void __launch_bounds__(256, 6) pack_kv_batched_kernel(const PackJob* __restrict__ jobs, int heads) {
   using T = __nv_bfloat16;
-  constexpr int D = 128, PAIRS = D / 2, ITEMS = 256 / PAIRS;
+  constexpr int D = 128, LANES = D, ITEMS = 256 / LANES;  // a lane pair per channel pair
+  static_assert(G == 32, "the fused kernels run group 32");
   const PackJob& j = jobs[blockIdx.y];
   const int b = static_cast<int>(blockIdx.x);
   if (b >= j.blocks) return;
   if (b < j.key_blocks) {
     const int groups = j.tokens / G;
-    const int item = b * ITEMS + threadIdx.x / PAIRS;
+    const int item = b * ITEMS + threadIdx.x / LANES;
     if (item >= groups * heads) return;
-    pack_key_item<T, KB, G>(static_cast<const T*>(j.k.x), j.k.stride_t, j.k.stride_h, j.tokens, D,
-                            static_cast<uint32_t*>(j.k.codes), static_cast<uint8_t*>(j.k.codes),
-                            static_cast<T*>(j.k.scale), static_cast<T*>(j.k.minimum), item % groups, item / groups,
-                            threadIdx.x % PAIRS);
+    pack_key_half_item<KB>(static_cast<const T*>(j.k.x), j.k.stride_t, j.k.stride_h, j.tokens, D,
+                           static_cast<uint32_t*>(j.k.codes), static_cast<uint8_t*>(j.k.codes),
+                           static_cast<T*>(j.k.scale), static_cast<T*>(j.k.minimum), item % groups, item / groups,
+                           (threadIdx.x % LANES) >> 1, threadIdx.x & 1);
   } else {
     const int64_t item = static_cast<int64_t>(b - j.key_blocks) * 256 + threadIdx.x;
     pack_value_item<T, VB, D, G, true>(static_cast<const T*>(j.v.x), j.v.stride_t, j.v.stride_h, j.tokens, heads,
@@ -773,7 +847,7 @@ extern "C" int ucb_kivi_pack_kv(const void* key, const void* value, int dtype, i
     return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv: problem too large");
   const ucb::PackSide k{key, key_stride_token, key_stride_head, key_codes, key_scale, key_minimum};
   const ucb::PackSide v{value, value_stride_token, value_stride_head, value_codes, value_scale, value_minimum};
-  const int key_blocks = static_cast<int>(((tokens / group_size) * heads + 3) / 4);
+  const int key_blocks = static_cast<int>(((tokens / group_size) * heads + 1) / 2);
   const int64_t value_items = tokens * heads * (head_dim / group_size);
   const int64_t blocks = key_blocks + (value_items + 255) / 256;
   if (blocks > 0x7fffffffLL) return set_error(UCB_ERR_INVALID, "ucb_kivi_pack_kv: problem too large");

@@ -166,7 +166,7 @@ class KiviPackBatch:
             job.v = _capi.UcbPackSide(value.data_ptr(), value.stride(0), value.stride(1), vc.data_ptr(),
                                       vs.data_ptr(), vm.data_ptr())
             job.tokens = tokens
-            job.key_blocks = -(-(tokens // 32) * heads // 4)
+            job.key_blocks = -(-(tokens // 32) * heads // 2)
             job.blocks = job.key_blocks + -(-tokens * heads * 4 // 256)
             max_blocks = max(max_blocks, job.blocks)
             jobs.append(job)
