@@ -35,7 +35,15 @@ def require_cuda(tensor: torch.Tensor, name: str) -> None:
         raise RuntimeError(f"{name} must be a CUDA tensor: the b200 backend has no CPU path")
 
 
+# The current stream's raw handle without building a torch Stream object
+# (0.15 vs 2.25 us per call on the B200 hosts; torch's generated code reads
+# it the same way), with the public call where that accessor is missing.
+_current_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(tensor: torch.Tensor) -> int:
+    if _current_raw_stream is not None:
+        return _current_raw_stream(tensor.device.index)
     return torch.cuda.current_stream(tensor.device).cuda_stream
 
 
